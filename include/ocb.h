@@ -1,0 +1,100 @@
+/*
+ * ocb.h -- C ABI of the B200 batch compiler for OpenCUDA's CUDA-C subset.
+ *
+ * The reference compiler (garrick247/opencuda) is a single-threaded Python
+ * program; its only "operator API" is five module functions plus the CLI.
+ * This header exports the batch forms of those functions.  Every entry point
+ * takes plain pointers and sizes; no exceptions cross the ABI: an `int`
+ * return of 0 means success, a negative value an API or CUDA error (text via
+ * ocb_last_error), and each translation unit (TU) carries its own status.
+ *
+ * A batch is one byte buffer holding every TU back to back plus an offset
+ * array `tu_off` of n_tu+1 entries: TU i is bytes [tu_off[i], tu_off[i+1]).
+ *
+ * Threading: one ocb_ctx per (host thread, GPU).  Contexts are independent;
+ * sharing one between threads needs external locking.
+ */
+#ifndef OCB_H
+#define OCB_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- per-TU status ------------------------------------------------------ */
+#define OCB_TU_OK                 0
+/* 1..0xFF: the reference raises on this TU; the value names the class.     */
+#define OCB_TU_RAISES_VALUEERROR  1   /* ValueError    (e.g. float.fromhex) */
+#define OCB_TU_RAISES_OVERFLOW    2   /* OverflowError (hex float too big)  */
+#define OCB_TU_RAISES_PARSEERROR  3   /* opencuda ParseError                */
+#define OCB_TU_RAISES_KEYERROR    4
+#define OCB_TU_RAISES_REERROR     5   /* re.error from macro templates      */
+#define OCB_TU_RAISES_OTHER       6
+/* the engine cannot reproduce the reference on this TU                     */
+#define OCB_TU_UNSUPPORTED        0x100
+/* a per-TU arena was too small                                             */
+#define OCB_TU_OVERFLOW           0x200
+/* a device loop hit its iteration cap                                      */
+#define OCB_TU_TIMEOUT            0x300
+
+/* ---- token record layout (lexer output) --------------------------------- */
+/* kindlen = kind << 24 | min(len, 0xFFFFFF).  kind is the numeric value of
+ * the reference's TokKind (opencuda/frontend/lexer.py:11-109); a hex-float
+ * literal has OCB_TOK_HEXFLOAT or-ed into its kind byte (its reference value
+ * is str(float.fromhex(span)), lexer.py:282-284).  start is the byte offset
+ * of the token in the batch buffer; line is the reference's Token.line.
+ * Each TU's token list ends with an EOF token (kind 88, length 0). */
+#define OCB_TOK_HEXFLOAT 0x80
+#define OCB_TOK_EOF      88
+
+typedef struct ocb_ctx ocb_ctx;
+typedef struct ocb_tokens ocb_tokens;
+
+/* Create a context on CUDA device `device`.  flags: reserved, pass 0.
+ * Replaces: nothing (the reference keeps no device state). */
+int  ocb_create(ocb_ctx **out, int device, uint32_t flags);
+void ocb_destroy(ocb_ctx *ctx);
+/* Last error text of this context (valid until the next call on it). */
+const char *ocb_last_error(ocb_ctx *ctx);
+/* Library build string (architecture, version). */
+const char *ocb_version(void);
+
+/* ---- lexer -------------------------------------------------------------- */
+/* Lex every TU of a host batch.  Replaces opencuda/frontend/lexer.py:258
+ * lex(source) -> list[Token], applied to each TU.  Inputs are copied to the
+ * device (directly when `src` is pinned); the result holds host copies and is
+ * owned by the library until ocb_tokens_free.  TU status is
+ * OCB_TU_RAISES_VALUEERROR/OVERFLOW when the reference's lex() raises on a
+ * hex float of that TU. */
+int  ocb_lex_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                   uint32_t n_tu, ocb_tokens **out);
+/* Host views of a token result: arrays of *n_tok entries (tu_tok_off and
+ * status: n_tu+1 and n_tu entries). */
+int  ocb_tokens_view(const ocb_tokens *t, uint64_t *n_tok,
+                     const uint32_t **start, const uint32_t **kindlen,
+                     const uint32_t **line, const uint64_t **tu_tok_off,
+                     const int32_t **status);
+void ocb_tokens_free(ocb_tokens *t);
+
+/* Device-resident form of ocb_lex_batch: every pointer is device memory
+ * (d_src 16-byte aligned), the work is queued on `stream` (a cudaStream_t,
+ * 0 = the legacy default stream) and the call does not synchronise.  Output
+ * arrays hold `tok_cap` tokens (d_line may be NULL); *d_n_tok (device, one
+ * uint64) receives the token count.  If the count exceeds tok_cap, no token
+ * is written beyond the capacity and the caller re-runs with larger buffers.
+ * Scratch memory is owned by the context and reused across calls.
+ * Replaces: lexer.py:258 lex(), batched. */
+int  ocb_lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
+                    const uint64_t *d_tu_off, uint32_t n_tu,
+                    uint32_t *d_start, uint32_t *d_kindlen, uint32_t *d_line,
+                    uint64_t tok_cap, uint64_t *d_tu_tok_off,
+                    int32_t *d_status, uint64_t *d_n_tok, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OCB_H */

@@ -1,0 +1,55 @@
+"""ctypes binding of ``libocb.so`` (the C ABI declared in ``include/ocb.h``).
+
+There is no CPU fallback: importing the product API without a built library,
+or calling it without a CUDA device, raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libocb.so"
+
+c_void_p = ctypes.c_void_p
+c_u32 = ctypes.c_uint32
+c_u64 = ctypes.c_uint64
+c_int = ctypes.c_int
+P = ctypes.POINTER
+
+# (name, restype, argtypes) for every symbol of include/ocb.h
+SIGNATURES = [
+    ("ocb_version", ctypes.c_char_p, []),
+    ("ocb_create", c_int, [P(c_void_p), c_int, c_u32]),
+    ("ocb_destroy", None, [c_void_p]),
+    ("ocb_last_error", ctypes.c_char_p, [c_void_p]),
+    ("ocb_lex_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
+    ("ocb_tokens_view", c_int, [c_void_p, P(c_u64), P(c_void_p), P(c_void_p),
+                                P(c_void_p), P(c_void_p), P(c_void_p)]),
+    ("ocb_tokens_free", None, [c_void_p]),
+    ("ocb_lex_device", c_int, [c_void_p, c_void_p, c_u64, c_void_p, c_u32,
+                               c_void_p, c_void_p, c_void_p, c_u64, c_void_p,
+                               c_void_p, c_void_p, c_void_p]),
+]
+
+_lib = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load ``libocb.so`` (raises LibraryMissing when it was never built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.is_file():
+        raise LibraryMissing(
+            f"{LIB_PATH} is missing: build it with `python -m opencuda_b200.build`")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, res, args in SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib

@@ -1,0 +1,167 @@
+// C ABI entry points (include/ocb.h): contexts, host-buffer wrappers around
+// the device pipelines, result objects.
+#include <cstring>
+#include <new>
+#include "ocb_internal.h"
+
+namespace ocb {
+
+int fail(ocb_ctx *ctx, const char *what, cudaError_t e) {
+    if (ctx) {
+        ctx->err = what;
+        ctx->err += ": ";
+        ctx->err += cudaGetErrorString(e);
+    }
+    return -(int)(e ? e : 1);
+}
+
+int fail(ocb_ctx *ctx, const std::string &msg) {
+    if (ctx) ctx->err = msg;
+    return -1;
+}
+
+}  // namespace ocb
+
+using namespace ocb;
+
+extern "C" {
+
+const char *ocb_version(void) {
+    return "opencuda-b200 0.1 (sm_100a)";
+}
+
+int ocb_create(ocb_ctx **out, int device, uint32_t flags) {
+    (void)flags;
+    if (!out) return -1;
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return -(int)e;
+    if (device < 0 || device >= n) return -1;
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return -(int)e;
+    ocb_ctx *ctx = new (std::nothrow) ocb_ctx();
+    if (!ctx) return -1;
+    ctx->device = device;
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return -(int)e;
+    }
+    *out = ctx;
+    return 0;
+}
+
+void ocb_destroy(ocb_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (DevBuf *b : {&ctx->lex_scratch, &ctx->cub_tmp, &ctx->d_src, &ctx->d_tu_off,
+                      &ctx->d_tok_start, &ctx->d_tok_kl, &ctx->d_tok_line, &ctx->d_tu_tok,
+                      &ctx->d_status, &ctx->d_count})
+        b->release();
+    ctx->h_stage.release();
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+const char *ocb_last_error(ocb_ctx *ctx) {
+    return ctx ? ctx->err.c_str() : "null context";
+}
+
+int ocb_lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes, const uint64_t *d_tu_off,
+                   uint32_t n_tu, uint32_t *d_start, uint32_t *d_kindlen, uint32_t *d_line,
+                   uint64_t tok_cap, uint64_t *d_tu_tok_off, int32_t *d_status, uint64_t *d_n_tok,
+                   void *stream) {
+    if (!ctx) return -1;
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
+    return lex_device(ctx, d_src, n_bytes, d_tu_off, n_tu, d_start, d_kindlen, d_line, tok_cap,
+                      d_tu_tok_off, d_status, d_n_tok, (cudaStream_t)stream);
+}
+
+int ocb_lex_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                  ocb_tokens **out) {
+    if (!ctx || !out || !tu_off) return fail(ctx, "ocb_lex_batch: null argument");
+    *out = nullptr;
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    if (tu_off[0] != 0) return fail(ctx, "ocb_lex_batch: tu_off[0] must be 0");
+    for (uint32_t i = 0; i < n_tu; ++i)
+        if (tu_off[i + 1] < tu_off[i]) return fail(ctx, "ocb_lex_batch: tu_off not monotone");
+    uint64_t N = tu_off[n_tu];
+    if (N && !src) return fail(ctx, "ocb_lex_batch: null source");
+    // host -> device: straight from the caller's buffer when it is pinned,
+    // else through the context's pinned staging buffer
+    const uint8_t *hs = src;
+    cudaPointerAttributes pa;
+    if (N && (cudaPointerGetAttributes(&pa, src) != cudaSuccess || pa.type != cudaMemoryTypeHost)) {
+        cudaGetLastError();  // clear a failed attribute query
+        OCB_TRY("pinned staging", ctx->h_stage.ensure(N));
+        memcpy(ctx->h_stage.p, src, N);
+        hs = ctx->h_stage.as<uint8_t>();
+    }
+    OCB_TRY("device source", ctx->d_src.ensure(N + 64));
+    OCB_TRY("device offsets", ctx->d_tu_off.ensure(8 * (size_t)(n_tu + 1)));
+    if (N) OCB_TRY("h2d source", cudaMemcpyAsync(ctx->d_src.p, hs, N, cudaMemcpyHostToDevice, st));
+    OCB_TRY("h2d offsets", cudaMemcpyAsync(ctx->d_tu_off.p, tu_off, 8 * (size_t)(n_tu + 1),
+                                           cudaMemcpyHostToDevice, st));
+    uint64_t cap = N + n_tu + 1;
+    OCB_TRY("device tokens", ctx->d_tok_start.ensure(4 * cap));
+    OCB_TRY("device tokens", ctx->d_tok_kl.ensure(4 * cap));
+    OCB_TRY("device tokens", ctx->d_tok_line.ensure(4 * cap));
+    OCB_TRY("device tu offsets", ctx->d_tu_tok.ensure(8 * (size_t)(n_tu + 1)));
+    OCB_TRY("device status", ctx->d_status.ensure(4 * (size_t)n_tu + 4));
+    OCB_TRY("device count", ctx->d_count.ensure(8));
+    int rc = lex_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(), n_tu,
+                        ctx->d_tok_start.as<uint32_t>(), ctx->d_tok_kl.as<uint32_t>(),
+                        ctx->d_tok_line.as<uint32_t>(), cap, ctx->d_tu_tok.as<uint64_t>(),
+                        ctx->d_status.as<int32_t>(), ctx->d_count.as<uint64_t>(), st);
+    if (rc) return rc;
+    uint64_t n_tok = 0;
+    OCB_TRY("d2h count", cudaMemcpyAsync(&n_tok, ctx->d_count.p, 8, cudaMemcpyDeviceToHost, st));
+    OCB_TRY("lex sync", cudaStreamSynchronize(st));
+    if (n_tok > cap) return fail(ctx, "ocb_lex_batch: token capacity exceeded");
+    ocb_tokens *t = new (std::nothrow) ocb_tokens();
+    if (!t) return fail(ctx, "ocb_lex_batch: out of host memory");
+    t->n_tok = n_tok;
+    t->n_tu = n_tu;
+    t->start.resize(n_tok);
+    t->kindlen.resize(n_tok);
+    t->line.resize(n_tok);
+    t->tu_tok_off.resize((size_t)n_tu + 1);
+    t->status.resize(n_tu);
+    cudaError_t e = cudaSuccess;
+    if (n_tok) {
+        e = cudaMemcpyAsync(t->start.data(), ctx->d_tok_start.p, 4 * n_tok, cudaMemcpyDeviceToHost, st);
+        if (!e) e = cudaMemcpyAsync(t->kindlen.data(), ctx->d_tok_kl.p, 4 * n_tok, cudaMemcpyDeviceToHost, st);
+        if (!e) e = cudaMemcpyAsync(t->line.data(), ctx->d_tok_line.p, 4 * n_tok, cudaMemcpyDeviceToHost, st);
+    }
+    if (!e) e = cudaMemcpyAsync(t->tu_tok_off.data(), ctx->d_tu_tok.p, 8 * ((size_t)n_tu + 1),
+                                cudaMemcpyDeviceToHost, st);
+    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->d_status.p, 4 * (size_t)n_tu,
+                                        cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    if (e) {
+        delete t;
+        return fail(ctx, "d2h tokens", e);
+    }
+    *out = t;
+    return 0;
+}
+
+int ocb_tokens_view(const ocb_tokens *t, uint64_t *n_tok, const uint32_t **start,
+                    const uint32_t **kindlen, const uint32_t **line, const uint64_t **tu_tok_off,
+                    const int32_t **status) {
+    if (!t) return -1;
+    if (n_tok) *n_tok = t->n_tok;
+    if (start) *start = t->start.data();
+    if (kindlen) *kindlen = t->kindlen.data();
+    if (line) *line = t->line.data();
+    if (tu_tok_off) *tu_tok_off = t->tu_tok_off.data();
+    if (status) *status = t->status.data();
+    return 0;
+}
+
+void ocb_tokens_free(ocb_tokens *t) { delete t; }
+
+}  // extern "C"

@@ -1,0 +1,94 @@
+// Internal host-side declarations shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+#include <vector>
+#include "../../include/ocb.h"
+
+namespace ocb {
+
+// Grow-only device allocation owned by a context.
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap && p) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    template <class T> T *as() const { return static_cast<T *>(p); }
+};
+
+// Grow-only pinned host allocation.
+struct HostBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap && p) return cudaSuccess;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        cudaError_t e = cudaMallocHost(&p, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+    }
+    template <class T> T *as() const { return static_cast<T *>(p); }
+};
+
+}  // namespace ocb
+
+struct ocb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    // lexer scratch
+    ocb::DevBuf lex_scratch, cub_tmp;
+    // staging for host-buffer entry points
+    ocb::DevBuf d_src, d_tu_off, d_tok_start, d_tok_kl, d_tok_line, d_tu_tok,
+        d_status, d_count;
+    ocb::HostBuf h_stage;
+    bool kw_ready = false;
+};
+
+struct ocb_tokens {
+    uint64_t n_tok = 0;
+    uint32_t n_tu = 0;
+    std::vector<uint32_t> start, kindlen, line;
+    std::vector<uint64_t> tu_tok_off;
+    std::vector<int32_t> status;
+};
+
+namespace ocb {
+int fail(ocb_ctx *ctx, const char *what, cudaError_t e);
+int fail(ocb_ctx *ctx, const std::string &msg);
+
+// Lexer pipeline on device buffers (lex.cu).
+int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
+               const uint64_t *d_tu_off, uint32_t n_tu, uint32_t *d_start,
+               uint32_t *d_kindlen, uint32_t *d_line, uint64_t tok_cap,
+               uint64_t *d_tu_tok_off, int32_t *d_status, uint64_t *d_n_tok,
+               cudaStream_t stream);
+}  // namespace ocb
+
+#define OCB_TRY(what, expr)                                    \
+    do {                                                       \
+        cudaError_t e_ = (expr);                               \
+        if (e_ != cudaSuccess) return ocb::fail(ctx, what, e_); \
+    } while (0)
