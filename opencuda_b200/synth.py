@@ -302,18 +302,32 @@ def _stress_pool(seed: int, n_lines: int) -> list[str]:
     return lines
 
 
+PART_BYTES = 256 << 20
+
+
 def lexstress_batch(total_bytes: int = 1 << 30, tu_bytes: int = 16384,
                     seed: int = 99, pool_lines: int = 200_000):
     """Stress text as (buffer bytes, tu_off int64[n+1]).
 
     TUs are assembled from a seeded pool of lines so that a GiB builds in
     seconds; each TU is cut at a line boundary once it reaches ``tu_bytes``.
+    Batches above 256 MiB are built as independent 256 MiB parts (seeds
+    seed, seed+1, ...), each larger than the GPU's L2.
     """
+    if total_bytes > PART_BYTES:
+        bufs, offs, base = [], [np.zeros(1, np.int64)], 0
+        left, k = total_bytes, 0
+        while left > 0:
+            b, o = lexstress_batch(min(left, PART_BYTES), tu_bytes, seed + k, pool_lines)
+            bufs.append(b)
+            offs.append(o[1:] + base)
+            base += len(b)
+            left -= PART_BYTES
+            k += 1
+        return b"".join(bufs), np.concatenate(offs)
     pool = _stress_pool(seed, pool_lines)
     enc = [(l + "\n").encode() for l in pool]
     lens = np.array([len(e) for e in enc], dtype=np.int64)
-    blob = np.frombuffer(b"".join(enc), dtype=np.uint8)
-    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
     rs = np.random.default_rng(seed)
     mean = float(lens.mean())
     n_pick = int(total_bytes / mean * 1.02) + 16
@@ -323,24 +337,8 @@ def lexstress_batch(total_bytes: int = 1 << 30, tu_bytes: int = 16384,
     n_keep = int(np.searchsorted(cum, total_bytes, side="right"))
     pick, plen, cum = pick[:n_keep], plen[:n_keep], cum[:n_keep]
     total = int(cum[-1]) if n_keep else 0
-    # Gather the picked lines into one buffer, a chunk of lines at a time
-    # (index arrays stay small), grouping equal lengths for fancy indexing.
-    out = np.empty(total, dtype=np.uint8)
-    dst_all = np.concatenate([[0], cum[:-1]]).astype(np.int64)
-    src_all = starts[pick].astype(np.int64)
-    CH = 1 << 18
-    for c0 in range(0, n_keep, CH):
-        plc = plen[c0:c0 + CH]
-        order = np.argsort(plc, kind="stable")
-        bounds = np.flatnonzero(np.diff(plc[order])) + 1
-        for grp in np.split(order, bounds):
-            if len(grp) == 0:
-                continue
-            L = int(plc[grp[0]])
-            ar = np.arange(L, dtype=np.int64)[None, :]
-            idx_src = src_all[c0 + grp][:, None] + ar
-            idx_dst = dst_all[c0 + grp][:, None] + ar
-            out[idx_dst.ravel()] = blob[idx_src.ravel()]
+    # Gather the picked lines into one buffer.
+    out = b"".join(map(enc.__getitem__, pick.tolist()))
     # TU cuts at the first line end at or past each tu_bytes boundary.
     cuts = [0]
     target = tu_bytes
@@ -354,7 +352,7 @@ def lexstress_batch(total_bytes: int = 1 << 30, tu_bytes: int = 16384,
         cuts.append(c)
         target = c + tu_bytes
     cuts.append(total)
-    return out.tobytes(), np.array(cuts, dtype=np.int64)
+    return out, np.array(cuts, dtype=np.int64)
 
 
 # --------------------------------------------------------------------------
