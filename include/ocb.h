@@ -93,6 +93,27 @@ int  ocb_lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
                     uint64_t tok_cap, uint64_t *d_tu_tok_off,
                     int32_t *d_status, uint64_t *d_n_tok, void *stream);
 
+/* Allocation-free form of ocb_lex_device, for callers that may not allocate
+ * device memory when they lex (a framework's memory pool or a fixed arena that
+ * forbids cudaMalloc/cudaFree after start-up, or a thread that must not take
+ * the allocator's lock).  It needs no context: all scratch lives in one 8 MiB
+ * device array inside libocb.so, which every GPU that loads the library holds
+ * until the process exits.  Limits: n_bytes <= 4 MiB and n_tu <= 16384;
+ * larger batches are rejected with -2 before any work is queued.  Arguments
+ * and outputs are those of ocb_lex_device (device pointers, work queued on
+ * `stream`, no synchronisation); `err` (may be NULL) receives a message of at
+ * most err_len-1 bytes on failure.  The first call on a device does a one-time
+ * set-up with that device current (the array's device address and the keyword
+ * table); make that first call before any stream capture.  Every call shares
+ * the one array, so calls whose work overlaps on the GPU (other streams, other
+ * host threads) race: serialise them.  No counterpart in the reference. */
+int  ocb_lex_device_static(const uint8_t *d_src, uint64_t n_bytes,
+                           const uint64_t *d_tu_off, uint32_t n_tu,
+                           uint32_t *d_start, uint32_t *d_kindlen, uint32_t *d_line,
+                           uint64_t tok_cap, uint64_t *d_tu_tok_off,
+                           int32_t *d_status, uint64_t *d_n_tok, void *stream,
+                           char *err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif
