@@ -136,28 +136,33 @@ struct Src {
     __device__ __forceinline__ uint32_t operator[](uint64_t i) const { return __ldg(s + i); }
 };
 
-__device__ __forceinline__ uint64_t run_digits(Src s, uint64_t q, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t run_digits(S s, uint64_t q, uint64_t e) {
     uint64_t r = q;
     while (r < e && is_dig(s[r])) r++;
     return r - q;
 }
-__device__ __forceinline__ uint64_t run_hex(Src s, uint64_t q, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t run_hex(S s, uint64_t q, uint64_t e) {
     uint64_t r = q;
     while (r < e && is_hex(s[r])) r++;
     return r - q;
 }
 // [cC][+-]?[0-9]+ with c the lower-case exponent letter
-__device__ __forceinline__ uint64_t match_exp(Src s, uint64_t q, uint64_t e, uint32_t c) {
+template <class S>
+__device__ __forceinline__ uint64_t match_exp(S s, uint64_t q, uint64_t e, uint32_t c) {
     if (q >= e || (s[q] | 0x20u) != c) return 0;
     uint64_t r = q + 1;
     if (r < e && (s[r] == '+' || s[r] == '-')) r++;
     uint64_t d = run_digits(s, r, e);
     return d ? r + d - q : 0;
 }
-__device__ __forceinline__ uint64_t opt_fF(Src s, uint64_t q, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t opt_fF(S s, uint64_t q, uint64_t e) {
     return (q < e && (s[q] | 0x20u) == 'f') ? 1 : 0;
 }
-__device__ __forceinline__ uint64_t opt_fFlL(Src s, uint64_t q, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t opt_fFlL(S s, uint64_t q, uint64_t e) {
     if (q >= e) return 0;
     uint32_t c = s[q] | 0x20u;
     return (c == 'f' || c == 'l') ? 1 : 0;
@@ -166,7 +171,8 @@ __device__ __forceinline__ uint64_t opt_fFlL(Src s, uint64_t q, uint64_t e) {
 // Keyword perfect hash: (3*L + 47*s[0] + 16*s[L-1] + s[min(2,L-1)]) mod 128
 // is collision-free over the 45 spellings of _KEYWORDS (lexer.py:120-166).
 struct KwEntry { char w[16]; uint8_t len; uint8_t kind; };
-__device__ __forceinline__ uint32_t kw_hash(Src s, uint64_t p, uint64_t L) {
+template <class S>
+__device__ __forceinline__ uint32_t kw_hash(S s, uint64_t p, uint64_t L) {
     uint32_t c0 = s[p], cl = s[p + L - 1], c2 = s[p + (L > 2 ? 2 : L - 1)];
     return (3u * (uint32_t)L + 47u * c0 + 16u * cl + c2) & 127u;
 }

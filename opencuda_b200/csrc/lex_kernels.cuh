@@ -234,7 +234,8 @@ k_lex_sync(const uint8_t *__restrict__ src, uint64_t N, const uint64_t *__restri
 // Verdict of float.fromhex on a hex-float token (lexer.py:282-284):
 // 0 ok, 1 ValueError (no digit either side of the point), 2 OverflowError
 // (the value rounds, half to even at 53 bits, to 2**1024 or more).
-__device__ __noinline__ uint32_t hexfloat_verdict(Src s, uint64_t p, uint64_t n) {
+template <class S>
+__device__ __noinline__ uint32_t hexfloat_verdict(S s, uint64_t p, uint64_t n) {
     uint64_t q = p + 2, end = p + n, i0 = q;
     while (q < end && is_hex(s[q])) q++;
     uint64_t ni = q - i0, f0 = q, nf = 0;
@@ -282,7 +283,8 @@ __device__ __noinline__ uint32_t hexfloat_verdict(Src s, uint64_t p, uint64_t n)
     return bits >= 54 ? 2 : 0;
 }
 
-__device__ __forceinline__ uint64_t match_hexfloat(Src s, uint64_t p, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t match_hexfloat(S s, uint64_t p, uint64_t e) {
     if (p + 1 >= e || s[p] != '0' || (s[p + 1] | 0x20u) != 'x') return 0;
     uint64_t q = p + 2, h = run_hex(s, q, e);
     if (q + h < e && s[q + h] == '.') {
@@ -298,7 +300,8 @@ __device__ __forceinline__ uint64_t match_hexfloat(Src s, uint64_t p, uint64_t e
     return 0;
 }
 
-__device__ __forceinline__ uint64_t match_float(Src s, uint64_t p, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t match_float(S s, uint64_t p, uint64_t e) {
     uint64_t d = run_digits(s, p, e);
     bool dot = p + d < e && s[p + d] == '.';
     if (dot) {
@@ -317,7 +320,8 @@ __device__ __forceinline__ uint64_t match_float(Src s, uint64_t p, uint64_t e) {
     return 0;
 }
 
-__device__ __forceinline__ uint64_t run_ul(Src s, uint64_t q, uint64_t e) {
+template <class S>
+__device__ __forceinline__ uint64_t run_ul(S s, uint64_t q, uint64_t e) {
     uint64_t r = q;
     while (r < e) {
         uint32_t c = s[r] | 0x20u;
@@ -333,7 +337,8 @@ struct Match {
     uint64_t len;
 };
 
-__device__ Match lex_one(Src s, uint64_t p, uint64_t e, const KwEntry *kw) {
+template <class S>
+__device__ Match lex_one(S s, uint64_t p, uint64_t e, const KwEntry *kw) {
     uint32_t c = s[p];
     uint32_t c1 = p + 1 < e ? s[p + 1] : 0x100u;
     uint32_t c2 = p + 2 < e ? s[p + 2] : 0x100u;
