@@ -52,6 +52,7 @@ extern "C" {
 
 typedef struct ocb_ctx ocb_ctx;
 typedef struct ocb_tokens ocb_tokens;
+typedef struct ocb_text ocb_text;
 
 /* Create a context on CUDA device `device`.  flags: reserved, pass 0.
  * Replaces: nothing (the reference keeps no device state). */
@@ -92,6 +93,23 @@ int  ocb_lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
                     uint32_t *d_start, uint32_t *d_kindlen, uint32_t *d_line,
                     uint64_t tok_cap, uint64_t *d_tu_tok_off,
                     int32_t *d_status, uint64_t *d_n_tok, void *stream);
+
+/* ---- preprocessor ------------------------------------------------------- */
+/* Preprocess every TU of a host batch.  Replaces
+ * opencuda/frontend/preprocess.py:178 preprocess(source, include_paths) as the
+ * CLI calls it (__main__.py:39-44) when no quoted include resolves to a file:
+ * include lines are blanked, lines spliced, directives and macros applied.
+ * The result holds the output text of every TU back to back (off: n_tu+1
+ * entries), a per-TU status (OCB_TU_RAISES_REERROR where the reference raises
+ * re.error, OCB_TU_UNSUPPORTED / OVERFLOW / TIMEOUT where the engine cannot
+ * reproduce it) and a per-TU flag set when a quoted #include line was blanked
+ * (a caller with include directories resolves those TUs on the host). */
+int  ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                          uint32_t n_tu, ocb_text **out);
+int  ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,
+                   const uint64_t **off, const int32_t **status,
+                   const uint32_t **qinclude);
+void ocb_text_free(ocb_text *t);
 
 /* Allocation-free form of ocb_lex_device, for callers that may not allocate
  * device memory when they lex (a framework's memory pool or a fixed arena that

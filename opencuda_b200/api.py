@@ -83,6 +83,18 @@ class TokenBatch:
         return out
 
 
+@dataclass
+class TextBatch:
+    """Preprocessed text of a batch (host copies)."""
+    data: bytes              # every TU's output back to back
+    off: np.ndarray          # uint64 [n_tu+1]
+    status: np.ndarray       # int32 per-TU status
+    qinclude: np.ndarray     # uint32: a quoted #include line was blanked
+
+    def text(self, i: int) -> str:
+        return self.data[int(self.off[i]):int(self.off[i + 1])].decode("utf-8", "surrogateescape")
+
+
 def _view(p, dt, cnt):
     if cnt == 0 or not p.value:
         return np.zeros(0, dtype=dt)
@@ -152,6 +164,29 @@ class Context:
         finally:
             self.lib.ocb_tokens_free(out)
 
+    # ---- preprocessor ----------------------------------------------------
+    def preprocess_batch(self, srcs=None, *, buf=None, tu_off=None) -> TextBatch:
+        """Preprocess every TU (``preprocess.py:178`` as the CLI calls it)."""
+        if srcs is not None:
+            buf, tu_off = pack_sources(srcs)
+        buf = np.ascontiguousarray(buf, dtype=np.uint8)
+        tu_off = np.ascontiguousarray(tu_off, dtype=np.uint64)
+        n_tu = len(tu_off) - 1
+        out = ctypes.c_void_p()
+        src_ptr = buf.ctypes.data if len(buf) else None
+        self._check(self.lib.ocb_preprocess_batch(self.h, src_ptr, tu_off.ctypes.data, n_tu,
+                                                  ctypes.byref(out)), "ocb_preprocess_batch")
+        try:
+            n = ctypes.c_uint64()
+            ps = [ctypes.c_void_p() for _ in range(4)]
+            self.lib.ocb_text_view(out, ctypes.byref(n), *[ctypes.byref(p) for p in ps])
+            data = ctypes.string_at(ps[0], n.value) if n.value else b""
+            return TextBatch(data=data, off=_view(ps[1], np.uint64, n_tu + 1),
+                             status=_view(ps[2], np.int32, n_tu),
+                             qinclude=_view(ps[3], np.uint32, n_tu))
+        finally:
+            self.lib.ocb_text_free(out)
+
     def lex_device(self, d_src: int, n_bytes: int, d_tu_off: int, n_tu: int,
                    d_start: int, d_kindlen: int, d_line: int, tok_cap: int,
                    d_tu_tok_off: int, d_status: int, d_n_tok: int, stream: int = 0):
@@ -173,3 +208,7 @@ def context(device: int = 0) -> Context:
 
 def lex_batch(srcs, device: int = 0) -> TokenBatch:
     return context(device).lex_batch(srcs)
+
+
+def preprocess_batch(srcs, device: int = 0) -> TextBatch:
+    return context(device).preprocess_batch(srcs)

@@ -58,7 +58,8 @@ void ocb_destroy(ocb_ctx *ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     for (DevBuf *b : {&ctx->lex_scratch, &ctx->cub_tmp, &ctx->d_src, &ctx->d_tu_off,
                       &ctx->d_tok_start, &ctx->d_tok_kl, &ctx->d_tok_line, &ctx->d_tu_tok,
-                      &ctx->d_status, &ctx->d_count})
+                      &ctx->d_status, &ctx->d_count, &ctx->pp_scratch, &ctx->pp_arena,
+                      &ctx->pp_text, &ctx->pp_off, &ctx->pp_status, &ctx->pp_qinc})
         b->release();
     ctx->h_stage.release();
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -163,5 +164,85 @@ int ocb_tokens_view(const ocb_tokens *t, uint64_t *n_tok, const uint32_t **start
 }
 
 void ocb_tokens_free(ocb_tokens *t) { delete t; }
+
+// Host batch -> device buffers (source copied through pinned staging when the
+// caller's buffer is pageable).
+static int upload_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                        uint64_t &N) {
+    if (tu_off[0] != 0) return fail(ctx, "tu_off[0] must be 0");
+    for (uint32_t i = 0; i < n_tu; ++i)
+        if (tu_off[i + 1] < tu_off[i]) return fail(ctx, "tu_off not monotone");
+    N = tu_off[n_tu];
+    if (N && !src) return fail(ctx, "null source");
+    cudaStream_t st = ctx->stream;
+    const uint8_t *hs = src;
+    cudaPointerAttributes pa;
+    if (N && (cudaPointerGetAttributes(&pa, src) != cudaSuccess || pa.type != cudaMemoryTypeHost)) {
+        cudaGetLastError();
+        OCB_TRY("pinned staging", ctx->h_stage.ensure(N));
+        memcpy(ctx->h_stage.p, src, N);
+        hs = ctx->h_stage.as<uint8_t>();
+    }
+    OCB_TRY("device source", ctx->d_src.ensure(N + 64));
+    OCB_TRY("device offsets", ctx->d_tu_off.ensure(8 * (size_t)(n_tu + 1)));
+    if (N) OCB_TRY("h2d source", cudaMemcpyAsync(ctx->d_src.p, hs, N, cudaMemcpyHostToDevice, st));
+    OCB_TRY("h2d offsets", cudaMemcpyAsync(ctx->d_tu_off.p, tu_off, 8 * (size_t)(n_tu + 1),
+                                           cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                         ocb_text **out) {
+    if (!ctx || !out || !tu_off) return fail(ctx, "ocb_preprocess_batch: null argument");
+    *out = nullptr;
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    uint64_t N = 0;
+    int rc = upload_batch(ctx, src, tu_off, n_tu, N);
+    if (rc) return rc;
+    OCB_TRY("device offsets", ctx->pp_off.ensure(8 * ((size_t)n_tu + 1)));
+    OCB_TRY("device status", ctx->pp_status.ensure(4 * (size_t)n_tu + 4));
+    OCB_TRY("device flags", ctx->pp_qinc.ensure(4 * (size_t)n_tu + 4));
+    uint64_t total = 0;
+    rc = pp_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(), n_tu, 2,
+                   ctx->pp_text, ctx->pp_off.as<uint64_t>(), ctx->pp_status.as<int32_t>(),
+                   ctx->pp_qinc.as<uint32_t>(), &total, st);
+    if (rc) return rc;
+    ocb_text *t = new (std::nothrow) ocb_text();
+    if (!t) return fail(ctx, "ocb_preprocess_batch: out of host memory");
+    t->n_tu = n_tu;
+    t->bytes.resize(total);
+    t->off.resize((size_t)n_tu + 1);
+    t->status.resize(n_tu);
+    t->qinclude.resize(n_tu);
+    cudaError_t e = cudaSuccess;
+    if (total) e = cudaMemcpyAsync(t->bytes.data(), ctx->pp_text.p, total, cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaMemcpyAsync(t->off.data(), ctx->pp_off.p, 8 * ((size_t)n_tu + 1),
+                                cudaMemcpyDeviceToHost, st);
+    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->pp_status.p, 4 * (size_t)n_tu,
+                                        cudaMemcpyDeviceToHost, st);
+    if (!e && n_tu) e = cudaMemcpyAsync(t->qinclude.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu,
+                                        cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    if (e) {
+        delete t;
+        return fail(ctx, "d2h text", e);
+    }
+    *out = t;
+    return 0;
+}
+
+int ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,
+                  const uint64_t **off, const int32_t **status, const uint32_t **qinclude) {
+    if (!t) return -1;
+    if (n_bytes) *n_bytes = t->bytes.size();
+    if (bytes) *bytes = t->bytes.data();
+    if (off) *off = t->off.data();
+    if (status) *status = t->status.data();
+    if (qinclude) *qinclude = t->qinclude.data();
+    return 0;
+}
+
+void ocb_text_free(ocb_text *t) { delete t; }
 
 }  // extern "C"

@@ -65,6 +65,16 @@ struct ocb_ctx {
         d_status, d_count;
     ocb::HostBuf h_stage;
     bool kw_ready = false;
+    // preprocessor scratch and outputs
+    ocb::DevBuf pp_scratch, pp_arena, pp_text, pp_off, pp_status, pp_qinc;
+};
+
+struct ocb_text {
+    uint32_t n_tu = 0;
+    std::vector<uint8_t> bytes;
+    std::vector<uint64_t> off;
+    std::vector<int32_t> status;
+    std::vector<uint32_t> qinclude;
 };
 
 struct ocb_tokens {
@@ -85,6 +95,11 @@ int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
                uint32_t *d_kindlen, uint32_t *d_line, uint64_t tok_cap,
                uint64_t *d_tu_tok_off, int32_t *d_status, uint64_t *d_n_tok,
                cudaStream_t stream);
+// Preprocessor on device buffers (pp.cu): output text packed into `out_text`
+// (grown as needed) at d_out_off[n_tu+1]; total bytes returned in *h_total.
+int pp_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_tu_off,
+              uint32_t n_tu, uint32_t scale, DevBuf &out_text, uint64_t *d_out_off,
+              int32_t *d_status, uint32_t *d_qinc, uint64_t *h_total, cudaStream_t st);
 }  // namespace ocb
 
 #define OCB_TRY(what, expr)                                    \

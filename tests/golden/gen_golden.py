@@ -61,6 +61,32 @@ def lex_cases():
     return cases
 
 
+PP_EDGE = [
+    "", "x", "#define A 1\nA", "#define A 1\n#undef A\nA", "#define F(a,b) a+b\nF(1,2)",
+    "#define F(a, b) b a\nF(b, 1)", "#define V(x, ...) f(x, __VA_ARGS__)\nV(1, 2, 3)",
+    "#define C(a, b) a ## b\nC(x, y)", "#define S \"A\"\nS A", "#ifdef A\nno\n#else\nyes\n#endif",
+    "#if 0\nno\n#elif 1\nelif\n#else\nelse\n#endif", "#if A && B\ntaken\n#endif",
+    "#define X 2\n#if X > 1\nbig\n#endif", "#if\nempty\n#endif", "#if(1)\nparen\n#endif",
+    "#endif // tail\nx", "a \\\nb", "a \\", "\\", "#define L long \\\n value\nL",
+    "#include \"missing.h\"\ny", "#include <stdio.h>\ny", "#  define  SP  7\nSP",
+    "#define A B\n#define B A\nA B", "#define A A+1\nA", "#define BAD x\\qy\nBAD",
+    "#define NL a\\nb\nNL", "#define F(x) [x]\nF(\"a\\tb\")", "#define F(x) x\nF((1, 2))",
+    "#define F(x) x\nF(unbalanced", "#define F (x)\nF", "#define E\n#ifdef E\nE\n#endif",
+    "#define AB 1\n#define A 2\nAB A", "#if 1 << -1\nneg\n#endif", "#if 010\noct\n#endif",
+    "#define Z // only comment\nZ", "#define F() k\nF() F( )",
+]
+
+
+def pp_cases():
+    from tests._helpers import pp_fuzz_sources
+    cases = list(PP_EDGE) + pp_fuzz_sources(400, 4242)
+    buf, off = synth.lexstress_batch(total_bytes=96 * 1024, tu_bytes=16384, seed=21,
+                                     pool_lines=4000)
+    cases += [buf[off[i]:off[i + 1]].decode() for i in range(len(off) - 1)]
+    cases += [synth.SGEMM_SRC]
+    return cases
+
+
 def write(name, obj):
     with gzip.open(HERE / name, "wt", encoding="utf-8") as f:
         json.dump(obj, f)
@@ -79,6 +105,18 @@ def main():
     write("lex_golden.json.gz", {"generator": "tests/golden/gen_golden.py",
                                  "gen_version": synth.GEN_VERSION, "cases": out})
     print(f"lex_golden: {len(out)} cases")
+    cases = pp_cases()
+    with ref_runner.RefPool() as pool:
+        res = pool.run(cases, what=("pp",), chunksize=16)
+    out = []
+    for src, r in zip(cases, res):
+        if "error" in r:
+            out.append({"src": src, "raises": r["error"][0]})
+        else:
+            out.append({"src": src, "pp": r["pp"]})
+    write("pp_golden.json.gz", {"generator": "tests/golden/gen_golden.py",
+                                "gen_version": synth.GEN_VERSION, "cases": out})
+    print(f"pp_golden: {len(out)} cases")
 
 
 if __name__ == "__main__":

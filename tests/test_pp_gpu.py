@@ -1,0 +1,67 @@
+"""GPU preprocessor parity: libocb's sm_100a preprocessor against the
+reference's preprocess() -- committed golden outputs, and the live reference
+(oracle/_ref/py, run in worker processes on this host) on seeded inputs."""
+import numpy as np
+import pytest
+
+from oracle import ref_runner
+from opencuda_b200 import synth
+from opencuda_b200.api import pack_sources, TU_UNSUPPORTED
+from tests._helpers import golden, pp_fuzz_sources
+
+pytestmark = pytest.mark.gpu
+
+REF_CODE = {"error": 5}
+
+
+def check_against(tb, srcs, ref, allow_unsupported=0.02):
+    unsup = 0
+    for i, (s, r) in enumerate(zip(srcs, ref)):
+        st = int(tb.status[i])
+        if st in (TU_UNSUPPORTED, 0x300):
+            unsup += 1
+            continue
+        if "raises" in r or "error" in r:
+            exc = r.get("raises") or r["error"][0]
+            assert exc == "error" and st == 5, (i, exc, st, s[:200])
+            continue
+        assert st == 0, (i, st, s[:200])
+        want = r.get("pp") if "pp" in r else r["pp"]
+        assert tb.text(i) == want, (i, s[:300])
+    assert unsup <= allow_unsupported * len(srcs), unsup
+
+
+def test_golden_preprocess(ctx):
+    cases = golden("pp_golden.json.gz")["cases"]
+    srcs = [c["src"] for c in cases]
+    tb = ctx.preprocess_batch(srcs)
+    check_against(tb, srcs, cases)
+
+
+@pytest.mark.parametrize("seed", [11, 12])
+def test_fuzz_against_live_reference(ctx, seed):
+    srcs = pp_fuzz_sources(3000, seed)
+    tb = ctx.preprocess_batch(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=("pp",), chunksize=32)
+    check_against(tb, srcs, ref)
+
+
+def test_workloads_against_live_reference(ctx):
+    buf, off = synth.lexstress_batch(total_bytes=8 << 20, tu_bytes=16384, seed=13,
+                                     pool_lines=50_000)
+    srcs = [buf[off[i]:off[i + 1]].decode() for i in range(len(off) - 1)]
+    srcs += [synth.SGEMM_SRC] + synth.random_batch(128, seed=8)
+    tb = ctx.preprocess_batch(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=("pp",), chunksize=4)
+    check_against(tb, srcs, ref, allow_unsupported=0.0)
+
+
+def test_plain_tus_pass_through(ctx):
+    srcs = synth.random_batch(512, seed=2) + ["", "x", "a\nb\n"]
+    buf, off = pack_sources(srcs)
+    tb = ctx.preprocess_batch(buf=buf, tu_off=off)
+    assert tb.data == buf.tobytes()
+    assert np.array_equal(tb.off, off)
+    assert not tb.status.any()
