@@ -513,247 +513,319 @@ __device__ __forceinline__ bool mul_ovf(int64_t a, int64_t b, int64_t *r) {
     return false;
 }
 
-struct Eval {
-    const uint8_t *s;
-    uint32_t n, i;
-    bool run;   // false: syntax pass, true: evaluation pass
-    int err;    // first error of the current pass
-    __device__ void fail(int e) {
-        if (!err) err = e;
+// Operators of the supported subset.  Precedence as in Python, low -> high:
+// comparisons < | < ^ < & < shifts < + - < * // % < unary + - ~ < **.
+enum : uint8_t {
+    OP_NONE = 0, OP_LT, OP_LE, OP_GT, OP_GE, OP_EQ, OP_NE,    // comparisons
+    OP_OR, OP_XOR, OP_AND, OP_SHL, OP_SHR, OP_ADD, OP_SUB,
+    OP_MUL, OP_FLOORDIV, OP_MOD, OP_DIV, OP_POW,
+    OP_NEG, OP_POS, OP_INV, OP_LPAREN,
+    RPN_NUM, RPN_BADNUM                                      // operand items
+};
+__device__ __forceinline__ int prec(uint8_t op) {
+    if (op <= OP_NE) return 1;
+    switch (op) {
+    case OP_OR: return 2;
+    case OP_XOR: return 3;
+    case OP_AND: return 4;
+    case OP_SHL: case OP_SHR: return 5;
+    case OP_ADD: case OP_SUB: return 6;
+    case OP_MUL: case OP_FLOORDIV: case OP_MOD: case OP_DIV: return 7;
+    case OP_NEG: case OP_POS: case OP_INV: return 8;
+    case OP_POW: return 9;
+    default: return 0;
     }
-    __device__ void ws() {
-        while (i < n && (s[i] == ' ' || s[i] == '\t' || s[i] == 0x0c)) ++i;
-        if (i < n && s[i] == '#') i = n;  // comment to end of line
-    }
-    __device__ bool peek(const char *op) {
-        ws();
-        uint32_t k = 0;
-        while (op[k]) {
-            if (i + k >= n || s[i + k] != (uint8_t)op[k]) return false;
-            ++k;
-        }
-        return true;
-    }
-    __device__ bool take(const char *op) {
-        if (!peek(op)) return false;
-        uint32_t k = 0;
-        while (op[k]) ++k;
-        i += k;
-        return true;
-    }
-    __device__ int64_t number() {
-        ws();
-        uint32_t a = i;
-        while (i < n && isw(s[i])) ++i;
-        if (i < n && s[i] == '.') { fail(EV_UNSUP); return 0; }
-        uint32_t L = i - a;
-        const uint8_t *p = s + a;
-        uint32_t base = 10, k = 0;
-        if (L >= 2 && p[0] == '0' && ((p[1] | 0x20u) == 'x' || (p[1] | 0x20u) == 'o' ||
-                                     (p[1] | 0x20u) == 'b')) {
-            base = (p[1] | 0x20u) == 'x' ? 16 : (p[1] | 0x20u) == 'o' ? 8 : 2;
-            k = 2;
-            if (k >= L) { fail(EV_SYNTAX); return 0; }
-        } else if (p[0] == '0') {
-            for (uint32_t j = 0; j < L; ++j)  // "0", "00", "0_0" only
-                if (p[j] != '0' && p[j] != '_') { fail(EV_SYNTAX); return 0; }
-        }
-        uint64_t v = 0;
-        bool need_digit = true;
-        for (; k < L; ++k) {
-            uint32_t c = p[k];
-            if (c == '_') {
-                if (need_digit) { fail(EV_SYNTAX); return 0; }
-                need_digit = true;
-                continue;
-            }
-            if (base == 10 && ((c | 0x20u) == 'e' || (c | 0x20u) == 'j')) { fail(EV_UNSUP); return 0; }
-            uint32_t d = c - '0' < 10u ? c - '0' : (c | 0x20u) - 'a' < 6u ? (c | 0x20u) - 'a' + 10 : 99;
-            if (d >= base) { fail(EV_SYNTAX); return 0; }
-            if (v > (0x7FFFFFFFFFFFFFFFull - d) / base) { fail(EV_UNSUP); return 0; }
-            v = v * base + d;
-            need_digit = false;
-        }
-        if (need_digit) { fail(EV_SYNTAX); return 0; }
-        return (int64_t)v;
-    }
-    __device__ int64_t atom() {
-        ws();
-        if (i >= n) { fail(EV_SYNTAX); return 0; }
-        uint32_t c = s[i];
-        if (c == '(') {
-            ++i;
-            if (peek(")")) { fail(EV_UNSUP); return 0; }  // empty tuple
-            int64_t v = test();
-            if (peek(",")) { fail(EV_UNSUP); return 0; }  // tuple
-            if (!take(")")) { fail(EV_SYNTAX); return 0; }
-            return v;
-        }
-        if (c - '0' < 10u) return number();
-        if (c == '.' || c == '"' || c == '\'' || c == '[' || c == '{' || c == '@' ||
-            c == '\\' || c >= 0x80)
-            fail(EV_UNSUP);
-        else
-            fail(EV_SYNTAX);
-        return 0;
-    }
-    __device__ int64_t power() {
-        int64_t b = atom();
-        if (take("**")) {
-            int64_t e = factor();
-            if (run && !err) {
-                if (e < 0) { fail(EV_UNSUP); return 0; }
-                int64_t r = 1;
-                for (int64_t k = 0; k < e; ++k) {
-                    if (mul_ovf(r, b, &r)) { fail(EV_UNSUP); return 0; }
-                    if (r == 0 || r == 1) break;
-                    if (r == -1) { r = (e - k - 1) % 2 ? -r : r; break; }
-                }
-                return r;
-            }
-            return 0;
-        }
-        return b;
-    }
-    __device__ int64_t factor() {
-        if (take("+")) return factor();
-        if (peek("-")) {
-            ++i;
-            int64_t v = factor();
-            if (run && !err && v == INT64_MIN) fail(EV_UNSUP);
-            return -v;
-        }
-        if (take("~")) return ~factor();
-        return power();
-    }
-    __device__ int64_t term() {
-        int64_t v = factor();
-        for (;;) {
-            if (peek("**")) return v;
-            if (take("//")) {
-                int64_t r = factor();
-                if (run && !err) {
-                    if (r == 0) { fail(EV_EXC); return 0; }
-                    if (v == INT64_MIN && r == -1) { fail(EV_UNSUP); return 0; }
-                    int64_t q = v / r;
-                    if ((v % r != 0) && ((v < 0) != (r < 0))) q -= 1;
-                    v = q;
-                }
-            } else if (take("*")) {
-                int64_t r = factor();
-                if (run && !err && mul_ovf(v, r, &v)) fail(EV_UNSUP);
-            } else if (take("%")) {
-                int64_t r = factor();
-                if (run && !err) {
-                    if (r == 0) { fail(EV_EXC); return 0; }
-                    if (r == -1) { v = 0; continue; }
-                    int64_t m = v % r;
-                    if (m != 0 && ((m < 0) != (r < 0))) m += r;
-                    v = m;
-                }
-            } else if (peek("/")) {
-                fail(EV_UNSUP);
-                return 0;
-            } else {
-                return v;
-            }
-        }
-    }
-    __device__ int64_t arith() {
-        int64_t v = term();
-        for (;;) {
-            if (take("+")) {
-                int64_t r = term();
-                if (run && !err && add_ovf(v, r, &v)) fail(EV_UNSUP);
-            } else if (peek("-") && !peek("->")) {
-                ++i;
-                int64_t r = term();
-                if (run && !err && sub_ovf(v, r, &v)) fail(EV_UNSUP);
-            } else {
-                return v;
-            }
-        }
-    }
-    __device__ int64_t shift() {
-        int64_t v = arith();
-        for (;;) {
-            bool l = take("<<");
-            if (!l && !take(">>")) return v;
-            int64_t r = arith();
-            if (run && !err) {
-                if (r < 0) { fail(EV_EXC); return 0; }
-                if (l) {
-                    if (v != 0 && (r >= 63 || (v > 0 ? v > (INT64_MAX >> r) : v < (INT64_MIN >> r))))
-                        { fail(EV_UNSUP); return 0; }
-                    v = v * ((int64_t)1 << r);
-                } else {
-                    v = r >= 63 ? (v < 0 ? -1 : 0) : (v >> r);
-                }
-            }
-        }
-    }
-    __device__ int64_t band() {
-        int64_t v = shift();
-        while (peek("&") && !peek("&&")) { ++i; v &= shift(); }
-        if (peek("&&")) fail(EV_SYNTAX);
-        return v;
-    }
-    __device__ int64_t bxor() {
-        int64_t v = band();
-        while (take("^")) v ^= band();
-        return v;
-    }
-    __device__ int64_t bor() {
-        int64_t v = bxor();
-        while (peek("|") && !peek("||")) { ++i; v |= bxor(); }
-        if (peek("||")) fail(EV_SYNTAX);
-        return v;
-    }
-    // comparison chain with short-circuit: once a link is false, later operands
-    // are parsed but not evaluated (their errors are not raised)
-    __device__ int64_t test() {
-        int64_t v = bor();
-        bool any = false, result = true;
-        for (;;) {
-            int op;
-            if (take("<=")) op = 1;
-            else if (take(">=")) op = 2;
-            else if (take("==")) op = 3;
-            else if (take("!=")) op = 4;
-            else if (peek("<") && !peek("<<")) { ++i; op = 5; }
-            else if (peek(">") && !peek(">>")) { ++i; op = 6; }
-            else break;
-            bool was_run = run;
-            if (!result) run = false;
-            int64_t r = bor();
-            if (run && !err) {
-                bool t = op == 1 ? v <= r : op == 2 ? v >= r : op == 3 ? v == r
-                       : op == 4 ? v != r : op == 5 ? v < r : v > r;
-                result = result && t;
-            }
-            run = was_run;
-            v = r;
-            any = true;
-        }
-        if (peek("=") || peek("!")) fail(EV_SYNTAX);
-        return any ? (result ? 1 : 0) : v;
-    }
+}
+
+struct RpnItem {
+    uint8_t op;       // operator, or RPN_NUM / RPN_BADNUM
+    uint8_t chain;    // comparison: 0 first link, 1 continuation
+    int64_t v;
 };
 
+// Values during evaluation.  kind: EV_OK, EV_EXC (the operation raised) or
+// EV_UNSUP; errors are carried as values so that an operand skipped by a
+// comparison chain's short-circuit raises nothing, as in Python.
+struct EVal {
+    int64_t v;
+    uint8_t kind;
+    uint8_t in_chain;  // a comparison chain value: v = result so far
+    int64_t last;      // the chain's last operand
+};
+
+// Tokenize + shunting-yard into `out`; returns EV_OK, EV_SYNTAX or EV_UNSUP.
+__device__ int to_rpn(const uint8_t *s, uint32_t n, RpnItem *out, uint32_t &no, uint8_t *ops,
+                      uint8_t *opchain, uint32_t cap) {
+    uint32_t nops = 0, i = 0;
+    no = 0;
+    bool want_operand = true;
+    int depth = 0;
+    auto emit = [&](uint8_t op, uint8_t chain, int64_t v) { out[no++] = RpnItem{op, chain, v}; };
+    while (true) {
+        while (i < n && (s[i] == ' ' || s[i] == '\t' || s[i] == 0x0c)) ++i;
+        if (i < n && s[i] == '#') i = n;  // comment
+        if (i >= n) break;
+        if (no + 2 >= cap || nops + 2 >= cap) return EV_UNSUP;
+        uint32_t c = s[i], c1 = i + 1 < n ? s[i + 1] : 0;
+        if (c - '0' < 10u) {
+            if (!want_operand) return EV_SYNTAX;
+            uint32_t a = i;
+            while (i < n && isw(s[i])) ++i;
+            if (i < n && s[i] == '.') return EV_UNSUP;
+            uint32_t L = i - a, k = 0, base = 10;
+            const uint8_t *p = s + a;
+            if (L >= 2 && p[0] == '0' && ((p[1] | 0x20u) == 'x' || (p[1] | 0x20u) == 'o' ||
+                                         (p[1] | 0x20u) == 'b')) {
+                base = (p[1] | 0x20u) == 'x' ? 16 : (p[1] | 0x20u) == 'o' ? 8 : 2;
+                k = 2;
+                if (k >= L) return EV_SYNTAX;
+            } else if (p[0] == '0') {
+                for (uint32_t j = 0; j < L; ++j)
+                    if (p[j] != '0' && p[j] != '_') return EV_SYNTAX;
+            }
+            uint64_t v = 0;
+            bool need_digit = true, big = false;
+            for (; k < L; ++k) {
+                uint32_t ch = p[k];
+                if (ch == '_') {
+                    if (need_digit) return EV_SYNTAX;
+                    need_digit = true;
+                    continue;
+                }
+                if (base == 10 && ((ch | 0x20u) == 'e' || (ch | 0x20u) == 'j')) return EV_UNSUP;
+                uint32_t d = ch - '0' < 10u ? ch - '0'
+                           : (ch | 0x20u) - 'a' < 6u ? (ch | 0x20u) - 'a' + 10 : 99;
+                if (d >= base) return EV_SYNTAX;
+                if (v > (0x7FFFFFFFFFFFFFFFull - d) / base) big = true;
+                else v = v * base + d;
+                need_digit = false;
+            }
+            if (need_digit) return EV_SYNTAX;
+            emit(big ? RPN_BADNUM : RPN_NUM, 0, (int64_t)v);
+            want_operand = false;
+            continue;
+        }
+        if (c == '(') {
+            if (!want_operand) return EV_UNSUP;  // a call: int object is not callable (TypeError) or worse
+            ops[nops] = OP_LPAREN;
+            opchain[nops++] = 0;
+            ++depth;
+            ++i;
+            continue;
+        }
+        if (c == ')') {
+            if (want_operand) return depth > 0 && i > 0 && s[i - 1] == '(' ? EV_UNSUP : EV_SYNTAX;
+            while (nops && ops[nops - 1] != OP_LPAREN) { --nops; emit(ops[nops], opchain[nops], 0); }
+            if (!nops) return EV_SYNTAX;
+            --nops;
+            --depth;
+            ++i;
+            continue;
+        }
+        uint8_t op = OP_NONE;
+        uint32_t len = 1;
+        if (want_operand) {
+            if (c == '-') op = OP_NEG;
+            else if (c == '+') op = OP_POS;
+            else if (c == '~') op = OP_INV;
+            else if (c == '.' || c == '"' || c == '\'' || c == '[' || c == '{' || c == '@' ||
+                     c == '\\' || c == ',' || c >= 0x80) return EV_UNSUP;
+            else return EV_SYNTAX;
+            ops[nops] = op;  // prefix operator
+            opchain[nops++] = 0;
+            ++i;
+            continue;
+        }
+        if (c == '*' && c1 == '*') { op = OP_POW; len = 2; }
+        else if (c == '/' && c1 == '/') { op = OP_FLOORDIV; len = 2; }
+        else if (c == '<' && c1 == '<') { op = OP_SHL; len = 2; }
+        else if (c == '>' && c1 == '>') { op = OP_SHR; len = 2; }
+        else if (c == '<' && c1 == '=') { op = OP_LE; len = 2; }
+        else if (c == '>' && c1 == '=') { op = OP_GE; len = 2; }
+        else if (c == '=' && c1 == '=') { op = OP_EQ; len = 2; }
+        else if (c == '!' && c1 == '=') { op = OP_NE; len = 2; }
+        else if (c == '<') op = OP_LT;
+        else if (c == '>') op = OP_GT;
+        else if (c == '|') op = OP_OR;
+        else if (c == '^') op = OP_XOR;
+        else if (c == '&') op = OP_AND;
+        else if (c == '+') op = OP_ADD;
+        else if (c == '-') op = OP_SUB;
+        else if (c == '*') op = OP_MUL;
+        else if (c == '%') op = OP_MOD;
+        else if (c == '/') op = OP_DIV;
+        else if (c == '.' || c == '"' || c == '\'' || c == '[' || c == '{' || c == '@' ||
+                 c == '\\' || c == ',' || c >= 0x80) return EV_UNSUP;
+        else return EV_SYNTAX;
+        i += len;
+        int p = prec(op);
+        uint8_t chain = 0;
+        if (p == 1) {
+            // comparisons chain: pop everything above the chain level; a
+            // comparison already on the stack is the previous link
+            while (nops && ops[nops - 1] != OP_LPAREN && prec(ops[nops - 1]) > 1) {
+                --nops;
+                emit(ops[nops], opchain[nops], 0);
+            }
+            if (nops && ops[nops - 1] != OP_LPAREN && prec(ops[nops - 1]) == 1) {
+                --nops;
+                emit(ops[nops], opchain[nops], 0);
+                chain = 1;
+            }
+        } else {
+            // left-associative, except ** (right); prefix operators below **
+            // stay on the stack when ** arrives
+            while (nops && ops[nops - 1] != OP_LPAREN) {
+                int q = prec(ops[nops - 1]);
+                bool pop = op == OP_POW ? q > p : q >= p;
+                if (!pop) break;
+                --nops;
+                emit(ops[nops], opchain[nops], 0);
+            }
+        }
+        ops[nops] = op;
+        opchain[nops++] = chain;
+        want_operand = true;
+    }
+    if (want_operand) return EV_SYNTAX;
+    while (nops) {
+        --nops;
+        if (ops[nops] == OP_LPAREN) return EV_SYNTAX;
+        emit(ops[nops], opchain[nops], 0);
+    }
+    return EV_OK;
+}
+
+__device__ EVal ev_bin(uint8_t op, EVal a, EVal b) {
+    EVal r{0, EV_OK, 0, 0};
+    if (a.kind != EV_OK) return a;
+    if (b.kind != EV_OK) return b;
+    int64_t x = a.v, y = b.v;
+    switch (op) {
+    case OP_OR: r.v = x | y; break;
+    case OP_XOR: r.v = x ^ y; break;
+    case OP_AND: r.v = x & y; break;
+    case OP_ADD: if (add_ovf(x, y, &r.v)) r.kind = EV_UNSUP; break;
+    case OP_SUB: if (sub_ovf(x, y, &r.v)) r.kind = EV_UNSUP; break;
+    case OP_MUL: if (mul_ovf(x, y, &r.v)) r.kind = EV_UNSUP; break;
+    case OP_DIV: r.kind = EV_UNSUP; break;  // a float result
+    case OP_FLOORDIV:
+        if (y == 0) { r.kind = EV_EXC; break; }
+        if (x == INT64_MIN && y == -1) { r.kind = EV_UNSUP; break; }
+        r.v = x / y;
+        if ((x % y != 0) && ((x < 0) != (y < 0))) r.v -= 1;
+        break;
+    case OP_MOD:
+        if (y == 0) { r.kind = EV_EXC; break; }
+        if (y == -1) { r.v = 0; break; }
+        r.v = x % y;
+        if (r.v != 0 && ((r.v < 0) != (y < 0))) r.v += y;
+        break;
+    case OP_SHL:
+        if (y < 0) { r.kind = EV_EXC; break; }
+        if (x != 0 && (y >= 63 || (x > 0 ? x > (INT64_MAX >> y) : x < (INT64_MIN >> y)))) {
+            r.kind = EV_UNSUP;
+            break;
+        }
+        r.v = x == 0 ? 0 : x * ((int64_t)1 << y);
+        break;
+    case OP_SHR:
+        if (y < 0) { r.kind = EV_EXC; break; }
+        r.v = y >= 63 ? (x < 0 ? -1 : 0) : (x >> y);
+        break;
+    case OP_POW: {
+        if (y < 0) { r.kind = EV_UNSUP; break; }  // a float result
+        int64_t acc = 1;
+        for (int64_t k = 0; k < y; ++k) {
+            if (mul_ovf(acc, x, &acc)) { r.kind = EV_UNSUP; break; }
+            if (acc == 0 || acc == 1) break;
+            if (acc == -1) { acc = ((y - k - 1) & 1) ? 1 : -1; break; }
+        }
+        r.v = acc;
+        break;
+    }
+    default: r.kind = EV_UNSUP;
+    }
+    return r;
+}
+
+__device__ bool cmp(uint8_t op, int64_t x, int64_t y) {
+    switch (op) {
+    case OP_LT: return x < y;
+    case OP_LE: return x <= y;
+    case OP_GT: return x > y;
+    case OP_GE: return x >= y;
+    case OP_EQ: return x == y;
+    default: return x != y;
+    }
+}
+
+// A chain value used as an operand becomes its truth value.
+__device__ __forceinline__ EVal settle(EVal a) {
+    if (a.in_chain && a.kind == EV_OK) return EVal{a.v ? 1 : 0, EV_OK, 0, 0};
+    a.in_chain = 0;
+    return a;
+}
+
 // Evaluate `e` per _eval_if_expr's final step.  Returns 1/0 (true/false) or
-// -1 when unsupported.
-__device__ int py_eval_bool(const uint8_t *e, uint32_t n) {
-    Eval ev{e, n, 0, false, 0};
-    ev.test();
-    ev.ws();
-    if (!ev.err && ev.i < n) ev.fail(EV_SYNTAX);
-    if (ev.err == EV_SYNTAX) return 1;
-    if (ev.err == EV_UNSUP) return -1;
-    Eval r{e, n, 0, true, 0};
-    int64_t v = r.test();
-    if (r.err == EV_UNSUP) return -1;
-    if (r.err) return 1;  // exception -> True
-    return v != 0;
+// -1 when unsupported.  Scratch: 3 * (n + 8) items from the TU pool.
+__device__ int py_eval_bool(Ctx &c, const uint8_t *e, uint32_t n) {
+    uint32_t cap = n + 8;
+    RpnItem *rpn = (RpnItem *)c.alloc(sizeof(RpnItem) * cap);
+    uint8_t *ops = c.alloc(2 * cap);
+    EVal *st = (EVal *)c.alloc(sizeof(EVal) * cap);
+    if (!rpn || !ops || !st) return 1;
+    uint32_t nr = 0;
+    int r = to_rpn(e, n, rpn, nr, ops, ops + cap, cap);
+    if (r == EV_SYNTAX) return 1;
+    if (r == EV_UNSUP) return -1;
+    uint32_t sp = 0;
+    for (uint32_t k = 0; k < nr; ++k) {
+        RpnItem it = rpn[k];
+        if (it.op == RPN_NUM || it.op == RPN_BADNUM) {
+            st[sp++] = EVal{it.v, (uint8_t)(it.op == RPN_NUM ? EV_OK : EV_UNSUP), 0, 0};
+            continue;
+        }
+        if (it.op == OP_NEG || it.op == OP_POS || it.op == OP_INV) {
+            EVal a = settle(st[sp - 1]);
+            if (a.kind == EV_OK) {
+                if (it.op == OP_NEG) {
+                    if (a.v == INT64_MIN) a.kind = EV_UNSUP;
+                    else a.v = -a.v;
+                } else if (it.op == OP_INV) {
+                    a.v = ~a.v;
+                }
+            }
+            st[sp - 1] = a;
+            continue;
+        }
+        EVal b = st[--sp];
+        EVal a = st[--sp];
+        if (prec(it.op) == 1) {
+            b = settle(b);
+            EVal out{0, EV_OK, 1, 0};
+            if (!it.chain) {
+                a = settle(a);
+                if (a.kind != EV_OK) out = a;
+                else if (b.kind != EV_OK) out = b;
+                else out = EVal{cmp(it.op, a.v, b.v) ? 1 : 0, EV_OK, 1, b.v};
+            } else {
+                // a is the chain so far; a false chain skips b entirely
+                if (a.kind != EV_OK) out = a;
+                else if (!a.v) out = a;
+                else if (b.kind != EV_OK) out = b;
+                else out = EVal{cmp(it.op, a.last, b.v) ? 1 : 0, EV_OK, 1, b.v};
+            }
+            out.in_chain = 1;
+            st[sp++] = out;
+            continue;
+        }
+        st[sp++] = ev_bin(it.op, settle(a), settle(b));
+    }
+    EVal res = settle(st[0]);
+    if (res.kind == EV_UNSUP) return -1;
+    if (res.kind == EV_EXC) return 1;
+    return res.v != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -896,7 +968,7 @@ struct TU {
                 ++i;
             }
         }
-        int v = py_eval_bool(oth.p, oth.n);
+        int v = py_eval_bool(c, oth.p, oth.n);
         if (v < 0) { c.set(ST_UNSUP); return 1; }
         return v;
     }
