@@ -71,7 +71,7 @@ struct Ctx {
         if (status == ST_OK) status = s;
     }
     __device__ uint8_t *alloc(uint32_t bytes) {
-        uint32_t a = (pool_used + 7u) & ~7u;
+        uint32_t a = (pool_used + 15u) & ~15u;
         if (a + bytes > pool_cap) {
             set(ST_OVF);
             return nullptr;
@@ -1296,16 +1296,20 @@ struct PPArgs {
     uint32_t *qinclude;          // per TU: 1 if a quoted include line was blanked
 };
 
-// Arena size of a TU of n bytes (output, two work buffers, pool), 16-aligned.
-__host__ __device__ __forceinline__ uint64_t arena_bytes(uint64_t n, uint32_t scale) {
-    uint64_t out = scale * n + 4096, work = 2 * (scale * n + 4096),
-             pool = (scale + 4) * n + 65536;
-    return (out + 2 * work + pool + 15) & ~15ull;
-}
+// Arena of a TU of n bytes: output | work A | work B | pool, each region a
+// multiple of 16 bytes so every region (and the pool's 16-aligned bump
+// allocations, which hold structs with pointers) is suitably aligned.
+__host__ __device__ __forceinline__ uint64_t align16(uint64_t x) { return (x + 15) & ~15ull; }
 __host__ __device__ __forceinline__ void arena_layout(uint64_t n, uint32_t scale, uint64_t &out,
-                                                       uint64_t &work) {
-    out = scale * n + 4096;
-    work = 2 * (scale * n + 4096);
+                                                       uint64_t &work, uint64_t &pool) {
+    out = align16(scale * n + 4096);
+    work = align16(2 * (scale * n + 4096));
+    pool = align16((scale + 4) * n + 65536);
+}
+__host__ __device__ __forceinline__ uint64_t arena_bytes(uint64_t n, uint32_t scale) {
+    uint64_t out, work, pool;
+    arena_layout(n, scale, out, work, pool);
+    return out + 2 * work + pool;
 }
 
 __device__ void preprocess_one(const PPArgs &A, uint32_t t, uint32_t scale) {
@@ -1313,12 +1317,11 @@ __device__ void preprocess_one(const PPArgs &A, uint32_t t, uint32_t scale) {
     const uint8_t *s = A.src + b;
     const uint32_t n = (uint32_t)(e - b);
     uint8_t *ar = A.arena + A.arena_off[t];
-    uint64_t out_cap, wcap;
-    arena_layout(n, scale, out_cap, wcap);
-    uint64_t total = A.arena_off[t + 1] - A.arena_off[t];
+    uint64_t out_cap, wcap, pool_cap;
+    arena_layout(n, scale, out_cap, wcap, pool_cap);
     TU u;
     u.c = Ctx{s, n, ar, 0, (uint32_t)out_cap, ar + out_cap, ar + out_cap + wcap, (uint32_t)wcap,
-              ar + out_cap + 2 * wcap, 0, (uint32_t)(total - out_cap - 2 * wcap), ST_OK};
+              ar + out_cap + 2 * wcap, 0, (uint32_t)pool_cap, ST_OK};
     u.obj = Dict{};
     u.fn = Dict{};
     u.depth = 0;
