@@ -558,13 +558,51 @@ __device__ int to_rpn(const uint8_t *s, uint32_t n, RpnItem *out, uint32_t &no, 
                       uint8_t *opchain, uint32_t cap) {
     uint32_t nops = 0, i = 0;
     no = 0;
-    bool want_operand = true;
+    bool want_operand = true, started = false, later_line = false;
     int depth = 0;
     auto emit = [&](uint8_t op, uint8_t chain, int64_t v) { out[no++] = RpnItem{op, chain, v}; };
     while (true) {
+        // Python's tokenizer: spaces, tabs and form feeds separate tokens; a
+        // newline inside parentheses is whitespace, blank lines before the
+        // expression are skipped (an indented first line is an error), and a
+        // newline after a complete expression must end the input
+        uint32_t ws0 = i;
         while (i < n && (s[i] == ' ' || s[i] == '\t' || s[i] == 0x0c)) ++i;
-        if (i < n && s[i] == '#') i = n;  // comment
+        bool indented = i > ws0;
+        if (i < n && s[i] == '#')
+            while (i < n && s[i] != '\n' && s[i] != '\r') ++i;  // comment
         if (i >= n) break;
+        if (s[i] == '\n' || s[i] == '\r') {
+            if (depth > 0) { ++i; continue; }
+            if (!started) { ++i; later_line = true; continue; }
+            if (want_operand) return EV_SYNTAX;
+            for (; i < n; ++i) {
+                uint32_t ch = s[i];
+                if (ch == '#') {
+                    while (i < n && s[i] != '\n' && s[i] != '\r') ++i;
+                    if (i >= n) break;
+                    continue;
+                }
+                if (ch != ' ' && ch != '\t' && ch != 0x0c && ch != '\n' && ch != '\r')
+                    return EV_SYNTAX;
+            }
+            {   // a last line of spaces or tabs only (no newline after it) is an
+                // IndentationError in eval
+                uint32_t k = n;
+                bool blank_indent = false;
+                while (k > 0 && s[k - 1] != '\n' && s[k - 1] != '\r') {
+                    uint32_t ch = s[k - 1];
+                    if (ch == ' ' || ch == '\t') blank_indent = true;
+                    else if (ch != 0x0c) { blank_indent = false; break; }
+                    --k;
+                }
+                if (blank_indent) return EV_SYNTAX;
+            }
+            break;
+        }
+        if (!started && later_line && indented) return EV_SYNTAX;  // IndentationError
+        started = true;
+        if (s[i] < 0x20 || s[i] == 0x7f) return EV_SYNTAX;  // non-printable character
         if (no + 2 >= cap || nops + 2 >= cap) return EV_UNSUP;
         uint32_t c = s[i], c1 = i + 1 < n ? s[i + 1] : 0;
         if (c - '0' < 10u) {
@@ -614,7 +652,8 @@ __device__ int to_rpn(const uint8_t *s, uint32_t n, RpnItem *out, uint32_t &no, 
             continue;
         }
         if (c == ')') {
-            if (want_operand) return depth > 0 && i > 0 && s[i - 1] == '(' ? EV_UNSUP : EV_SYNTAX;
+            // "()" is the empty tuple
+            if (want_operand) return nops && ops[nops - 1] == OP_LPAREN ? EV_UNSUP : EV_SYNTAX;
             while (nops && ops[nops - 1] != OP_LPAREN) { --nops; emit(ops[nops], opchain[nops], 0); }
             if (!nops) return EV_SYNTAX;
             --nops;
