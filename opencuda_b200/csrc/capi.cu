@@ -191,6 +191,26 @@ static int upload_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off
     return 0;
 }
 
+static int download_text(ocb_ctx *ctx, ocb_text *t, uint32_t n_tu, uint64_t total) {
+    cudaStream_t st = ctx->stream;
+    t->n_tu = n_tu;
+    t->bytes.resize(total);
+    t->off.resize((size_t)n_tu + 1);
+    t->status.resize(n_tu);
+    t->qinclude.resize(n_tu);
+    cudaError_t e = cudaSuccess;
+    if (total) e = cudaMemcpyAsync(t->bytes.data(), ctx->pp_text.p, total, cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaMemcpyAsync(t->off.data(), ctx->pp_off.p, 8 * ((size_t)n_tu + 1),
+                                cudaMemcpyDeviceToHost, st);
+    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->pp_status.p, 4 * (size_t)n_tu,
+                                        cudaMemcpyDeviceToHost, st);
+    if (!e && n_tu) e = cudaMemcpyAsync(t->qinclude.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu,
+                                        cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    if (e) return fail(ctx, "d2h text", e);
+    return 0;
+}
+
 int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
                          ocb_text **out) {
     if (!ctx || !out || !tu_off) return fail(ctx, "ocb_preprocess_batch: null argument");
@@ -210,23 +230,57 @@ int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_of
     if (rc) return rc;
     ocb_text *t = new (std::nothrow) ocb_text();
     if (!t) return fail(ctx, "ocb_preprocess_batch: out of host memory");
-    t->n_tu = n_tu;
-    t->bytes.resize(total);
-    t->off.resize((size_t)n_tu + 1);
-    t->status.resize(n_tu);
-    t->qinclude.resize(n_tu);
-    cudaError_t e = cudaSuccess;
-    if (total) e = cudaMemcpyAsync(t->bytes.data(), ctx->pp_text.p, total, cudaMemcpyDeviceToHost, st);
-    if (!e) e = cudaMemcpyAsync(t->off.data(), ctx->pp_off.p, 8 * ((size_t)n_tu + 1),
-                                cudaMemcpyDeviceToHost, st);
-    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->pp_status.p, 4 * (size_t)n_tu,
-                                        cudaMemcpyDeviceToHost, st);
-    if (!e && n_tu) e = cudaMemcpyAsync(t->qinclude.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu,
-                                        cudaMemcpyDeviceToHost, st);
-    if (!e) e = cudaStreamSynchronize(st);
-    if (e) {
+    rc = download_text(ctx, t, n_tu, total);
+    if (rc) {
         delete t;
-        return fail(ctx, "d2h text", e);
+        return rc;
+    }
+    // TUs whose arena was too small (macro growth) run again, alone, with a
+    // larger arena; their output replaces the first attempt's.
+    for (uint32_t scale = 32; scale <= 512; scale *= 16) {
+        std::vector<uint32_t> redo;
+        for (uint32_t i = 0; i < n_tu; ++i)
+            if (t->status[i] == OCB_TU_OVERFLOW) redo.push_back(i);
+        if (redo.empty()) break;
+        std::vector<uint64_t> sub_off(redo.size() + 1, 0);
+        for (size_t k = 0; k < redo.size(); ++k)
+            sub_off[k + 1] = sub_off[k] + (tu_off[redo[k] + 1] - tu_off[redo[k]]);
+        std::vector<uint8_t> sub(sub_off.back() + 1);
+        for (size_t k = 0; k < redo.size(); ++k)
+            memcpy(sub.data() + sub_off[k], src + tu_off[redo[k]], sub_off[k + 1] - sub_off[k]);
+        uint64_t sN = 0;
+        rc = upload_batch(ctx, sub.data(), sub_off.data(), (uint32_t)redo.size(), sN);
+        uint64_t stotal = 0;
+        if (!rc)
+            rc = pp_device(ctx, ctx->d_src.as<uint8_t>(), sN, ctx->d_tu_off.as<uint64_t>(),
+                           (uint32_t)redo.size(), scale, ctx->pp_text, ctx->pp_off.as<uint64_t>(),
+                           ctx->pp_status.as<int32_t>(), ctx->pp_qinc.as<uint32_t>(), &stotal, st);
+        ocb_text r;
+        if (!rc) rc = download_text(ctx, &r, (uint32_t)redo.size(), stotal);
+        if (rc) {
+            delete t;
+            return rc;
+        }
+        // splice the retried TUs into the result
+        ocb_text m;
+        m.n_tu = n_tu;
+        m.off.resize((size_t)n_tu + 1);
+        m.status = t->status;
+        m.qinclude = t->qinclude;
+        size_t k = 0;
+        for (uint32_t i = 0; i < n_tu; ++i) {
+            m.off[i] = m.bytes.size();
+            if (k < redo.size() && redo[k] == i) {
+                m.bytes.insert(m.bytes.end(), r.bytes.begin() + r.off[k], r.bytes.begin() + r.off[k + 1]);
+                m.status[i] = r.status[k];
+                m.qinclude[i] = r.qinclude[k];
+                ++k;
+            } else {
+                m.bytes.insert(m.bytes.end(), t->bytes.begin() + t->off[i], t->bytes.begin() + t->off[i + 1]);
+            }
+        }
+        m.off[n_tu] = m.bytes.size();
+        *t = std::move(m);
     }
     *out = t;
     return 0;
