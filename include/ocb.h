@@ -111,6 +111,19 @@ int  ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,
                    const uint32_t **qinclude);
 void ocb_text_free(ocb_text *t);
 
+/* ---- parser ------------------------------------------------------------- */
+/* Preprocess, lex and parse every TU of a host batch.  Replaces
+ * opencuda/frontend/parser.py:4446 parse(source) applied to the preprocessed
+ * text (the CLI's __main__.py:39-51 path up to the IR).  Each TU's output is
+ * its IR as canonical text (one line per kernel, parameter, shared/local
+ * array, block, instruction and terminator; the line grammar of the oracle's
+ * IR dump).  Status per TU: OCB_TU_OK, OCB_TU_RAISES_* where the reference
+ * raises (ParseError, ValueError, ...), OCB_TU_UNSUPPORTED for constructs this
+ * engine does not reproduce, OCB_TU_OVERFLOW when arena retries ran out.
+ * Free the result with ocb_text_free. */
+int  ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                     uint32_t n_tu, ocb_text **out);
+
 /* Allocation-free form of ocb_lex_device, for callers that may not allocate
  * device memory when they lex (a framework's memory pool or a fixed arena that
  * forbids cudaMalloc/cudaFree after start-up, or a thread that must not take

@@ -167,6 +167,14 @@ class Context:
     # ---- preprocessor ----------------------------------------------------
     def preprocess_batch(self, srcs=None, *, buf=None, tu_off=None) -> TextBatch:
         """Preprocess every TU (``preprocess.py:178`` as the CLI calls it)."""
+        return self._text_call("ocb_preprocess_batch", srcs, buf, tu_off)
+
+    def parse_batch(self, srcs=None, *, buf=None, tu_off=None) -> TextBatch:
+        """Preprocess, lex and parse every TU (``parser.py:4446 parse``); each
+        TU's text is its IR in the canonical line format."""
+        return self._text_call("ocb_parse_batch", srcs, buf, tu_off)
+
+    def _text_call(self, fn, srcs, buf, tu_off) -> TextBatch:
         if srcs is not None:
             buf, tu_off = pack_sources(srcs)
         buf = np.ascontiguousarray(buf, dtype=np.uint8)
@@ -174,8 +182,8 @@ class Context:
         n_tu = len(tu_off) - 1
         out = ctypes.c_void_p()
         src_ptr = buf.ctypes.data if len(buf) else None
-        self._check(self.lib.ocb_preprocess_batch(self.h, src_ptr, tu_off.ctypes.data, n_tu,
-                                                  ctypes.byref(out)), "ocb_preprocess_batch")
+        self._check(getattr(self.lib, fn)(self.h, src_ptr, tu_off.ctypes.data, n_tu,
+                                          ctypes.byref(out)), fn)
         try:
             n = ctypes.c_uint64()
             ps = [ctypes.c_void_p() for _ in range(4)]
@@ -212,3 +220,7 @@ def lex_batch(srcs, device: int = 0) -> TokenBatch:
 
 def preprocess_batch(srcs, device: int = 0) -> TextBatch:
     return context(device).preprocess_batch(srcs)
+
+
+def parse_batch(srcs, device: int = 0) -> TextBatch:
+    return context(device).parse_batch(srcs)

@@ -286,6 +286,92 @@ int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_of
     return 0;
 }
 
+// Run the back half (lex + parse) over TUs already preprocessed on the host;
+// TUs that outgrow their arena run again alone with larger arenas.
+static int compile_text(ocb_ctx *ctx, const ocb_text &pp, ocb_text *out) {
+    cudaStream_t st = ctx->stream;
+    uint32_t n_tu = pp.n_tu;
+    out->n_tu = n_tu;
+    out->status.assign(n_tu, 0);
+    out->qinclude = pp.qinclude;
+    out->off.assign((size_t)n_tu + 1, 0);
+    out->bytes.clear();
+    std::vector<uint32_t> todo(n_tu);
+    for (uint32_t i = 0; i < n_tu; ++i) todo[i] = i;
+    std::vector<std::vector<uint8_t>> res(n_tu);
+    for (uint32_t scale = 1; !todo.empty(); scale *= 8) {
+        // sub-batch of the pending TUs
+        std::vector<uint64_t> off(todo.size() + 1, 0);
+        for (size_t k = 0; k < todo.size(); ++k)
+            off[k + 1] = off[k] + (pp.off[todo[k] + 1] - pp.off[todo[k]]);
+        std::vector<uint8_t> text(off.back() + 1);
+        std::vector<int32_t> in_st(todo.size());
+        for (size_t k = 0; k < todo.size(); ++k) {
+            memcpy(text.data() + off[k], pp.bytes.data() + pp.off[todo[k]], off[k + 1] - off[k]);
+            in_st[k] = pp.status[todo[k]];
+        }
+        uint64_t N = 0;
+        int rc = upload_batch(ctx, text.data(), off.data(), (uint32_t)todo.size(), N);
+        if (rc) return rc;
+        size_t nt = todo.size();
+        OCB_TRY("device status", ctx->cc_in_status.ensure(4 * nt + 4));
+        OCB_TRY("device status", ctx->cc_status.ensure(4 * nt + 4));
+        OCB_TRY("device offsets", ctx->cc_off.ensure(8 * (nt + 1)));
+        OCB_TRY("h2d status", cudaMemcpyAsync(ctx->cc_in_status.p, in_st.data(), 4 * nt,
+                                              cudaMemcpyHostToDevice, st));
+        uint64_t total = 0;
+        rc = cc_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(),
+                       (uint32_t)nt, ctx->cc_in_status.as<int32_t>(), scale, ctx->cc_text,
+                       ctx->cc_off.as<uint64_t>(), ctx->cc_status.as<int32_t>(), &total, st);
+        if (rc) return rc;
+        std::vector<uint8_t> bytes(total);
+        std::vector<uint64_t> o(nt + 1);
+        std::vector<int32_t> s(nt);
+        cudaError_t e = cudaSuccess;
+        if (total) e = cudaMemcpyAsync(bytes.data(), ctx->cc_text.p, total, cudaMemcpyDeviceToHost, st);
+        if (!e) e = cudaMemcpyAsync(o.data(), ctx->cc_off.p, 8 * (nt + 1), cudaMemcpyDeviceToHost, st);
+        if (!e) e = cudaMemcpyAsync(s.data(), ctx->cc_status.p, 4 * nt, cudaMemcpyDeviceToHost, st);
+        if (!e) e = cudaStreamSynchronize(st);
+        if (e) return fail(ctx, "d2h compile output", e);
+        std::vector<uint32_t> next;
+        for (size_t k = 0; k < nt; ++k) {
+            uint32_t i = todo[k];
+            out->status[i] = s[k];
+            if (s[k] == OCB_TU_OVERFLOW && scale < 64) next.push_back(i);
+            else res[i].assign(bytes.begin() + o[k], bytes.begin() + o[k + 1]);
+        }
+        todo.swap(next);
+    }
+    for (uint32_t i = 0; i < n_tu; ++i) {
+        out->off[i] = out->bytes.size();
+        out->bytes.insert(out->bytes.end(), res[i].begin(), res[i].end());
+    }
+    out->off[n_tu] = out->bytes.size();
+    return 0;
+}
+
+int ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                    ocb_text **out) {
+    if (!ctx || !out || !tu_off) return fail(ctx, "ocb_parse_batch: null argument");
+    *out = nullptr;
+    ocb_text *pp = nullptr;
+    int rc = ocb_preprocess_batch(ctx, src, tu_off, n_tu, &pp);
+    if (rc) return rc;
+    ocb_text *t = new (std::nothrow) ocb_text();
+    if (!t) {
+        delete pp;
+        return fail(ctx, "ocb_parse_batch: out of host memory");
+    }
+    rc = compile_text(ctx, *pp, t);
+    delete pp;
+    if (rc) {
+        delete t;
+        return rc;
+    }
+    *out = t;
+    return 0;
+}
+
 int ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,
                   const uint64_t **off, const int32_t **status, const uint32_t **qinclude) {
     if (!t) return -1;

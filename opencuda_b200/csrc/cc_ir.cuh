@@ -1,0 +1,392 @@
+// Compiler core data model (host+device C++): per-TU arena, strings, types,
+// and the SSA IR of opencuda/ir/nodes.py:23-289 / ir/types.py:15-142.
+//
+// One thread compiles one TU inside a private arena of global memory; every
+// container grows inside that arena (nothing is freed until the TU is done).
+// Running out of arena sets `oom`, which the driver reports as
+// OCB_TU_OVERFLOW and retries with a larger arena.
+#pragma once
+#include <stdint.h>
+#include <string.h>
+
+#ifndef OCB_HD
+#define OCB_HD __host__ __device__
+#endif
+// Large or recursive routines stay out of line: inlining them all into one
+// kernel only grows compile time and register pressure.
+#ifndef OCB_NI
+#ifdef __CUDACC__
+#define OCB_NI __noinline__
+#else
+#define OCB_NI __attribute__((noinline))
+#endif
+#endif
+
+namespace ocb {
+namespace cc {
+
+// ---------------------------------------------------------------------------
+// arena + growable vectors
+// ---------------------------------------------------------------------------
+struct Arena {
+    uint8_t *base;
+    uint64_t used, cap;
+    bool oom;
+    OCB_HD void *alloc(uint64_t n, uint64_t align = 8) {
+        uint64_t a = (used + align - 1) & ~(align - 1);
+        if (a + n > cap) {
+            oom = true;
+            return nullptr;
+        }
+        used = a + n;
+        return base + a;
+    }
+};
+
+template <class T>
+struct Vec {
+    T *p;
+    uint32_t n, cap;
+    OCB_HD void init() { p = nullptr; n = cap = 0; }
+    OCB_HD bool reserve(Arena &a, uint32_t want) {
+        if (want <= cap) return true;
+        uint32_t nc = cap ? cap * 2 : 8;
+        while (nc < want) nc *= 2;
+        T *np = (T *)a.alloc(sizeof(T) * (uint64_t)nc, alignof(T) < 8 ? 8 : alignof(T));
+        if (!np) return false;
+        for (uint32_t i = 0; i < n; ++i) np[i] = p[i];
+        p = np;
+        cap = nc;
+        return true;
+    }
+    OCB_HD bool push(Arena &a, const T &v) {
+        if (n == cap && !reserve(a, n + 1)) return false;
+        p[n++] = v;
+        return true;
+    }
+    OCB_HD T &operator[](uint32_t i) { return p[i]; }
+    OCB_HD const T &operator[](uint32_t i) const { return p[i]; }
+    OCB_HD T &back() { return p[n - 1]; }
+    OCB_HD void erase(uint32_t i) {
+        for (uint32_t k = i + 1; k < n; ++k) p[k - 1] = p[k];
+        --n;
+    }
+    OCB_HD bool insert(Arena &a, uint32_t i, const T &v) {
+        if (n == cap && !reserve(a, n + 1)) return false;
+        for (uint32_t k = n; k > i; --k) p[k] = p[k - 1];
+        p[i] = v;
+        ++n;
+        return true;
+    }
+    OCB_HD Vec copy(Arena &a) const {
+        Vec r;
+        r.init();
+        if (n && r.reserve(a, n)) {
+            for (uint32_t i = 0; i < n; ++i) r.p[i] = p[i];
+            r.n = n;
+        }
+        return r;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// strings (not NUL terminated)
+// ---------------------------------------------------------------------------
+struct Str {
+    const char *p;
+    uint32_t n;
+};
+OCB_HD inline uint32_t cstrlen(const char *s) {
+    uint32_t n = 0;
+    while (s[n]) ++n;
+    return n;
+}
+OCB_HD inline Str S(const char *s) { return Str{s, cstrlen(s)}; }
+OCB_HD inline bool eq(Str a, Str b) {
+    if (a.n != b.n) return false;
+    for (uint32_t i = 0; i < a.n; ++i)
+        if (a.p[i] != b.p[i]) return false;
+    return true;
+}
+OCB_HD inline bool eq(Str a, const char *b) {
+    uint32_t i = 0;
+    for (; i < a.n; ++i)
+        if (b[i] != a.p[i] || !b[i]) return false;
+    return b[i] == 0;
+}
+OCB_HD inline bool starts(Str a, const char *b) {
+    uint32_t i = 0;
+    for (; b[i]; ++i)
+        if (i >= a.n || a.p[i] != b[i]) return false;
+    return true;
+}
+OCB_HD inline uint32_t hash(Str s) {
+    uint32_t h = 2166136261u;
+    for (uint32_t i = 0; i < s.n; ++i) h = (h ^ (uint8_t)s.p[i]) * 16777619u;
+    return h;
+}
+// a ++ b (++ c)
+OCB_HD inline Str cat(Arena &a, Str x, Str y, Str z = Str{nullptr, 0}) {
+    char *d = (char *)a.alloc(x.n + y.n + z.n + 1, 1);
+    if (!d) return Str{"?", 1};
+    uint32_t k = 0;
+    for (uint32_t i = 0; i < x.n; ++i) d[k++] = x.p[i];
+    for (uint32_t i = 0; i < y.n; ++i) d[k++] = y.p[i];
+    for (uint32_t i = 0; i < z.n; ++i) d[k++] = z.p[i];
+    d[k] = 0;
+    return Str{d, k};
+}
+OCB_HD inline Str utoa(Arena &a, uint64_t v) {
+    char tmp[24];
+    int k = 0;
+    do {
+        tmp[k++] = (char)('0' + v % 10);
+        v /= 10;
+    } while (v);
+    char *d = (char *)a.alloc(k + 1, 1);
+    if (!d) return Str{"0", 1};
+    for (int i = 0; i < k; ++i) d[i] = tmp[k - 1 - i];
+    d[k] = 0;
+    return Str{d, (uint32_t)k};
+}
+
+// ---------------------------------------------------------------------------
+// types (ir/types.py): packed so that == is the reference's structural ==
+//   bits 0-3 scalar, 4-5 pointer depth, 6-8 outer address space,
+//   9 volatile of the innermost pointer, 10 volatile of the outer pointer
+// ---------------------------------------------------------------------------
+typedef uint32_t Ty;
+enum : uint32_t {
+    S_VOID = 0, S_BOOL, S_INT8, S_UINT8, S_INT16, S_UINT16, S_INT32, S_UINT32,
+    S_INT64, S_UINT64, S_FLOAT, S_DOUBLE, S_HALF
+};
+enum : uint32_t { AS_GENERIC = 0, AS_GLOBAL, AS_SHARED, AS_LOCAL, AS_CONST };
+
+OCB_HD inline Ty ty_s(uint32_t s) { return s; }
+OCB_HD inline uint32_t ty_depth(Ty t) { return (t >> 4) & 3; }
+OCB_HD inline bool is_ptr(Ty t) { return ty_depth(t) != 0; }
+OCB_HD inline uint32_t ty_scalar(Ty t) { return t & 15; }
+OCB_HD inline uint32_t ty_as(Ty t) { return (t >> 6) & 7; }
+OCB_HD inline bool ty_vol(Ty t) {  // PtrTy.volatile of the outermost pointer
+    return ty_depth(t) == 1 ? ((t >> 9) & 1) : ((t >> 10) & 1);
+}
+// PtrTy(pointee, as, vol); representable when only the outermost pointer has a
+// non-global address space and volatile sits on the innermost or outer one.
+OCB_HD inline Ty ty_ptr(Ty pointee, uint32_t as, bool vol, bool &ok) {
+    uint32_t d = ty_depth(pointee);
+    if (d == 0) return pointee | (1u << 4) | (as << 6) | (vol ? 1u << 9 : 0);
+    if (d >= 2 || ty_as(pointee) != AS_GLOBAL || ((pointee >> 10) & 1)) {
+        ok = false;
+        return pointee;
+    }
+    return (pointee & ~((3u << 4) | (7u << 6))) | (2u << 4) | (as << 6) | (vol ? 1u << 10 : 0);
+}
+OCB_HD inline Ty ty_pointee(Ty t) {
+    uint32_t d = ty_depth(t);
+    if (d <= 1) return t & 15;
+    return (t & ~((3u << 4) | (7u << 6) | (1u << 10))) | (1u << 4) | (AS_GLOBAL << 6);
+}
+OCB_HD inline uint32_t ty_size(Ty t) {
+    if (is_ptr(t)) return 8;
+    switch (ty_scalar(t)) {
+    case S_VOID: return 0;
+    case S_BOOL: case S_INT8: case S_UINT8: return 1;
+    case S_INT16: case S_UINT16: case S_HALF: return 2;
+    case S_INT32: case S_UINT32: case S_FLOAT: return 4;
+    default: return 8;
+    }
+}
+OCB_HD inline bool ty_is_float(Ty t) {
+    uint32_t s = ty_scalar(t);
+    return !is_ptr(t) && (s == S_FLOAT || s == S_DOUBLE || s == S_HALF);
+}
+OCB_HD inline bool ty_is_signed(Ty t) {
+    uint32_t s = ty_scalar(t);
+    return !is_ptr(t) && (s == S_INT8 || s == S_INT16 || s == S_INT32 || s == S_INT64);
+}
+// str(ty) equality key (ir/types.py __str__): pointers ignore address space
+OCB_HD inline uint32_t ty_strkey(Ty t) { return is_ptr(t) ? (t & ~(7u << 6)) : t; }
+OCB_HD inline const char *scalar_name(uint32_t s) {
+    switch (s) {
+    case S_VOID: return "void";
+    case S_BOOL: return "bool";
+    case S_INT8: return "char";
+    case S_UINT8: return "unsigned char";
+    case S_INT16: return "short";
+    case S_UINT16: return "unsigned short";
+    case S_INT32: return "int";
+    case S_UINT32: return "unsigned int";
+    case S_INT64: return "long long";
+    case S_UINT64: return "unsigned long long";
+    case S_FLOAT: return "float";
+    case S_DOUBLE: return "double";
+    default: return "half";
+    }
+}
+OCB_HD inline const char *as_name(uint32_t a) {
+    switch (a) {
+    case AS_GENERIC: return "generic";
+    case AS_GLOBAL: return "global";
+    case AS_SHARED: return "shared";
+    case AS_LOCAL: return "local";
+    default: return "const";
+    }
+}
+
+// ---------------------------------------------------------------------------
+// IR
+// ---------------------------------------------------------------------------
+struct Value {
+    uint32_t id;
+    Ty ty;
+    Str name;
+};
+struct Const {
+    Ty ty;
+    uint8_t pyfloat;  // the reference holds a Python float (else an int)
+    int64_t i;
+    double f;
+};
+enum : uint8_t { O_NONE = 0, O_VAL = 1, O_CONST = 2 };
+struct Opnd {
+    uint8_t k;
+    uint32_t x;  // index into values / consts
+};
+OCB_HD inline Opnd ov(uint32_t v) { return Opnd{O_VAL, v}; }
+OCB_HD inline Opnd oc(uint32_t c) { return Opnd{O_CONST, c}; }
+OCB_HD inline Opnd onone() { return Opnd{O_NONE, 0}; }
+
+enum : uint8_t { BO_ADD = 0, BO_SUB, BO_MUL, BO_DIV, BO_MOD, BO_AND, BO_OR, BO_XOR, BO_SHL, BO_SHR };
+enum : uint8_t { CO_EQ = 0, CO_NE, CO_LT, CO_LE, CO_GT, CO_GE };
+OCB_HD inline const char *binop_name(uint8_t o) {
+    const char *n[] = {"add", "sub", "mul", "div", "mod", "and", "or", "xor", "shl", "shr"};
+    return n[o];
+}
+OCB_HD inline const char *cmpop_name(uint8_t o) {
+    const char *n[] = {"==", "!=", "<", "<=", ">", ">="};
+    return n[o];
+}
+
+enum : uint8_t { I_BIN = 0, I_CMP, I_SELECT, I_LOAD, I_STORE, I_CVT, I_CALL, I_PARAM };
+struct Inst {
+    uint8_t kind, op;
+    int32_t dest;     // value index, -1 = none
+    Opnd a, b, c;     // bin/cmp: a op b; select: c ? a : b; load: a; store: a <- b; cvt: a
+    Str func;         // call: builtin name; param: name
+    uint32_t pidx;    // param index
+    Vec<Opnd> args;   // call arguments
+};
+
+enum : uint8_t { T_NONE = 0, T_RET, T_BR, T_CBR };
+struct Term {
+    uint8_t kind;
+    Opnd v;           // ret value / branch condition
+    Str t, f;         // targets
+};
+
+struct Block {
+    Str label;
+    Vec<uint32_t> insts;  // instruction indices
+    Term term;
+};
+
+struct Param {
+    Str name;
+    Ty ty;
+};
+struct SharedDecl {
+    Str name;
+    Ty ty;
+    int64_t count;
+};
+struct LocalDecl {
+    Str name;
+    Ty ty;
+    int64_t count;
+    uint32_t val;
+};
+
+struct Kernel {
+    Str name;
+    Vec<Param> params;
+    Vec<uint32_t> blocks;     // block indices, in reference order
+    uint32_t next_id;
+    int64_t launch[2];
+    uint8_t n_launch;
+    Vec<SharedDecl> shared;
+    Vec<LocalDecl> locals;
+    bool has_locals;           // the reference created _local_decls
+};
+
+// All IR objects of one TU.
+struct Module {
+    Arena *ar;
+    Vec<Value> vals;
+    Vec<Const> consts;
+    Vec<Inst> insts;
+    Vec<Block> blocks;
+    Vec<Kernel> kernels;
+    bool unsup;               // the engine cannot reproduce this TU
+    int raises;               // reference exception (OCB_TU_RAISES_*) or 0
+
+    OCB_HD void init(Arena *a) {
+        ar = a;
+        vals.init();
+        consts.init();
+        insts.init();
+        blocks.init();
+        kernels.init();
+        unsup = false;
+        raises = 0;
+    }
+    OCB_HD uint32_t add_val(uint32_t id, Ty ty, Str name) {
+        vals.push(*ar, Value{id, ty, name});
+        return vals.n - 1;
+    }
+    OCB_HD Opnd cint(Ty ty, int64_t v) {
+        Const c{ty, 0, v, 0.0};
+        consts.push(*ar, c);
+        return oc(consts.n - 1);
+    }
+    OCB_HD Opnd cfloat(Ty ty, double v) {
+        Const c{ty, 1, 0, v};
+        consts.push(*ar, c);
+        return oc(consts.n - 1);
+    }
+    // Const(ty, 0.0 if ty.is_float else 0)
+    OCB_HD Opnd czero(Ty ty) { return ty_is_float(ty) ? cfloat(ty, 0.0) : cint(ty, 0); }
+    OCB_HD Ty opty(Opnd o) const {
+        if (o.k == O_VAL) return vals[o.x].ty;
+        if (o.k == O_CONST) return consts[o.x].ty;
+        return S_VOID;
+    }
+    OCB_HD uint32_t new_block(Str label) {
+        Block b;
+        b.label = label;
+        b.insts.init();
+        b.term = Term{T_NONE, onone(), Str{nullptr, 0}, Str{nullptr, 0}};
+        blocks.push(*ar, b);
+        return blocks.n - 1;
+    }
+    OCB_HD uint32_t add_inst(const Inst &i) {
+        insts.push(*ar, i);
+        return insts.n - 1;
+    }
+};
+
+OCB_HD inline Inst mk_inst(uint8_t kind, uint8_t op, int32_t dest, Opnd a, Opnd b) {
+    Inst i;
+    i.kind = kind;
+    i.op = op;
+    i.dest = dest;
+    i.a = a;
+    i.b = b;
+    i.c = onone();
+    i.func = Str{nullptr, 0};
+    i.pidx = 0;
+    i.args.init();
+    return i;
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -1,0 +1,1106 @@
+// Parser, expressions: parser.py:368-2249 restated for the supported subset.
+#pragma once
+#include "cc_parse.cuh"
+
+namespace ocb {
+namespace cc {
+
+// str.isupper() for an identifier token of <= 2 chars (template parameter
+// heuristic of _parse_type, parser.py:464-468)
+OCB_HD inline bool py_isupper(Str s) {
+    bool cased = false;
+    for (uint32_t i = 0; i < s.n; ++i) {
+        char c = s.p[i];
+        if (c >= 'a' && c <= 'z') return false;
+        if (c >= 'A' && c <= 'Z') cased = true;
+    }
+    return cased;
+}
+
+// typedef names registered in Parser.__init__ (parser.py:73-86)
+OCB_HD inline bool typedef_scalar(Str v, Ty &t) {
+    if (eq(v, "bool")) { t = S_INT32; return true; }
+    if (eq(v, "size_t") || eq(v, "uintptr_t") || eq(v, "uint64_t")) { t = S_UINT64; return true; }
+    if (eq(v, "ptrdiff_t") || eq(v, "intptr_t") || eq(v, "int64_t")) { t = S_INT64; return true; }
+    if (eq(v, "int8_t") || eq(v, "int16_t") || eq(v, "int32_t")) { t = S_INT32; return true; }
+    if (eq(v, "uint8_t") || eq(v, "uint16_t") || eq(v, "uint32_t")) { t = S_UINT32; return true; }
+    return false;
+}
+// CUDA vector types registered as structs (parser.py:98-128)
+OCB_HD inline bool vector_type_name(Str v) {
+    const char *n[] = {"float2", "float3", "float4", "double2", "int2", "int3", "int4",
+                       "uint2", "uint3", "uint4", "short2", "ushort2", "char2", "uchar2",
+                       "char4", "uchar4", "long2", "ulong2", "longlong2", "ulonglong2"};
+    for (auto s : n)
+        if (eq(v, s)) return true;
+    return false;
+}
+
+
+// --- intrinsic name tables of _parse_primary_expr (parser.py:1929-2033) ---
+// Each list is one space-delimited string, so it lives in code on host and device.
+OCB_HD inline bool in_list(Str n, const char *l) {
+    for (uint32_t i = 0; l[i]; ++i) {
+        if (l[i] != ' ') continue;
+        uint32_t j = 0;
+        while (j < n.n && l[i + 1 + j] == n.p[j]) ++j;
+        if (j == n.n && n.n && l[i + 1 + j] == ' ') return true;
+    }
+    return false;
+}
+OCB_HD inline bool contains(Str s, const char *sub) {
+    uint32_t k = cstrlen(sub);
+    for (uint32_t i = 0; i + k <= s.n; ++i) {
+        uint32_t j = 0;
+        while (j < k && s.p[i + j] == sub[j]) ++j;
+        if (j == k) return true;
+    }
+    return false;
+}
+#define kTexFetch " tex1Dfetch tex2D tex3D "
+#define kSurfVoid " surf1Dwrite "
+#define kVoidStmts " __threadfence __threadfence_block __threadfence_system __nanosleep __trap __brkpt "
+#define kSyncReduce " __syncthreads_count __syncthreads_and __syncthreads_or "
+#define kIntOps " __popc __popcll __clz __clzll __brev __brevll __ffs __ffsll "
+#define kPredInt " isnan isinf isfinite __isnan __isinf __isfinite __isnanf __isinff __isfinitef "
+#define kFloat2Int                                                                          \
+    " __float2int_rn __float2int_rd __float2int_ru __float2int_rz __float2uint_rn"          \
+    " __float2uint_rd __float2uint_ru __float2uint_rz __float2ll_rn __float2ll_rd"          \
+    " __float2ll_ru __float2ll_rz __float2ull_rn __float2ull_rd __float2ull_ru"             \
+    " __float2ull_rz __double2int_rn __double2int_rz __double2uint_rn __double2uint_rz"     \
+    " __double2ll_rn __double2ll_rz __double2ull_rn __double2ull_rz __float_as_int"         \
+    " __float_as_uint __double_as_longlong __double_as_ulonglong "
+#define kInt2Float                                                                          \
+    " __int2float_rn __int2float_rd __int2float_ru __int2float_rz __uint2float_rn"          \
+    " __uint2float_rd __uint2float_ru __uint2float_rz __ll2float_rn __ll2float_rz"          \
+    " __ull2float_rn __ull2float_rz __int2double_rn __ll2double_rn __uint2double_rn"        \
+    " __ull2double_rn __int_as_float __uint_as_float __longlong_as_double"                  \
+    " __ulonglong_as_double "
+#define kWarpReduceInt " __reduce_add_sync __reduce_min_sync __reduce_max_sync "
+#define kWarpReduceUint " __reduce_and_sync __reduce_or_sync __reduce_xor_sync __reduce_umin_sync __reduce_umax_sync "
+#define kIntBinary2 " __mul24 __mulhi "
+#define kUintBinary2 " __umul24 __umulhi __rhadd __byte_perm __funnelshift_l __funnelshift_r __funnelshift_lc __funnelshift_rc "
+#define kHalfUnary                                                                          \
+    " __habs __hneg __hsqrt __hrcp __hrsqrt __hexp __hlog __hceil __hfloor __hrint"         \
+    " __htrunc __hcos __hsin __hexp2 __hlog2 __hlog10 __half2float __low2float"             \
+    " __high2float "
+#define kHalfBinary " __hmul __hmul_rn __hmul_sat __hadd_rn __hsub __hsub_rn __hdiv __hfmin __hfmax __hmin __hmax "
+#define kHalfTernary " __hfma __hfma_sat __hfma_relu "
+#define kHalfCmpInt " __hgt __hlt __hge __hle __heq __hne __hisnan __hisinf "
+#define kHalfCvt                                                                            \
+    " __float2half __float2half_rn __float2half_rd __float2half_ru __float2half_rz"         \
+    " __int2half_rn __int2half_rd __int2half_ru __int2half_rz __uint2half_rn"               \
+    " __uint2half_rd __uint2half_ru __uint2half_rz __short2half_rn __ushort2half_rn"        \
+    " __ll2half_rn __ll2half_rz __ull2half_rn __ull2half_rz __ushort_as_half"               \
+    " __short_as_half "
+#define kHalf2Int                                                                           \
+    " __half2int_rn __half2int_rz __half2uint_rn __half2uint_rz __half2short_rn"            \
+    " __half2short_rz __half2ushort_rn __half2ushort_rz __half2ll_rn __half2ll_rz"          \
+    " __half2ull_rn __half2ull_rz "
+#define kFloatUnary                                                                         \
+    " sqrtf rsqrtf rcpf fabsf sinf cosf tanf expf exp2f exp10f logf log2f log10f"           \
+    " floorf ceilf roundf truncf atanf asinf acosf sqrt rsqrt fabs sin cos exp exp2"        \
+    " exp10 log log2 log10 floor ceil round trunc atan asin acos __fsqrt_rn __fsqrt_rd"     \
+    " __fsqrt_ru __fsqrt_rz __frcp_rn __frcp_rd __frcp_ru __frcp_rz __frsqrt_rn "
+#define kFloatBinary " fminf fmaxf fmodf powf fmin fmax fmod pow hypotf atan2f "
+#define kFloatTernary " fmaf fma __fmaf_rn __fmaf_rd __fmaf_ru __fmaf_rz __fma_rn __fma_rd __fma_ru __fma_rz "
+
+// _parse_type (parser.py:368-472)
+OCB_HD inline bool Parser::parse_type(Ty &out) {
+    while (peek() == TK_VOLATILE || peek() == TK_CONST) advance();
+    uint32_t k = peek();
+    switch (k) {
+    case TK_VOID: advance(); out = S_VOID; return true;
+    case TK_FLOAT: advance(); out = S_FLOAT; return true;
+    case TK_DOUBLE: advance(); out = S_DOUBLE; return true;
+    case TK_HALF: advance(); out = S_HALF; return true;
+    case TK_INT: advance(); out = S_INT32; return true;
+    case TK_UNSIGNED:
+        advance();
+        if (match(TK_INT)) {
+        } else if (match(TK_SHORT)) {
+            match(TK_INT);
+            out = S_UINT16;
+            return true;
+        } else if (match(TK_CHAR)) {
+            out = S_UINT8;
+            return true;
+        } else if (match(TK_LONG)) {
+            if (match(TK_LONG)) {
+                match(TK_INT);
+                out = S_UINT64;
+                return true;
+            }
+            match(TK_INT);
+        }
+        out = S_UINT32;
+        return true;
+    case TK_LONG:
+        advance();
+        if (match(TK_LONG)) {
+            match(TK_INT);
+            out = S_INT64;
+            return true;
+        }
+        match(TK_INT);
+        out = S_INT32;
+        return true;
+    case TK_SHORT: advance(); match(TK_INT); out = S_INT16; return true;
+    case TK_SIGNED:
+        advance();
+        if (match(TK_CHAR)) { out = S_INT8; return true; }
+        if (match(TK_SHORT)) { match(TK_INT); out = S_INT16; return true; }
+        if (match(TK_LONG)) {
+            if (match(TK_LONG)) { match(TK_INT); out = S_INT64; return true; }
+            match(TK_INT);
+            out = S_INT32;
+            return true;
+        }
+        match(TK_INT);
+        out = S_INT32;
+        return true;
+    case TK_CHAR: advance(); out = S_INT8; return true;
+    case TK_BOOL: advance(); out = S_INT32; return true;
+    default: break;
+    }
+    if (k == TK_STRUCT || k == TK_UNION) {
+        unsup();  // struct types are outside the subset
+        return false;
+    }
+    if (k == TK_ENUM) {
+        advance();
+        if (at(TK_IDENT)) advance();
+        out = S_INT32;
+        return true;
+    }
+    if (k == TK_IDENT) {
+        Str v = peekv();
+        Ty t;
+        if (typedef_scalar(v, t)) {
+            advance();
+            out = t;
+            return true;
+        }
+        if (vector_type_name(v)) {
+            unsup();
+            return false;
+        }
+        if (v.n <= 2 && py_isupper(v)) {
+            advance();
+            out = S_FLOAT;
+            return true;
+        }
+    }
+    perr();
+    return false;
+}
+
+// _parse_type_with_ptr (parser.py:474-508)
+OCB_HD inline bool Parser::parse_type_with_ptr(Ty &out) {
+    match(TK_STATIC);
+    bool pv = match(TK_VOLATILE);
+    bool pc = match(TK_CONST);
+    if (match(TK_VOLATILE)) pv = true;
+    match(TK_STATIC);
+    Ty base;
+    if (!parse_type(base)) return false;
+    if (match(TK_CONST)) pc = true;
+    if (match(TK_VOLATILE)) pv = true;
+    while (match(TK_STAR)) {
+        match(TK_CONST);
+        match(TK_VOLATILE);
+        bool ok = true;
+        base = ty_ptr(base, AS_GLOBAL, pv, ok);
+        if (!ok) { unsup(); return false; }
+        pv = false;
+    }
+    bool restrict_ = at(TK_IDENT) && eq(peekv(), "__restrict__");
+    if (restrict_) advance();
+    if (pc && restrict_ && is_ptr(base)) base = (base & ~(7u << 6)) | (AS_CONST << 6);
+    out = base;
+    return true;
+}
+
+OCB_HD inline Opnd Parser::parse_expr() {
+    Opnd r = parse_assign_expr();
+    while (!bad() && match(TK_COMMA)) r = parse_assign_expr();
+    return r;
+}
+
+// _parse_assign_expr (parser.py:521-692)
+OCB_HD inline Opnd Parser::parse_assign_expr() {
+    if (++nest > MAX_NEST) { unsup(); --nest; return onone(); }
+    Str lhs_orig{nullptr, 0};
+    if (at(TK_IDENT)) {
+        Str cand = peekv();
+        uint32_t np = pos + 1;
+        if (np < tk.n && is_assign_op(kind_at(np)) && vars.has(cand)) lhs_orig = cand;
+    }
+    Opnd lhs = parse_or_expr();
+    Opnd result = lhs;
+    if (bad()) goto out;
+    if (match(TK_QUESTION)) {
+        Opnd tv = parse_expr();
+        if (bad() || !expect(TK_COLON)) goto out;
+        Opnd fv = parse_assign_expr();
+        if (bad()) goto out;
+        Ty rt = result_type(tv, fv);
+        uint32_t dest = new_val("ternary", rt);
+        uint32_t tb = new_block("tern_true"), fb = new_block("tern_false"),
+                 mb = new_block("tern_merge");
+        B().term = Term{T_CBR, lhs, m.blocks[tb].label, m.blocks[fb].label};
+        cur = tb;
+        emit_bin(dest, BO_ADD, tv, m.czero(rt));
+        m.blocks[tb].term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        cur = fb;
+        emit_bin(dest, BO_ADD, fv, m.czero(rt));
+        m.blocks[fb].term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        cur = mb;
+        result = ov(dest);
+        goto out;
+    }
+    if (match(TK_ASSIGN)) {
+        Opnd rhs = parse_assign_expr();
+        if (bad()) goto out;
+        if (isval(lhs) && is_ptr(tyof(lhs))) {
+            if (lhs_orig.p && vars.has(lhs_orig) && !shared_scalars.has(lhs_orig)) {
+                vars.set(ar, lhs_orig, rhs);
+                result = rhs;
+                goto out;
+            }
+            Ty pt = ty_pointee(tyof(lhs));
+            Ty rt = tyof(rhs);
+            if (isval(rhs) && !is_ptr(rt) && !is_ptr(pt) && rt != pt) {
+                uint32_t co = new_val("coerce", pt);
+                emit_cvt(co, rhs);
+                rhs = ov(co);
+            } else if (iscon(rhs) && !is_ptr(pt) && !is_ptr(rt) && rt != pt && !ty_is_float(rt) &&
+                       !ty_is_float(pt)) {
+                Const c = m.consts[rhs.x];
+                c.ty = pt;
+                m.consts.push(ar, c);
+                rhs = oc(m.consts.n - 1);
+            }
+            emit_store(lhs, rhs);
+            result = rhs;
+            goto out;
+        }
+        Str un = lhs_orig.p ? lhs_orig : (isval(lhs) ? vname(lhs) : Str{nullptr, 0});
+        if (un.p && vars.has(un)) {
+            Opnd prev = *vars.get(un);
+            if (prev.k == O_VAL && !is_ptr(tyof(prev)) && (rhs.k == O_VAL || rhs.k == O_CONST) &&
+                !is_ptr(tyof(rhs))) {
+                if (iscon(rhs) || (isval(rhs) && !eq(vname(rhs), un))) {
+                    Ty pt = tyof(prev);
+                    uint32_t mat = new_val(un, pt);
+                    emit_bin(mat, BO_ADD, rhs, m.czero(pt));
+                    rhs = ov(mat);
+                }
+            }
+            vars.set(ar, un, rhs);
+        }
+        result = rhs;
+        goto out;
+    }
+    {
+        static const uint32_t toks[] = {TK_PLUS_EQ, TK_MINUS_EQ, TK_STAR_EQ, TK_SLASH_EQ,
+                                        TK_PERCENT_EQ, TK_AMP_EQ, TK_PIPE_EQ, TK_CARET_EQ,
+                                        TK_LSHIFT_EQ, TK_RSHIFT_EQ};
+        static const uint8_t ops[] = {BO_ADD, BO_SUB, BO_MUL, BO_DIV, BO_MOD,
+                                      BO_AND, BO_OR, BO_XOR, BO_SHL, BO_SHR};
+        for (int k = 0; k < 10; ++k) {
+            if (match(toks[k])) {
+                Opnd rhs = parse_assign_expr();
+                if (bad()) goto out;
+                if (isval(lhs)) {
+                    uint32_t nv = new_val(cat(ar, vname(lhs), S("_compound")), tyof(lhs));
+                    emit_bin(nv, ops[k], lhs, rhs);
+                    Str un = lhs_orig.p ? lhs_orig : vname(lhs);
+                    if (vars.has(un)) vars.set(ar, un, ov(nv));
+                    result = ov(nv);
+                    goto out;
+                }
+            }
+        }
+    }
+out:
+    --nest;
+    return result;
+}
+
+// _parse_or_expr / _parse_and_expr (parser.py:694-782): short-circuit blocks
+OCB_HD inline Opnd Parser::parse_or_expr() {
+    Opnd lhs = parse_and_expr();
+    while (!bad() && match(TK_OR)) {
+        uint32_t dest = new_val("lor", S_INT32);
+        uint32_t rb = new_block("lor_rhs"), sb = new_block("lor_skip"), mb = new_block("lor_merge");
+        B().term = Term{T_CBR, lhs, m.blocks[sb].label, m.blocks[rb].label};
+        VarMap before = vars.copy(ar);
+        cur = rb;
+        Opnd rhs = parse_and_expr();
+        if (bad()) return lhs;
+        emit_bin(dest, BO_ADD, rhs, m.cint(S_INT32, 0));
+        B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        struct RB { Opnd nv, old; };
+        Vec<RB> reb;
+        reb.init();
+        for (uint32_t i = 0; i < vars.e.n; ++i) {
+            const VarEnt &en = vars.e[i];
+            if (!en.live || en.v.k != O_VAL) continue;
+            Opnd *o = before.get(en.name);
+            if (!o || o->k != O_VAL || o->x == en.v.x) continue;
+            reb.push(ar, RB{en.v, *o});
+        }
+        cur = sb;
+        emit_bin(dest, BO_ADD, m.cint(S_INT32, 1), m.cint(S_INT32, 0));
+        for (uint32_t i = 0; i < reb.n; ++i)
+            emit_bin(reb[i].nv.x, BO_ADD, reb[i].old, m.czero(tyof(reb[i].nv)));
+        B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        cur = mb;
+        lhs = ov(dest);
+    }
+    return lhs;
+}
+
+OCB_HD inline Opnd Parser::parse_and_expr() {
+    Opnd lhs = parse_bitor_expr();
+    while (!bad() && match(TK_AND)) {
+        uint32_t dest = new_val("land", S_INT32);
+        uint32_t rb = new_block("land_rhs"), sb = new_block("land_skip"), mb = new_block("land_merge");
+        B().term = Term{T_CBR, lhs, m.blocks[rb].label, m.blocks[sb].label};
+        VarMap before = vars.copy(ar);
+        cur = rb;
+        Opnd rhs = parse_bitor_expr();
+        if (bad()) return lhs;
+        emit_bin(dest, BO_ADD, rhs, m.cint(S_INT32, 0));
+        B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        struct RB { Opnd nv, old; };
+        Vec<RB> reb;
+        reb.init();
+        for (uint32_t i = 0; i < vars.e.n; ++i) {
+            const VarEnt &en = vars.e[i];
+            if (!en.live || en.v.k != O_VAL) continue;
+            Opnd *o = before.get(en.name);
+            if (!o || o->k != O_VAL || o->x == en.v.x) continue;
+            reb.push(ar, RB{en.v, *o});
+        }
+        cur = sb;
+        emit_bin(dest, BO_ADD, m.cint(S_INT32, 0), m.cint(S_INT32, 0));
+        for (uint32_t i = 0; i < reb.n; ++i)
+            emit_bin(reb[i].nv.x, BO_ADD, reb[i].old, m.czero(tyof(reb[i].nv)));
+        B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+        cur = mb;
+        lhs = ov(dest);
+    }
+    return lhs;
+}
+
+#define OCB_BITLEVEL(FN, NEXT, TOK, OP, NAME)                          \
+    OCB_HD inline Opnd Parser::FN() {                                  \
+        Opnd lhs = NEXT();                                             \
+        while (!bad() && match(TOK)) {                                 \
+            Opnd rhs = NEXT();                                         \
+            if (bad()) return lhs;                                     \
+            Opnd f;                                                    \
+            if (const_fold(OP, lhs, rhs, f)) {                         \
+                lhs = f;                                               \
+            } else {                                                   \
+                uint32_t d = new_val(NAME, result_type(lhs, rhs));    \
+                emit_bin(d, OP, lhs, rhs);                             \
+                lhs = ov(d);                                           \
+            }                                                          \
+        }                                                              \
+        return lhs;                                                    \
+    }
+OCB_BITLEVEL(parse_bitor_expr, parse_bitxor_expr, TK_PIPE, BO_OR, "bitor")
+OCB_BITLEVEL(parse_bitxor_expr, parse_bitand_expr, TK_CARET, BO_XOR, "bitxor")
+OCB_BITLEVEL(parse_bitand_expr, parse_cmp_expr, TK_AMP, BO_AND, "bitand")
+#undef OCB_BITLEVEL
+
+// _parse_cmp_expr (parser.py:823-839): one comparison, its RHS an add-expr
+OCB_HD inline Opnd Parser::parse_cmp_expr() {
+    Opnd lhs = parse_shift_expr();
+    if (bad()) return lhs;
+    static const uint32_t toks[] = {TK_EQ, TK_NE, TK_LT, TK_LE, TK_GT, TK_GE};
+    static const uint8_t ops[] = {CO_EQ, CO_NE, CO_LT, CO_LE, CO_GT, CO_GE};
+    for (int k = 0; k < 6; ++k) {
+        if (match(toks[k])) {
+            Opnd rhs = parse_add_expr();
+            if (bad()) return lhs;
+            uint32_t d = new_val("cmp", S_BOOL);
+            emit_cmp(d, ops[k], lhs, rhs);
+            return ov(d);
+        }
+    }
+    return lhs;
+}
+
+OCB_HD inline Opnd Parser::parse_shift_expr() {
+    Opnd lhs = parse_add_expr();
+    for (;;) {
+        if (bad()) return lhs;
+        uint8_t op;
+        const char *nm;
+        if (match(TK_LSHIFT)) { op = BO_SHL; nm = "shl"; }
+        else if (match(TK_RSHIFT)) { op = BO_SHR; nm = "shr"; }
+        else break;
+        Opnd rhs = parse_add_expr();
+        if (bad()) return lhs;
+        Opnd f;
+        if (const_fold(op, lhs, rhs, f)) {
+            lhs = f;
+        } else {
+            Ty lt = (isval(lhs) || iscon(lhs)) ? tyof(lhs) : (Ty)S_INT32;
+            uint32_t d = new_val(nm, lt);
+            emit_bin(d, op, lhs, rhs);
+            lhs = ov(d);
+        }
+    }
+    return lhs;
+}
+
+OCB_HD inline Opnd Parser::parse_add_expr() {
+    Opnd lhs = parse_mul_expr();
+    for (;;) {
+        if (bad()) return lhs;
+        if (match(TK_PLUS)) {
+            Opnd rhs = parse_mul_expr();
+            if (bad()) return lhs;
+            Ty lt = tyof(lhs), rt = tyof(rhs);
+            if (is_ptr(lt) && !is_ptr(rt)) rhs = scale_ptr_off(lt, rhs);
+            else if (is_ptr(rt) && !is_ptr(lt)) lhs = scale_ptr_off(rt, lhs);
+            Opnd f;
+            if (const_fold(BO_ADD, lhs, rhs, f)) {
+                lhs = f;
+            } else {
+                uint32_t d = new_val("add", result_type(lhs, rhs));
+                emit_bin(d, BO_ADD, lhs, rhs);
+                lhs = ov(d);
+            }
+        } else if (match(TK_MINUS)) {
+            Opnd rhs = parse_mul_expr();
+            if (bad()) return lhs;
+            Ty lt = tyof(lhs), rt = tyof(rhs);
+            if (is_ptr(lt) && !is_ptr(rt)) rhs = scale_ptr_off(lt, rhs);
+            Opnd f;
+            if (const_fold(BO_SUB, lhs, rhs, f)) {
+                lhs = f;
+            } else {
+                uint32_t d = new_val("sub", result_type(lhs, rhs));
+                emit_bin(d, BO_SUB, lhs, rhs);
+                lhs = ov(d);
+            }
+        } else {
+            break;
+        }
+    }
+    return lhs;
+}
+
+OCB_HD inline Opnd Parser::parse_mul_expr() {
+    Opnd lhs = parse_unary_expr();
+    for (;;) {
+        if (bad()) return lhs;
+        uint8_t op;
+        const char *nm;
+        if (match(TK_STAR)) { op = BO_MUL; nm = "mul"; }
+        else if (match(TK_SLASH)) { op = BO_DIV; nm = "div"; }
+        else if (match(TK_PERCENT)) { op = BO_MOD; nm = "mod"; }
+        else break;
+        Opnd rhs = parse_unary_expr();
+        if (bad()) return lhs;
+        Opnd f;
+        if (const_fold(op, lhs, rhs, f)) {
+            lhs = f;
+        } else {
+            uint32_t d = new_val(nm, result_type(lhs, rhs));
+            emit_bin(d, op, lhs, rhs);
+            lhs = ov(d);
+        }
+    }
+    return lhs;
+}
+
+// _parse_unary_expr (parser.py:972-1287)
+OCB_HD inline Opnd Parser::parse_unary_expr() {
+    if (++nest > MAX_NEST) { unsup(); --nest; return onone(); }
+    Opnd r = onone();
+    if (match(TK_AMP)) {
+        bool generic = true;
+        if (at(TK_IDENT)) {
+            Str name = peekv();
+            Opnd *vp = vars.get(name);
+            if (vp) {
+                Opnd var = *vp;
+                Ty vt = tyof(var);
+                if (is_ptr(vt)) {
+                    advance();
+                    if (match(TK_LBRACKET)) {
+                        Opnd index = parse_expr();
+                        if (bad() || !expect(TK_RBRACKET)) goto out;
+                        uint32_t es = ty_size(ty_pointee(vt));
+                        if (es != 1) {
+                            Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                            uint32_t s = new_val("scale", it);
+                            emit_bin(s, BO_MUL, index, m.cint(it, es));
+                            index = ov(s);
+                        }
+                        uint32_t a = new_val("addr", vt);
+                        emit_bin(a, BO_ADD, var, index);
+                        r = ov(a);
+                        goto out;
+                    }
+                    if (at(TK_ARROW) || at(TK_DOT)) {
+                        pos -= 1;  // fall through to the generic handler
+                    } else {
+                        r = var;
+                        goto out;
+                    }
+                } else {
+                    unsup();  // &scalar spills to .local
+                    goto out;
+                }
+            }
+        }
+        if (generic) {
+            Opnd o = parse_unary_expr();
+            if (bad()) goto out;
+            if (o.k == O_VAL && is_ptr(tyof(o))) { r = o; goto out; }
+            if (o.k == O_VAL) { unsup(); goto out; }
+            r = o;
+            goto out;
+        }
+    }
+    if (match(TK_STAR)) {
+        Opnd o = parse_unary_expr();
+        if (bad()) goto out;
+        if (o.k == O_VAL && is_ptr(tyof(o))) {
+            uint32_t d = new_val("deref", ty_pointee(tyof(o)));
+            emit_load(d, o);
+            r = ov(d);
+            goto out;
+        }
+        // not a pointer: the reference carries on with the next checks
+    }
+    if (match(TK_SIZEOF)) {
+        // sizeof(type) or sizeof(expr); any exception in the type tries the expr
+        if (!expect(TK_LPAREN)) goto out;
+        uint32_t saved = pos;
+        Ty st;
+        int64_t size;
+        if (parse_type_with_ptr(st)) {
+            size = ty_size(st);
+        } else {
+            if (!catch_any()) goto out;
+            pos = saved;
+            Opnd e = parse_expr();
+            if (bad()) goto out;
+            size = ty_size((isval(e) || iscon(e)) ? tyof(e) : (Ty)S_INT32);
+        }
+        if (!expect(TK_RPAREN)) goto out;
+        r = m.cint(S_INT32, size);
+        goto out;
+    }
+    if (match(TK_PLUS)) { r = parse_unary_expr(); goto out; }
+    if (match(TK_MINUS)) {
+        Opnd o = parse_unary_expr();
+        if (bad()) goto out;
+        Ty t = (isval(o) || iscon(o)) ? tyof(o) : (Ty)S_INT32;
+        Opnd zero = ty_is_float(t) ? m.cfloat(S_FLOAT, 0.0) : m.cint(t, 0);
+        Opnd f;
+        if (const_fold(BO_SUB, zero, o, f)) { r = f; goto out; }
+        if (bad()) goto out;
+        uint32_t d = new_val("neg", t);
+        emit_bin(d, BO_SUB, zero, o);
+        r = ov(d);
+        goto out;
+    }
+    if (match(TK_TILDE)) {
+        Opnd o = parse_unary_expr();
+        if (bad()) goto out;
+        Ty t = (isval(o) || iscon(o)) ? tyof(o) : (Ty)S_INT32;
+        Opnd ones = !is_ptr(t) ? m.cint(t, -1) : m.cint(S_INT32, -1);
+        Opnd f;
+        if (const_fold(BO_XOR, o, ones, f)) { r = f; goto out; }
+        if (bad()) goto out;
+        uint32_t d = new_val("bnot", t);
+        emit_bin(d, BO_XOR, o, ones);
+        r = ov(d);
+        goto out;
+    }
+    if (match(TK_BANG)) {
+        Opnd o = parse_unary_expr();
+        if (bad()) goto out;
+        uint32_t d = new_val("lnot", S_BOOL);
+        emit_cmp(d, CO_EQ, o, m.cint(S_INT32, 0));
+        r = ov(d);
+        goto out;
+    }
+    if (at(TK_PLUSPLUS) || at(TK_MINUSMINUS)) {
+        bool inc = match(TK_PLUSPLUS);
+        if (!inc) advance();
+        Str pre{nullptr, 0};
+        if (at(TK_IDENT)) pre = peekv();
+        Opnd o = parse_unary_expr();
+        if (bad()) goto out;
+        if (o.k == O_VAL) {
+            Ty t = tyof(o);
+            Opnd step = is_ptr(t) ? scale_ptr_off(t, m.cint(S_INT32, 1)) : m.cint(t, 1);
+            uint32_t nv = new_val(cat(ar, vname(o), S(inc ? "_preinc" : "_predec")), t);
+            emit_bin(nv, inc ? BO_ADD : BO_SUB, o, step);
+            Str un = vname(o);
+            if (pre.p) {
+                Opnd *pv = vars.get(pre);
+                if (pv && pv->k == O_VAL && pv->x == o.x) un = pre;
+            }
+            vars.set(ar, un, ov(nv));
+            r = ov(nv);
+            goto out;
+        }
+        r = o;
+        goto out;
+    }
+    if (at(TK_LPAREN)) {
+        // cast: (type)expr; a ParseError anywhere inside restores the position
+        uint32_t saved = pos;
+        advance();
+        Ty ct;
+        bool ok = parse_type(ct);
+        while (ok && match(TK_STAR)) {
+            bool pok = true;
+            ct = ty_ptr(ct, AS_GLOBAL, false, pok);
+            if (!pok) { unsup(); goto out; }
+        }
+        if (ok && expect(TK_RPAREN)) {
+            Opnd o = parse_unary_expr();
+            if (!bad()) {
+                if (is_ptr(ct) && o.k == O_VAL && is_ptr(tyof(o)) && ty_as(tyof(o)) != AS_GLOBAL) {
+                    bool pok = true;
+                    ct = ty_ptr(ty_pointee(ct), ty_as(tyof(o)), false, pok);
+                    if (!pok) { unsup(); goto out; }
+                }
+                uint32_t d = new_val("cast", ct);
+                emit_cvt(d, o);
+                r = ov(d);
+                goto out;
+            }
+        }
+        if (!catch_parse()) goto out;  // except ParseError: self._pos = saved
+        pos = saved;
+    }
+    r = parse_postfix_expr();
+out:
+    --nest;
+    return r;
+}
+
+// _parse_postfix_expr (parser.py:1289-1530)
+OCB_HD inline Opnd Parser::parse_postfix_expr() {
+    Str src_name{nullptr, 0};
+    if (at(TK_IDENT) && vars.has(peekv())) src_name = peekv();
+    Opnd lhs = parse_primary_expr();
+    for (;;) {
+        if (bad()) return lhs;
+        if (at(TK_PLUSPLUS) || at(TK_MINUSMINUS)) {
+            bool inc = at(TK_PLUSPLUS);
+            advance();
+            if (lhs.k == O_VAL) {
+                Ty t = tyof(lhs);
+                Opnd step = is_ptr(t) ? scale_ptr_off(t, m.cint(S_INT32, 1)) : m.cint(t, 1);
+                uint32_t nv = new_val(cat(ar, vname(lhs), S(inc ? "_inc" : "_dec")), t);
+                emit_bin(nv, inc ? BO_ADD : BO_SUB, lhs, step);
+                Str un = src_name.p ? src_name : vname(lhs);
+                vars.set(ar, un, ov(nv));
+            }
+            src_name = Str{nullptr, 0};
+            continue;
+        }
+        if (match(TK_LBRACKET)) {
+            Opnd index = parse_expr();
+            if (bad() || !expect(TK_RBRACKET)) return lhs;
+            if (lhs.k == O_VAL && is_ptr(tyof(lhs))) {
+                Ty lt = tyof(lhs);
+                Opnd *rs = row_strides.get(vname(lhs));
+                if (rs && at(TK_LBRACKET)) {
+                    Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                    uint32_t s = new_val("scale", it);
+                    emit_bin(s, BO_MUL, index, m.cint(it, m.consts[rs->x].i));
+                    uint32_t a = new_val("addr", lt);
+                    emit_bin(a, BO_ADD, lhs, ov(s));
+                    lhs = ov(a);
+                    continue;
+                }
+                Ty pt = ty_pointee(lt);
+                uint32_t es = ty_size(pt);
+                if (es != 1) {
+                    Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                    uint32_t s = new_val("scale", it);
+                    emit_bin(s, BO_MUL, index, m.cint(it, es));
+                    index = ov(s);
+                }
+                uint32_t a = new_val("addr", lt);
+                emit_bin(a, BO_ADD, lhs, index);
+                if (is_assign_op(peek())) {
+                    lhs = ov(a);
+                } else {
+                    uint32_t d = new_val("elem", pt);
+                    emit_load(d, ov(a));
+                    lhs = ov(d);
+                }
+            }
+            continue;
+        }
+        if (match(TK_DOT)) {
+            if (!at(TK_IDENT)) { perr(); return lhs; }
+            Str member = peekv();
+            advance();
+            if (lhs.k == O_VAL) {
+                Str n = vname(lhs);
+                if (eq(n, "threadIdx") || eq(n, "blockIdx") || eq(n, "blockDim") || eq(n, "gridDim")) {
+                    Str bi = cat(ar, n, S("."), member);
+                    Str vn = cat(ar, n, S("_"), member);
+                    uint32_t d = new_val(vn, S_UINT32);
+                    Inst c = mk_inst(I_CALL, 0, (int32_t)d, onone(), onone());
+                    c.func = bi;
+                    emit(c);
+                    lhs = ov(d);
+                }
+            }
+            continue;
+        }
+        if (match(TK_ARROW)) {
+            if (!at(TK_IDENT)) { perr(); return lhs; }
+            advance();
+            continue;
+        }
+        break;
+    }
+    return lhs;
+}
+
+// Correctly rounded decimal -> double for literals the fast path covers
+// (Clinger: <= 15 significant digits... up to 2^53, |exponent| <= 22).
+OCB_HD inline bool parse_decimal(Str s, double &out) {
+    uint64_t mant = 0;
+    int digits = 0, exp10 = 0;
+    uint32_t i = 0;
+    bool any = false;
+    for (; i < s.n && s.p[i] >= '0' && s.p[i] <= '9'; ++i) {
+        any = true;
+        if (mant == 0 && s.p[i] == '0') continue;
+        if (digits >= 19) return false;
+        mant = mant * 10 + (s.p[i] - '0');
+        ++digits;
+    }
+    if (i < s.n && s.p[i] == '.') {
+        ++i;
+        for (; i < s.n && s.p[i] >= '0' && s.p[i] <= '9'; ++i) {
+            any = true;
+            if (mant == 0 && s.p[i] == '0') { --exp10; continue; }
+            if (digits >= 19) return false;
+            mant = mant * 10 + (s.p[i] - '0');
+            ++digits;
+            --exp10;
+        }
+    }
+    if (!any) return false;
+    if (i < s.n && (s.p[i] == 'e' || s.p[i] == 'E')) {
+        ++i;
+        bool neg = false;
+        if (i < s.n && (s.p[i] == '+' || s.p[i] == '-')) neg = s.p[i++] == '-';
+        int e = 0;
+        bool ed = false;
+        for (; i < s.n && s.p[i] >= '0' && s.p[i] <= '9'; ++i) {
+            ed = true;
+            if (e < 100000) e = e * 10 + (s.p[i] - '0');
+        }
+        if (!ed) return false;
+        exp10 += neg ? -e : e;
+    }
+    if (i != s.n) return false;
+    if (mant == 0) { out = 0.0; return true; }
+    if (mant > (1ull << 53) || exp10 < -22 || exp10 > 22) return false;
+    const double p10[] = {1e0, 1e1, 1e2, 1e3, 1e4, 1e5, 1e6, 1e7, 1e8, 1e9, 1e10, 1e11,
+                          1e12, 1e13, 1e14, 1e15, 1e16, 1e17, 1e18, 1e19, 1e20, 1e21, 1e22};
+    double v = (double)mant;
+    out = exp10 >= 0 ? v * p10[exp10] : v / p10[-exp10];
+    return true;
+}
+
+// _parse_primary_expr (parser.py:1532-2249)
+OCB_HD inline Opnd Parser::parse_primary_expr() {
+    uint32_t k = peek();
+    if (bad()) return onone();
+    Str v = peekv();
+    if (k == TK_CHAR_LIT) {
+        advance();
+        Str raw{v.p + 1, v.n >= 2 ? v.n - 2 : 0};
+        int64_t iv = 0;
+        if (raw.n >= 2 && raw.p[0] == '\\') {
+            char e = raw.p[1];
+            switch (e) {
+            case 'n': iv = 10; break;
+            case 't': iv = 9; break;
+            case 'r': iv = 13; break;
+            case '0': iv = 0; break;
+            case '\\': iv = 92; break;
+            case '\'': iv = 39; break;
+            case '"': iv = 34; break;
+            default: iv = (uint8_t)e;
+            }
+        } else {
+            iv = raw.n ? (uint8_t)raw.p[0] : 0;
+        }
+        if (iv >= 0x80) unsup();
+        return m.cint(S_INT32, iv);
+    }
+    if (k == TK_TRUE) { advance(); return m.cint(S_INT32, 1); }
+    if (k == TK_FALSE) { advance(); return m.cint(S_INT32, 0); }
+    if (k == TK_INT_LIT) {
+        advance();
+        uint32_t e = v.n;
+        bool has_u = false, has_l = false;
+        while (e > 0) {
+            char c = v.p[e - 1] | 0x20;
+            if (c == 'u') has_u = true;
+            else if (c == 'l') has_l = true;
+            else break;
+            --e;
+        }
+        // int(stripped, 0) with C octal rewritten to 0o...
+        uint64_t val = 0;
+        uint32_t i = 0, base = 10;
+        if (e >= 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'x') { base = 16; i = 2; }
+        else if (e >= 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'b') { base = 2; i = 2; }
+        else if (e >= 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'o') { base = 8; i = 2; }
+        else if (e > 1 && v.p[0] == '0') { base = 8; i = 1; }
+        if (i >= e) { raise_(R_VALUE); return onone(); }
+        for (; i < e; ++i) {
+            char c = v.p[i];
+            uint32_t d = (c >= '0' && c <= '9') ? c - '0' : ((c | 0x20) >= 'a' && (c | 0x20) <= 'f') ? (c | 0x20) - 'a' + 10 : 99;
+            if (d >= base) {  // int() rejects it: ValueError
+                raise_(R_VALUE);
+                return onone();
+            }
+            if (val > (0x7FFFFFFFFFFFFFFFull - d) / base) { unsup(); return onone(); }
+            val = val * base + d;
+        }
+        Ty t;
+        if (has_l || val > 0xFFFFFFFFull) t = has_u ? S_UINT64 : S_INT64;
+        else if (has_u || val > 0x7FFFFFFFull) t = S_UINT32;
+        else t = S_INT32;
+        return m.cint(t, (int64_t)val);
+    }
+    if (k == TK_FLOAT_LIT) {
+        advance();
+        uint32_t e = v.n;
+        while (e > 0 && (v.p[e - 1] | 0x20) == 'f') --e;
+        double d;
+        if (!parse_decimal(Str{v.p, e}, d)) { unsup(); return onone(); }
+        return m.cfloat(S_FLOAT, d);
+    }
+    if (k == TK_IDENT || k == TK_HALF) {
+        Str name = v;
+        advance();
+        while (at(TK_COLON) && pos + 1 < tk.n && kind_at(pos + 1) == TK_COLON) {
+            advance();
+            advance();
+            if (at(TK_IDENT)) {
+                name = peekv();
+                advance();
+            }
+        }
+        if (eq(name, "nullptr")) return m.cint(S_UINT64, 0);
+        if ((eq(name, "static_cast") || eq(name, "reinterpret_cast") || eq(name, "const_cast")) &&
+            at(TK_LT)) {
+            unsup();
+            return onone();
+        }
+        if (match(TK_LPAREN)) return parse_call(name);
+        Opnd *vp = vars.get(name);
+        if (vp) {
+            Opnd var = *vp;
+            if (shared_scalars.has(name) && var.k == O_VAL && is_ptr(tyof(var)) &&
+                !at(TK_LBRACKET) && !at(TK_DOT)) {
+                uint32_t d = new_val(name, ty_pointee(tyof(var)));
+                emit_load(d, var);
+                return ov(d);
+            }
+            return var;
+        }
+        if (Opnd *g = global_consts.get(name)) return *g;
+        if (eq(name, "true")) return m.cint(S_INT32, 1);
+        if (eq(name, "false")) return m.cint(S_INT32, 0);
+        if (eq(name, "NULL")) return m.cint(S_UINT64, 0);
+        if (eq(name, "threadIdx") || eq(name, "blockIdx") || eq(name, "blockDim") ||
+            eq(name, "gridDim"))
+            return ov(m.add_val(0, S_INT32, name));  // placeholder, no id taken
+        if (eq(name, "warpSize")) {
+            uint32_t d = new_val("warpSize", S_UINT32);
+            Inst c = mk_inst(I_CALL, 0, (int32_t)d, onone(), onone());
+            c.func = S("warpSize");
+            emit(c);
+            return ov(d);
+        }
+        perr();
+        return onone();
+    }
+    if (k == TK_STRING_LIT) { unsup(); return onone(); }
+    if (k == TK_LPAREN) {
+        advance();
+        uint32_t pk = peek();
+        bool type_ahead = pk == TK_VOID || pk == TK_INT || pk == TK_FLOAT || pk == TK_DOUBLE ||
+                          pk == TK_HALF || pk == TK_CHAR || pk == TK_BOOL || pk == TK_SHORT ||
+                          pk == TK_LONG || pk == TK_SIGNED || pk == TK_UNSIGNED ||
+                          pk == TK_STRUCT || pk == TK_UNION || pk == TK_ENUM || pk == TK_CONST ||
+                          pk == TK_VOLATILE;
+        if (!type_ahead && pk == TK_IDENT) {
+            Ty t;
+            if (typedef_scalar(peekv(), t) || vector_type_name(peekv())) type_ahead = true;
+        }
+        if (type_ahead) {
+            uint32_t saved = pos;
+            Ty ct;
+            bool ok = parse_type_with_ptr(ct);
+            if (ok && at(TK_RPAREN)) {
+                advance();
+                Opnd o = parse_unary_expr();
+                if (!bad()) {
+                    uint32_t d = new_val("cast", ct);
+                    emit_cvt(d, o);
+                    return ov(d);
+                }
+            }
+            if (bad()) {  // except Exception: self._pos = _saved
+                if (!catch_any()) return onone();
+                pos = saved;
+            }
+        }
+        Opnd e = parse_expr();
+        if (bad() || !expect(TK_RPAREN)) return e;
+        return e;
+    }
+    perr();
+    return onone();
+}
+
+// Built-in calls of _parse_primary_expr (parser.py:1635-2138) in the subset.
+OCB_HD inline Opnd Parser::parse_call(Str name) {
+    Vec<Opnd> args;
+    args.init();
+    if (!at(TK_RPAREN)) {
+        args.push(ar, parse_assign_expr());
+        while (!bad() && match(TK_COMMA)) args.push(ar, parse_assign_expr());
+    }
+    if (bad() || !expect(TK_RPAREN)) return onone();
+    auto call = [&](int32_t dest, Str func) {
+        Inst c = mk_inst(I_CALL, 0, dest, onone(), onone());
+        c.func = func;
+        c.args = args;
+        emit(c);
+    };
+    if (eq(name, "__syncthreads")) {
+        call(-1, name);
+        return m.cint(S_VOID, 0);
+    }
+    if (eq(name, "__all_sync") || eq(name, "__any_sync")) {
+        uint32_t d = new_val(Str{name.p + 2, name.n - 2}, S_INT32);
+        call((int32_t)d, name);
+        return ov(d);
+    }
+    if (eq(name, "__shfl_sync") || eq(name, "__shfl_up_sync") || eq(name, "__shfl_down_sync") ||
+        eq(name, "__shfl_xor_sync") || eq(name, "__ballot_sync")) {
+        Ty rt = S_INT32;
+        if (eq(name, "__ballot_sync")) rt = S_UINT32;
+        else if (args.n > 1 && (args[1].k == O_VAL || args[1].k == O_CONST) && !is_ptr(tyof(args[1])))
+            rt = tyof(args[1]);
+        uint32_t d = new_val(Str{name.p + 2, name.n - 2}, rt);
+        call((int32_t)d, name);
+        return ov(d);
+    }
+    if (eq(name, "atomicAdd") || eq(name, "atomicSub") || eq(name, "atomicMin") ||
+        eq(name, "atomicMax") || eq(name, "atomicAnd") || eq(name, "atomicOr") ||
+        eq(name, "atomicXor") || eq(name, "atomicExch") || eq(name, "atomicCAS")) {
+        if (args.n >= 2) {
+            Ty rt = args[1].k == O_VAL ? tyof(args[1]) : (Ty)S_INT32;
+            uint32_t d = new_val(cat(ar, S("atomic_"), name), rt);
+            call((int32_t)d, name);
+            return ov(d);
+        }
+        return m.cint(S_INT32, 0);
+    }
+    if (eq(name, "__ldg") || eq(name, "__ldcg") || eq(name, "__ldcs") || eq(name, "__ldlu") ||
+        eq(name, "__ldca")) {
+        if (args.n && args[0].k == O_VAL && is_ptr(tyof(args[0]))) {
+            Ty pt = tyof(args[0]);
+            if (eq(name, "__ldg")) {
+                bool ok = true;
+                Ty nct = ty_ptr(ty_pointee(pt), AS_CONST, false, ok);
+                if (!ok) { unsup(); return onone(); }
+                // Value(ptr.name, PtrTy(pointee, CONST), ptr.id): a second object, same id
+                uint32_t nc = m.add_val(m.vals[args[0].x].id, nct, vname(args[0]));
+                uint32_t d = new_val("ldg", ty_pointee(pt));
+                emit_load(d, ov(nc));
+                return ov(d);
+            }
+            uint32_t d = new_val(Str{name.p + 2, name.n - 2}, ty_pointee(pt));
+            emit_load(d, args[0]);
+            return ov(d);
+        }
+        return m.cint(S_INT32, 0);
+    }
+    if (in_list(name, kTexFetch) || in_list(name, kSurfVoid) || eq(name, "printf") ||
+        in_list(name, " surf1Dread __cp_async_bulk_tensor_1d __cp_async_bulk_tensor_2d"
+                      " __cp_async_bulk_commit_group __cp_async_bulk_wait_group __mbarrier_init"
+                      " __mbarrier_try_wait_parity ")) {
+        unsup();  // texture/surface/TMA/mbarrier intrinsics and printf
+        return onone();
+    }
+    // generic intrinsic call (parser.py:1929-2138); __device__ functions never
+    // reach here because a TU that defines one is outside the subset
+    if (in_list(name, kVoidStmts) || eq(name, "__syncwarp")) {
+        call(-1, name);
+        return m.cint(S_VOID, 0);
+    }
+    Ty rt = S_INT32;
+    auto a0ty = [&](Ty dflt) -> Ty {
+        return (args.n && (args[0].k == O_VAL || args[0].k == O_CONST)) ? tyof(args[0]) : dflt;
+    };
+    if (in_list(name, kSyncReduce)) rt = S_INT32;
+    else if (eq(name, "__activemask")) rt = S_UINT32;
+    else if (in_list(name, kIntOps)) rt = eq(name, "__brevll") ? (Ty)S_UINT64 : eq(name, "__brev") ? (Ty)S_UINT32 : (Ty)S_INT32;
+    else if (eq(name, "clock64") || eq(name, "__clock64") || eq(name, "clock")) rt = contains(name, "64") ? S_UINT64 : S_UINT32;
+    else if (in_list(name, kPredInt)) rt = S_INT32;
+    else if (in_list(name, kFloat2Int)) rt = (contains(name, "ll") || contains(name, "longlong")) ? S_INT64 : S_INT32;
+    else if (in_list(name, kInt2Float)) rt = contains(name, "double") ? S_DOUBLE : S_FLOAT;
+    else if (eq(name, "__sad") || eq(name, "__usad")) rt = eq(name, "__usad") ? S_UINT32 : S_INT32;
+    else if (in_list(name, " __dp4a __dp4a_u __dp4a_su __dp4a_us ")) rt = S_INT32;
+    else if (in_list(name, kWarpReduceInt)) rt = S_INT32;
+    else if (in_list(name, kWarpReduceUint) || eq(name, "__match_any_sync") || eq(name, "__match_all_sync")) rt = S_UINT32;
+    else if (in_list(name, kIntBinary2)) rt = S_INT32;
+    else if (in_list(name, kUintBinary2)) rt = S_UINT32;
+    else if (in_list(name, kHalfUnary)) rt = (!eq(name, "__half2float") && !contains(name, "float")) ? S_HALF : S_FLOAT;
+    else if (in_list(name, kHalfBinary) || in_list(name, kHalfTernary) || in_list(name, kHalfCvt)) rt = S_HALF;
+    else if (in_list(name, kHalfCmpInt)) rt = S_INT32;
+    else if (eq(name, "__half_as_ushort") || eq(name, "__half_as_short")) rt = S_UINT16;
+    else if (in_list(name, kHalf2Int)) {
+        if (contains(name, "ll")) rt = contains(name, "ull") ? S_UINT64 : S_INT64;
+        else if (contains(name, "uint") || contains(name, "ushort")) rt = S_UINT32;
+        else rt = S_INT32;
+    } else if (eq(name, "__hadd") || eq(name, "__hadd_sat")) {
+        Ty at = (args.n && args[0].k == O_VAL) ? tyof(args[0]) : (Ty)S_INT32;
+        rt = at == S_HALF ? S_HALF : S_INT32;
+    } else if (in_list(name, kFloatUnary) || in_list(name, kFloatBinary) || in_list(name, kFloatTernary)) {
+        rt = a0ty(S_FLOAT) == S_DOUBLE ? S_DOUBLE : S_FLOAT;
+    } else if (eq(name, "abs")) {
+        rt = a0ty(S_INT32);
+    } else if (eq(name, "min") || eq(name, "max")) {
+        rt = args.n > 1 ? result_type(args[0], args[1]) : a0ty(S_INT32);
+    }
+    uint32_t d = new_val(name, rt);
+    call((int32_t)d, name);
+    return ov(d);
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -1,0 +1,1009 @@
+// Parser, statements and top level: parser.py:2287-3705 (_parse_stmt,
+// _parse_lvalue_or_expr, _parse_stmt_or_block), :3701-3874 (_parse_kernel)
+// and :4194-4443 (parse_module), restated for the supported subset.
+#pragma once
+#include "cc_parse_expr.cuh"
+
+namespace ocb {
+namespace cc {
+
+OCB_HD inline bool is_decl_start_kind(uint32_t k) {
+    return k == TK_INT || k == TK_UNSIGNED || k == TK_SIGNED || k == TK_FLOAT || k == TK_DOUBLE ||
+           k == TK_VOID || k == TK_LONG || k == TK_HALF || k == TK_CHAR || k == TK_SHORT ||
+           k == TK_BOOL || k == TK_STRUCT || k == TK_UNION || k == TK_ENUM;
+}
+
+// int(const.value) of an array dimension; floats are outside the subset
+OCB_HD inline bool const_dim(Parser &P, Opnd o, int64_t &out) {
+    if (o.k != O_CONST) {
+        out = 1;
+        return true;
+    }
+    const Const &c = P.m.consts[o.x];
+    if (c.pyfloat) {
+        P.unsup();
+        return false;
+    }
+    out = c.i;
+    return true;
+}
+
+OCB_HD inline bool mul_dim(Parser &P, int64_t &size, int64_t d) {
+    int64_t r;
+    if (Parser::mul_ovf_(size, d, r)) {
+        P.unsup();
+        return false;
+    }
+    size = r;
+    return true;
+}
+
+// _parse_lvalue_or_expr (parser.py:3414-3665)
+OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
+    uint32_t k = peek();
+    if (bad()) return onone();
+    if (k == TK_STAR && pos + 1 < tk.n && kind_at(pos + 1) == TK_IDENT) {
+        Opnd *vp = vars.get(val_at(pos + 1));
+        if (vp && is_ptr(tyof(*vp))) {
+            pos += 2;
+            return *vp;
+        }
+    }
+    if (k == TK_IDENT) {
+        Str name = peekv();
+        Opnd *vp = vars.get(name);
+        if (vp && is_ptr(tyof(*vp))) {
+            Opnd var = *vp;
+            Ty vt = tyof(var);
+            advance();
+            if (match(TK_LBRACKET)) {
+                Opnd index = parse_expr();
+                if (bad() || !expect(TK_RBRACKET)) return onone();
+                Opnd addr;
+                Opnd *rs = row_strides.get(name);
+                if (rs && at(TK_LBRACKET)) {
+                    Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                    uint32_t s = new_val("scale", it);
+                    emit_bin(s, BO_MUL, index, m.cint(it, m.consts[rs->x].i));
+                    uint32_t a = new_val("addr", vt);
+                    emit_bin(a, BO_ADD, var, ov(s));
+                    advance();
+                    Opnd index2 = parse_expr();
+                    if (bad() || !expect(TK_RBRACKET)) return onone();
+                    uint32_t es = ty_size(ty_pointee(vt));
+                    if (es != 1) {
+                        Ty it2 = isval(index2) ? tyof(index2) : (Ty)S_INT32;
+                        uint32_t s2 = new_val("scale", it2);
+                        emit_bin(s2, BO_MUL, index2, m.cint(it2, es));
+                        index2 = ov(s2);
+                    }
+                    uint32_t f = new_val("addr", vt);
+                    emit_bin(f, BO_ADD, ov(a), index2);
+                    addr = ov(f);
+                } else {
+                    uint32_t es = ty_size(ty_pointee(vt));
+                    if (es != 1) {
+                        Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                        uint32_t s = new_val("scale", it);
+                        emit_bin(s, BO_MUL, index, m.cint(it, es));
+                        index = ov(s);
+                    }
+                    uint32_t a = new_val("addr", vt);
+                    emit_bin(a, BO_ADD, var, index);
+                    addr = ov(a);
+                    Ty pt = ty_pointee(vt);
+                    if (at(TK_LBRACKET) && is_ptr(pt)) {  // T**: load the row pointer
+                        uint32_t rp = new_val("rowptr", pt);
+                        emit_load(rp, addr);
+                        advance();
+                        Opnd index2 = parse_expr();
+                        if (bad() || !expect(TK_RBRACKET)) return onone();
+                        uint32_t es2 = ty_size(ty_pointee(pt));
+                        if (es2 != 1) {
+                            Ty it2 = isval(index2) ? tyof(index2) : (Ty)S_INT32;
+                            uint32_t s2 = new_val("scale", it2);
+                            emit_bin(s2, BO_MUL, index2, m.cint(it2, es2));
+                            index2 = ov(s2);
+                        }
+                        uint32_t f = new_val("addr", pt);
+                        emit_bin(f, BO_ADD, ov(rp), index2);
+                        addr = ov(f);
+                    }
+                }
+                return addr;
+            }
+            return var;
+        }
+    }
+    return parse_expr();
+}
+
+OCB_HD inline void Parser::parse_stmt_or_block() {
+    if (match(TK_LBRACE)) {
+        VarMap outer = vars.copy(ar);
+        NameSet ns;
+        ns.init();
+        scopes.push(ar, ns);
+        while (!bad() && !match(TK_RBRACE)) parse_stmt();
+        if (bad()) return;
+        NameSet inner = scopes.back();
+        scopes.n--;
+        pop_scope(inner, outer);
+    } else {
+        parse_stmt();
+    }
+}
+
+// End of a block scope: names declared inside either get their outer binding
+// back or leave the map.  The reference walks a Python set, whose order only
+// matters when two names are re-inserted at the end; that case is declined.
+OCB_HD inline void Parser::pop_scope(NameSet &inner, VarMap &outer) {
+    uint32_t reinserted = 0;
+    for (uint32_t i = 0; i < inner.v.n; ++i) {
+        Str name = inner.v[i];
+        Opnd *o = outer.get(name);
+        if (o) {
+            if (!vars.has(name)) reinserted++;
+            vars.set(ar, name, *o);
+        } else if (vars.has(name)) {
+            vars.del(ar, name);
+        }
+    }
+    if (reinserted > 1) unsup();
+}
+
+// __shared__ declarations inside a kernel (parser.py:2377-2469)
+OCB_HD inline void Parser::parse_shared(bool vol) {
+    advance();
+    Ty ty;
+    if (!parse_type(ty)) return;
+    if (!at(TK_IDENT)) { perr(); return; }
+    Str name = peekv();
+    advance();
+    bool ok = true;
+    Ty smem = ty_ptr(ty, AS_SHARED, vol, ok);
+    if (!ok) { unsup(); return; }
+    auto scalar = [&](Str n) {
+        uint32_t v = new_val(n, smem);
+        vars.set(ar, n, ov(v));
+        shared_scalars.add(ar, n);
+        kern->shared.push(ar, SharedDecl{n, ty, 1});
+    };
+    if (match(TK_SEMI)) {
+        scalar(name);
+        return;
+    }
+    if (at(TK_COMMA)) {
+        scalar(name);
+        while (!bad() && match(TK_COMMA)) {
+            if (!at(TK_IDENT)) { perr(); return; }
+            Str extra = peekv();
+            advance();
+            scalar(extra);
+        }
+        expect(TK_SEMI);
+        return;
+    }
+    if (!expect(TK_LBRACKET)) return;
+    if (at(TK_RBRACKET)) {  // extern __shared__ T name[]: dynamic, size 0
+        advance();
+        if (!expect(TK_SEMI)) return;
+        uint32_t v = new_val(name, smem);
+        vars.set(ar, name, ov(v));
+        kern->shared.push(ar, SharedDecl{name, ty, 0});
+        return;
+    }
+    auto array = [&](Str n, bool first) -> bool {
+        if (!first) {
+            if (!at(TK_IDENT)) { perr(); return false; }
+            n = peekv();
+            advance();
+            if (!expect(TK_LBRACKET)) return false;
+        }
+        Opnd so = parse_assign_expr();
+        if (bad()) return false;
+        int64_t size;
+        if (!const_dim(*this, so, size)) return false;
+        if (!expect(TK_RBRACKET)) return false;
+        int64_t inner = 1;
+        bool has_inner = false;
+        while (!bad() && at(TK_LBRACKET)) {
+            advance();
+            Opnd dop = parse_assign_expr();
+            if (bad()) return false;
+            int64_t d;
+            if (!const_dim(*this, dop, d)) return false;
+            has_inner = true;
+            if (!mul_dim(*this, inner, d) || !mul_dim(*this, size, d)) return false;
+            if (!expect(TK_RBRACKET)) return false;
+        }
+        if (bad()) return false;
+        if (has_inner) {
+            int64_t st = inner;
+            if (!mul_dim(*this, st, ty_size(ty))) return false;
+            row_strides.set(ar, n, m.cint(S_INT32, st));
+        }
+        uint32_t v = new_val(n, smem);
+        vars.set(ar, n, ov(v));
+        declare_local(n);
+        kern->shared.push(ar, SharedDecl{n, ty, size});
+        return true;
+    };
+    if (!array(name, true)) return;
+    while (!bad() && match(TK_COMMA))
+        if (!array(name, false)) return;
+    if (!bad()) expect(TK_SEMI);
+}
+
+// Variable declarations (parser.py:2472-2741); `ty` is already parsed.
+OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
+    for (;;) {
+        Ty dty = ty;
+        while (match(TK_STAR)) {
+            bool ok = true;
+            dty = ty_ptr(dty, AS_GLOBAL, false, ok);
+            if (!ok) { unsup(); return; }
+        }
+        Str name;
+        if (!expect_ident(name)) return;
+        while (at(TK_IDENT) && eq(peekv(), "__attribute__")) {
+            advance();
+            if (at(TK_LPAREN)) {
+                int depth = 1;
+                advance();
+                while (depth > 0 && !at(TK_EOF)) {
+                    if (bad()) return;
+                    uint32_t kk = peek();
+                    if (kk == TK_LPAREN) depth++;
+                    else if (kk == TK_RPAREN) depth--;
+                    advance();
+                }
+            }
+        }
+        if (bad()) return;
+        if (at(TK_LBRACKET)) {  // local array in .local
+            advance();
+            Opnd so = parse_assign_expr();
+            if (bad() || !expect(TK_RBRACKET)) return;
+            int64_t size;
+            if (!const_dim(*this, so, size)) return;
+            int64_t inner = 1;
+            bool has_inner = false;
+            while (!bad() && at(TK_LBRACKET)) {
+                advance();
+                Opnd dop = parse_assign_expr();
+                if (bad()) return;
+                int64_t d;
+                if (!const_dim(*this, dop, d)) return;
+                has_inner = true;
+                if (!mul_dim(*this, inner, d) || !mul_dim(*this, size, d)) return;
+                if (!expect(TK_RBRACKET)) return;
+            }
+            if (bad()) return;
+            if (has_inner) {
+                int64_t st = inner;
+                if (!mul_dim(*this, st, is_ptr(dty) ? 8 : ty_size(dty))) return;
+                row_strides.set(ar, name, m.cint(S_INT32, st));
+            }
+            bool ok = true;
+            Ty aty = ty_ptr(dty, AS_LOCAL, false, ok);
+            if (!ok) { unsup(); return; }
+            uint32_t v = new_val(name, aty);
+            vars.set(ar, name, ov(v));
+            declare_local(name);
+            kern->locals.push(ar, LocalDecl{name, dty, size, v});
+            if (match(TK_ASSIGN) && at(TK_LBRACE)) {
+                advance();
+                int64_t esz = is_ptr(dty) ? 8 : ty_size(dty);
+                int64_t idx = 0;
+                // _emit_flat_elems: nested braces flatten into one element list.
+                // State machine of the recursive walk; `depth` = open inner braces.
+                int depth = 0;
+                for (;;) {
+                    if (bad()) return;
+                    bool level_end = at(TK_RBRACE) || at(TK_EOF);
+                    if (!level_end && at(TK_LBRACE)) {
+                        advance();
+                        if (++depth > MAX_NEST) { unsup(); return; }
+                        continue;
+                    }
+                    if (!level_end) {
+                        Opnd ev = parse_assign_expr();
+                        if (bad()) return;
+                        if (idx < size) {
+                            uint32_t ea = new_val("earr", aty);
+                            emit_bin(ea, BO_ADD, ov(v), m.cint(S_INT32, idx * esz));
+                            if (ev.k == O_CONST && m.consts[ev.x].ty != dty) {
+                                Const c = m.consts[ev.x];
+                                c.ty = dty;
+                                m.consts.push(ar, c);
+                                ev = oc(m.consts.n - 1);
+                            }
+                            emit_store(ov(ea), ev);
+                        }
+                        idx++;
+                        if (match(TK_COMMA)) continue;
+                    }
+                    // this level is done; close it and continue the parent level
+                    bool finished = false;
+                    for (;;) {
+                        if (bad()) return;
+                        if (depth == 0) { finished = true; break; }
+                        if (!expect(TK_RBRACE)) return;
+                        depth--;
+                        if (match(TK_COMMA)) break;  // parent level goes on
+                    }
+                    if (finished) break;
+                }
+                if (!expect(TK_RBRACE)) return;
+            }
+            if (bad()) return;
+            if (!match(TK_COMMA)) break;
+            continue;
+        }
+        uint32_t v = new_val(name, dty);
+        vars.set(ar, name, ov(v));
+        declare_local(name);
+        if (match(TK_ASSIGN)) {
+            Opnd rhs = parse_assign_expr();
+            if (bad()) return;
+            vars.set(ar, name, rhs.k == O_VAL ? rhs : ov(v));
+            if (rhs.k == O_CONST) {
+                emit_bin(v, BO_ADD, rhs, m.cint(dty, 0));
+                vars.set(ar, name, ov(v));
+            } else if (rhs.k == O_VAL && !val_eq(rhs.x, v)) {
+                Ty rt = tyof(rhs);
+                if (!is_ptr(dty) && !is_ptr(rt) && dty != rt) {
+                    emit_cvt(v, rhs);
+                } else {
+                    emit_bin(v, BO_ADD, rhs, m.cint(dty, 0));
+                }
+                vars.set(ar, name, ov(v));
+            }
+        } else {
+            Opnd z = m.czero(dty);
+            emit_bin(v, BO_ADD, z, z);
+        }
+        if (!match(TK_COMMA)) break;
+    }
+    if (!bad()) expect(TK_SEMI);
+}
+
+// if statement (parser.py:2743-2787)
+OCB_HD inline void Parser::parse_if() {
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    Opnd c = parse_expr();
+    if (bad() || !expect(TK_RPAREN)) return;
+    uint32_t tb = new_block("if_true"), fb = new_block("if_false"), mb = new_block("if_merge");
+    B().term = Term{T_CBR, c, m.blocks[tb].label, m.blocks[fb].label};
+    VarMap before = vars.copy(ar);
+    cur = tb;
+    parse_stmt_or_block();
+    if (bad()) return;
+    loop_writeback(before);
+    if (B().term.kind == T_NONE) B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+    vars = before.copy(ar);
+    cur = fb;
+    if (match(TK_ELSE)) {
+        parse_stmt_or_block();
+        if (bad()) return;
+    }
+    loop_writeback(before);
+    if (B().term.kind == T_NONE) B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+    vars = before.copy(ar);
+    cur = mb;
+}
+
+OCB_HD inline void Parser::push_loop(Str brk, Str cont, VarMap &snap) {
+    break_targets.push(ar, brk);
+    break_snaps.push(ar, snap);
+    continue_targets.push(ar, cont);
+    continue_snaps.push(ar, snap);
+}
+OCB_HD inline void Parser::pop_loop() {
+    break_targets.n--;
+    break_snaps.n--;
+    continue_targets.n--;
+    continue_snaps.n--;
+}
+
+// for loop (parser.py:2789-2900)
+OCB_HD inline void Parser::parse_for() {
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    VarMap for_outer = vars.copy(ar);
+    NameSet ns;
+    ns.init();
+    scopes.push(ar, ns);
+    parse_stmt();  // init
+    if (bad()) return;
+    uint32_t cond_start = pos;
+    int depth = 0;
+    for (;;) {
+        uint32_t kk = peek();
+        if (bad()) return;
+        if (kk == TK_SEMI && depth == 0) break;
+        if (kk == TK_LPAREN) depth++;
+        if (kk == TK_RPAREN) depth--;
+        advance();
+    }
+    advance();
+    uint32_t inc_start = pos;
+    depth = 0;
+    for (;;) {
+        uint32_t kk = peek();
+        if (bad()) return;
+        if (kk == TK_RPAREN && depth == 0) break;
+        if (kk == TK_LPAREN) depth++;
+        if (kk == TK_RPAREN) depth--;
+        advance();
+    }
+    if (!expect(TK_RPAREN)) return;
+    uint32_t body_resume = pos;
+    VarMap loop_vars = vars.copy(ar);
+    uint32_t cb = new_block("for_cond"), bb = new_block("for_body"), ib = new_block("for_inc"),
+             eb = new_block("for_exit");
+    B().term = Term{T_BR, onone(), m.blocks[cb].label, Str{nullptr, 0}};
+    cur = cb;
+    pos = cond_start;
+    Opnd c;
+    if (kind_at(cond_start) == TK_SEMI) {
+        c = m.cint(S_INT32, 1);
+    } else {
+        c = parse_expr();
+        if (bad()) return;
+    }
+    B().term = Term{T_CBR, c, m.blocks[bb].label, m.blocks[eb].label};
+    pos = body_resume;
+    cur = bb;
+    push_loop(m.blocks[eb].label, m.blocks[ib].label, loop_vars);
+    parse_stmt_or_block();
+    if (bad()) return;
+    pop_loop();
+    if (B().term.kind == T_NONE) {
+        loop_writeback(loop_vars);
+        B().term = Term{T_BR, onone(), m.blocks[ib].label, Str{nullptr, 0}};
+    }
+    cur = ib;
+    uint32_t saved = pos;
+    pos = inc_start;
+    if (kind_at(inc_start) != TK_RPAREN) {
+        parse_assign_expr();
+        while (!bad() && match(TK_COMMA)) parse_assign_expr();
+        if (bad()) return;
+    }
+    pos = saved;
+    for (uint32_t i = 0; i < loop_vars.e.n; ++i) {
+        const VarEnt &en = loop_vars.e[i];
+        if (!en.live || en.v.k != O_VAL) continue;
+        Opnd *cv = vars.get(en.name);
+        if (!cv || (cv->k == O_VAL && cv->x == en.v.x)) continue;
+        if (cv->k == O_VAL) {
+            emit_bin(en.v.x, BO_ADD, *cv, m.cint(tyof(en.v), 0));
+            vars.set(ar, en.name, en.v);
+        }
+    }
+    B().term = Term{T_BR, onone(), m.blocks[cb].label, Str{nullptr, 0}};
+    cur = eb;
+    NameSet inner = scopes.back();
+    scopes.n--;
+    pop_scope(inner, for_outer);
+}
+
+// while and do/while loops (parser.py:2902-2998)
+OCB_HD inline void Parser::parse_while() {
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    VarMap entry = vars.copy(ar);
+    uint32_t cb = new_block("while_cond"), bb = new_block("while_body"),
+             eb = new_block("while_exit");
+    B().term = Term{T_BR, onone(), m.blocks[cb].label, Str{nullptr, 0}};
+    cur = cb;
+    Opnd c = parse_expr();
+    if (bad() || !expect(TK_RPAREN)) return;
+    B().term = Term{T_CBR, c, m.blocks[bb].label, m.blocks[eb].label};
+    cur = bb;
+    push_loop(m.blocks[eb].label, m.blocks[cb].label, entry);
+    parse_stmt_or_block();
+    if (bad()) return;
+    pop_loop();
+    loop_writeback(entry);
+    if (B().term.kind == T_NONE) B().term = Term{T_BR, onone(), m.blocks[cb].label, Str{nullptr, 0}};
+    cur = eb;
+}
+
+OCB_HD inline void Parser::parse_do() {
+    advance();
+    VarMap entry = vars.copy(ar);
+    uint32_t bb = new_block("do_body"), cb = new_block("do_cond"), eb = new_block("do_exit");
+    B().term = Term{T_BR, onone(), m.blocks[bb].label, Str{nullptr, 0}};
+    cur = bb;
+    push_loop(m.blocks[eb].label, m.blocks[cb].label, entry);
+    parse_stmt_or_block();
+    if (bad()) return;
+    pop_loop();
+    loop_writeback(entry);
+    if (B().term.kind == T_NONE) B().term = Term{T_BR, onone(), m.blocks[cb].label, Str{nullptr, 0}};
+    cur = cb;
+    if (!expect(TK_WHILE) || !expect(TK_LPAREN)) return;
+    Opnd c = parse_expr();
+    if (bad() || !expect(TK_RPAREN) || !expect(TK_SEMI)) return;
+    B().term = Term{T_CBR, c, m.blocks[bb].label, m.blocks[eb].label};
+    cur = eb;
+}
+
+// Expression statement (parser.py:3186-3412)
+OCB_HD inline void Parser::parse_expr_stmt() {
+    Str stmt_lhs{nullptr, 0};
+    if (at(TK_IDENT)) {
+        Str cand = peekv();
+        uint32_t np = pos + 1;
+        if (np < tk.n) {
+            uint32_t nk = kind_at(np);
+            if ((nk == TK_ASSIGN || nk == TK_PLUS_EQ || nk == TK_MINUS_EQ || nk == TK_STAR_EQ) &&
+                vars.has(cand))
+                stmt_lhs = cand;
+        }
+    }
+    if (bad()) return;
+    Opnd lhs = parse_lvalue_or_expr();
+    if (bad()) return;
+    if (match(TK_ASSIGN)) {
+        Opnd rhs = parse_expr();
+        if (bad()) return;
+        if (isval(lhs) && is_ptr(tyof(lhs))) {
+            if (stmt_lhs.p && shared_scalars.has(stmt_lhs)) stmt_lhs = Str{nullptr, 0};
+            Str un = stmt_lhs.p ? stmt_lhs : vname(lhs);
+            if (stmt_lhs.p && vars.has(un)) {
+                vars.set(ar, un, rhs);
+            } else {
+                Ty pt = ty_pointee(tyof(lhs));
+                if (isval(rhs) && !is_ptr(tyof(rhs)) && !is_ptr(pt) && tyof(rhs) != pt) {
+                    uint32_t co = new_val("coerce", pt);
+                    emit_cvt(co, rhs);
+                    rhs = ov(co);
+                }
+                emit_store(lhs, rhs);
+            }
+        } else if (isval(lhs)) {
+            Str un = stmt_lhs.p ? stmt_lhs : vname(lhs);
+            Opnd *pp = vars.get(un);
+            if (pp) {
+                Opnd prev = *pp;
+                if (isval(rhs) && prev.k == O_VAL && !is_ptr(tyof(prev)) && !is_ptr(tyof(rhs)) &&
+                    !eq(vname(rhs), un)) {
+                    Ty pt = tyof(prev);
+                    uint32_t mat = new_val(un, pt);
+                    emit_bin(mat, BO_ADD, rhs, m.czero(pt));
+                    rhs = ov(mat);
+                }
+                vars.set(ar, un, rhs);
+            }
+        }
+        while (!bad() && match(TK_COMMA)) {
+            Str l2name{nullptr, 0};
+            if (at(TK_IDENT)) l2name = peekv();
+            Opnd l2 = parse_lvalue_or_expr();
+            if (bad()) return;
+            if (match(TK_ASSIGN)) {
+                Opnd r2 = parse_assign_expr();
+                if (bad()) return;
+                if (isval(l2) && !is_ptr(tyof(l2))) {
+                    Str u2 = l2name.p ? l2name : vname(l2);
+                    if (vars.has(u2)) vars.set(ar, u2, r2);
+                }
+            }
+        }
+        if (!bad()) expect(TK_SEMI);
+        return;
+    }
+    static const uint32_t toks[] = {TK_PLUS_EQ, TK_MINUS_EQ, TK_STAR_EQ, TK_SLASH_EQ,
+                                    TK_PERCENT_EQ, TK_AMP_EQ, TK_PIPE_EQ, TK_CARET_EQ,
+                                    TK_LSHIFT_EQ, TK_RSHIFT_EQ};
+    static const uint8_t ops[] = {BO_ADD, BO_SUB, BO_MUL, BO_DIV, BO_MOD,
+                                  BO_AND, BO_OR, BO_XOR, BO_SHL, BO_SHR};
+    for (int kx = 0; kx < 10; ++kx) {
+        if (!match(toks[kx])) continue;
+        uint8_t op = ops[kx];
+        Opnd rhs = parse_expr();
+        if (bad()) return;
+        if (isval(lhs) && is_ptr(tyof(lhs))) {
+            Ty lt = tyof(lhs);
+            bool is_ptr_var = stmt_lhs.p && vars.has(stmt_lhs) && !shared_scalars.has(stmt_lhs);
+            if (is_ptr_var && (op == BO_ADD || op == BO_SUB)) {
+                Opnd sc = scale_ptr_off(lt, rhs);
+                if (bad()) return;
+                uint32_t r = new_val("compound", lt);
+                emit_bin(r, op, lhs, sc);
+                vars.set(ar, stmt_lhs, ov(r));
+            } else {
+                uint32_t cv = new_val("cur", ty_pointee(lt));
+                emit_load(cv, lhs);
+                uint32_t r = new_val("compound", ty_pointee(lt));
+                emit_bin(r, op, ov(cv), rhs);
+                emit_store(lhs, ov(r));
+            }
+        } else {
+            uint32_t r = new_val("compound", isval(lhs) ? tyof(lhs) : (Ty)S_INT32);
+            emit_bin(r, op, lhs, rhs);
+            Str un = stmt_lhs.p ? stmt_lhs : (isval(lhs) ? vname(lhs) : Str{nullptr, 0});
+            if (un.p && vars.has(un)) vars.set(ar, un, ov(r));
+        }
+        expect(TK_SEMI);
+        return;
+    }
+    for (int kx = 0; kx < 2; ++kx) {
+        if (!match(kx == 0 ? TK_PLUSPLUS : TK_MINUSMINUS)) continue;
+        uint8_t op = kx == 0 ? BO_ADD : BO_SUB;
+        if (isval(lhs)) {
+            Ty lt = tyof(lhs);
+            if (is_ptr(lt)) {
+                Str un = stmt_lhs.p ? stmt_lhs : vname(lhs);
+                bool is_ptr_var = vars.has(un) && !shared_scalars.has(un);
+                if (is_ptr_var) {
+                    Ty pt = ty_pointee(lt);
+                    int64_t step = is_ptr(pt) ? 1 : ty_size(pt);
+                    uint32_t np = new_val(cat(ar, vname(lhs), S("_inc")), lt);
+                    emit_bin(np, op, lhs, m.cint(S_UINT64, step));
+                    vars.set(ar, un, ov(np));
+                } else {
+                    Ty pt = ty_pointee(lt);
+                    uint32_t cv = new_val("cur", pt);
+                    emit_load(cv, lhs);
+                    uint32_t r = new_val("compound", pt);
+                    emit_bin(r, op, ov(cv), m.cint(pt, 1));
+                    emit_store(lhs, ov(r));
+                }
+            } else {
+                uint32_t nv = new_val(cat(ar, vname(lhs), S("_inc")), lt);
+                emit_bin(nv, op, lhs, m.cint(lt, 1));
+                Str un = stmt_lhs.p ? stmt_lhs : vname(lhs);
+                if (vars.has(un)) vars.set(ar, un, ov(nv));
+            }
+        }
+        expect(TK_SEMI);
+        return;
+    }
+    while (!bad() && match(TK_COMMA)) parse_assign_expr();
+    if (!bad()) expect(TK_SEMI);
+}
+
+// _parse_stmt (parser.py:2287-3412)
+OCB_HD inline void Parser::parse_stmt() {
+    if (++nest > MAX_NEST) { unsup(); --nest; return; }
+    parse_stmt_inner();
+    --nest;
+}
+
+OCB_HD inline void Parser::parse_stmt_inner() {
+    uint32_t k = peek();
+    bool vol = false;
+    while (k == TK_CONST || k == TK_VOLATILE || k == TK_STATIC) {
+        if (k == TK_VOLATILE) vol = true;
+        advance();
+        k = peek();
+    }
+    if (bad()) return;
+    if (k == TK_SEMI) { advance(); return; }
+    if (k == TK_GOTO) {
+        advance();
+        if (at(TK_IDENT)) advance();
+        match(TK_SEMI);
+        return;
+    }
+    if (k == TK_IDENT && pos + 1 < tk.n && kind_at(pos + 1) == TK_COLON) {
+        pos += 2;  // label: a no-op
+        return;
+    }
+    if (k == TK_LBRACE) { parse_stmt_or_block(); return; }
+    if (k == TK_IDENT) {
+        Str v = peekv();
+        if (eq(v, "asm") || eq(v, "__asm__") || eq(v, "__asm")) { unsup(); return; }
+    }
+    if (k == TK_SHARED) { parse_shared(vol); return; }
+    bool decl = is_decl_start_kind(k);
+    if (!decl && k == TK_IDENT) {
+        Ty t;
+        decl = typedef_scalar(peekv(), t) || vector_type_name(peekv());
+    }
+    if (decl) {
+        Ty ty;
+        if (!parse_type_with_ptr(ty)) return;
+        parse_decl(ty, vol);
+        return;
+    }
+    switch (k) {
+    case TK_IF: parse_if(); return;
+    case TK_FOR: parse_for(); return;
+    case TK_WHILE: parse_while(); return;
+    case TK_DO: parse_do(); return;
+    case TK_SWITCH: unsup(); return;
+    case TK_BREAK:
+    case TK_CONTINUE: {
+        bool brk = k == TK_BREAK;
+        advance();
+        if (!expect(TK_SEMI)) return;
+        Vec<Str> &tg = brk ? break_targets : continue_targets;
+        Vec<VarMap> &sn = brk ? break_snaps : continue_snaps;
+        if (!tg.n) { perr(); return; }
+        if (sn.n) loop_writeback(sn.back());
+        B().term = Term{T_BR, onone(), tg.back(), Str{nullptr, 0}};
+        cur = new_block(brk ? "after_break" : "after_continue");
+        return;
+    }
+    case TK_RETURN: {
+        advance();
+        Opnd rv = onone();
+        if (at(TK_SEMI)) {
+            advance();
+        } else {
+            rv = parse_expr();
+            if (bad() || !expect(TK_SEMI)) return;
+        }
+        B().term = Term{T_RET, rv, Str{nullptr, 0}, Str{nullptr, 0}};
+        return;
+    }
+    default: break;
+    }
+    parse_expr_stmt();
+}
+
+OCB_HD inline bool is_fn_qualifier(Str v) {
+    return eq(v, "__launch_bounds__") || eq(v, "__attribute__") || eq(v, "__noinline__") ||
+           eq(v, "__forceinline__") || eq(v, "__inline__");
+}
+
+// int(token.value) of a __launch_bounds__ argument: decimal digits only
+OCB_HD inline bool py_int_decimal(Str s, int64_t &out) {
+    if (!s.n || s.n > 18) return false;
+    int64_t v = 0;
+    for (uint32_t i = 0; i < s.n; ++i) {
+        if (s.p[i] < '0' || s.p[i] > '9') return false;
+        v = v * 10 + (s.p[i] - '0');
+    }
+    out = v;
+    return true;
+}
+
+// _parse_kernel (parser.py:3701-3874)
+OCB_HD inline void Parser::parse_kernel() {
+    if (!expect(TK_GLOBAL)) return;
+    int64_t lb[2];
+    bool lb_set[2] = {false, false};
+    auto skip_qual = [&]() {
+        Str qn = peekv();
+        advance();
+        if (!at(TK_LPAREN)) return;
+        advance();
+        if (eq(qn, "__launch_bounds__")) {
+            uint32_t kk = peek();
+            if (kk == TK_INT_LIT || kk == TK_IDENT) {
+                int64_t v;
+                if (py_int_decimal(peekv(), v)) { lb[0] = v; lb_set[0] = true; }
+                else if (kk == TK_INT_LIT && peekv().n > 18) unsup();
+                advance();
+                if (match(TK_COMMA)) {
+                    kk = peek();
+                    if (kk == TK_INT_LIT || kk == TK_IDENT) {
+                        if (py_int_decimal(peekv(), v)) { lb[1] = v; lb_set[1] = true; }
+                        else if (kk == TK_INT_LIT && peekv().n > 18) unsup();
+                        advance();
+                    }
+                }
+            }
+        }
+        int depth = 1;
+        while (depth > 0) {
+            uint32_t kk = peek();
+            if (bad()) return;
+            if (kk == TK_LPAREN) depth++;
+            if (kk == TK_RPAREN) depth--;
+            advance();
+        }
+    };
+    while (!bad() && at(TK_IDENT) && is_fn_qualifier(peekv())) skip_qual();
+    Ty rt;
+    if (bad() || !parse_type(rt)) return;
+    while (!bad() && at(TK_IDENT) && is_fn_qualifier(peekv())) skip_qual();
+    if (bad()) return;
+    if (!at(TK_IDENT)) { perr(); return; }
+    Str name = peekv();
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    Vec<Param> params;
+    params.init();
+    if (at(TK_VOID) && kind_at(pos + 1) == TK_RPAREN) advance();
+    if (bad()) return;
+    if (!at(TK_RPAREN)) {
+        for (;;) {
+            Ty pty;
+            if (!parse_type_with_ptr(pty)) return;
+            Str pname;
+            if (!expect_ident(pname)) return;
+            if (at(TK_LBRACKET)) {  // array parameter: PtrTy(ty, 0) in the reference
+                unsup();
+                return;
+            }
+            while (at(TK_IDENT) && eq(peekv(), "__attribute__")) {
+                advance();
+                if (at(TK_LPAREN)) {
+                    int depth = 1;
+                    advance();
+                    while (depth > 0 && !at(TK_EOF)) {
+                        if (bad()) return;
+                        uint32_t kk = peek();
+                        if (kk == TK_LPAREN) depth++;
+                        else if (kk == TK_RPAREN) depth--;
+                        advance();
+                    }
+                }
+            }
+            if (bad()) return;
+            params.push(ar, Param{pname, pty});
+            if (!match(TK_COMMA)) break;
+        }
+    }
+    if (bad() || !expect(TK_RPAREN)) return;
+    Kernel kk;
+    kk.name = name;
+    kk.params = params;
+    kk.blocks.init();
+    kk.next_id = 0;
+    kk.n_launch = 0;
+    if (lb_set[0]) {
+        kk.launch[kk.n_launch++] = lb[0];
+        if (lb_set[1]) kk.launch[kk.n_launch++] = lb[1];
+    }
+    kk.shared.init();
+    kk.locals.init();
+    kk.has_locals = false;
+    m.kernels.push(ar, kk);
+    kern = &m.kernels.back();
+    kidx = m.kernels.n - 1;
+    vars.init();
+    block_count = 0;
+    copy_chain.init();
+    uint32_t entry = new_block("entry");
+    cur = entry;
+    NameSet seen;
+    seen.init();
+    for (uint32_t i = 0; i < params.n; ++i) {
+        if (seen.has(params[i].name)) continue;
+        uint32_t v = new_val(params[i].name, params[i].ty);
+        Inst pi = mk_inst(I_PARAM, 0, (int32_t)v, onone(), onone());
+        pi.pidx = i;
+        pi.func = params[i].name;
+        emit(pi);
+        vars.set(ar, params[i].name, ov(v));
+        seen.add(ar, params[i].name);
+    }
+    for (uint32_t i = 0; i < module_shared.n; ++i) {
+        bool ok = true;
+        Ty st = ty_ptr(module_shared[i].ty, AS_SHARED, false, ok);
+        if (!ok) { unsup(); return; }
+        uint32_t v = new_val(module_shared[i].name, st);
+        vars.set(ar, module_shared[i].name, ov(v));
+        kern->shared.push(ar, SharedDecl{module_shared[i].name, module_shared[i].ty,
+                                         module_shared[i].count});
+    }
+    if (!expect(TK_LBRACE)) return;
+    while (!bad() && !match(TK_RBRACE)) parse_stmt();
+    if (bad()) return;
+    if (B().term.kind == T_NONE) B().term = Term{T_RET, onone(), Str{nullptr, 0}, Str{nullptr, 0}};
+}
+
+// parse_module (parser.py:4194-4437): pass 1 registers module-level names and
+// records kernel positions; pass 2 parses the kernels in order.
+OCB_HD inline void Parser::parse_module() {
+    Vec<uint32_t> kpos;
+    kpos.init();
+    while (!bad() && !at(TK_EOF)) {
+        while (at(TK_STATIC)) advance();
+        if (bad()) return;
+        if (at(TK_CONST)) {
+            uint32_t saved = pos;
+            advance();
+            Ty t;
+            bool done = false;
+            if (parse_type_with_ptr(t)) {
+                if (at(TK_IDENT)) {
+                    Str name = peekv();
+                    advance();
+                    if (match(TK_ASSIGN)) {
+                        Opnd vo = parse_assign_expr();
+                        if (!bad()) {
+                            if (vo.k == O_CONST) global_consts.set(ar, name, vo);
+                            while (!at(TK_SEMI) && !at(TK_EOF)) advance();
+                            match(TK_SEMI);
+                            done = true;
+                        }
+                    }
+                }
+            }
+            if (done) continue;
+            if (bad() && !catch_any()) return;
+            pos = saved;
+        }
+        if (bad()) return;
+        if (at(TK_IDENT) && eq(peekv(), "namespace")) {
+            advance();
+            if (at(TK_IDENT)) advance();
+            if (at(TK_LBRACE)) advance();
+            continue;
+        }
+        if (at(TK_IDENT) && eq(peekv(), "template")) {
+            advance();
+            if (at(TK_LT)) {
+                advance();
+                int depth = 1;
+                while (depth > 0 && !at(TK_EOF)) {
+                    uint32_t kk = peek();
+                    if (kk == TK_LT) depth++;
+                    else if (kk == TK_GT) depth--;
+                    advance();
+                }
+            }
+            continue;
+        }
+        uint32_t k = peek();
+        if (k == TK_GLOBAL) {
+            uint32_t la = pos + 1;
+            bool fwd = false;
+            while (la < tk.n) {
+                uint32_t lk = kind_at(la);
+                if (lk == TK_LBRACE) break;
+                if (lk == TK_SEMI) { fwd = true; break; }
+                la++;
+            }
+            if (fwd) {
+                while (!at(TK_SEMI) && !at(TK_EOF)) advance();
+                if (at(TK_SEMI)) advance();
+            } else {
+                kpos.push(ar, pos);
+                while (!at(TK_LBRACE) && !at(TK_EOF)) advance();
+                if (at(TK_LBRACE)) {
+                    int depth = 1;
+                    advance();
+                    while (depth > 0 && !at(TK_EOF)) {
+                        uint32_t kk = peek();
+                        if (kk == TK_LBRACE) depth++;
+                        else if (kk == TK_RBRACE) depth--;
+                        advance();
+                    }
+                }
+            }
+        } else if (k == TK_DEVICE || k == TK_STRUCT || k == TK_UNION || k == TK_TYPEDEF ||
+                   k == TK_ENUM || k == TK_CONSTANT) {
+            unsup();  // __device__ functions/variables, structs, typedefs, enums, __constant__
+            return;
+        } else if (k == TK_SHARED) {
+            advance();
+            Ty t;
+            if (!parse_type(t)) return;
+            if (!at(TK_IDENT)) { perr(); return; }
+            Str name = peekv();
+            advance();
+            if (!expect(TK_LBRACKET)) return;
+            int64_t count = 0;
+            if (!at(TK_RBRACKET)) {
+                Opnd so = parse_assign_expr();
+                if (bad()) return;
+                if (!const_dim(*this, so, count)) return;
+            }
+            if (!expect(TK_RBRACKET)) return;
+            match(TK_SEMI);
+            module_shared.push(ar, SharedInit{name, t, count});
+        } else {
+            advance();
+        }
+    }
+    if (bad()) return;
+    for (uint32_t i = 0; i < kpos.n && !bad(); ++i) {
+        pos = kpos[i];
+        parse_kernel();
+    }
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -67,6 +67,8 @@ struct ocb_ctx {
     bool kw_ready = false;
     // preprocessor scratch and outputs
     ocb::DevBuf pp_scratch, pp_arena, pp_text, pp_off, pp_status, pp_qinc;
+    // compiler back half (tokens -> IR -> PTX) scratch and outputs
+    ocb::DevBuf cc_tok, cc_scratch, cc_arena, cc_out, cc_text, cc_off, cc_status, cc_in_status;
 };
 
 struct ocb_text {
@@ -100,6 +102,12 @@ int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
 int pp_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_tu_off,
               uint32_t n_tu, uint32_t scale, DevBuf &out_text, uint64_t *d_out_off,
               int32_t *d_status, uint32_t *d_qinc, uint64_t *h_total, cudaStream_t st);
+// Back half on device buffers (cc.cu): lex the preprocessed text of each TU,
+// parse it and write the TU's IR text into `out_text` at d_out_off[n_tu+1].
+// d_in_status holds the earlier stages' verdicts; d_status gets the final ones.
+int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d_off,
+              uint32_t n_tu, const int32_t *d_in_status, uint32_t scale, DevBuf &out_text,
+              uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total, cudaStream_t st);
 }  // namespace ocb
 
 #define OCB_TRY(what, expr)                                    \

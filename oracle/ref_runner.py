@@ -52,6 +52,11 @@ def _worker_init():
     import opencuda.frontend.parser  # noqa: F401
     import opencuda.ir.optimize  # noqa: F401
     import opencuda.codegen.emit  # noqa: F401
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("oracle_ir_dump", HERE / "ir_dump.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    sys.modules["oracle_ir_dump"] = mod
     _EMPTY_INC = tempfile.mkdtemp(prefix="ocb-empty-inc-")
 
 
@@ -93,6 +98,19 @@ def _job(args):
             res["tok"] = [(t.kind.value, t.value, t.line) for t in lex(pp)]
         except Exception as e:  # noqa: BLE001
             res["error"] = [type(e).__name__, str(e)[:200], "lex"]
+            return res
+    if "ir" in what or "opt" in what:
+        from opencuda.frontend.parser import parse
+        from opencuda.ir.optimize import optimize
+        from oracle_ir_dump import dump_module
+        try:
+            module = parse(pp)
+            if "ir" in what:
+                res["ir"] = dump_module(module)
+            if "opt" in what:
+                res["opt"] = dump_module(optimize(module))
+        except Exception as e:  # noqa: BLE001
+            res["error"] = [type(e).__name__, str(e)[:200], "parse"]
             return res
     if "ptx" in what:
         from opencuda.frontend.parser import parse

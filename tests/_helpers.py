@@ -77,3 +77,228 @@ def pp_fuzz_sources(n: int, seed: int):
                                        'y = AB + FG;', 'defined', 'F("a\\n")', 'G(\'q\')']))
         out.append("\n".join(lines) + r.choice(["", "\n"]))
     return out
+
+
+# Hand-written kernels covering the parser's constructs (and its error paths);
+# the expected IR always comes from the reference itself.
+PARSE_CASES = [
+    # control flow: while / do / break / continue / nested loops
+    """__global__ void k(int *a, int n) {
+    int i = threadIdx.x; int s = 0;
+    while (i < n) { s += a[i]; if (s > 100) break; i += blockDim.x; }
+    do { s--; if (s & 1) continue; s = s >> 1; } while (s > 10);
+    for (int j = 0; j < 4; j++) for (int q = j; q < 4; ++q) { s ^= q * j; }
+    a[threadIdx.x] = s;
+}""",
+    # ternary, && and || with side effects in the rhs
+    """__global__ void k(float *x, int *y, int n) {
+    int t = blockIdx.x * blockDim.x + threadIdx.x;
+    int v = 0;
+    float f = t < n ? x[t] : 0.0f;
+    if (t < n && (v = y[t]) != 0) f += 1.0f;
+    if (t >= n || y[t] == 3) f -= 2.0f;
+    int m = (t > 5) ? t : -t;
+    x[t] = f * m + v;
+}""",
+    # casts, sizeof, unsigned / long long literals, shifts, ~ and !
+    """__global__ void k(unsigned int *o, long long *p, const float * __restrict__ in) {
+    unsigned int u = 0xFFFFFFFFu;
+    long long q = 123456789012LL;
+    int b = (int)in[threadIdx.x];
+    float c = (float)b / 3;
+    unsigned long long z = (unsigned long long)u << 3;
+    o[0] = u >> 4; o[1] = ~u; o[2] = !b; o[3] = sizeof(float) + sizeof(double*);
+    p[0] = q * 2 + z; p[1] = (long long)c;
+    o[4] = 017 + 0x1F + 10u + 'a' + '\\n';
+}""",
+    # shared arrays (1D, 2D, scalar, extern), __syncthreads, 2D indexing
+    """__global__ void k(float *out) {
+    __shared__ float tile[16][17];
+    __shared__ int cnt;
+    extern __shared__ float dyn[];
+    __shared__ float a[32], b[64];
+    int tx = threadIdx.x, ty = threadIdx.y;
+    tile[ty][tx] = out[ty * 16 + tx];
+    if (tx == 0) cnt = 0;
+    __syncthreads();
+    a[tx] = tile[tx][ty] + dyn[tx];
+    b[tx] = a[tx] * 2.0f + cnt;
+    out[ty * 16 + tx] = b[tx];
+}""",
+    # local arrays with aggregate initializers, compound stores, ++ on elements
+    """__global__ void k(int *o) {
+    int w[4] = {1, 2, 3, 4};
+    int m[2][3] = {{1, 2, 3}, {4, 5, 6}};
+    float acc[8];
+    w[1] += 5; w[2]++; w[3] <<= 1;
+    acc[threadIdx.x & 7] = 1.5f;
+    o[threadIdx.x] = w[threadIdx.x & 3] + m[1][2] + (int)acc[0];
+}""",
+    # pointer arithmetic, pointer variables, *p stores, p++ / p += n
+    """__global__ void k(float *base, int n) {
+    float *p = base + threadIdx.x;
+    float *q = p;
+    *p = 1.0f;
+    p++;
+    p += 2;
+    *p = *q + 3.0f;
+    q = q - 1;
+    q[0] = p[1];
+    float *r = &base[4];
+    *r += 2.0f;
+}""",
+    # intrinsics: shuffles, ballot, atomics, __ldg, math, min/max, warpSize
+    """__global__ void k(float *x, int *c, unsigned int *m) {
+    float v = __ldg(&x[threadIdx.x]);
+    v += __shfl_down_sync(0xffffffff, v, 16);
+    v = fmaxf(v, 0.0f) + sqrtf(fabsf(v)) + expf(v) + __fmaf_rn(v, v, 1.0f);
+    unsigned int b = __ballot_sync(0xffffffffu, v > 1.0f);
+    int pc = __popc(b) + __clz(b) + min(threadIdx.x, 3u) + max(1, 2) + warpSize;
+    atomicAdd(&c[0], pc);
+    atomicMax(&c[1], pc);
+    atomicCAS(&c[2], 0, 1);
+    m[threadIdx.x] = b + __any_sync(0xffffffff, pc > 3) + __all_sync(0xffffffff, pc);
+    __threadfence();
+    __syncwarp();
+    x[threadIdx.x] = v;
+}""",
+    # half and double types, typedef'd ints, launch bounds, multiple kernels
+    """__global__ void __launch_bounds__(256, 2) k1(double *d, int64_t *e, size_t n) {
+    double a = d[0] * 2.0;
+    uint32_t u = 7;
+    e[0] = (int64_t)a + u + n;
+}
+__global__ void k2(half *h, bool flag) {
+    half x = h[0];
+    if (flag) h[1] = x;
+}""",
+    # scoping: shadowing in blocks, for-init scope, labels, goto, empty statements
+    """__global__ void k(int *a) {
+    int x = a[0];
+    { int x = 5; a[1] = x; }
+    for (int x = 0; x < 3; x++) { a[2] += x; }
+    ;;
+    lbl: a[3] = x;
+    goto lbl;
+    if (x) { int y = x * 2; x = y; } else { int y = 3; x -= y; }
+    a[4] = x;
+}""",
+    # module-level consts, __shared__ and templates, static, namespace, forward decl
+    """const int N = 64;
+static const float SCALE = 0.5f;
+__shared__ float gsh[128];
+__global__ void fwd(int *a);
+namespace ns {
+template <typename T>
+__global__ void k(float *o, int *a) {
+    gsh[threadIdx.x] = o[threadIdx.x] * SCALE;
+    a[threadIdx.x % N] = N;
+}
+}""",
+    # comma expressions, compound assignment chains, assignment in conditions
+    """__global__ void k(int *a, int n) {
+    int i, j = 1, k2;
+    i = 0, j = 2;
+    for (i = 0, k2 = n; i < k2; i += 2, k2--) { a[i] = k2; }
+    int t = (j = 5, j + 1);
+    a[0] = t; a[1] = j;
+    a[2] = (a[3] = 7);
+    int u = 3; u *= u += 2;
+    a[4] = u;
+}""",
+    # volatile, const qualifiers, unsigned char/short, signed types, enum type
+    """__global__ void k(volatile int *flag, const unsigned char *b, short *s, unsigned short *us) {
+    volatile __shared__ int v;
+    signed char c = b[0];
+    unsigned short w = us[0];
+    enum E e = 0;
+    long int li = 3;
+    signed long long sl = -1;
+    v = c + w + li + sl + e;
+    flag[0] = v;
+    s[0] = (short)v;
+}""",
+    # float constant folding and literal forms
+    """__global__ void k(float *o) {
+    float a = 1.5f * 2.0f + 3.25e-2f - .5f + 1.f;
+    float b = 10 / 4 + 10 % 3 - (-7) / 2 + (-7) % 2;
+    double c = 1e10 * 3.0;
+    int d = (1 << 4) | (0xF0 >> 2) ^ 3 & 7;
+    o[0] = a + b + c + d;
+    o[1] = 1.0f / 0.0f;
+}""",
+    # parse errors (the reference raises ParseError)
+    """__global__ void k(int *a) { a[0] = ; }""",
+    """__global__ void k(int *a) { int x = undefined_var + 1; a[0] = x; }""",
+    """__global__ void k(int *a) { break; }""",
+    """__global__ void k(int *a) { a[0] = 1 }""",
+    """__global__ void k(int *a { }""",
+    # ValueError from int() of a malformed literal
+    """__global__ void k(int *a) { a[0] = 09; }""",
+    # unterminated kernel body (IndexError / ParseError at EOF)
+    """__global__ void k(int *a) { a[0] = 1;""",
+    # no kernels at all
+    """int x; float y;""",
+    "",
+    # template-parameter type heuristic: (N) casts, (N + 1) parses as an expression
+    """__global__ void k(float *o, int N) {
+    o[0] = (N) * 2;
+    o[1] = (N + 1);
+    o[2] = (T)3;
+}""",
+    # return statements with and without values, code after return
+    """__global__ void k(int *a, int n) {
+    if (n < 0) return;
+    a[0] = n;
+    return;
+    a[1] = 2;
+}""",
+    # pointer-to-pointer indexing and casts between address spaces
+    """__global__ void k(float **rows, int r, int c) {
+    rows[r][c] = 1.0f;
+    float *row = rows[r];
+    row[c + 1] = rows[0][0];
+    float *g = (float *)row;
+    g[0] = 2.0f;
+}""",
+    # nested ternary / logical mixes inside loops with loop-carried values
+    """__global__ void k(int *a, int n) {
+    int s = 0, p = 1;
+    for (int i = 0; i < n; i++) {
+        s = (i & 1) ? s + i : s - i;
+        p = (p > 100 || s < 0) ? 1 : p * 2;
+        if (s > 10 && p < 50) { s -= p; continue; }
+        a[i] = s + p;
+    }
+    a[n] = s;
+}""",
+]
+
+
+def mutate_sources(n: int, seed: int):
+    """Seeded token-level mutations (delete / insert / replace) of the hand
+    cases and of generated kernels: inputs for the parser's error paths."""
+    import re
+    from opencuda_b200 import synth
+    r = random.Random(seed)
+    base = PARSE_CASES + synth.random_batch(50, seed=seed)
+    toks_re = re.compile(r"\s+|[A-Za-z_]\w*|\d+\.?\d*[fFuUlL]*|\S")
+    extra = ['(', ')', '{', '}', ';', ',', '*', '&', '[', ']', '=', '+', '?', ':', 'int',
+             'float', 'if', 'for', 'while', 'x', 'N', '0', '1.0f', '&&', '||', '++', '--',
+             'return', 'break', '__shared__', 'unsigned', 'T', 'sizeof', '->', '.', '<<', '!']
+    out = []
+    for _ in range(n):
+        t = toks_re.findall(r.choice(base))
+        for _ in range(r.randint(1, 3)):
+            if not t:
+                break
+            j = r.randrange(len(t))
+            op = r.random()
+            if op < 0.4:
+                del t[j]
+            elif op < 0.7:
+                t.insert(j, ' ' + r.choice(extra) + ' ')
+            else:
+                t[j] = ' ' + r.choice(extra) + ' '
+        out.append(''.join(t))
+    return out

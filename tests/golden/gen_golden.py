@@ -87,6 +87,12 @@ def pp_cases():
     return cases
 
 
+def ir_cases():
+    from tests._helpers import PARSE_CASES, mutate_sources
+    return (list(PARSE_CASES) + [synth.SGEMM_SRC] + synth.random_batch(48, seed=99)
+            + mutate_sources(300, 4243))
+
+
 def write(name, obj):
     with gzip.open(HERE / name, "wt", encoding="utf-8") as f:
         json.dump(obj, f)
@@ -117,6 +123,22 @@ def main():
     write("pp_golden.json.gz", {"generator": "tests/golden/gen_golden.py",
                                 "gen_version": synth.GEN_VERSION, "cases": out})
     print(f"pp_golden: {len(out)} cases")
+    cases = ir_cases()
+    with ref_runner.RefPool() as pool:
+        res = pool.run(cases, what=("ir", "opt", "ptx"), chunksize=4)
+    out = []
+    for src, r in zip(cases, res):
+        c = {"src": src}
+        for k in ("ir", "opt", "ptx"):
+            if k in r:
+                c[k] = r[k]
+        if "error" in r:
+            c["raises"] = r["error"][0]
+            c["stage"] = r["error"][2]
+        out.append(c)
+    write("ir_golden.json.gz", {"generator": "tests/golden/gen_golden.py",
+                                "gen_version": synth.GEN_VERSION, "cases": out})
+    print(f"ir_golden: {len(out)} cases")
 
 
 if __name__ == "__main__":
