@@ -124,6 +124,12 @@ void ocb_text_free(ocb_text *t);
 int  ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
                      uint32_t n_tu, ocb_text **out);
 
+/* As ocb_parse_batch, then optimize every kernel.  Replaces
+ * opencuda/ir/optimize.py:1443 optimize(module) (with the unroller of
+ * ir/unroll.py); the text is the optimized IR in the same line format. */
+int  ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                        uint32_t n_tu, ocb_text **out);
+
 /* Allocation-free form of ocb_lex_device, for callers that may not allocate
  * device memory when they lex (a framework's memory pool or a fixed arena that
  * forbids cudaMalloc/cudaFree after start-up, or a thread that must not take

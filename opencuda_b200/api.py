@@ -174,6 +174,11 @@ class Context:
         TU's text is its IR in the canonical line format."""
         return self._text_call("ocb_parse_batch", srcs, buf, tu_off)
 
+    def optimize_batch(self, srcs=None, *, buf=None, tu_off=None) -> TextBatch:
+        """As parse_batch, then ``optimize.py:1443 optimize``; each TU's text is
+        its optimized IR."""
+        return self._text_call("ocb_optimize_batch", srcs, buf, tu_off)
+
     def _text_call(self, fn, srcs, buf, tu_off) -> TextBatch:
         if srcs is not None:
             buf, tu_off = pack_sources(srcs)
@@ -224,3 +229,7 @@ def preprocess_batch(srcs, device: int = 0) -> TextBatch:
 
 def parse_batch(srcs, device: int = 0) -> TextBatch:
     return context(device).parse_batch(srcs)
+
+
+def optimize_batch(srcs, device: int = 0) -> TextBatch:
+    return context(device).optimize_batch(srcs)

@@ -288,7 +288,7 @@ int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_of
 
 // Run the back half (lex + parse) over TUs already preprocessed on the host;
 // TUs that outgrow their arena run again alone with larger arenas.
-static int compile_text(ocb_ctx *ctx, const ocb_text &pp, ocb_text *out) {
+static int compile_text(ocb_ctx *ctx, const ocb_text &pp, int stage, ocb_text *out) {
     cudaStream_t st = ctx->stream;
     uint32_t n_tu = pp.n_tu;
     out->n_tu = n_tu;
@@ -321,7 +321,7 @@ static int compile_text(ocb_ctx *ctx, const ocb_text &pp, ocb_text *out) {
                                               cudaMemcpyHostToDevice, st));
         uint64_t total = 0;
         rc = cc_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(),
-                       (uint32_t)nt, ctx->cc_in_status.as<int32_t>(), scale, ctx->cc_text,
+                       (uint32_t)nt, ctx->cc_in_status.as<int32_t>(), stage, scale, ctx->cc_text,
                        ctx->cc_off.as<uint64_t>(), ctx->cc_status.as<int32_t>(), &total, st);
         if (rc) return rc;
         std::vector<uint8_t> bytes(total);
@@ -350,9 +350,9 @@ static int compile_text(ocb_ctx *ctx, const ocb_text &pp, ocb_text *out) {
     return 0;
 }
 
-int ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
-                    ocb_text **out) {
-    if (!ctx || !out || !tu_off) return fail(ctx, "ocb_parse_batch: null argument");
+static int stage_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                       int stage, ocb_text **out) {
+    if (!ctx || !out || !tu_off) return fail(ctx, "null argument");
     *out = nullptr;
     ocb_text *pp = nullptr;
     int rc = ocb_preprocess_batch(ctx, src, tu_off, n_tu, &pp);
@@ -360,9 +360,9 @@ int ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, ui
     ocb_text *t = new (std::nothrow) ocb_text();
     if (!t) {
         delete pp;
-        return fail(ctx, "ocb_parse_batch: out of host memory");
+        return fail(ctx, "out of host memory");
     }
-    rc = compile_text(ctx, *pp, t);
+    rc = compile_text(ctx, *pp, stage, t);
     delete pp;
     if (rc) {
         delete t;
@@ -370,6 +370,16 @@ int ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, ui
     }
     *out = t;
     return 0;
+}
+
+int ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                    ocb_text **out) {
+    return stage_batch(ctx, src, tu_off, n_tu, 0, out);
+}
+
+int ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                       ocb_text **out) {
+    return stage_batch(ctx, src, tu_off, n_tu, 1, out);
 }
 
 int ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,

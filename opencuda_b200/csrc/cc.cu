@@ -6,10 +6,13 @@
 #include <cub/cub.cuh>
 #include "ocb_internal.h"
 #include "cc_parse_stmt.cuh"
+#include "cc_opt.cuh"
 #include "cc_dump.cuh"
 
 namespace ocb {
 namespace cc {
+
+enum { CC_STAGE_IR = 0, CC_STAGE_OPT = 1 };
 
 // Per-TU arena and output sizes (bytes, 16-aligned) from the token counts.
 __global__ void k_cc_sizes(const uint64_t *tu_tok_off, uint32_t n_tu, uint32_t scale,
@@ -22,7 +25,7 @@ __global__ void k_cc_sizes(const uint64_t *tu_tok_off, uint32_t n_tu, uint32_t s
         return;
     }
     uint64_t nt = tu_tok_off[i + 1] - tu_tok_off[i];
-    arena_sz[i] = ((65536ull + 1024ull * nt) * scale + 15) & ~15ull;
+    arena_sz[i] = ((65536ull + 2048ull * nt) * scale + 15) & ~15ull;
     out_sz[i] = ((4096ull + 256ull * nt) * scale + 15) & ~15ull;
 }
 
@@ -39,9 +42,13 @@ struct CCArgs {
     const uint64_t *out_off;     // capacity offsets
     uint64_t *out_len;           // n_tu + 1 (last = 0)
     int32_t *status;
+    int stage;                   // CC_STAGE_*
 };
 
-__global__ void __launch_bounds__(64) k_cc_parse(CCArgs A) {
+// One thread per TU: parse, then (stage >= CC_STAGE_OPT) optimize, then write
+// the IR text.  The TU's arena slice is split: 3/4 for the IR, 1/4 scratch
+// for the optimizer's per-pass tables.
+__global__ void __launch_bounds__(64) k_cc_compile(CCArgs A) {
     uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i > A.n_tu) return;
     if (i == A.n_tu) {
@@ -54,7 +61,10 @@ __global__ void __launch_bounds__(64) k_cc_parse(CCArgs A) {
         A.status[i] = st0;
         return;
     }
-    Arena ar{A.arena + A.arena_off[i], 0, A.arena_off[i + 1] - A.arena_off[i], false};
+    uint64_t sz = A.arena_off[i + 1] - A.arena_off[i];
+    uint64_t ir_sz = (sz / 4 * 3) & ~15ull;
+    Arena ar{A.arena + A.arena_off[i], 0, ir_sz, false};
+    Arena tmp{A.arena + A.arena_off[i] + ir_sz, 0, sz - ir_sz, false};
     Module *m = (Module *)ar.alloc(sizeof(Module), 16);
     Parser *P = (Parser *)ar.alloc(sizeof(Parser), 16);
     if (!m || !P) {
@@ -77,6 +87,17 @@ __global__ void __launch_bounds__(64) k_cc_parse(CCArgs A) {
     if (P->err) {
         A.status[i] = m->raises;
         return;
+    }
+    if (A.stage >= CC_STAGE_OPT) {
+        optimize_module(*m, tmp);
+        if (ar.oom || tmp.oom) {
+            A.status[i] = OCB_TU_OVERFLOW;
+            return;
+        }
+        if (m->unsup) {
+            A.status[i] = OCB_TU_UNSUPPORTED;
+            return;
+        }
     }
     Out o{(char *)A.out + A.out_off[i], 0, A.out_off[i + 1] - A.out_off[i], false};
     dump_module(o, *m);
@@ -111,8 +132,9 @@ __global__ void k_cc_pack(const uint8_t *out, const uint64_t *cap_off, const uin
 static constexpr size_t kCCStack = 64 * 1024;
 
 int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d_off,
-              uint32_t n_tu, const int32_t *d_in_status, uint32_t scale, DevBuf &out_text,
-              uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total, cudaStream_t st) {
+              uint32_t n_tu, const int32_t *d_in_status, int stage, uint32_t scale,
+              DevBuf &out_text, uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total,
+              cudaStream_t st) {
     using namespace cc;
     if (n_tu == 0) {
         *h_total = 0;
@@ -161,8 +183,8 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     OCB_TRY("cc: stack limit", cudaDeviceGetLimit(&cur_stack, cudaLimitStackSize));
     if (cur_stack < kCCStack) OCB_TRY("cc: stack limit", cudaDeviceSetLimit(cudaLimitStackSize, kCCStack));
     CCArgs A{d_text, tstart, tkl, tu_tok, d_status, n_tu, ctx->cc_arena.as<uint8_t>(), arena_off,
-             ctx->cc_out.as<uint8_t>(), out_cap_off, out_len, d_status};
-    k_cc_parse<<<(unsigned)((n1 + 63) / 64), 64, 0, st>>>(A);
+             ctx->cc_out.as<uint8_t>(), out_cap_off, out_len, d_status, stage};
+    k_cc_compile<<<(unsigned)((n1 + 63) / 64), 64, 0, st>>>(A);
     OCB_TRY("cc: parse launch", cudaGetLastError());
     OCB_TRY("cc: pack scan",
             cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, out_len, d_out_off, (int)n1, st));

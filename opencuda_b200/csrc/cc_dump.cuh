@@ -33,6 +33,17 @@ struct Out {  // bounded text sink
         if (v < 0) put('-');
         while (k) put(t[--k]);
     }
+    OCB_HD void put_i128(pyint v) {
+        char t[48];
+        int k = 0;
+        unsigned __int128 u = v < 0 ? (unsigned __int128)0 - (unsigned __int128)v : (unsigned __int128)v;
+        do {
+            t[k++] = (char)('0' + (int)(u % 10));
+            u /= 10;
+        } while (u);
+        if (v < 0) put('-');
+        while (k) put(t[--k]);
+    }
     OCB_HD void put_hex64(uint64_t v) {
         const char *h = "0123456789abcdef";
         for (int s = 60; s >= 0; s -= 4) put(h[(v >> s) & 15]);
@@ -76,7 +87,7 @@ OCB_HD inline void dump_opnd(Out &o, const Module &m, Opnd x) {
         o.put_hex64(bits);
     } else {
         o.put(":i:");
-        o.put_i64(c.i);
+        o.put_i128(c.i);
     }
 }
 

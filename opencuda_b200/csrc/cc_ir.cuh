@@ -26,6 +26,50 @@ namespace ocb {
 namespace cc {
 
 // ---------------------------------------------------------------------------
+// Python int values of constants: 128-bit, kept inside +-2^120 (a TU whose
+// constant arithmetic leaves that range is outside the subset)
+// ---------------------------------------------------------------------------
+typedef __int128 pyint;
+#define PYINT_LIM (((pyint)1) << 120)
+OCB_HD inline bool py_ok(pyint v) { return v < PYINT_LIM && v > -PYINT_LIM; }
+OCB_HD inline pyint py_abs(pyint v) { return v < 0 ? -v : v; }
+// a * b, false when the product leaves the range
+OCB_HD inline bool py_mul(pyint a, pyint b, pyint &r) {
+    if (a == 0 || b == 0) {
+        r = 0;
+        return true;
+    }
+    if (py_abs(a) > PYINT_LIM / py_abs(b)) return false;
+    r = a * b;
+    return py_ok(r);
+}
+// number of bits of |v| (int.bit_length)
+OCB_HD inline int py_bitlen(pyint v) {
+    unsigned __int128 u = (unsigned __int128)py_abs(v);
+    int n = 0;
+    while (u) {
+        u >>= 1;
+        ++n;
+    }
+    return n;
+}
+// a << s for s >= 0
+OCB_HD inline bool py_shl(pyint a, pyint s, pyint &r) {
+    if (a == 0) {
+        r = 0;
+        return true;
+    }
+    if (s < 0 || s > 120 || py_bitlen(a) + (int)s >= 120) return false;
+    r = a * (((pyint)1) << (int)s);
+    return true;
+}
+// a >> s for s >= 0 (floor semantics, like Python)
+OCB_HD inline pyint py_shr(pyint a, pyint s) {
+    if (s >= 127) return a < 0 ? -1 : 0;
+    return a >> (int)s;
+}
+
+// ---------------------------------------------------------------------------
 // arena + growable vectors
 // ---------------------------------------------------------------------------
 struct Arena {
@@ -244,7 +288,7 @@ struct Value {
 struct Const {
     Ty ty;
     uint8_t pyfloat;  // the reference holds a Python float (else an int)
-    int64_t i;
+    pyint i;
     double f;
 };
 enum : uint8_t { O_NONE = 0, O_VAL = 1, O_CONST = 2 };
@@ -343,7 +387,7 @@ struct Module {
         vals.push(*ar, Value{id, ty, name});
         return vals.n - 1;
     }
-    OCB_HD Opnd cint(Ty ty, int64_t v) {
+    OCB_HD Opnd cint(Ty ty, pyint v) {
         Const c{ty, 0, v, 0.0};
         consts.push(*ar, c);
         return oc(consts.n - 1);

@@ -1,0 +1,2093 @@
+// IR optimizer: restates opencuda/ir/optimize.py (passes and the pass
+// schedule of optimize(), :1443-1607) and opencuda/ir/unroll.py for one
+// kernel at a time, on the IR built by the parser.  Every pass keeps the
+// reference's visiting order, its in-place mutation of instructions and its
+// change counts (the counts steer the fixpoint loops of the schedule).
+//
+// Constants carry Python semantics: an int (pyint) or a float, whatever the
+// IR type says; folds follow Python's int/float arithmetic.
+#pragma once
+#include "cc_ir.cuh"
+
+namespace ocb {
+namespace cc {
+
+// ---------------------------------------------------------------------------
+// Python value helpers for Const
+// ---------------------------------------------------------------------------
+struct PyVal {
+    uint8_t isf;  // 1 = float
+    pyint i;
+    double f;
+};
+OCB_HD inline PyVal pv_int(pyint i) { return PyVal{0, i, 0.0}; }
+OCB_HD inline PyVal pv_float(double f) { return PyVal{1, 0, f}; }
+OCB_HD inline PyVal pv_of(const Const &c) { return PyVal{c.pyfloat, c.i, c.f}; }
+OCB_HD inline bool is_finite(double f) { return f == f && f - f == 0.0; }
+
+// exact comparison of an int with a float (Python int/float ordering)
+// returns -1, 0, 1; 2 when b is NaN (unordered)
+OCB_HD inline int cmp_int_float(pyint a, double b) {
+    if (b != b) return 2;
+    if (b >= 1.7e38) return -1;   // beyond any kept pyint
+    if (b <= -1.7e38) return 1;
+    double fb = floor(b);
+    pyint ib = (pyint)fb;
+    if (a < ib) return -1;
+    if (a > ib) return 1;
+    return b == fb ? 0 : -1;
+}
+// Python ==
+OCB_HD inline bool pv_eq(const PyVal &a, const PyVal &b) {
+    if (!a.isf && !b.isf) return a.i == b.i;
+    if (a.isf && b.isf) return a.f == b.f;
+    if (a.isf) return cmp_int_float(b.i, a.f) == 0;
+    return cmp_int_float(a.i, b.f) == 0;
+}
+// Python a > b (False when unordered)
+OCB_HD inline bool pv_gt(const PyVal &a, const PyVal &b) {
+    if (!a.isf && !b.isf) return a.i > b.i;
+    if (a.isf && b.isf) return a.f > b.f;
+    if (a.isf) {
+        int c = cmp_int_float(b.i, a.f);
+        return c == -1;
+    }
+    int c = cmp_int_float(a.i, b.f);
+    return c == 1;
+}
+OCB_HD inline bool pv_eq_int(const PyVal &a, pyint v) { return pv_eq(a, pv_int(v)); }
+OCB_HD inline bool pv_truthy(const PyVal &a) { return a.isf ? a.f != 0.0 : a.i != 0; }
+// int(value): false when Python raises (NaN/inf) or leaves the kept range
+OCB_HD inline bool pv_to_int(const PyVal &a, pyint &out) {
+    if (!a.isf) {
+        out = a.i;
+        return true;
+    }
+    if (!is_finite(a.f) || a.f >= 1.3e36 || a.f <= -1.3e36) return false;
+    out = (pyint)trunc(a.f);
+    return true;
+}
+OCB_HD inline double pv_to_float(const PyVal &a) { return a.isf ? a.f : (double)a.i; }
+
+// Python float % (CPython float_rem: fmod, then the sign of the divisor)
+OCB_HD inline double py_fmod(double vx, double wx) {
+    double mod = fmod(vx, wx);
+    if (mod != 0.0) {
+        if ((wx < 0) != (mod < 0)) mod += wx;
+    } else {
+        mod = copysign(0.0, wx);
+    }
+    return mod;
+}
+
+// _mask_int (optimize.py:53-70): wrap to the type's width with its sign.
+// `ok` is false where the reference would keep an unbounded value we cannot.
+OCB_HD inline pyint mask_int_wrapped(pyint wrapped_low, Ty ty) {
+    uint32_t bits = ty_size(ty) * 8;
+    unsigned __int128 mask = bits >= 128 ? ~(unsigned __int128)0
+                                         : (((unsigned __int128)1) << bits) - 1;
+    unsigned __int128 v = (unsigned __int128)wrapped_low & mask;
+    if (ty_is_signed(ty) && bits && ((v >> (bits - 1)) & 1)) {
+        return (pyint)v - (pyint)(((unsigned __int128)1) << bits);
+    }
+    return (pyint)v;
+}
+OCB_HD inline bool masks(Ty ty) { return !is_ptr(ty) && !ty_is_float(ty); }
+
+// ---------------------------------------------------------------------------
+// per-pass scratch: id-indexed arrays and a label -> block map
+// ---------------------------------------------------------------------------
+template <class T>
+struct IdArr {
+    T *p;
+    uint32_t n;
+    T dflt;
+    OCB_HD void init(Arena &a, uint32_t size, T d) {
+        n = size;
+        dflt = d;
+        p = (T *)a.alloc(sizeof(T) * (uint64_t)(size ? size : 1), 16);
+        if (p)
+            for (uint32_t i = 0; i < size; ++i) p[i] = d;
+        else
+            n = 0;
+    }
+    OCB_HD T get(uint32_t id) const { return id < n ? p[id] : dflt; }
+    OCB_HD bool set(uint32_t id, T v) {
+        if (id >= n) return false;
+        p[id] = v;
+        return true;
+    }
+};
+
+struct LabelMap {
+    int32_t *ht;
+    uint32_t cap;
+    const Module *m;
+    OCB_HD void build(Arena &a, const Module &mod, const Vec<uint32_t> &blocks) {
+        m = &mod;
+        cap = 16;
+        while (cap < 2 * blocks.n + 2) cap *= 2;
+        ht = (int32_t *)a.alloc(4ull * cap, 16);
+        if (!ht) {
+            cap = 0;
+            return;
+        }
+        for (uint32_t i = 0; i < cap; ++i) ht[i] = -1;
+        for (uint32_t i = 0; i < blocks.n; ++i) put(blocks[i]);
+    }
+    OCB_HD void put(uint32_t b) {  // last wins, like a dict comprehension
+        Str l = m->blocks[b].label;
+        uint32_t h = hash(l) & (cap - 1);
+        while (ht[h] >= 0) {
+            if (eq(m->blocks[ht[h]].label, l)) {
+                ht[h] = (int32_t)b;
+                return;
+            }
+            h = (h + 1) & (cap - 1);
+        }
+        ht[h] = (int32_t)b;
+    }
+    OCB_HD int32_t get(Str l) const {
+        if (!cap) return -1;
+        uint32_t h = hash(l) & (cap - 1);
+        while (ht[h] >= 0) {
+            if (eq(m->blocks[ht[h]].label, l)) return ht[h];
+            h = (h + 1) & (cap - 1);
+        }
+        return -1;
+    }
+};
+
+// A set of labels (open addressing over Str).
+struct LabelSet {
+    Str *ht;
+    uint32_t cap, n;
+    OCB_HD void init(Arena &a, uint32_t want) {
+        cap = 16;
+        while (cap < 2 * want + 2) cap *= 2;
+        n = 0;
+        ht = (Str *)a.alloc(sizeof(Str) * (uint64_t)cap, 16);
+        if (!ht) {
+            cap = 0;
+            return;
+        }
+        for (uint32_t i = 0; i < cap; ++i) ht[i] = Str{nullptr, 0};
+    }
+    OCB_HD bool has(Str l) const {
+        if (!cap) return false;
+        uint32_t h = hash(l) & (cap - 1);
+        while (ht[h].p) {
+            if (eq(ht[h], l)) return true;
+            h = (h + 1) & (cap - 1);
+        }
+        return false;
+    }
+    OCB_HD bool add(Str l) {  // true when newly added
+        if (!cap) return false;
+        uint32_t h = hash(l) & (cap - 1);
+        while (ht[h].p) {
+            if (eq(ht[h], l)) return false;
+            h = (h + 1) & (cap - 1);
+        }
+        if (2 * (n + 1) > cap) return false;  // sized by the caller
+        ht[h] = l;
+        ++n;
+        return true;
+    }
+};
+
+// CSE keys (optimize.py:397-640)
+struct OKey {
+    uint8_t tag;  // 0 'const', 1 'val'
+    PyVal c;
+    uint32_t id;
+};
+struct CKey {
+    uint8_t kind;  // 0 bin, 1 cvt, 2 cmp, 3 pure call
+    uint8_t op;
+    OKey l, r;
+    uint32_t t1, t2;  // str(type) keys
+    Str func;
+};
+OCB_HD inline bool okey_eq(const OKey &a, const OKey &b) {
+    if (a.tag != b.tag) return false;
+    if (a.tag == 1) return a.id == b.id;
+    return pv_eq(a.c, b.c);
+}
+// tuple a > tuple b for ('const', v) / ('val', id)
+OCB_HD inline bool okey_gt(const OKey &a, const OKey &b) {
+    if (a.tag != b.tag) return a.tag > b.tag;
+    if (a.tag == 1) return a.id > b.id;
+    if (pv_eq(a.c, b.c)) return false;
+    return pv_gt(a.c, b.c);
+}
+OCB_HD inline uint32_t okey_hash(const OKey &k) {
+    if (k.tag == 1) return k.id * 2654435761u + 7;
+    // numeric hash: integral floats hash like ints
+    pyint iv;
+    if (k.c.isf) {
+        double f = k.c.f;
+        if (is_finite(f) && f == trunc(f) && f < 1e30 && f > -1e30) iv = (pyint)f;
+        else {
+            uint64_t b;
+            memcpy(&b, &f, 8);
+            return (uint32_t)(b ^ (b >> 29)) * 0x9E3779B1u;
+        }
+    } else {
+        iv = k.c.i;
+    }
+    uint64_t lo = (uint64_t)iv, hi = (uint64_t)((unsigned __int128)iv >> 64);
+    return (uint32_t)((lo ^ (lo >> 31) ^ (hi * 31)) * 0x9E3779B1u);
+}
+OCB_HD inline bool ckey_eq(const CKey &a, const CKey &b) {
+    if (a.kind != b.kind) return false;
+    if (a.kind == 3) return eq(a.func, b.func);
+    if (a.kind != 1 && a.op != b.op) return false;
+    if (!okey_eq(a.l, b.l)) return false;
+    if (a.kind == 1) return a.t1 == b.t1 && a.t2 == b.t2;
+    if (!okey_eq(a.r, b.r)) return false;
+    return a.kind == 2 || a.t1 == b.t1;
+}
+OCB_HD inline uint32_t ckey_hash(const CKey &k) {
+    if (k.kind == 3) return hash(k.func) ^ 0x55u;
+    uint32_t h = k.kind * 31u + (k.kind == 1 ? 0 : k.op);
+    h = h * 1000003u ^ okey_hash(k.l);
+    if (k.kind != 1) h = h * 1000003u ^ okey_hash(k.r);
+    if (k.kind != 2) h = h * 1000003u ^ k.t1;
+    if (k.kind == 1) h = h * 1000003u ^ k.t2;
+    return h;
+}
+
+// The `seen` dict of one block: key -> value index.
+struct Seen {
+    struct E {
+        CKey k;
+        uint32_t v;
+        uint8_t used;
+    };
+    E *t;
+    uint32_t cap, n;
+    OCB_HD bool init(Arena &a, uint32_t c) {
+        cap = 16;
+        while (cap < c) cap *= 2;
+        n = 0;
+        t = (E *)a.alloc(sizeof(E) * (uint64_t)cap, 16);
+        if (!t) return false;
+        for (uint32_t i = 0; i < cap; ++i) t[i].used = 0;
+        return true;
+    }
+    OCB_HD int32_t find(const CKey &k) const {
+        uint32_t h = ckey_hash(k) & (cap - 1);
+        while (t[h].used) {
+            if (ckey_eq(t[h].k, k)) return (int32_t)t[h].v;
+            h = (h + 1) & (cap - 1);
+        }
+        return -1;
+    }
+    OCB_HD bool grow(Arena &a) {
+        Seen s2;
+        if (!s2.init(a, cap * 2)) return false;
+        for (uint32_t i = 0; i < cap; ++i)
+            if (t[i].used) s2.put_new(t[i].k, t[i].v);
+        *this = s2;
+        return true;
+    }
+    OCB_HD void put_new(const CKey &k, uint32_t v) {
+        uint32_t h = ckey_hash(k) & (cap - 1);
+        while (t[h].used) {
+            if (ckey_eq(t[h].k, k)) {
+                t[h].v = v;
+                return;
+            }
+            h = (h + 1) & (cap - 1);
+        }
+        t[h].k = k;
+        t[h].v = v;
+        t[h].used = 1;
+        n++;
+    }
+    OCB_HD bool put(Arena &a, const CKey &k, uint32_t v) {
+        if (2 * (n + 1) > cap && !grow(a)) return false;
+        put_new(k, v);
+        return true;
+    }
+    OCB_HD bool copy_from(Arena &a, const Seen &o) {
+        cap = o.cap;
+        n = o.n;
+        t = (E *)a.alloc(sizeof(E) * (uint64_t)cap, 16);
+        if (!t) return false;
+        for (uint32_t i = 0; i < cap; ++i) t[i] = o.t[i];
+        return true;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// the optimizer of one kernel
+// ---------------------------------------------------------------------------
+struct Opt {
+    Module &m;
+    Arena &ar;   // the IR's arena (persistent)
+    Arena &tmp;  // per-pass scratch, reset between passes
+    Kernel *k;
+
+    OCB_HD Opt(Module &mod, Arena &tmp_) : m(mod), ar(*mod.ar), tmp(tmp_), k(nullptr) {}
+
+    OCB_HD bool bad() const { return m.unsup || ar.oom || tmp.oom; }
+#ifdef OCB_TRAP_UNSUP
+    void unsup(int line = __builtin_LINE()) {
+        fprintf(stderr, "opt unsupported at cc_opt.cuh:%d\n", line);
+        m.unsup = true;
+    }
+#else
+    OCB_HD void unsup() { m.unsup = true; }
+#endif
+    OCB_HD Inst &I(uint32_t ix) { return m.insts[ix]; }
+    OCB_HD Block &B(uint32_t b) { return m.blocks[b]; }
+    OCB_HD uint32_t vid(Opnd o) const { return m.vals[o.x].id; }
+    OCB_HD uint32_t did(const Inst &i) const { return m.vals[(uint32_t)i.dest].id; }
+    OCB_HD bool has_dest(const Inst &i) const { return i.dest >= 0; }
+    OCB_HD Ty dty(const Inst &i) const { return m.vals[(uint32_t)i.dest].ty; }
+    OCB_HD PyVal cv(Opnd o) const { return pv_of(m.consts[o.x]); }
+    OCB_HD bool cis(Opnd o, pyint v) const { return o.k == O_CONST && pv_eq_int(cv(o), v); }
+    OCB_HD uint32_t new_value(const char *name, Ty ty) {
+        return m.add_val(k->next_id++, ty, S(name));
+    }
+    OCB_HD uint32_t new_value(Str name, Ty ty) { return m.add_val(k->next_id++, ty, name); }
+    OCB_HD Opnd cint(Ty t, pyint v) { return m.cint(t, v); }
+    OCB_HD Opnd cflt(Ty t, double v) { return m.cfloat(t, v); }
+    OCB_HD Opnd cpv(Ty t, const PyVal &v) { return v.isf ? m.cfloat(t, v.f) : m.cint(t, v.i); }
+    OCB_HD uint32_t add_inst(const Inst &i) { return m.add_inst(i); }
+    OCB_HD uint32_t nid() const { return k->next_id; }
+    OCB_HD void reset_tmp() {
+        tmp.used = 0;
+    }
+    // dest ids of all instructions (hasattr(inst,'dest') and inst.dest is not None)
+    OCB_HD IdArr<uint32_t> def_counts() {
+        IdArr<uint32_t> dc;
+        dc.init(tmp, nid(), 0);
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.dest >= 0) {
+                    uint32_t d = did(in);
+                    dc.set(d, dc.get(d) + 1);
+                }
+            }
+        }
+        return dc;
+    }
+    OCB_HD void set_br(uint32_t b, Str t) { B(b).term = Term{T_BR, onone(), t, Str{nullptr, 0}}; }
+
+    // ---- _fold_bin (optimize.py:73-106) -----------------------------------
+    // Result: 0 = None, 1 = value in *out (exact), 2 = int value known only
+    // modulo 2^128 (the caller masks it, or declines the TU)
+    OCB_HD int fold_bin(uint8_t op, PyVal a, PyVal b, bool is_float, PyVal &out) {
+        if (is_float) {
+            double x = pv_to_float(a), y = pv_to_float(b);
+            switch (op) {
+            case BO_ADD: out = pv_float(x + y); return 1;
+            case BO_SUB: out = pv_float(x - y); return 1;
+            case BO_MUL: out = pv_float(x * y); return 1;
+            case BO_DIV:
+                if (y != 0.0) { out = pv_float(x / y); return 1; }
+                return 0;
+            case BO_MOD:
+                if (y != 0.0) { out = pv_float(py_fmod(x, y)); return 1; }
+                return 0;
+            default: break;
+            }
+            PyVal ia, ib;
+            pyint xi, yi;
+            if (!pv_to_int(pv_float(x), xi) || !pv_to_int(pv_float(y), yi)) {
+                if (!is_finite(x) || !is_finite(y)) return 0;  // int() raises: no fold
+                unsup();
+                return 0;
+            }
+            ia = pv_int(xi);
+            ib = pv_int(yi);
+            return fold_int(op, ia.i, ib.i, out);
+        }
+        pyint x, y;
+        if (!pv_to_int(a, x) || !pv_to_int(b, y)) {
+            bool fa = a.isf && !is_finite(a.f), fb = b.isf && !is_finite(b.f);
+            if (fa || fb) return 0;  // int(nan/inf) raises inside the try: None
+            unsup();
+            return 0;
+        }
+        return fold_int(op, x, y, out);
+    }
+    OCB_HD int fold_int(uint8_t op, pyint x, pyint y, PyVal &out) {
+        switch (op) {
+        case BO_ADD: out = pv_int(x + y); return py_ok(out.i) ? 1 : 2;
+        case BO_SUB: out = pv_int(x - y); return py_ok(out.i) ? 1 : 2;
+        case BO_MUL: {
+            pyint r;
+            if (py_mul(x, y, r)) { out = pv_int(r); return 1; }
+            out = pv_int((pyint)((unsigned __int128)x * (unsigned __int128)y));
+            return 2;
+        }
+        case BO_DIV: {
+            if (y == 0) return 0;
+            pyint q = py_abs(x) / py_abs(y);
+            out = pv_int(((x >= 0) == (y >= 0)) ? q : -q);
+            return 1;
+        }
+        case BO_MOD: {
+            if (y == 0) return 0;
+            pyint q = py_abs(x) / py_abs(y);
+            pyint rem = py_abs(x) - q * py_abs(y);
+            out = pv_int(x >= 0 ? rem : -rem);
+            return 1;
+        }
+        case BO_AND: out = pv_int(x & y); return 1;
+        case BO_OR: out = pv_int(x | y); return 1;
+        case BO_XOR: out = pv_int(x ^ y); return 1;
+        case BO_SHL: {
+            if (y < 0) return 0;  // ValueError: negative shift count
+            pyint r;
+            if (py_shl(x, y, r)) { out = pv_int(r); return 1; }
+            out = pv_int(y >= 128 ? 0 : (pyint)((unsigned __int128)x << (int)y));
+            return 2;
+        }
+        case BO_SHR:
+            if (y < 0) return 0;
+            out = pv_int(py_shr(x, y));
+            return 1;
+        }
+        return 0;
+    }
+
+    // ---- constant_fold (optimize.py:109-387) -------------------------------
+    OCB_HD uint32_t constant_fold() {
+        uint32_t folded = 0;
+        // per-block replacements: id -> const operand; stamp = block ordinal
+        uint32_t n0 = nid();
+        IdArr<uint32_t> stamp;
+        stamp.init(tmp, n0, 0xFFFFFFFFu);
+        Opnd *rep = (Opnd *)tmp.alloc(sizeof(Opnd) * (uint64_t)(n0 ? n0 : 1), 16);
+        if (!rep || bad()) return 0;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            uint32_t bidx = k->blocks[bi];
+            auto resolve = [&](Opnd o) -> Opnd {
+                if (o.k == O_VAL) {
+                    uint32_t id = vid(o);
+                    if (stamp.get(id) == bi) return rep[id];  // always a Const
+                }
+                return o;
+            };
+            Vec<uint32_t> nl;
+            nl.init();
+            bool rebuilt = false;
+            Vec<uint32_t> &old = B(bidx).insts;
+            for (uint32_t ii = 0; ii < old.n; ++ii) {
+                uint32_t ix = old[ii];
+                Inst &in = I(ix);
+                if (in.kind == I_BIN) {
+                    in.a = resolve(in.a);
+                    in.b = resolve(in.b);
+                    Ty dt = dty(in);
+                    bool is_float = ty_is_float(dt);
+                    bool lc = in.a.k == O_CONST, rc = in.b.k == O_CONST;
+                    PyVal lv = lc ? cv(in.a) : PyVal{}, rv = rc ? cv(in.b) : PyVal{};
+                    PyVal res;
+                    int fr = (lc && rc) ? fold_bin(in.op, lv, rv, is_float, res) : 0;
+                    if (bad()) return folded;
+                    bool rv_int = rc && !rv.isf, lv_int = lc && !lv.isf;
+                    auto pow2 = [](pyint v) { return v > 0 && (v & (v - 1)) == 0; };
+                    if (fr) {
+                        Opnd fc;
+                        if (is_float) {
+                            if (fr == 2) { unsup(); return folded; }
+                            fc = cpv(dt, res);
+                            in.a = fc;
+                            in.b = cflt(dt, 0.0);
+                        } else {
+                            if (!masks(dt) && fr == 2) { unsup(); return folded; }
+                            pyint v = res.i;
+                            if (masks(dt)) {
+                                if (ty_size(dt) == 0) { unsup(); return folded; }
+                                v = mask_int_wrapped(res.i, dt);
+                            }
+                            fc = cint(dt, v);
+                            in.a = fc;
+                            in.b = cint(dt, 0);
+                        }
+                        in.op = BO_ADD;
+                        uint32_t id = did(in);
+                        if (stamp.set(id, bi)) rep[id] = fc;
+                        else { unsup(); return folded; }
+                        folded++;
+                    } else if (in.op == BO_MUL && rc && pv_eq_int(rv, 1) && in.a.k == O_VAL) {
+                        in.op = BO_ADD;
+                        in.b = is_float ? cflt(dt, 0.0) : cint(dt, 0);
+                        folded++;
+                    } else if (in.op == BO_MUL && lc && pv_eq_int(lv, 1) && in.b.k == O_VAL) {
+                        in.op = BO_ADD;
+                        in.a = in.b;
+                        in.b = is_float ? cflt(dt, 0.0) : cint(dt, 0);
+                        folded++;
+                    } else if (in.op == BO_DIV && rc && pv_eq_int(rv, 1) && in.a.k == O_VAL) {
+                        in.op = BO_ADD;
+                        in.b = cint(dt, 0);
+                        folded++;
+                    } else if (!is_float && in.op == BO_MUL && rv_int && pow2(rv.i)) {
+                        in.op = BO_SHL;
+                        in.b = cint(dt, py_bitlen(rv.i) - 1);
+                        folded++;
+                    } else if (!is_float && in.op == BO_MUL && lv_int && pow2(lv.i)) {
+                        in.op = BO_SHL;
+                        in.a = in.b;
+                        in.b = cint(dt, py_bitlen(lv.i) - 1);
+                        folded++;
+                    } else if (!is_float && in.op == BO_DIV && rv_int && rv.i > 1 && pow2(rv.i) &&
+                               !is_ptr(dt) && !ty_is_signed(dt)) {
+                        in.op = BO_SHR;
+                        in.b = cint(dt, py_bitlen(rv.i) - 1);
+                        folded++;
+                    } else if (!is_float && in.op == BO_DIV && rv_int && rv.i > 1 && pow2(rv.i) &&
+                               !is_ptr(dt) && ty_is_signed(dt)) {
+                        int kk = py_bitlen(rv.i) - 1;
+                        int bits = (int)ty_size(dt) * 8;
+                        Ty tu = bits == 32 ? S_UINT32 : S_UINT64;
+                        Opnd n = in.a;
+                        uint32_t t1 = new_value("_sdiv_sign", dt);
+                        uint32_t t2 = new_value("_sdiv_bias", tu);
+                        uint32_t t3 = new_value("_sdiv_adj", dt);
+                        if (!rebuilt) { nl = old.copy(ar); nl.n = ii; rebuilt = true; }
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_SHR, (int32_t)t1, n, cint(dt, bits - 1))));
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_SHR, (int32_t)t2, ov(t1), cint(tu, bits - kk))));
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_ADD, (int32_t)t3, n, ov(t2))));
+                        Inst &in2 = I(ix);  // m.insts may have grown
+                        in2.op = BO_SHR;
+                        in2.a = ov(t3);
+                        in2.b = cint(dt, kk);
+                        folded++;
+                    } else if (!is_float && in.op == BO_MOD && rv_int && pow2(rv.i) && !is_ptr(dt) &&
+                               !ty_is_signed(dt)) {
+                        in.op = BO_AND;
+                        in.b = cint(dt, rv.i - 1);
+                        folded++;
+                    } else if (!is_float && in.op == BO_MOD && rv_int && pow2(rv.i) && !is_ptr(dt) &&
+                               ty_is_signed(dt)) {
+                        int kk = py_bitlen(rv.i) - 1;
+                        int bits = (int)ty_size(dt) * 8;
+                        Ty tu = bits == 32 ? S_UINT32 : S_UINT64;
+                        Opnd n = in.a;
+                        uint32_t t1 = new_value("_smod_sign", dt);
+                        uint32_t t2 = new_value("_smod_bias", tu);
+                        uint32_t t3 = new_value("_smod_adj", dt);
+                        uint32_t t4 = new_value("_smod_masked", dt);
+                        if (!rebuilt) { nl = old.copy(ar); nl.n = ii; rebuilt = true; }
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_SHR, (int32_t)t1, n, cint(dt, bits - 1))));
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_SHR, (int32_t)t2, ov(t1), cint(tu, bits - kk))));
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_ADD, (int32_t)t3, n, ov(t2))));
+                        nl.push(ar, add_inst(mk_inst(I_BIN, BO_AND, (int32_t)t4, ov(t3), cint(dt, rv.i - 1))));
+                        Inst &in2 = I(ix);
+                        in2.op = BO_SUB;
+                        in2.a = ov(t4);
+                        in2.b = ov(t2);
+                        folded++;
+                    } else if (in.op == BO_MUL && ((rc && pv_eq_int(rv, 0)) || (lc && pv_eq_int(lv, 0)))) {
+                        in.a = cint(dt, 0);
+                        in.b = cint(dt, 0);
+                        in.op = BO_ADD;
+                        folded++;
+                    } else if (!is_float && in.op == BO_AND &&
+                               ((rc && pv_eq_int(rv, 0)) || (lc && pv_eq_int(lv, 0)))) {
+                        in.a = cint(dt, 0);
+                        in.b = cint(dt, 0);
+                        in.op = BO_ADD;
+                        folded++;
+                    } else if (!is_float && in.op == BO_AND && !is_ptr(dt)) {
+                        if (ty_size(dt) == 0) { unsup(); return folded; }
+                        pyint ones = mask_int_wrapped(-1, dt);
+                        if (rc && pv_eq_int(rv, ones) && in.a.k == O_VAL) {
+                            in.op = BO_ADD;
+                            in.b = cint(dt, 0);
+                            folded++;
+                        } else if (lc && pv_eq_int(lv, ones) && in.b.k == O_VAL) {
+                            in.op = BO_ADD;
+                            in.a = in.b;
+                            in.b = cint(dt, 0);
+                            folded++;
+                        }
+                    } else if (!is_float && in.op == BO_OR && !is_ptr(dt)) {
+                        if (ty_size(dt) == 0) { unsup(); return folded; }
+                        pyint ones = mask_int_wrapped(-1, dt);
+                        if ((rc && pv_eq_int(rv, ones)) || (lc && pv_eq_int(lv, ones))) {
+                            in.a = cint(dt, ones);
+                            in.b = cint(dt, 0);
+                            in.op = BO_ADD;
+                            folded++;
+                        }
+                    } else if (!is_float && (in.op == BO_SUB || in.op == BO_XOR) && in.a.k == O_VAL &&
+                               in.b.k == O_VAL && vid(in.a) == vid(in.b)) {
+                        in.a = cint(dt, 0);
+                        in.b = cint(dt, 0);
+                        in.op = BO_ADD;
+                        folded++;
+                    } else if (!is_float && (in.op == BO_AND || in.op == BO_OR) && in.a.k == O_VAL &&
+                               in.b.k == O_VAL && vid(in.a) == vid(in.b)) {
+                        in.op = BO_ADD;
+                        in.b = cint(dt, 0);
+                        folded++;
+                    }
+                } else if (in.kind == I_CMP) {
+                    in.a = resolve(in.a);
+                    in.b = resolve(in.b);
+                } else if (in.kind == I_CVT) {
+                    Opnd src = resolve(in.a);
+                    in.a = src;
+                    if (src.k == O_CONST) {
+                        Ty dt = dty(in);
+                        bool dfl = ty_is_float(dt);
+                        const Const &sc = m.consts[src.x];
+                        bool sfl = ty_is_float(sc.ty);
+                        PyVal sv = pv_of(sc);
+                        bool ok = true;
+                        PyVal fv;
+                        if (dfl) {
+                            fv = pv_float(pv_to_float(sv));
+                        } else {
+                            PyVal raw = sfl ? pv_float(pv_to_float(sv)) : sv;
+                            pyint iv;
+                            if (!pv_to_int(raw, iv)) {
+                                if (raw.isf && !is_finite(raw.f)) ok = false;  // raises: kept
+                                else { unsup(); return folded; }
+                            } else {
+                                if (masks(dt)) {
+                                    if (ty_size(dt) == 0) { unsup(); return folded; }
+                                    iv = mask_int_wrapped(iv, dt);
+                                }
+                                fv = pv_int(iv);
+                            }
+                        }
+                        if (ok) {
+                            Opnd l = cpv(dt, fv);
+                            Opnd r = dfl ? cflt(dt, 0.0) : cint(dt, 0);
+                            uint32_t nb = add_inst(mk_inst(I_BIN, BO_ADD, I(ix).dest, l, r));
+                            if (!rebuilt) { nl = old.copy(ar); nl.n = ii; rebuilt = true; }
+                            nl.push(ar, nb);
+                            folded++;
+                            continue;
+                        }
+                    }
+                } else if (in.kind == I_LOAD) {
+                    in.a = resolve(in.a);
+                } else if (in.kind == I_STORE) {
+                    in.a = resolve(in.a);
+                    in.b = resolve(in.b);
+                }
+                if (rebuilt) nl.push(ar, ix);
+            }
+            if (rebuilt) B(bidx).insts = nl;
+            Term &t = B(bidx).term;
+            if (t.kind == T_CBR) {
+                Opnd c = t.v.k == O_VAL ? resolve(t.v) : t.v;
+                if (c.k == O_CONST) {
+                    Str tg = pv_truthy(cv(c)) ? t.t : t.f;
+                    set_br(bidx, tg);
+                    folded++;
+                }
+            }
+            if (bad()) return folded;
+        }
+        return folded;
+    }
+
+    // ---- cse (optimize.py:397-640) -------------------------------------------
+    OCB_HD uint32_t cse() {
+        IdArr<uint32_t> gdc = def_counts();
+        uint32_t n0 = nid();
+        uint32_t eliminated = 0;
+        // global replacements: id -> value index (0xFFFFFFFF none)
+        IdArr<uint32_t> grep;
+        grep.init(tmp, n0, 0xFFFFFFFFu);
+        // predecessor lists (with duplicates, like the reference's list)
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        uint32_t nb = k->blocks.n;
+        uint32_t *npred = (uint32_t *)tmp.alloc(4ull * (nb + 1), 16);
+        int32_t *pred0 = (int32_t *)tmp.alloc(4ull * (nb + 1), 16);
+        Seen *final_seen = (Seen *)tmp.alloc(sizeof(Seen) * (uint64_t)(nb + 1), 16);
+        uint8_t *has_final = (uint8_t *)tmp.alloc(nb + 1, 16);
+        // block ordinal by label (the reference keys dicts by label: last wins)
+        if (!npred || !pred0 || !final_seen || !has_final || bad()) return 0;
+        IdArr<uint32_t> ord_of_block;  // block index -> ordinal
+        ord_of_block.init(tmp, m.blocks.n, 0xFFFFFFFFu);
+        for (uint32_t i = 0; i < nb; ++i) {
+            npred[i] = 0;
+            pred0[i] = -1;
+            has_final[i] = 0;
+        }
+        // the dict {bb.label: []} has one entry per distinct label: use the
+        // ordinal of the last block with that label
+        for (uint32_t i = 0; i < nb; ++i) ord_of_block.set(k->blocks[i], i);
+        auto lab_ord = [&](Str l) -> int32_t {
+            int32_t b = lm.get(l);
+            return b < 0 ? -1 : (int32_t)ord_of_block.get((uint32_t)b);
+        };
+        for (uint32_t i = 0; i < nb; ++i) {
+            Block &b = B(k->blocks[i]);
+            const Term &t = b.term;
+            Str tg[2];
+            int nt = 0;
+            if (t.kind == T_BR) tg[nt++] = t.t;
+            else if (t.kind == T_CBR) { tg[nt++] = t.t; tg[nt++] = t.f; }
+            for (int q = 0; q < nt; ++q) {
+                int32_t o = lab_ord(tg[q]);
+                if (o < 0) continue;
+                if (npred[o] == 0) pred0[o] = (int32_t)i;
+                npred[o]++;
+            }
+        }
+        IdArr<uint32_t> rstamp;  // per-block replacements: stamp = ordinal
+        rstamp.init(tmp, n0, 0xFFFFFFFFu);
+        uint32_t *rval = (uint32_t *)tmp.alloc(4ull * (n0 ? n0 : 1), 16);
+        IdArr<uint32_t> wstamp;  // written_ids
+        wstamp.init(tmp, n0, 0xFFFFFFFFu);
+        if (!rval || bad()) return 0;
+        bool any_rep = false;
+        for (uint32_t bi = 0; bi < nb; ++bi) {
+            uint32_t bidx = k->blocks[bi];
+            Block &b = B(bidx);
+            int32_t my = lab_ord(b.label);
+            Seen seen;
+            // pred lists are keyed by label; a duplicate label shares the last one's
+            uint32_t np = my >= 0 ? npred[my] : 0;
+            int32_t p0 = my >= 0 ? pred0[my] : -1;
+            if (np == 1 && p0 >= 0 && has_final[lab_ord(B(k->blocks[p0]).label)]) {
+                if (!seen.copy_from(tmp, final_seen[lab_ord(B(k->blocks[p0]).label)])) return eliminated;
+            } else {
+                if (!seen.init(tmp, 64)) return eliminated;
+            }
+            auto in_rep = [&](uint32_t id) { return rstamp.get(id) == bi; };
+            auto rep1 = [&](Opnd o) -> Opnd {  // single-step replacement
+                if (o.k == O_VAL && in_rep(vid(o))) return ov(rval[vid(o)]);
+                return o;
+            };
+            auto key = [&](Opnd o) -> OKey {
+                OKey r;
+                if (o.k == O_VAL) {
+                    uint32_t v = o.x;
+                    uint32_t guard = 0;
+                    while (in_rep(m.vals[v].id)) {
+                        v = rval[m.vals[v].id];
+                        if (++guard > 1000000) { unsup(); break; }
+                    }
+                    r.tag = 1;
+                    r.id = m.vals[v].id;
+                    r.c = PyVal{};
+                    return r;
+                }
+                r.tag = 0;
+                r.id = 0;
+                r.c = cv(o);
+                if (r.c.isf && r.c.f != r.c.f) unsup();
+                return r;
+            };
+            auto written = [&](uint32_t id) { return wstamp.get(id) == bi; };
+            auto mark_written = [&](uint32_t id) {
+                if (!wstamp.set(id, bi)) unsup();
+            };
+            Vec<uint32_t> rep_ids;
+            rep_ids.init();
+            auto add_rep = [&](uint32_t id, uint32_t v) {
+                if (!rstamp.set(id, bi)) { unsup(); return; }
+                rval[id] = v;
+                rep_ids.push(tmp, id);
+            };
+            uint32_t w = 0;
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                uint32_t ix = b.insts[ii];
+                Inst &in = I(ix);
+                bool keep = true;
+                if (in.kind == I_BIN) {
+                    in.a = rep1(in.a);
+                    in.b = rep1(in.b);
+                    uint32_t d = did(in);
+                    if (written(d)) {
+                    } else if (gdc.get(d) >= 2) {
+                        mark_written(d);
+                    } else {
+                        CKey ck;
+                        ck.kind = 0;
+                        ck.op = in.op;
+                        OKey lk = key(in.a), rk = key(in.b);
+                        bool comm = in.op == BO_ADD || in.op == BO_MUL || in.op == BO_AND ||
+                                    in.op == BO_OR || in.op == BO_XOR;
+                        if (comm && okey_gt(lk, rk)) { OKey t = lk; lk = rk; rk = t; }
+                        ck.l = lk;
+                        ck.r = rk;
+                        ck.t1 = ty_strkey(dty(in));
+                        ck.t2 = 0;
+                        ck.func = Str{nullptr, 0};
+                        int32_t f = seen.find(ck);
+                        if (f >= 0) {
+                            add_rep(d, (uint32_t)f);
+                            eliminated++;
+                            keep = false;
+                        } else {
+                            if (!seen.put(tmp, ck, (uint32_t)in.dest)) return eliminated;
+                            mark_written(d);
+                        }
+                    }
+                } else if (in.kind == I_CVT) {
+                    in.a = rep1(in.a);
+                    uint32_t d = did(in);
+                    if (!written(d) && gdc.get(d) < 2) {
+                        CKey ck;
+                        ck.kind = 1;
+                        ck.op = 0;
+                        ck.l = key(in.a);
+                        ck.r = OKey{};
+                        ck.t1 = ty_strkey(dty(in));
+                        ck.t2 = ty_strkey(m.opty(in.a));
+                        ck.func = Str{nullptr, 0};
+                        int32_t f = seen.find(ck);
+                        if (f >= 0) {
+                            add_rep(d, (uint32_t)f);
+                            eliminated++;
+                            keep = false;
+                        } else {
+                            if (!seen.put(tmp, ck, (uint32_t)in.dest)) return eliminated;
+                            mark_written(d);
+                        }
+                    }
+                } else if (in.kind == I_CMP) {
+                    in.a = rep1(in.a);
+                    in.b = rep1(in.b);
+                    uint32_t d = did(in);
+                    if (!written(d) && gdc.get(d) < 2) {
+                        OKey lk = key(in.a), rk = key(in.b);
+                        uint8_t op = in.op;
+                        if ((op == CO_EQ || op == CO_NE) && okey_gt(lk, rk)) {
+                            OKey t = lk; lk = rk; rk = t;
+                        } else if ((op == CO_LT || op == CO_GT || op == CO_LE || op == CO_GE) &&
+                                   okey_gt(lk, rk)) {
+                            OKey t = lk; lk = rk; rk = t;
+                            op = op == CO_LT ? CO_GT : op == CO_GT ? CO_LT : op == CO_LE ? CO_GE : CO_LE;
+                        }
+                        CKey ck;
+                        ck.kind = 2;
+                        ck.op = op;
+                        ck.l = lk;
+                        ck.r = rk;
+                        ck.t1 = ck.t2 = 0;
+                        ck.func = Str{nullptr, 0};
+                        int32_t f = seen.find(ck);
+                        if (f >= 0) {
+                            add_rep(d, (uint32_t)f);
+                            eliminated++;
+                            keep = false;
+                        } else {
+                            if (!seen.put(tmp, ck, (uint32_t)in.dest)) return eliminated;
+                            mark_written(d);
+                        }
+                    }
+                } else if (in.kind == I_CALL) {
+                    if (in.dest >= 0 && is_pure_builtin(in.func)) {
+                        uint32_t d = did(in);
+                        if (!written(d) && gdc.get(d) < 2) {
+                            CKey ck;
+                            ck.kind = 3;
+                            ck.op = 0;
+                            ck.l = ck.r = OKey{};
+                            ck.t1 = ck.t2 = 0;
+                            ck.func = in.func;
+                            int32_t f = seen.find(ck);
+                            if (f >= 0) {
+                                add_rep(d, (uint32_t)f);
+                                eliminated++;
+                                keep = false;
+                            } else {
+                                if (!seen.put(tmp, ck, (uint32_t)in.dest)) return eliminated;
+                                mark_written(d);
+                            }
+                        }
+                    }
+                } else if (in.kind == I_LOAD) {
+                    in.a = rep1(in.a);
+                } else if (in.kind == I_STORE) {
+                    in.a = rep1(in.a);
+                    in.b = rep1(in.b);
+                }
+                if (bad()) return eliminated;
+                if (keep) b.insts[w++] = ix;
+            }
+            b.insts.n = w;
+            // global_replacements.update(replacements)
+            for (uint32_t q = 0; q < rep_ids.n; ++q) {
+                grep.set(rep_ids[q], rval[rep_ids[q]]);
+                any_rep = true;
+            }
+            if (my >= 0) {
+                final_seen[my] = seen;
+                has_final[my] = 1;
+            }
+        }
+        if (any_rep) {
+            auto chase = [&](Opnd o) -> Opnd {
+                if (o.k != O_VAL) return o;
+                uint32_t v = o.x, guard = 0;
+                while (grep.get(m.vals[v].id) != 0xFFFFFFFFu) {
+                    v = grep.get(m.vals[v].id);
+                    if (++guard > 1000000) { unsup(); break; }
+                }
+                return ov(v);
+            };
+            for (uint32_t bi = 0; bi < nb; ++bi) {
+                Block &b = B(k->blocks[bi]);
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    Inst &in = I(b.insts[ii]);
+                    switch (in.kind) {
+                    case I_BIN:
+                    case I_CMP:
+                    case I_STORE:
+                        in.a = chase(in.a);
+                        in.b = chase(in.b);
+                        break;
+                    case I_CVT:
+                    case I_LOAD: in.a = chase(in.a); break;
+                    case I_CALL:
+                        if (in.args.n) {
+                            Vec<Opnd> na = in.args.copy(ar);
+                            for (uint32_t q = 0; q < na.n; ++q) na[q] = chase(na[q]);
+                            in.args = na;
+                        }
+                        break;
+                    default: break;
+                    }
+                }
+                Term &t = b.term;
+                if (t.kind == T_CBR && t.v.k == O_VAL) t.v = chase(t.v);
+            }
+        }
+        return eliminated;
+    }
+    OCB_HD static bool is_pure_builtin(Str f) {
+        return eq(f, "threadIdx.x") || eq(f, "threadIdx.y") || eq(f, "threadIdx.z") ||
+               eq(f, "blockIdx.x") || eq(f, "blockIdx.y") || eq(f, "blockIdx.z") ||
+               eq(f, "blockDim.x") || eq(f, "blockDim.y") || eq(f, "blockDim.z") ||
+               eq(f, "gridDim.x") || eq(f, "gridDim.y") || eq(f, "gridDim.z");
+    }
+
+    // ---- dead_block_elim (optimize.py:643-675) ---------------------------------
+    OCB_HD uint32_t dead_block_elim() {
+        if (!k->blocks.n) return 0;
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        LabelSet reach;
+        reach.init(tmp, k->blocks.n * 3 + 4);
+        Vec<Str> queue;
+        queue.init();
+        queue.push(tmp, B(k->blocks[0]).label);
+        while (queue.n && !bad()) {
+            Str l = queue.back();
+            queue.n--;
+            if (reach.has(l)) continue;
+            reach.add(l);
+            int32_t b = lm.get(l);
+            if (b >= 0) {
+                const Term &t = B((uint32_t)b).term;
+                if (t.kind == T_BR) queue.push(tmp, t.t);
+                else if (t.kind == T_CBR) {
+                    queue.push(tmp, t.t);
+                    queue.push(tmp, t.f);
+                }
+            }
+        }
+        uint32_t w = 0, removed = 0;
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            if (reach.has(B(k->blocks[i]).label)) k->blocks[w++] = k->blocks[i];
+            else removed++;
+        }
+        k->blocks.n = w;
+        return removed;
+    }
+
+    // ---- identity_fold (optimize.py:678-776) -----------------------------------
+    OCB_HD uint32_t identity_fold() {
+        IdArr<uint32_t> dc = def_counts();
+        uint32_t n0 = nid();
+        IdArr<uint8_t> has;
+        has.init(tmp, n0, 0);
+        Opnd *src = (Opnd *)tmp.alloc(sizeof(Opnd) * (uint64_t)(n0 ? n0 : 1), 16);
+        if (!src || bad()) return 0;
+        bool any = false;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind != I_BIN || dc.get(did(in)) != 1) continue;
+                uint8_t op = in.op;
+                bool rz = (op == BO_ADD || op == BO_SUB || op == BO_SHL || op == BO_SHR ||
+                           op == BO_XOR || op == BO_OR) && cis(in.b, 0);
+                bool lz = (op == BO_ADD || op == BO_XOR || op == BO_OR) && cis(in.a, 0);
+                if (rz) {
+                    has.set(did(in), 1);
+                    src[did(in)] = in.a;
+                    any = true;
+                } else if (lz) {
+                    has.set(did(in), 1);
+                    src[did(in)] = in.b;
+                    any = true;
+                }
+            }
+        }
+        if (!any) return 0;
+        IdArr<uint32_t> vis;  // cycle guard of _resolve, stamped per call
+        vis.init(tmp, n0, 0);
+        uint32_t call_no = 0;
+        auto resolve = [&](Opnd o) -> Opnd {
+            if (o.k != O_VAL || !has.get(vid(o))) return o;
+            ++call_no;
+            vis.set(vid(o), call_no);
+            Opnd r = src[vid(o)];
+            while (r.k == O_VAL && has.get(vid(r))) {
+                if (vis.get(vid(r)) == call_no) break;
+                vis.set(vid(r), call_no);
+                r = src[vid(r)];
+            }
+            return r;
+        };
+        uint32_t eliminated = 0;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            uint32_t w = 0;
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                uint32_t ix = b.insts[ii];
+                Inst &in = I(ix);
+                if (in.kind == I_BIN && has.get(did(in))) {
+                    eliminated++;
+                    continue;
+                }
+                switch (in.kind) {
+                case I_BIN:
+                case I_CMP:
+                case I_STORE:
+                    in.a = resolve(in.a);
+                    in.b = resolve(in.b);
+                    break;
+                case I_LOAD:
+                case I_CVT: in.a = resolve(in.a); break;
+                case I_CALL:
+                    if (in.args.n) {
+                        Vec<Opnd> na = in.args.copy(ar);
+                        for (uint32_t q = 0; q < na.n; ++q) na[q] = resolve(na[q]);
+                        in.args = na;
+                    }
+                    break;
+                default: break;
+                }
+                b.insts[w++] = ix;
+            }
+            b.insts.n = w;
+            if (b.term.kind == T_CBR) b.term.v = resolve(b.term.v);
+        }
+        return eliminated;
+    }
+
+    // ---- dead_inst_elim (optimize.py:779-832) ----------------------------------
+    OCB_HD uint32_t dead_inst_elim() {
+        uint32_t eliminated = 0;
+        bool changed = true;
+        while (changed && !bad()) {
+            changed = false;
+            size_t mark = tmp.used;
+            IdArr<uint8_t> used;
+            used.init(tmp, nid(), 0);
+            if (bad()) return eliminated;
+            auto use = [&](Opnd o) {
+                if (o.k == O_VAL) used.set(vid(o), 1);
+            };
+            for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+                Block &b = B(k->blocks[bi]);
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    const Inst &in = I(b.insts[ii]);
+                    switch (in.kind) {
+                    case I_BIN:
+                    case I_CMP:
+                    case I_STORE:
+                        use(in.a);
+                        use(in.b);
+                        break;
+                    case I_CVT:
+                    case I_LOAD: use(in.a); break;
+                    default: break;
+                    }
+                    for (uint32_t q = 0; q < in.args.n; ++q) use(in.args[q]);
+                }
+                const Term &t = b.term;
+                if (t.kind == T_CBR || t.kind == T_RET) use(t.v);
+            }
+            for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+                Block &b = B(k->blocks[bi]);
+                uint32_t w = 0;
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    uint32_t ix = b.insts[ii];
+                    const Inst &in = I(ix);
+                    if ((in.kind == I_BIN || in.kind == I_CMP || in.kind == I_CVT) &&
+                        !used.get(did(in))) {
+                        eliminated++;
+                        changed = true;
+                        continue;
+                    }
+                    b.insts[w++] = ix;
+                }
+                b.insts.n = w;
+            }
+            tmp.used = mark;
+        }
+        return eliminated;
+    }
+
+    // ---- loops (optimize.py:835-948) -----------------------------------------
+    struct Loop {
+        Str header, preheader, backedge_src;
+        LabelSet body;
+    };
+    OCB_HD int succs(uint32_t b, Str *out) {
+        const Term &t = B(b).term;
+        if (t.kind == T_BR) { out[0] = t.t; return 1; }
+        if (t.kind == T_CBR) { out[0] = t.t; out[1] = t.f; return 2; }
+        return 0;
+    }
+    // predecessor lists keyed by label (entries in block order, duplicates kept)
+    struct Preds {
+        uint32_t *start, *cnt, *items;  // by block ordinal of the label's last block
+    };
+    OCB_HD bool build_preds(LabelMap &lm, IdArr<uint32_t> &ordm, Preds &P) {
+        uint32_t nb = k->blocks.n;
+        P.start = (uint32_t *)tmp.alloc(4ull * (nb + 1), 16);
+        P.cnt = (uint32_t *)tmp.alloc(4ull * (nb + 1), 16);
+        P.items = (uint32_t *)tmp.alloc(4ull * (2 * nb + 1), 16);
+        if (!P.start || !P.cnt || !P.items) return false;
+        for (uint32_t i = 0; i <= nb; ++i) P.cnt[i] = 0;
+        Str s[2];
+        for (uint32_t i = 0; i < nb; ++i) {
+            int ns = succs(k->blocks[i], s);
+            for (int q = 0; q < ns; ++q) {
+                int32_t b = lm.get(s[q]);
+                if (b >= 0) P.cnt[ordm.get((uint32_t)b)]++;
+            }
+        }
+        uint32_t acc = 0;
+        for (uint32_t i = 0; i < nb; ++i) {
+            P.start[i] = acc;
+            acc += P.cnt[i];
+            P.cnt[i] = 0;
+        }
+        for (uint32_t i = 0; i < nb; ++i) {
+            int ns = succs(k->blocks[i], s);
+            for (int q = 0; q < ns; ++q) {
+                int32_t b = lm.get(s[q]);
+                if (b >= 0) {
+                    uint32_t o = ordm.get((uint32_t)b);
+                    P.items[P.start[o] + P.cnt[o]++] = i;  // predecessor's ordinal
+                }
+            }
+        }
+        return true;
+    }
+
+    OCB_HD bool find_loops(Vec<Loop> &loops) {
+        loops.init();
+        uint32_t nb = k->blocks.n;
+        if (!nb) return true;
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        IdArr<uint32_t> ordm;
+        ordm.init(tmp, m.blocks.n, 0);
+        for (uint32_t i = 0; i < nb; ++i) ordm.set(k->blocks[i], i);
+        Preds P;
+        if (!build_preds(lm, ordm, P)) return false;
+        // iterative DFS with the recursion's visiting order
+        uint8_t *visited = (uint8_t *)tmp.alloc(nb + 1, 16);
+        uint8_t *onst = (uint8_t *)tmp.alloc(nb + 1, 16);
+        struct Fr { uint32_t o; uint8_t next; };
+        Fr *st = (Fr *)tmp.alloc(sizeof(Fr) * (uint64_t)(nb + 1), 16);
+        struct BE { uint32_t src, hdr; };
+        Vec<BE> back;
+        back.init();
+        if (!visited || !onst || !st) return false;
+        for (uint32_t i = 0; i < nb; ++i) visited[i] = onst[i] = 0;
+        auto ord_of = [&](Str l) -> int32_t {
+            int32_t b = lm.get(l);
+            return b < 0 ? -1 : (int32_t)ordm.get((uint32_t)b);
+        };
+        int32_t e = ord_of(B(k->blocks[0]).label);
+        uint32_t sp = 0;
+        if (e >= 0) {
+            visited[e] = 1;
+            onst[e] = 1;
+            st[sp++] = Fr{(uint32_t)e, 0};
+        }
+        while (sp) {
+            Fr &f = st[sp - 1];
+            Str s[2];
+            int ns = succs(k->blocks[f.o], s);
+            if (f.next >= ns) {
+                onst[f.o] = 0;
+                sp--;
+                continue;
+            }
+            Str sl = s[f.next++];
+            int32_t so = ord_of(sl);
+            if (so < 0) continue;
+            if (onst[so]) {
+                back.push(tmp, BE{f.o, (uint32_t)so});
+            } else if (!visited[so]) {
+                if (sp >= 990) {  // the reference's recursive DFS hits Python's limit
+                    unsup();
+                    return false;
+                }
+                visited[so] = 1;
+                onst[so] = 1;
+                st[sp++] = Fr{(uint32_t)so, 0};
+            }
+        }
+        // one loop per distinct back edge with a unique preheader
+        for (uint32_t bi = 0; bi < back.n; ++bi) {
+            bool dup = false;
+            for (uint32_t bj = 0; bj < bi && !dup; ++bj)
+                dup = back[bj].src == back[bi].src && back[bj].hdr == back[bi].hdr;
+            if (dup) continue;
+            Loop L;
+            L.header = B(k->blocks[back[bi].hdr]).label;
+            L.backedge_src = B(k->blocks[back[bi].src]).label;
+            L.body.init(tmp, nb + 2);
+            L.body.add(L.header);
+            Vec<uint32_t> work;
+            work.init();
+            work.push(tmp, back[bi].src);
+            while (work.n) {
+                uint32_t c = work.back();
+                work.n--;
+                Str cl = B(k->blocks[c]).label;
+                if (L.body.has(cl)) continue;
+                L.body.add(cl);
+                int32_t co = ord_of(cl);
+                if (co < 0) continue;
+                for (uint32_t q = 0; q < P.cnt[co]; ++q) {
+                    uint32_t p = P.items[P.start[co] + q];
+                    if (!L.body.has(B(k->blocks[p]).label)) work.push(tmp, p);
+                }
+            }
+            int32_t ho = (int32_t)back[bi].hdr;
+            uint32_t nnl = 0, pre = 0;
+            for (uint32_t q = 0; q < P.cnt[ho]; ++q) {
+                uint32_t p = P.items[P.start[ho] + q];
+                if (!L.body.has(B(k->blocks[p]).label)) {
+                    nnl++;
+                    pre = p;
+                }
+            }
+            if (nnl != 1) continue;
+            L.preheader = B(k->blocks[pre]).label;
+            loops.push(tmp, L);
+        }
+        return !bad();
+    }
+
+    // ---- licm (optimize.py:951-1073) -------------------------------------------
+    OCB_HD uint32_t licm() {
+        Vec<Loop> loops;
+        if (!find_loops(loops) || !loops.n) return 0;
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        uint32_t nb = k->blocks.n;
+        IdArr<uint32_t> idx_of;  // label_to_idx (last wins) by block index
+        idx_of.init(tmp, m.blocks.n, 0);
+        for (uint32_t i = 0; i < nb; ++i) idx_of.set(k->blocks[i], i);
+        IdArr<uint32_t> dc = def_counts();
+        IdArr<uint8_t> cond;
+        cond.init(tmp, nid(), 0);
+        for (uint32_t i = 0; i < nb; ++i) {
+            const Term &t = B(k->blocks[i]).term;
+            if (t.kind == T_CBR && t.v.k == O_VAL) cond.set(vid(t.v), 1);
+        }
+        uint32_t total = 0;
+        for (uint32_t li = 0; li < loops.n && !bad(); ++li) {
+            Loop &L = loops[li];
+            int32_t pre = lm.get(L.preheader);
+            if (pre < 0) continue;
+            size_t mark = tmp.used;
+            IdArr<uint8_t> ldef, inv;
+            ldef.init(tmp, nid(), 0);
+            inv.init(tmp, nid(), 0);
+            for (uint32_t i = 0; i < k->blocks.n; ++i) {
+                Block &b = B(k->blocks[i]);
+                if (!L.body.has(b.label)) continue;
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    const Inst &in = I(b.insts[ii]);
+                    if (in.dest >= 0) ldef.set(did(in), 1);
+                }
+            }
+            for (uint32_t i = 0; i < k->blocks.n; ++i) {
+                Block &b = B(k->blocks[i]);
+                if (L.body.has(b.label)) continue;
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    const Inst &in = I(b.insts[ii]);
+                    if (in.dest >= 0 && !ldef.get(did(in))) inv.set(did(in), 1);
+                }
+            }
+            auto is_inv = [&](Opnd o) { return o.k == O_CONST || (o.k == O_VAL && inv.get(vid(o))); };
+            // body labels sorted by their block index (label_to_idx; absent -> 0)
+            Vec<uint32_t> order;  // block indices of body labels, sorted
+            order.init();
+            for (uint32_t i = 0; i < nb; ++i) {
+                Str l = B(k->blocks[i]).label;
+                if (!L.body.has(l)) continue;
+                int32_t b = lm.get(l);
+                if (b != (int32_t)k->blocks[i]) continue;  // a label counts once
+                order.push(tmp, (uint32_t)b);
+            }
+            // label_to_idx maps a label to its last index; order by that index
+            for (uint32_t a = 1; a < order.n; ++a) {
+                uint32_t x = order[a];
+                int32_t j = (int32_t)a - 1;
+                while (j >= 0 && idx_of.get(order[j]) > idx_of.get(x)) {
+                    order[j + 1] = order[j];
+                    --j;
+                }
+                order[j + 1] = x;
+            }
+            bool changed = true;
+            while (changed && !bad()) {
+                changed = false;
+                for (uint32_t oi = 0; oi < order.n; ++oi) {
+                    uint32_t bidx = order[oi];
+                    Block &b = B(bidx);
+                    if (eq(b.label, L.header)) continue;
+                    uint32_t w = 0;
+                    for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                        uint32_t ix = b.insts[ii];
+                        const Inst &in = I(ix);
+                        bool hoist = false;
+                        if ((in.kind == I_BIN || in.kind == I_CVT) && dc.get(did(in)) == 1 &&
+                            !cond.get(did(in))) {
+                            hoist = in.kind == I_BIN ? (is_inv(in.a) && is_inv(in.b)) : is_inv(in.a);
+                        }
+                        if (hoist) {
+                            B((uint32_t)pre).insts.push(ar, ix);
+                            inv.set(did(in), 1);
+                            total++;
+                            changed = true;
+                            continue;
+                        }
+                        b.insts[w++] = ix;
+                    }
+                    b.insts.n = w;
+                }
+            }
+            tmp.used = mark;
+        }
+        return total;
+    }
+
+    // ---- merge_linear_chains (optimize.py:1076-1131) ---------------------------
+    OCB_HD uint32_t merge_linear_chains() {
+        if (!k->blocks.n) return 0;
+        uint32_t merged = 0;
+        bool changed = true;
+        while (changed && !bad()) {
+            changed = false;
+            size_t mark = tmp.used;
+            LabelMap lm;
+            lm.build(tmp, m, k->blocks);
+            IdArr<uint32_t> pc;  // pred count by block index of the label's last block
+            pc.init(tmp, m.blocks.n, 0);
+            for (uint32_t i = 0; i < k->blocks.n; ++i) {
+                Str s[2];
+                int ns = succs(k->blocks[i], s);
+                for (int q = 0; q < ns; ++q) {
+                    int32_t b = lm.get(s[q]);
+                    if (b >= 0) pc.set((uint32_t)b, pc.get((uint32_t)b) + 1);
+                }
+            }
+            for (uint32_t i = 0; i < k->blocks.n; ++i) {
+                uint32_t bb = k->blocks[i];
+                const Term &t = B(bb).term;
+                if (t.kind != T_BR) continue;
+                Str tl = t.t;
+                int32_t tb = lm.get(tl);
+                if (tb < 0) continue;
+                if (pc.get((uint32_t)tb) != 1) continue;
+                Block &T = B((uint32_t)tb);
+                uint32_t tn = T.insts.n;
+                for (uint32_t q = 0; q < tn; ++q) B(bb).insts.push(ar, T.insts[q]);
+                B(bb).term = B((uint32_t)tb).term;
+                uint32_t w = 0;
+                for (uint32_t j = 0; j < k->blocks.n; ++j)
+                    if (!eq(B(k->blocks[j]).label, tl)) k->blocks[w++] = k->blocks[j];
+                k->blocks.n = w;
+                merged++;
+                changed = true;
+                break;
+            }
+            tmp.used = mark;
+        }
+        return merged;
+    }
+
+    // ---- thread_empty_blocks (optimize.py:1134-1238) ---------------------------
+    OCB_HD uint32_t thread_empty_blocks() {
+        if (!k->blocks.n) return 0;
+        Str entry = B(k->blocks[0]).label;
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        LabelSet transparent;
+        transparent.init(tmp, k->blocks.n + 2);
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            const Block &b = B(k->blocks[i]);
+            if (!eq(b.label, entry) && b.insts.n == 0 && b.term.kind == T_BR) transparent.add(b.label);
+        }
+        if (!transparent.n) return 0;
+        LabelSet visited;
+        auto forward = [&](Str l) -> Str {
+            visited.init(tmp, k->blocks.n + 2);
+            for (;;) {
+                if (visited.has(l)) return l;
+                int32_t b = lm.get(l);
+                if (b < 0) return l;
+                if (eq(l, entry)) return l;
+                const Block &bb = B((uint32_t)b);
+                if (bb.insts.n == 0 && bb.term.kind == T_BR) {
+                    visited.add(l);
+                    l = bb.term.t;
+                } else {
+                    return l;
+                }
+            }
+        };
+        // fwd map: transparent label -> target (computed before any rewrite)
+        struct FE { Str from, to; };
+        Vec<FE> fwd;
+        fwd.init();
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            const Block &b = B(k->blocks[i]);
+            if (!transparent.has(b.label)) continue;
+            bool dup = false;
+            for (uint32_t q = 0; q < fwd.n && !dup; ++q) dup = eq(fwd[q].from, b.label);
+            if (dup) continue;
+            size_t mark = tmp.used;
+            Str to = forward(b.label);
+            tmp.used = mark;
+            fwd.push(tmp, FE{b.label, to});
+        }
+        LabelMap fm;  // from -> index into fwd, via a small open table
+        uint32_t fcap = 16;
+        while (fcap < 2 * fwd.n + 2) fcap *= 2;
+        int32_t *fht = (int32_t *)tmp.alloc(4ull * fcap, 16);
+        if (!fht || bad()) return 0;
+        for (uint32_t i = 0; i < fcap; ++i) fht[i] = -1;
+        for (uint32_t i = 0; i < fwd.n; ++i) {
+            uint32_t h = hash(fwd[i].from) & (fcap - 1);
+            while (fht[h] >= 0) h = (h + 1) & (fcap - 1);
+            fht[h] = (int32_t)i;
+        }
+        (void)fm;
+        auto F = [&](Str l) -> Str {
+            uint32_t h = hash(l) & (fcap - 1);
+            while (fht[h] >= 0) {
+                if (eq(fwd[fht[h]].from, l)) return fwd[fht[h]].to;
+                h = (h + 1) & (fcap - 1);
+            }
+            return l;
+        };
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            Term &t = B(k->blocks[i]).term;
+            if (t.kind == T_BR) {
+                Str nt = F(t.t);
+                if (!eq(nt, t.t)) t.t = nt;
+            } else if (t.kind == T_CBR) {
+                Str ntr = F(t.t), nfa = F(t.f);
+                if (!eq(ntr, t.t) || !eq(nfa, t.f)) {
+                    if (eq(ntr, nfa)) t = Term{T_BR, onone(), ntr, Str{nullptr, 0}};
+                    else {
+                        t.t = ntr;
+                        t.f = nfa;
+                    }
+                }
+            }
+        }
+        LabelSet ref;
+        ref.init(tmp, 2 * k->blocks.n + 4);
+        ref.add(entry);
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            const Term &t = B(k->blocks[i]).term;
+            if (t.kind == T_BR) ref.add(t.t);
+            else if (t.kind == T_CBR) {
+                ref.add(t.t);
+                ref.add(t.f);
+            }
+        }
+        uint32_t removed = 0, w = 0;
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            Str l = B(k->blocks[i]).label;
+            if (transparent.has(l) && !ref.has(l)) removed++;
+            else k->blocks[w++] = k->blocks[i];
+        }
+        k->blocks.n = w;
+        return removed;
+    }
+
+    // ---- fold_empty_ret_blocks (optimize.py:1241-1294) -------------------------
+    OCB_HD uint32_t fold_empty_ret_blocks() {
+        if (!k->blocks.n) return 0;
+        Str entry = B(k->blocks[0]).label;
+        LabelMap er;  // label -> block with an empty ret (last wins)
+        Vec<uint32_t> ers;
+        ers.init();
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            const Block &b = B(k->blocks[i]);
+            if (eq(b.label, entry)) continue;
+            if (b.insts.n == 0 && b.term.kind == T_RET) ers.push(tmp, k->blocks[i]);
+        }
+        if (!ers.n) return 0;
+        er.build(tmp, m, ers);
+        uint32_t folded = 0;
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            Term &t = B(k->blocks[i]).term;
+            if (t.kind != T_BR) continue;
+            int32_t r = er.get(t.t);
+            if (r < 0) continue;
+            Opnd rv = B((uint32_t)r).term.v;
+            t = Term{T_RET, rv, Str{nullptr, 0}, Str{nullptr, 0}};
+            folded++;
+        }
+        return folded;
+    }
+
+    // ---- fma_fuse (optimize.py:1297-1440) ----------------------------------------
+    OCB_HD uint32_t fma_fuse() {
+        IdArr<uint32_t> dc, uc;
+        dc.init(tmp, nid(), 0);
+        uc.init(tmp, nid(), 0);
+        auto tally = [&](Opnd o) {
+            if (o.k == O_VAL) uc.set(vid(o), uc.get(vid(o)) + 1);
+        };
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.dest >= 0) dc.set(did(in), dc.get(did(in)) + 1);
+                switch (in.kind) {
+                case I_BIN:
+                case I_CMP:
+                case I_STORE:
+                    tally(in.a);
+                    tally(in.b);
+                    break;
+                case I_CVT:
+                case I_LOAD: tally(in.a); break;
+                case I_CALL:
+                    for (uint32_t q = 0; q < in.args.n; ++q) tally(in.args[q]);
+                    break;
+                default: break;
+                }
+            }
+            if (b.term.kind == T_CBR) tally(b.term.v);
+        }
+        IdArr<uint8_t> fus;
+        fus.init(tmp, nid(), 0);
+        bool any = false;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind != I_BIN || in.op != BO_MUL) continue;
+                Ty dt = dty(in);
+                if (!ty_is_float(dt)) continue;
+                if (m.opty(in.a) != dt || m.opty(in.b) != dt) continue;
+                if (dc.get(did(in)) != 1 || uc.get(did(in)) != 1) continue;
+                fus.set(did(in), 1);
+                any = true;
+            }
+        }
+        if (!any) return 0;
+        uint32_t fused = 0;
+        IdArr<uint32_t> local;  // mul id -> inst index + 1 (last in block wins)
+        local.init(tmp, nid(), 0);
+        IdArr<uint8_t> fmul;
+        fmul.init(tmp, nid(), 0);
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            Vec<uint32_t> lids;
+            lids.init();
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind == I_BIN && in.op == BO_MUL && fus.get(did(in))) {
+                    local.set(did(in), b.insts[ii] + 1);
+                    lids.push(tmp, did(in));
+                }
+            }
+            if (!lids.n) continue;
+            // ADDs consuming a local mul: position -> mul inst (0 = none)
+            uint32_t *fz = (uint32_t *)tmp.alloc(4ull * (b.insts.n + 1), 16);
+            if (!fz) return fused;
+            bool anyf = false;
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                fz[ii] = 0;
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind != I_BIN || in.op != BO_ADD || !ty_is_float(dty(in))) continue;
+                if (in.a.k == O_VAL && local.get(vid(in.a))) fz[ii] = local.get(vid(in.a)) * 2;
+                else if (in.b.k == O_VAL && local.get(vid(in.b))) fz[ii] = local.get(vid(in.b)) * 2 + 1;
+                if (fz[ii]) anyf = true;
+            }
+            if (anyf) {
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii)
+                    if (fz[ii]) fmul.set(did(I(fz[ii] / 2 - 1)), 1);
+                uint32_t w = 0;
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    uint32_t ix = b.insts[ii];
+                    const Inst &in = I(ix);
+                    if (in.kind == I_BIN && in.op == BO_MUL && fmul.get(did(in))) continue;
+                    if (fz[ii]) {
+                        const Inst &mul = I(fz[ii] / 2 - 1);
+                        Opnd addend = (fz[ii] & 1) ? in.a : in.b;
+                        bool dbl = ty_scalar(dty(in)) == S_DOUBLE;
+                        Inst c = mk_inst(I_CALL, 0, in.dest, onone(), onone());
+                        c.func = S(dbl ? "fma" : "fmaf");
+                        c.args.push(ar, mul.a);
+                        c.args.push(ar, mul.b);
+                        c.args.push(ar, addend);
+                        b.insts[w++] = add_inst(c);
+                        fused++;
+                        continue;
+                    }
+                    b.insts[w++] = ix;
+                }
+                b.insts.n = w;
+            }
+            // local_muls is per block
+            for (uint32_t q = 0; q < lids.n; ++q) local.set(lids[q], 0);
+        }
+        return fused;
+    }
+
+    // ---- unroll (unroll.py) --------------------------------------------------------
+    struct Carried { uint32_t cid; uint32_t cval; Opnd nval; };
+    struct Sec { uint32_t cid; uint32_t cval; pyint init, step; };
+    struct ULoop {
+        uint32_t cond_b, body_b, inc_b, exit_b;
+        uint32_t ind;  // induction value index
+        pyint init, step, trip;
+        Vec<Carried> carried;
+        Vec<Sec> sec;
+    };
+    // int(const.value) for the unroller's bound/init/step reads.  Floats
+    // beyond the kept range saturate (they only ever fail the trip-count
+    // checks); `sat_seen` records it so a loop that would still be unrolled
+    // with such a value is declined.  NaN/inf raise in the reference.
+    bool sat_seen = false;
+    OCB_HD bool opnd_int(Opnd o, pyint &out) {
+        PyVal v = cv(o);
+        if (pv_to_int(v, out)) return true;
+        if (!is_finite(v.f)) {
+            unsup();
+            return false;
+        }
+        out = v.f > 0 ? PYINT_LIM : -PYINT_LIM;
+        sat_seen = true;
+        return true;
+    }
+    // _resolve_const_value (unroll.py:21-45)
+    OCB_HD bool resolve_const_value(uint32_t id, pyint &out) {
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.dest < 0 || did(in) != id) continue;
+                if (in.kind == I_CVT && in.a.k == O_CONST) return opnd_int(in.a, out);
+                if (in.kind == I_BIN && in.op == BO_ADD) {
+                    if (in.b.k == O_CONST && cis(in.b, 0)) {
+                        if (in.a.k == O_CONST) return opnd_int(in.a, out);
+                    } else if (in.a.k == O_CONST && cis(in.a, 0)) {
+                        if (in.b.k == O_CONST) return opnd_int(in.b, out);
+                    }
+                }
+            }
+        }
+        return false;
+    }
+    OCB_HD void carried_put(Vec<Carried> &c, uint32_t cid, uint32_t cval, Opnd nval) {
+        for (uint32_t i = 0; i < c.n; ++i)
+            if (c[i].cid == cid) {
+                c[i].cval = cval;
+                c[i].nval = nval;
+                return;
+            }
+        c.push(tmp, Carried{cid, cval, nval});
+    }
+    OCB_HD bool find_unrollable(Vec<ULoop> &out) {
+        out.init();
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            uint32_t cb = k->blocks[bi];
+            sat_seen = false;
+            if (B(cb).term.kind != T_CBR) continue;
+            int32_t cmpi = -1;
+            for (uint32_t ii = 0; ii < B(cb).insts.n; ++ii)
+                if (I(B(cb).insts[ii]).kind == I_CMP) cmpi = (int32_t)B(cb).insts[ii];
+            if (cmpi < 0) continue;
+            const Inst cmp = I((uint32_t)cmpi);
+            bool have = false;
+            pyint bound = 0;
+            Opnd ind = onone();
+            if (cmp.op == CO_LT && cmp.b.k == O_CONST && cmp.a.k == O_VAL) {
+                if (!opnd_int(cmp.b, bound)) return false;
+                ind = cmp.a;
+                have = true;
+            } else if (cmp.op == CO_LT && cmp.b.k == O_VAL && cmp.a.k == O_VAL) {
+                pyint r;
+                if (resolve_const_value(vid(cmp.b), r)) {
+                    bound = r;
+                    ind = cmp.a;
+                    have = true;
+                }
+                if (bad()) return false;
+            } else if (cmp.op == CO_GT && cmp.a.k == O_CONST && cmp.b.k == O_VAL) {
+                if (!opnd_int(cmp.a, bound)) return false;
+                ind = cmp.b;
+                have = true;
+            } else if (cmp.op == CO_LE && cmp.b.k == O_CONST && cmp.a.k == O_VAL) {
+                if (!opnd_int(cmp.b, bound)) return false;
+                bound += 1;
+                ind = cmp.a;
+                have = true;
+            } else if (cmp.op == CO_LE && cmp.b.k == O_VAL && cmp.a.k == O_VAL) {
+                pyint r;
+                if (resolve_const_value(vid(cmp.b), r)) {
+                    bound = r + 1;
+                    ind = cmp.a;
+                    have = true;
+                }
+                if (bad()) return false;
+            } else if (cmp.op == CO_GE && cmp.a.k == O_CONST && cmp.b.k == O_VAL) {
+                if (!opnd_int(cmp.a, bound)) return false;
+                bound += 1;
+                ind = cmp.b;
+                have = true;
+            }
+            if (!have || ind.k != O_VAL) continue;
+            const Term &ct = B(cb).term;
+            if (!(ct.v.k == O_VAL && vid(ct.v) == did(cmp))) continue;
+            if (bound <= 0 || bound > 64) continue;
+            int32_t body = lm.get(ct.t), ex = lm.get(ct.f);
+            if (body < 0 || ex < 0) continue;
+            if (B((uint32_t)body).term.kind != T_BR) continue;
+            int32_t inc = lm.get(B((uint32_t)body).term.t);
+            if (inc < 0) continue;
+            if (B((uint32_t)inc).term.kind != T_BR) continue;
+            if (!eq(B((uint32_t)inc).term.t, B(cb).label)) continue;
+            ULoop L;
+            L.cond_b = cb;
+            L.body_b = (uint32_t)body;
+            L.inc_b = (uint32_t)inc;
+            L.exit_b = (uint32_t)ex;
+            L.ind = ind.x;
+            L.carried.init();
+            L.sec.init();
+            uint32_t chk[2] = {(uint32_t)body, (uint32_t)inc};
+            for (int q = 0; q < 2; ++q) {
+                Block &b = B(chk[q]);
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    const Inst &in = I(b.insts[ii]);
+                    if (in.kind != I_BIN || in.op != BO_ADD) continue;
+                    if (in.b.k == O_CONST && cis(in.b, 0)) {
+                        if (in.a.k == O_VAL) carried_put(L.carried, did(in), (uint32_t)in.dest, in.a);
+                    } else if (in.a.k == O_CONST && cis(in.a, 0)) {
+                        if (in.b.k == O_VAL) carried_put(L.carried, did(in), (uint32_t)in.dest, in.b);
+                    }
+                }
+            }
+            Str ll[3] = {B(cb).label, B((uint32_t)body).label, B((uint32_t)inc).label};
+            auto in_loop = [&](Str l) { return eq(l, ll[0]) || eq(l, ll[1]) || eq(l, ll[2]); };
+            uint32_t ind_id = vid(ind);
+            pyint init = 0;
+            for (uint32_t sb = 0; sb < k->blocks.n; ++sb) {
+                Block &b = B(k->blocks[sb]);
+                if (in_loop(b.label)) continue;
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                    const Inst &in = I(b.insts[ii]);
+                    if (in.kind != I_BIN || in.op != BO_ADD || did(in) != ind_id) continue;
+                    pyint z;
+                    if (in.b.k == O_CONST) {
+                        if (!opnd_int(in.b, z)) return false;
+                        if (z == 0) {
+                            if (in.a.k == O_CONST && !opnd_int(in.a, init)) return false;
+                            continue;
+                        }
+                    }
+                    if (in.b.k != O_CONST || z != 0) {
+                        if (in.a.k == O_CONST) {
+                            if (!opnd_int(in.a, z)) return false;
+                            if (z == 0 && in.b.k == O_CONST && !opnd_int(in.b, init)) return false;
+                        }
+                    }
+                }
+            }
+            pyint step = 1;
+            Block &ib = B((uint32_t)inc);
+            for (uint32_t ii = 0; ii < ib.insts.n; ++ii) {
+                const Inst &in = I(ib.insts[ii]);
+                if (in.kind != I_BIN || in.op != BO_ADD) continue;
+                pyint s;
+                if (in.a.k == O_VAL && vid(in.a) == ind_id && in.b.k == O_CONST) {
+                    if (!opnd_int(in.b, s)) return false;
+                    if (s > 0) step = s;
+                } else if (in.b.k == O_VAL && vid(in.b) == ind_id && in.a.k == O_CONST) {
+                    if (!opnd_int(in.a, s)) return false;
+                    if (s > 0) step = s;
+                }
+            }
+            pyint span = bound - init;
+            if (span <= 0) continue;
+            if (span % step != 0) continue;
+            pyint trip = span / step;
+            if (trip > 64) continue;
+            // secondary induction variables
+            for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
+                const Carried &c = L.carried[ci];
+                if (c.cid == ind_id) continue;
+                if (c.nval.k != O_VAL) continue;
+                int32_t di = -1;
+                for (uint32_t ii = 0; ii < ib.insts.n; ++ii) {
+                    const Inst &in = I(ib.insts[ii]);
+                    if (in.dest >= 0 && did(in) == vid(c.nval)) di = (int32_t)ib.insts[ii];
+                }
+                if (di < 0 || I((uint32_t)di).kind != I_BIN) continue;
+                const Inst &dfi = I((uint32_t)di);
+                if (dfi.op != BO_ADD && dfi.op != BO_SUB) continue;
+                pyint sstep;
+                if (dfi.a.k == O_VAL && vid(dfi.a) == c.cid && dfi.b.k == O_CONST) {
+                    pyint raw;
+                    if (!opnd_int(dfi.b, raw)) return false;
+                    sstep = dfi.op == BO_SUB ? -raw : raw;
+                } else if (dfi.op == BO_ADD && dfi.b.k == O_VAL && vid(dfi.b) == c.cid &&
+                           dfi.a.k == O_CONST) {
+                    if (!opnd_int(dfi.a, sstep)) return false;
+                } else {
+                    continue;
+                }
+                bool have_init = false;
+                pyint sinit = 0;
+                for (uint32_t sb = 0; sb < k->blocks.n; ++sb) {
+                    Block &b = B(k->blocks[sb]);
+                    if (in_loop(b.label)) continue;
+                    for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                        const Inst &in = I(b.insts[ii]);
+                        if (in.kind != I_BIN || in.op != BO_ADD || did(in) != c.cid) continue;
+                        pyint z;
+                        if (in.b.k == O_CONST) {
+                            if (!opnd_int(in.b, z)) return false;
+                            if (z == 0) {
+                                if (in.a.k == O_CONST) {
+                                    if (!opnd_int(in.a, sinit)) return false;
+                                    have_init = true;
+                                }
+                                continue;
+                            }
+                        }
+                        if (in.a.k == O_CONST) {
+                            if (!opnd_int(in.a, z)) return false;
+                            if (z == 0 && in.b.k == O_CONST) {
+                                if (!opnd_int(in.b, sinit)) return false;
+                                have_init = true;
+                            }
+                        }
+                    }
+                }
+                if (have_init) {
+                    bool found = false;
+                    for (uint32_t q = 0; q < L.sec.n; ++q)
+                        if (L.sec[q].cid == c.cid) {
+                            L.sec[q] = Sec{c.cid, c.cval, sinit, sstep};
+                            found = true;
+                        }
+                    if (!found) L.sec.push(tmp, Sec{c.cid, c.cval, sinit, sstep});
+                }
+            }
+            L.init = init;
+            L.step = step;
+            L.trip = trip;
+            if (sat_seen) {  // a saturated value reached an unrolled loop
+                unsup();
+                return false;
+            }
+            out.push(tmp, L);
+        }
+        return !bad();
+    }
+
+    OCB_HD uint32_t unroll_loops(uint32_t max_unroll) {
+        Vec<ULoop> loops;
+        if (!find_unrollable(loops)) return 0;
+        uint32_t count = 0;
+        for (uint32_t li = 0; li < loops.n && !bad(); ++li) {
+            ULoop &L = loops[li];
+            if (L.trip > (pyint)max_unroll) continue;
+            // id-indexed remap: stamp per iteration
+            uint32_t cap = nid() + (uint32_t)L.trip * (B(L.body_b).insts.n + 2) + 8;
+            IdArr<uint32_t> st;
+            st.init(tmp, cap, 0xFFFFFFFFu);
+            Opnd *rm = (Opnd *)tmp.alloc(sizeof(Opnd) * (uint64_t)cap, 16);
+            IdArr<uint32_t> cst;  // carried_remap: id -> value index + 1
+            cst.init(tmp, cap, 0);
+            if (!rm || bad()) return count;
+            Vec<uint32_t> all;
+            all.init();
+            Ty ind_ty = m.vals[L.ind].ty;
+            uint32_t ind_id = m.vals[L.ind].id;
+            for (pyint it = 0; it < L.trip; ++it) {
+                uint32_t itn = (uint32_t)it;
+                auto rset = [&](uint32_t id, Opnd o) {
+                    if (!st.set(id, itn)) { unsup(); return; }
+                    rm[id] = o;
+                };
+                // remap = dict(carried_remap)
+                for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
+                    uint32_t v = cst.get(L.carried[ci].cid);
+                    if (v) rset(L.carried[ci].cid, ov(v - 1));
+                }
+                rset(ind_id, cint(ind_ty, L.init + L.step * it));
+                for (uint32_t q = 0; q < L.sec.n; ++q)
+                    rset(L.sec[q].cid, cint(m.vals[L.sec[q].cval].ty, L.sec[q].init + L.sec[q].step * it));
+                auto R = [&](Opnd o) -> Opnd {
+                    if (o.k == O_VAL && st.get(vid(o)) == itn) return rm[vid(o)];
+                    return o;
+                };
+                // iter_new_vals: body dest id -> new dest (value index + 1)
+                IdArr<uint32_t> inv_new;
+                inv_new.init(tmp, nid(), 0);
+                Block &bb = B(L.body_b);
+                for (uint32_t ii = 0; ii < bb.insts.n; ++ii) {
+                    const Inst in = I(bb.insts[ii]);
+                    Inst ni = in;
+                    bool has_new_dest = false;
+                    switch (in.kind) {
+                    case I_BIN:
+                    case I_CMP:
+                        ni.a = R(in.a);
+                        ni.b = R(in.b);
+                        has_new_dest = true;
+                        break;
+                    case I_LOAD:
+                    case I_CVT:
+                        ni.a = R(in.a);
+                        has_new_dest = true;
+                        break;
+                    case I_STORE:
+                        ni.a = R(in.a);
+                        ni.b = R(in.b);
+                        break;
+                    case I_CALL:
+                        if (eq(in.func, "__syncthreads")) break;
+                        ni.args = in.args.copy(ar);
+                        for (uint32_t q = 0; q < ni.args.n; ++q) ni.args[q] = R(ni.args[q]);
+                        has_new_dest = in.dest >= 0;
+                        break;
+                    default: break;
+                    }
+                    if (has_new_dest) {
+                        const Value &ov_ = m.vals[(uint32_t)in.dest];
+                        Str nm = cat(ar, ov_.name, S("_u"), utoa(ar, itn));
+                        uint32_t nd = new_value(nm, ov_.ty);
+                        ni.dest = (int32_t)nd;
+                        rset(ov_.id, ov(nd));
+                        if (!inv_new.set(ov_.id, nd + 1)) { unsup(); return count; }
+                    }
+                    all.push(ar, add_inst(ni));
+                }
+                for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
+                    uint32_t v = inv_new.get(L.carried[ci].cid);
+                    if (v) cst.set(L.carried[ci].cid, v);
+                }
+                if (bad()) return count;
+            }
+            for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
+                uint32_t v = cst.get(L.carried[ci].cid);
+                if (!v) continue;
+                Ty cty = m.vals[L.carried[ci].cval].ty;
+                Opnd z = ty_is_float(cty) ? cflt(cty, 0.0) : cint(cty, 0);
+                all.push(ar, add_inst(mk_inst(I_BIN, BO_ADD, (int32_t)L.carried[ci].cval, ov(v - 1), z)));
+            }
+            B(L.cond_b).insts = all;
+            set_br(L.cond_b, B(L.exit_b).label);
+            Str bl = B(L.body_b).label, il = B(L.inc_b).label;
+            uint32_t w = 0;
+            for (uint32_t j = 0; j < k->blocks.n; ++j) {
+                Str l = B(k->blocks[j]).label;
+                if (!eq(l, bl) && !eq(l, il)) k->blocks[w++] = k->blocks[j];
+            }
+            k->blocks.n = w;
+            count++;
+        }
+        return count;
+    }
+
+    // ---- optimize() schedule (optimize.py:1493-1582) ------------------------------
+#define OCB_PASS(call) (reset_tmp(), (call))
+    OCB_HD void run() {
+        for (int r = 0; r < 8 && !bad(); ++r) {
+            uint32_t n = OCB_PASS(unroll_loops(16));
+            if (n == 0) break;
+            OCB_PASS(constant_fold());
+            OCB_PASS(dead_block_elim());
+            OCB_PASS(dead_inst_elim());
+            OCB_PASS(merge_linear_chains());
+        }
+        OCB_PASS(constant_fold());
+        OCB_PASS(cse());
+        OCB_PASS(dead_block_elim());
+        OCB_PASS(identity_fold());
+        OCB_PASS(constant_fold());
+        OCB_PASS(dead_inst_elim());
+        OCB_PASS(licm());
+        OCB_PASS(fma_fuse());
+        OCB_PASS(cse());
+        OCB_PASS(identity_fold());
+        OCB_PASS(constant_fold());
+        OCB_PASS(dead_inst_elim());
+        OCB_PASS(thread_empty_blocks());
+        OCB_PASS(fold_empty_ret_blocks());
+        for (int r = 0; r < 8 && !bad(); ++r) {
+            uint32_t a = OCB_PASS(dead_block_elim());
+            uint32_t b = OCB_PASS(dead_inst_elim());
+            uint32_t c = OCB_PASS(thread_empty_blocks());
+            if (a == 0 && b == 0 && c == 0) break;
+        }
+        for (int r = 0; r < 8 && !bad(); ++r) {
+            uint32_t n = 0;
+            n += OCB_PASS(unroll_loops(16));
+            n += OCB_PASS(constant_fold());
+            n += OCB_PASS(cse());
+            n += OCB_PASS(identity_fold());
+            n += OCB_PASS(fma_fuse());
+            n += OCB_PASS(dead_inst_elim());
+            n += OCB_PASS(dead_block_elim());
+            n += OCB_PASS(thread_empty_blocks());
+            n += OCB_PASS(fold_empty_ret_blocks());
+            if (n == 0) break;
+            OCB_PASS(merge_linear_chains());
+        }
+        reset_tmp();
+    }
+#undef OCB_PASS
+};
+
+// optimize(module) for the kernels of a TU
+OCB_HD inline void optimize_module(Module &m, Arena &tmp) {
+    Opt o(m, tmp);
+    for (uint32_t ki = 0; ki < m.kernels.n && !o.bad(); ++ki) {
+        o.k = &m.kernels[ki];
+        o.run();
+    }
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -367,51 +367,37 @@ struct Parser {
             unsup();
             return false;
         }
-        int64_t x = a.i, y = b.i, res = 0;
-        bool ovf = false;
+        pyint x = a.i, y = b.i, res = 0;
+        bool ok = true;
         switch (op) {
-        case BO_ADD: ovf = add_ovf_(x, y, res, 0); break;
-        case BO_SUB: ovf = add_ovf_(x, -y, res, y == INT64_MIN); break;
-        case BO_MUL: ovf = mul_ovf_(x, y, res); break;
-        case BO_DIV: {
+        case BO_ADD: res = x + y; break;
+        case BO_SUB: res = x - y; break;
+        case BO_MUL: ok = py_mul(x, y, res); break;
+        case BO_DIV: {  // C truncation toward zero; x / 0 folds to 0
             if (y == 0) { res = 0; break; }
-            if (x == INT64_MIN || y == INT64_MIN) { ovf = true; break; }
-            int64_t q = (x < 0 ? -x : x) / (y < 0 ? -y : y);
+            pyint q = py_abs(x) / py_abs(y);
             res = ((x >= 0) == (y >= 0)) ? q : -q;
             break;
         }
         case BO_MOD: {
             if (y == 0) { res = 0; break; }
-            if (x == INT64_MIN || y == INT64_MIN) { ovf = true; break; }
-            int64_t ax = x < 0 ? -x : x, ay = y < 0 ? -y : y;
+            pyint ax = py_abs(x), ay = py_abs(y);
             res = (ax - (ax / ay) * ay) * (x >= 0 ? 1 : -1);
             break;
         }
         case BO_OR: res = x | y; break;
         case BO_AND: res = x & y; break;
         case BO_XOR: res = x ^ y; break;
-        case BO_SHL: {
-            int s = (int)(y & 63);
-            if (s >= 63 || (x > 0 ? x > (INT64_MAX >> s) : x < (INT64_MIN >> s))) {
-                if (x != 0) { ovf = true; break; }
-            }
-            res = (int64_t)((uint64_t)x << s);
-            break;
-        }
-        case BO_SHR: res = x >> (y & 63); break;
+        case BO_SHL: ok = py_shl(x, y & 63, res); break;
+        case BO_SHR: res = py_shr(x, y & 63); break;
         default: return false;
         }
-        if (ovf) {  // a Python int beyond 64 bits
+        if (!ok || !py_ok(res)) {  // a Python int beyond the kept range
             unsup();
             return false;
         }
         out = m.cint(ty, res);
         return true;
-    }
-    OCB_HD static bool add_ovf_(int64_t x, int64_t y, int64_t &r, bool force) {
-        uint64_t u = (uint64_t)x + (uint64_t)y;
-        r = (int64_t)u;
-        return force || (((x >= 0) == (y >= 0)) && ((r >= 0) != (x >= 0)));
     }
     OCB_HD static bool mul_ovf_(int64_t x, int64_t y, int64_t &r) {
         if (x == 0 || y == 0) { r = 0; return false; }
@@ -448,7 +434,9 @@ struct Parser {
         if (iscon(v)) {
             const Const c = m.consts[v.x];
             if (c.pyfloat) { unsup(); return v; }
-            return m.cint(it, c.i * es);
+            pyint r;
+            if (!py_mul(c.i, es, r)) { unsup(); return v; }
+            return m.cint(it, r);
         }
         uint32_t s = new_val("ptr_off", it);
         emit_bin(s, BO_MUL, v, m.cint(it, es));

@@ -868,7 +868,7 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
             --e;
         }
         // int(stripped, 0) with C octal rewritten to 0o...
-        uint64_t val = 0;
+        pyint val = 0;
         uint32_t i = 0, base = 10;
         if (e >= 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'x') { base = 16; i = 2; }
         else if (e >= 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'b') { base = 2; i = 2; }
@@ -882,14 +882,14 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
                 raise_(R_VALUE);
                 return onone();
             }
-            if (val > (0x7FFFFFFFFFFFFFFFull - d) / base) { unsup(); return onone(); }
+            if (val > PYINT_LIM / 16) { unsup(); return onone(); }
             val = val * base + d;
         }
         Ty t;
-        if (has_l || val > 0xFFFFFFFFull) t = has_u ? S_UINT64 : S_INT64;
-        else if (has_u || val > 0x7FFFFFFFull) t = S_UINT32;
+        if (has_l || val > 0xFFFFFFFFll) t = has_u ? S_UINT64 : S_INT64;
+        else if (has_u || val > 0x7FFFFFFFll) t = S_UINT32;
         else t = S_INT32;
-        return m.cint(t, (int64_t)val);
+        return m.cint(t, val);
     }
     if (k == TK_FLOAT_LIT) {
         advance();

@@ -20,11 +20,11 @@ OCB_HD inline bool const_dim(Parser &P, Opnd o, int64_t &out) {
         return true;
     }
     const Const &c = P.m.consts[o.x];
-    if (c.pyfloat) {
+    if (c.pyfloat || c.i > INT64_MAX / 2 || c.i < INT64_MIN / 2) {
         P.unsup();
         return false;
     }
-    out = c.i;
+    out = (int64_t)c.i;
     return true;
 }
 

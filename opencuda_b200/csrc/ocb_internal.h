@@ -103,11 +103,13 @@ int pp_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_
               uint32_t n_tu, uint32_t scale, DevBuf &out_text, uint64_t *d_out_off,
               int32_t *d_status, uint32_t *d_qinc, uint64_t *h_total, cudaStream_t st);
 // Back half on device buffers (cc.cu): lex the preprocessed text of each TU,
-// parse it and write the TU's IR text into `out_text` at d_out_off[n_tu+1].
+// parse (and optimize) it and write the TU's IR text into `out_text` at d_out_off[n_tu+1].
 // d_in_status holds the earlier stages' verdicts; d_status gets the final ones.
+// `stage`: 0 = IR after parse(), 1 = IR after optimize().
 int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d_off,
-              uint32_t n_tu, const int32_t *d_in_status, uint32_t scale, DevBuf &out_text,
-              uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total, cudaStream_t st);
+              uint32_t n_tu, const int32_t *d_in_status, int stage, uint32_t scale,
+              DevBuf &out_text, uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total,
+              cudaStream_t st);
 }  // namespace ocb
 
 #define OCB_TRY(what, expr)                                    \

@@ -16,7 +16,7 @@ RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError"
                 "error": 5}
 
 
-def check_ir(tb, srcs, ref, allow_unsupported=0.0):
+def check_ir(tb, srcs, ref, allow_unsupported=0.0, key="ir"):
     unsup = 0
     for i, (s, r) in enumerate(zip(srcs, ref)):
         st = int(tb.status[i])
@@ -24,11 +24,11 @@ def check_ir(tb, srcs, ref, allow_unsupported=0.0):
             unsup += 1
             continue
         exc = r.get("raises") or (r["error"][0] if "error" in r else None)
-        if exc is not None and "ir" not in r:
+        if exc is not None and key not in r:
             assert st == RAISE_STATUS.get(exc, 6), (i, exc, st, s[:300])
             continue
         assert st == 0, (i, st, s[:300])
-        assert tb.text(i) == r["ir"], (i, s[:300])
+        assert tb.text(i) == r[key], (i, s[:300])
     assert unsup <= allow_unsupported * len(srcs), unsup
 
 
@@ -58,3 +58,28 @@ def test_mutations_against_live_reference(ctx):
     with ref_runner.RefPool() as pool:
         ref = pool.run(srcs, what=("ir",), chunksize=16)
     check_ir(tb, srcs, ref, allow_unsupported=0.02)
+
+
+# ---- optimizer (optimize.py:1443 optimize, unroll.py) -----------------------
+
+def test_golden_optimized_ir(ctx):
+    cases = golden("ir_golden.json.gz")["cases"]
+    srcs = [c["src"] for c in cases]
+    check_ir(ctx.optimize_batch(srcs), srcs, cases, allow_unsupported=0.02, key="opt")
+
+
+@pytest.mark.parametrize("seed", [5, 6])
+def test_optimized_kernels_against_live_reference(ctx, seed):
+    srcs = [synth.SGEMM_SRC] + synth.random_batch(600, seed=seed)
+    tb = ctx.optimize_batch(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=("opt",), chunksize=8)
+    check_ir(tb, srcs, ref, allow_unsupported=0.005, key="opt")
+
+
+def test_optimized_mutations_against_live_reference(ctx):
+    srcs = mutate_sources(1500, 78)
+    tb = ctx.optimize_batch(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=("opt",), chunksize=16)
+    check_ir(tb, srcs, ref, allow_unsupported=0.02, key="opt")
