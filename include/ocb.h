@@ -130,6 +130,18 @@ int  ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
 int  ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
                         uint32_t n_tu, ocb_text **out);
 
+/* ---- compiler ------------------------------------------------------------ */
+/* Compile every TU of a host batch to PTX: preprocess, lex, parse, optimize,
+ * allocate registers and emit.  Replaces the CLI path
+ * `python -m opencuda X.cu --emit-ptx` (opencuda/__main__.py:36-85:
+ * preprocess -> parse -> optimize -> codegen/emit.py:3126 ir_to_ptx -> module
+ * text with `.target sm_120`).  Each TU's text is the whole PTX module the CLI
+ * would write.  Status per TU as for ocb_parse_batch; a TU where the
+ * reference raises during emission (e.g. OverflowError packing a float
+ * literal) reports that exception. */
+int  ocb_compile_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                       uint32_t n_tu, ocb_text **out);
+
 /* Allocation-free form of ocb_lex_device, for callers that may not allocate
  * device memory when they lex (a framework's memory pool or a fixed arena that
  * forbids cudaMalloc/cudaFree after start-up, or a thread that must not take

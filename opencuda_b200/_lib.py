@@ -35,6 +35,7 @@ SIGNATURES = [
     ("ocb_text_free", None, [c_void_p]),
     ("ocb_parse_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_optimize_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
+    ("ocb_compile_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_lex_device_static", c_int, [c_void_p, c_u64, c_void_p, c_u32, c_void_p,
                                       c_void_p, c_void_p, c_u64, c_void_p, c_void_p,
                                       c_void_p, c_void_p, ctypes.c_char_p, ctypes.c_size_t]),

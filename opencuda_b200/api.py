@@ -179,6 +179,11 @@ class Context:
         its optimized IR."""
         return self._text_call("ocb_optimize_batch", srcs, buf, tu_off)
 
+    def compile_batch(self, srcs=None, *, buf=None, tu_off=None) -> TextBatch:
+        """Compile every TU to its PTX module text (the reference CLI's
+        ``--emit-ptx`` output, ``__main__.py:36-85``)."""
+        return self._text_call("ocb_compile_batch", srcs, buf, tu_off)
+
     def _text_call(self, fn, srcs, buf, tu_off) -> TextBatch:
         if srcs is not None:
             buf, tu_off = pack_sources(srcs)
@@ -233,3 +238,7 @@ def parse_batch(srcs, device: int = 0) -> TextBatch:
 
 def optimize_batch(srcs, device: int = 0) -> TextBatch:
     return context(device).optimize_batch(srcs)
+
+
+def compile_batch(srcs, device: int = 0) -> TextBatch:
+    return context(device).compile_batch(srcs)

@@ -23,7 +23,7 @@ BUILD = PKG / "_build"
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",
-    "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-Wno-attributes",
     "--expt-relaxed-constexpr",
 ]
 

@@ -382,6 +382,11 @@ int ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
     return stage_batch(ctx, src, tu_off, n_tu, 1, out);
 }
 
+int ocb_compile_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                      ocb_text **out) {
+    return stage_batch(ctx, src, tu_off, n_tu, 2, out);
+}
+
 int ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,
                   const uint64_t **off, const int32_t **status, const uint32_t **qinclude) {
     if (!t) return -1;

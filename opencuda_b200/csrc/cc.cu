@@ -2,17 +2,16 @@
 // translation unit.  Each TU gets a private slice of one arena buffer sized
 // from its token count; a TU that outgrows it reports OCB_TU_OVERFLOW and the
 // host runs it again with a larger slice.
-#include <new>
 #include <cub/cub.cuh>
 #include "ocb_internal.h"
-#include "cc_parse_stmt.cuh"
-#include "cc_opt.cuh"
-#include "cc_dump.cuh"
+#include "cc_state.cuh"
 
 namespace ocb {
 namespace cc {
 
-enum { CC_STAGE_IR = 0, CC_STAGE_OPT = 1 };
+cudaError_t launch_k_cc_parse(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
+cudaError_t launch_k_cc_opt(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
+cudaError_t launch_k_cc_emit(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
 
 // Per-TU arena and output sizes (bytes, 16-aligned) from the token counts.
 __global__ void k_cc_sizes(const uint64_t *tu_tok_off, uint32_t n_tu, uint32_t scale,
@@ -27,86 +26,6 @@ __global__ void k_cc_sizes(const uint64_t *tu_tok_off, uint32_t n_tu, uint32_t s
     uint64_t nt = tu_tok_off[i + 1] - tu_tok_off[i];
     arena_sz[i] = ((65536ull + 2048ull * nt) * scale + 15) & ~15ull;
     out_sz[i] = ((4096ull + 256ull * nt) * scale + 15) & ~15ull;
-}
-
-struct CCArgs {
-    const uint8_t *src;          // preprocessed text of the batch
-    const uint32_t *tok_start;   // token starts (batch offsets)
-    const uint32_t *tok_kl;      // kind << 24 | length
-    const uint64_t *tu_tok_off;  // n_tu + 1
-    const int32_t *in_status;    // status of the earlier stages (0 = go on)
-    uint32_t n_tu;
-    uint8_t *arena;
-    const uint64_t *arena_off;
-    uint8_t *out;
-    const uint64_t *out_off;     // capacity offsets
-    uint64_t *out_len;           // n_tu + 1 (last = 0)
-    int32_t *status;
-    int stage;                   // CC_STAGE_*
-};
-
-// One thread per TU: parse, then (stage >= CC_STAGE_OPT) optimize, then write
-// the IR text.  The TU's arena slice is split: 3/4 for the IR, 1/4 scratch
-// for the optimizer's per-pass tables.
-__global__ void __launch_bounds__(64) k_cc_compile(CCArgs A) {
-    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i > A.n_tu) return;
-    if (i == A.n_tu) {
-        A.out_len[i] = 0;
-        return;
-    }
-    A.out_len[i] = 0;
-    int32_t st0 = A.in_status[i];
-    if (st0 != 0) {
-        A.status[i] = st0;
-        return;
-    }
-    uint64_t sz = A.arena_off[i + 1] - A.arena_off[i];
-    uint64_t ir_sz = (sz / 4 * 3) & ~15ull;
-    Arena ar{A.arena + A.arena_off[i], 0, ir_sz, false};
-    Arena tmp{A.arena + A.arena_off[i] + ir_sz, 0, sz - ir_sz, false};
-    Module *m = (Module *)ar.alloc(sizeof(Module), 16);
-    Parser *P = (Parser *)ar.alloc(sizeof(Parser), 16);
-    if (!m || !P) {
-        A.status[i] = OCB_TU_OVERFLOW;
-        return;
-    }
-    m->init(&ar);
-    uint64_t t0 = A.tu_tok_off[i];
-    Tokens t{A.src, A.tok_start + t0, A.tok_kl + t0, (uint32_t)(A.tu_tok_off[i + 1] - t0)};
-    new (P) Parser(ar, *m, t);
-    P->parse_module();
-    if (ar.oom) {
-        A.status[i] = OCB_TU_OVERFLOW;
-        return;
-    }
-    if (m->unsup) {
-        A.status[i] = OCB_TU_UNSUPPORTED;
-        return;
-    }
-    if (P->err) {
-        A.status[i] = m->raises;
-        return;
-    }
-    if (A.stage >= CC_STAGE_OPT) {
-        optimize_module(*m, tmp);
-        if (ar.oom || tmp.oom) {
-            A.status[i] = OCB_TU_OVERFLOW;
-            return;
-        }
-        if (m->unsup) {
-            A.status[i] = OCB_TU_UNSUPPORTED;
-            return;
-        }
-    }
-    Out o{(char *)A.out + A.out_off[i], 0, A.out_off[i + 1] - A.out_off[i], false};
-    dump_module(o, *m);
-    if (o.full) {
-        A.status[i] = OCB_TU_OVERFLOW;
-        return;
-    }
-    A.out_len[i] = o.n;
-    A.status[i] = OCB_TU_OK;
 }
 
 __global__ void merge_status(int32_t *st, const int32_t *lex_st, uint32_t n_tu) {
@@ -182,10 +101,12 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     size_t cur_stack = 0;
     OCB_TRY("cc: stack limit", cudaDeviceGetLimit(&cur_stack, cudaLimitStackSize));
     if (cur_stack < kCCStack) OCB_TRY("cc: stack limit", cudaDeviceSetLimit(cudaLimitStackSize, kCCStack));
-    CCArgs A{d_text, tstart, tkl, tu_tok, d_status, n_tu, ctx->cc_arena.as<uint8_t>(), arena_off,
+    CCArgs A{d_text, tstart, tkl, tu_tok, n_tu, ctx->cc_arena.as<uint8_t>(), arena_off,
              ctx->cc_out.as<uint8_t>(), out_cap_off, out_len, d_status, stage};
-    k_cc_compile<<<(unsigned)((n1 + 63) / 64), 64, 0, st>>>(A);
-    OCB_TRY("cc: parse launch", cudaGetLastError());
+    unsigned g64 = (unsigned)((n1 + 63) / 64);
+    OCB_TRY("cc: parse launch", launch_k_cc_parse(A, g64, 64, st));
+    if (stage >= CC_STAGE_OPT) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, g64, 64, st));
+    OCB_TRY("cc: emit launch", launch_k_cc_emit(A, g64, 64, st));
     OCB_TRY("cc: pack scan",
             cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, out_len, d_out_off, (int)n1, st));
     uint64_t total = 0;

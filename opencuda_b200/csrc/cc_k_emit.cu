@@ -1,0 +1,43 @@
+// Compiler kernel 3 of 3: write each TU's output text -- the PTX module
+// (stage PTX) or the IR in canonical text (stages IR / OPT).
+#include <cuda_runtime.h>
+#include "../../include/ocb.h"
+#include "cc_state.cuh"
+#include "cc_emit_kernel.cuh"
+#include "cc_dump.cuh"
+
+namespace ocb {
+namespace cc {
+
+__global__ void __launch_bounds__(64) k_cc_emit(CCArgs A) {
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i > A.n_tu) return;
+    A.out_len[i] = 0;
+    if (i == A.n_tu || A.status[i] != 0) return;
+    TUState *S = tu_state(A, i);
+    Module &m = S->m;
+    m.ar = &S->ar;
+    Out o{(char *)A.out + A.out_off[i], 0, A.out_off[i + 1] - A.out_off[i], false};
+    int32_t st = OCB_TU_OK;
+    if (A.stage >= CC_STAGE_PTX) {
+        S->tmp.used = 0;
+        bool ok = emit_module(m, S->tmp, o, "sm_120");
+        if (S->ar.oom || S->tmp.oom || o.full) st = OCB_TU_OVERFLOW;
+        else if (m.unsup || (!ok && !m.raises)) st = OCB_TU_UNSUPPORTED;
+        else if (!ok) st = m.raises;
+    } else {
+        dump_module(o, m);
+        if (o.full) st = OCB_TU_OVERFLOW;
+    }
+    A.status[i] = st;
+    if (st == OCB_TU_OK) A.out_len[i] = o.n;
+}
+
+// host-side launcher (kernels of separate objects are launched from here)
+cudaError_t launch_k_cc_emit(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st) {
+    k_cc_emit<<<grid, block, 0, st>>>(A);
+    return cudaGetLastError();
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -1,0 +1,32 @@
+// Compiler kernel 2 of 3: optimize each TU's IR in place (one thread per TU).
+#include <cuda_runtime.h>
+#include "../../include/ocb.h"
+#include "cc_state.cuh"
+#include "cc_opt.cuh"
+
+namespace ocb {
+namespace cc {
+
+__global__ void __launch_bounds__(64) k_cc_opt(CCArgs A) {
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= A.n_tu) return;
+    TUState *S = tu_state(A, i);
+    if (A.status[i] != 0) return;
+    S->m.ar = &S->ar;
+    S->tmp.used = 0;
+    optimize_module(S->m, S->tmp);
+    int32_t st = 0;
+    if (S->ar.oom || S->tmp.oom) st = OCB_TU_OVERFLOW;
+    else if (S->m.unsup) st = OCB_TU_UNSUPPORTED;
+    S->status = st;
+    A.status[i] = st;
+}
+
+// host-side launcher (kernels of separate objects are launched from here)
+cudaError_t launch_k_cc_opt(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st) {
+    k_cc_opt<<<grid, block, 0, st>>>(A);
+    return cudaGetLastError();
+}
+
+}  // namespace cc
+}  // namespace ocb

@@ -117,22 +117,6 @@ struct VarMap {
     }
 };
 
-// A set of names (the reference's per-block scope sets); order irrelevant.
-struct NameSet {
-    Vec<Str> v;
-    OCB_HD void init() { v.init(); }
-    OCB_HD void add(Arena &a, Str s) {
-        for (uint32_t i = 0; i < v.n; ++i)
-            if (eq(v.p[i], s)) return;
-        v.push(a, s);
-    }
-    OCB_HD bool has(Str s) const {
-        for (uint32_t i = 0; i < v.n; ++i)
-            if (eq(v.p[i], s)) return true;
-        return false;
-    }
-};
-
 struct Tokens {
     const uint8_t *src;        // batch bytes (token starts are batch offsets)
     const uint32_t *start;     // this TU's tokens

@@ -37,74 +37,6 @@ OCB_HD inline bool vector_type_name(Str v) {
 }
 
 
-// --- intrinsic name tables of _parse_primary_expr (parser.py:1929-2033) ---
-// Each list is one space-delimited string, so it lives in code on host and device.
-OCB_HD inline bool in_list(Str n, const char *l) {
-    for (uint32_t i = 0; l[i]; ++i) {
-        if (l[i] != ' ') continue;
-        uint32_t j = 0;
-        while (j < n.n && l[i + 1 + j] == n.p[j]) ++j;
-        if (j == n.n && n.n && l[i + 1 + j] == ' ') return true;
-    }
-    return false;
-}
-OCB_HD inline bool contains(Str s, const char *sub) {
-    uint32_t k = cstrlen(sub);
-    for (uint32_t i = 0; i + k <= s.n; ++i) {
-        uint32_t j = 0;
-        while (j < k && s.p[i + j] == sub[j]) ++j;
-        if (j == k) return true;
-    }
-    return false;
-}
-#define kTexFetch " tex1Dfetch tex2D tex3D "
-#define kSurfVoid " surf1Dwrite "
-#define kVoidStmts " __threadfence __threadfence_block __threadfence_system __nanosleep __trap __brkpt "
-#define kSyncReduce " __syncthreads_count __syncthreads_and __syncthreads_or "
-#define kIntOps " __popc __popcll __clz __clzll __brev __brevll __ffs __ffsll "
-#define kPredInt " isnan isinf isfinite __isnan __isinf __isfinite __isnanf __isinff __isfinitef "
-#define kFloat2Int                                                                          \
-    " __float2int_rn __float2int_rd __float2int_ru __float2int_rz __float2uint_rn"          \
-    " __float2uint_rd __float2uint_ru __float2uint_rz __float2ll_rn __float2ll_rd"          \
-    " __float2ll_ru __float2ll_rz __float2ull_rn __float2ull_rd __float2ull_ru"             \
-    " __float2ull_rz __double2int_rn __double2int_rz __double2uint_rn __double2uint_rz"     \
-    " __double2ll_rn __double2ll_rz __double2ull_rn __double2ull_rz __float_as_int"         \
-    " __float_as_uint __double_as_longlong __double_as_ulonglong "
-#define kInt2Float                                                                          \
-    " __int2float_rn __int2float_rd __int2float_ru __int2float_rz __uint2float_rn"          \
-    " __uint2float_rd __uint2float_ru __uint2float_rz __ll2float_rn __ll2float_rz"          \
-    " __ull2float_rn __ull2float_rz __int2double_rn __ll2double_rn __uint2double_rn"        \
-    " __ull2double_rn __int_as_float __uint_as_float __longlong_as_double"                  \
-    " __ulonglong_as_double "
-#define kWarpReduceInt " __reduce_add_sync __reduce_min_sync __reduce_max_sync "
-#define kWarpReduceUint " __reduce_and_sync __reduce_or_sync __reduce_xor_sync __reduce_umin_sync __reduce_umax_sync "
-#define kIntBinary2 " __mul24 __mulhi "
-#define kUintBinary2 " __umul24 __umulhi __rhadd __byte_perm __funnelshift_l __funnelshift_r __funnelshift_lc __funnelshift_rc "
-#define kHalfUnary                                                                          \
-    " __habs __hneg __hsqrt __hrcp __hrsqrt __hexp __hlog __hceil __hfloor __hrint"         \
-    " __htrunc __hcos __hsin __hexp2 __hlog2 __hlog10 __half2float __low2float"             \
-    " __high2float "
-#define kHalfBinary " __hmul __hmul_rn __hmul_sat __hadd_rn __hsub __hsub_rn __hdiv __hfmin __hfmax __hmin __hmax "
-#define kHalfTernary " __hfma __hfma_sat __hfma_relu "
-#define kHalfCmpInt " __hgt __hlt __hge __hle __heq __hne __hisnan __hisinf "
-#define kHalfCvt                                                                            \
-    " __float2half __float2half_rn __float2half_rd __float2half_ru __float2half_rz"         \
-    " __int2half_rn __int2half_rd __int2half_ru __int2half_rz __uint2half_rn"               \
-    " __uint2half_rd __uint2half_ru __uint2half_rz __short2half_rn __ushort2half_rn"        \
-    " __ll2half_rn __ll2half_rz __ull2half_rn __ull2half_rz __ushort_as_half"               \
-    " __short_as_half "
-#define kHalf2Int                                                                           \
-    " __half2int_rn __half2int_rz __half2uint_rn __half2uint_rz __half2short_rn"            \
-    " __half2short_rz __half2ushort_rn __half2ushort_rz __half2ll_rn __half2ll_rz"          \
-    " __half2ull_rn __half2ull_rz "
-#define kFloatUnary                                                                         \
-    " sqrtf rsqrtf rcpf fabsf sinf cosf tanf expf exp2f exp10f logf log2f log10f"           \
-    " floorf ceilf roundf truncf atanf asinf acosf sqrt rsqrt fabs sin cos exp exp2"        \
-    " exp10 log log2 log10 floor ceil round trunc atan asin acos __fsqrt_rn __fsqrt_rd"     \
-    " __fsqrt_ru __fsqrt_rz __frcp_rn __frcp_rd __frcp_ru __frcp_rz __frsqrt_rn "
-#define kFloatBinary " fminf fmaxf fmodf powf fmin fmax fmod pow hypotf atan2f "
-#define kFloatTernary " fmaf fma __fmaf_rn __fmaf_rd __fmaf_ru __fmaf_rz __fma_rn __fma_rd __fma_ru __fma_rz "
-
 // _parse_type (parser.py:368-472)
 OCB_HD inline bool Parser::parse_type(Ty &out) {
     while (peek() == TK_VOLATILE || peek() == TK_CONST) advance();

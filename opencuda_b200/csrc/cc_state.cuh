@@ -1,0 +1,38 @@
+// Per-TU state kept at the start of the TU's arena slice between the
+// compiler's kernels (parse -> optimize -> emit): the two arenas and the IR.
+#pragma once
+#include "cc_ir.cuh"
+
+namespace ocb {
+namespace cc {
+
+enum { CC_STAGE_IR = 0, CC_STAGE_OPT = 1, CC_STAGE_PTX = 2 };
+
+struct TUState {
+    Arena ar;    // the IR (3/4 of the slice after this header)
+    Arena tmp;   // per-pass scratch (1/4)
+    Module m;
+    int32_t status;  // OCB_TU_* (0 = carry on)
+};
+
+struct CCArgs {
+    const uint8_t *src;          // preprocessed text of the batch
+    const uint32_t *tok_start;   // token starts (batch offsets)
+    const uint32_t *tok_kl;      // kind << 24 | length
+    const uint64_t *tu_tok_off;  // n_tu + 1
+    uint32_t n_tu;
+    uint8_t *arena;
+    const uint64_t *arena_off;
+    uint8_t *out;
+    const uint64_t *out_off;     // capacity offsets
+    uint64_t *out_len;           // n_tu + 1 (last = 0)
+    int32_t *status;             // in: earlier stages' verdicts; out: final
+    int stage;
+};
+
+OCB_HD inline TUState *tu_state(const CCArgs &A, uint32_t i) {
+    return (TUState *)(A.arena + A.arena_off[i]);
+}
+
+}  // namespace cc
+}  // namespace ocb
