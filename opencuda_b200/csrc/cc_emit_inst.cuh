@@ -1005,7 +1005,7 @@ OCB_HD inline void Emit::emit_term(const Term &t) {
                 Block &M = B((uint32_t)mb);
                 for (uint32_t q = 0; q < M.insts.n && !bad(); ++q) emit_inst(M.insts[q]);
                 if (M.term.kind != T_NONE) {
-                    if (++term_depth > 64) { unsup(); return; }
+                    if (++term_depth > 24) { unsup(); return; }
                     emit_term(M.term);
                     --term_depth;
                 }
@@ -1054,12 +1054,12 @@ OCB_HD inline void Emit::emit_term(const Term &t) {
                             skip.add(ml);
                             put("    ret;");
                         } else {
-                            if (++term_depth > 64) { unsup(); return; }
+                            if (++term_depth > 24) { unsup(); return; }
                             emit_term(T.term);
                             --term_depth;
                         }
                     } else if (T.term.kind != T_NONE) {
-                        if (++term_depth > 64) { unsup(); return; }
+                        if (++term_depth > 24) { unsup(); return; }
                         emit_term(T.term);
                         --term_depth;
                     }

@@ -387,10 +387,18 @@ struct Module {
         kernels.init();
         unsup = false;
         raises = 0;
+        // Reserved up front so the tables are never empty-and-unallocated: a
+        // push that fails later (arena exhausted, TU reported as OVERFLOW)
+        // then returns an existing index instead of one past an empty table.
+        vals.reserve(*a, 64);
+        consts.reserve(*a, 64);
+        insts.reserve(*a, 64);
+        blocks.reserve(*a, 16);
+        kernels.reserve(*a, 4);
     }
     OCB_HD uint32_t add_val(uint32_t id, Ty ty, Str name) {
-        vals.push(*ar, Value{id, ty, name});
-        return vals.n - 1;
+        if (!vals.push(*ar, Value{id, ty, name}) && vals.n == 0) return 0;
+        return vals.n ? vals.n - 1 : 0;
     }
     OCB_HD Opnd cint(Ty ty, pyint v) {
         Const c{ty, 0, v, 0.0};

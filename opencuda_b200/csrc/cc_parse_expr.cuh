@@ -178,6 +178,7 @@ OCB_HD inline Opnd Parser::parse_assign_expr() {
         if (bad()) goto out;
         Ty rt = result_type(tv, fv);
         uint32_t dest = new_val("ternary", rt);
+        if (bad()) goto out;  // outside a kernel: AttributeError in new_value
         uint32_t tb = new_block("tern_true"), fb = new_block("tern_false"),
                  mb = new_block("tern_merge");
         B().term = Term{T_CBR, lhs, m.blocks[tb].label, m.blocks[fb].label};
@@ -265,6 +266,7 @@ OCB_HD inline Opnd Parser::parse_or_expr() {
     Opnd lhs = parse_and_expr();
     while (!bad() && match(TK_OR)) {
         uint32_t dest = new_val("lor", S_INT32);
+        if (bad()) return lhs;  // outside a kernel: AttributeError in new_value
         uint32_t rb = new_block("lor_rhs"), sb = new_block("lor_skip"), mb = new_block("lor_merge");
         B().term = Term{T_CBR, lhs, m.blocks[sb].label, m.blocks[rb].label};
         VarMap before = vars.copy(ar);
@@ -298,6 +300,7 @@ OCB_HD inline Opnd Parser::parse_and_expr() {
     Opnd lhs = parse_bitor_expr();
     while (!bad() && match(TK_AND)) {
         uint32_t dest = new_val("land", S_INT32);
+        if (bad()) return lhs;  // outside a kernel: AttributeError in new_value
         uint32_t rb = new_block("land_rhs"), sb = new_block("land_skip"), mb = new_block("land_merge");
         B().term = Term{T_CBR, lhs, m.blocks[rb].label, m.blocks[sb].label};
         VarMap before = vars.copy(ar);

@@ -858,7 +858,7 @@ OCB_HD inline void Parser::parse_kernel() {
     kk.shared.init();
     kk.locals.init();
     kk.has_locals = false;
-    m.kernels.push(ar, kk);
+    if (!m.kernels.push(ar, kk)) return;  // arena exhausted
     kern = &m.kernels.back();
     kidx = m.kernels.n - 1;
     vars.init();
@@ -896,6 +896,10 @@ OCB_HD inline void Parser::parse_kernel() {
 // parse_module (parser.py:4194-4437): pass 1 registers module-level names and
 // records kernel positions; pass 2 parses the kernels in order.
 OCB_HD inline void Parser::parse_module() {
+    if (bad() || !m.vals.cap || !m.blocks.cap || !m.insts.cap || !m.consts.cap) {
+        ar.oom = true;
+        return;
+    }
     Vec<uint32_t> kpos;
     kpos.init();
     while (!bad() && !at(TK_EOF)) {
