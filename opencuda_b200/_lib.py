@@ -8,7 +8,11 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libocb.so"
+import os
+
+# OCB_LIBRARY selects another build of the same C ABI (e.g. a register-capped
+# variant for tuning); the default is the in-tree libocb.so.
+LIB_PATH = Path(os.environ.get("OCB_LIBRARY") or (Path(__file__).resolve().parent / "libocb.so"))
 
 c_void_p = ctypes.c_void_p
 c_u32 = ctypes.c_uint32

@@ -1,8 +1,26 @@
 // C ABI entry points (include/ocb.h): contexts, host-buffer wrappers around
 // the device pipelines, result objects.
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include "ocb_internal.h"
+
+PhaseTimer::PhaseTimer(cudaStream_t s) : st(s) {
+    const char *v = getenv("OCB_TIMING");
+    on = v && *v && *v != '0';
+    t0 = 0;
+    if (on) mark(nullptr);
+}
+void PhaseTimer::mark(const char *what) {
+    if (!on) return;
+    cudaStreamSynchronize(st);
+    double t = std::chrono::duration<double, std::milli>(
+                   std::chrono::steady_clock::now().time_since_epoch()).count();
+    if (what) fprintf(stderr, "[ocb] %-22s %9.2f ms\n", what, t - t0);
+    t0 = t;
+}
 
 namespace ocb {
 
@@ -299,6 +317,7 @@ static int compile_text(ocb_ctx *ctx, const ocb_text &pp, int stage, ocb_text *o
     std::vector<uint32_t> todo(n_tu);
     for (uint32_t i = 0; i < n_tu; ++i) todo[i] = i;
     std::vector<std::vector<uint8_t>> res(n_tu);
+    PhaseTimer T(st);
     for (uint32_t scale = 1; !todo.empty(); scale *= 8) {
         // sub-batch of the pending TUs
         std::vector<uint64_t> off(todo.size() + 1, 0);
@@ -320,6 +339,7 @@ static int compile_text(ocb_ctx *ctx, const ocb_text &pp, int stage, ocb_text *o
         OCB_TRY("h2d status", cudaMemcpyAsync(ctx->cc_in_status.p, in_st.data(), 4 * nt,
                                               cudaMemcpyHostToDevice, st));
         uint64_t total = 0;
+        T.mark(scale == 1 ? "cc: upload" : "cc: upload (retry)");
         rc = cc_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(),
                        (uint32_t)nt, ctx->cc_in_status.as<int32_t>(), stage, scale, ctx->cc_text,
                        ctx->cc_off.as<uint64_t>(), ctx->cc_status.as<int32_t>(), &total, st);
@@ -333,6 +353,7 @@ static int compile_text(ocb_ctx *ctx, const ocb_text &pp, int stage, ocb_text *o
         if (!e) e = cudaMemcpyAsync(s.data(), ctx->cc_status.p, 4 * nt, cudaMemcpyDeviceToHost, st);
         if (!e) e = cudaStreamSynchronize(st);
         if (e) return fail(ctx, "d2h compile output", e);
+        T.mark("cc: download");
         std::vector<uint32_t> next;
         for (size_t k = 0; k < nt; ++k) {
             uint32_t i = todo[k];
@@ -355,8 +376,10 @@ static int stage_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
     if (!ctx || !out || !tu_off) return fail(ctx, "null argument");
     *out = nullptr;
     ocb_text *pp = nullptr;
+    PhaseTimer T(ctx->stream);
     int rc = ocb_preprocess_batch(ctx, src, tu_off, n_tu, &pp);
     if (rc) return rc;
+    T.mark("preprocess (host api)");
     ocb_text *t = new (std::nothrow) ocb_text();
     if (!t) {
         delete pp;

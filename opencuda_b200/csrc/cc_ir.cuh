@@ -66,7 +66,10 @@ OCB_HD inline bool py_shl(pyint a, pyint s, pyint &r) {
 // a >> s for s >= 0 (floor semantics, like Python)
 OCB_HD inline pyint py_shr(pyint a, pyint s) {
     if (s >= 127) return a < 0 ? -1 : 0;
-    return a >> (int)s;
+    int k = (int)s;
+    // written with unsigned shifts: floor(a / 2^k) for both signs
+    if (a >= 0) return (pyint)((unsigned __int128)a >> k);
+    return ~(pyint)((unsigned __int128)~a >> k);
 }
 
 // ---------------------------------------------------------------------------
@@ -83,8 +86,14 @@ struct Arena {
             return nullptr;
         }
         used = a + n;
+#ifdef OCB_ARENA_PEAK
+        if (used > peak) peak = used;
+#endif
         return base + a;
     }
+#ifdef OCB_ARENA_PEAK
+    uint64_t peak = 0;
+#endif
 };
 
 template <class T>

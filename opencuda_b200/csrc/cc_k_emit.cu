@@ -9,11 +9,11 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(64) k_cc_emit(CCArgs A) {
-    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i > A.n_tu) return;
+__global__ void __launch_bounds__(128) k_cc_emit(CCArgs A) {
+    uint32_t i = cc_tu_index(A);
+    if (i >= A.n_tu) return;
     A.out_len[i] = 0;
-    if (i == A.n_tu || A.status[i] != 0) return;
+    if (A.status[i] != 0) return;
     TUState *S = tu_state(A, i);
     Module &m = S->m;
     m.ar = &S->ar;
@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(64) k_cc_emit(CCArgs A) {
     }
     A.status[i] = st;
     if (st == OCB_TU_OK) A.out_len[i] = o.n;
+    if (A.peak) A.peak[i] = S->ar.used;
 }
 
 // host-side launcher (kernels of separate objects are launched from here)

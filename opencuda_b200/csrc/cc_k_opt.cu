@@ -7,8 +7,8 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(64) k_cc_opt(CCArgs A) {
-    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(128) k_cc_opt(CCArgs A) {
+    uint32_t i = cc_tu_index(A);
     if (i >= A.n_tu) return;
     TUState *S = tu_state(A, i);
     if (A.status[i] != 0) return;

@@ -8,8 +8,8 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(64) k_cc_parse(CCArgs A) {
-    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(128) k_cc_parse(CCArgs A) {
+    uint32_t i = cc_tu_index(A);
     if (i >= A.n_tu) return;
     uint64_t sz = A.arena_off[i + 1] - A.arena_off[i];
     TUState *S = tu_state(A, i);
@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(64) k_cc_parse(CCArgs A) {
     if (S->status != 0) return;
     uint8_t *base = A.arena + A.arena_off[i] + ((sizeof(TUState) + 15) & ~(size_t)15);
     uint64_t rest = sz - ((sizeof(TUState) + 15) & ~(size_t)15);
-    uint64_t ir_sz = (rest / 4 * 3) & ~15ull;
+    uint64_t ir_sz = (rest / 1000 * A.ir_permille) & ~15ull;
     S->ar = Arena{base, 0, ir_sz, false};
     S->tmp = Arena{base + ir_sz, 0, rest - ir_sz, false};
     S->m.init(&S->ar);

@@ -2061,6 +2061,13 @@ struct Opt {
             uint32_t c = OCB_PASS(thread_empty_blocks());
             if (a == 0 && b == 0 && c == 0) break;
         }
+        // The reference runs this loop until a round reports no change; the
+        // counts include no-op refolds of `add c, 0`, so it usually runs all 8
+        // rounds.  Every pass is a function of the IR's content (and the next
+        // value id), so a round that leaves the content unchanged is a fixed
+        // point: the remaining rounds cannot change anything and are skipped.
+        uint64_t fp_prev[2] = {0, 0};
+        bool have_fp = false;
         for (int r = 0; r < 8 && !bad(); ++r) {
             uint32_t n = 0;
             n += OCB_PASS(unroll_loops(16));
@@ -2074,8 +2081,77 @@ struct Opt {
             n += OCB_PASS(fold_empty_ret_blocks());
             if (n == 0) break;
             OCB_PASS(merge_linear_chains());
+            uint64_t fp[2];
+            fingerprint(fp);
+            if (have_fp && fp[0] == fp_prev[0] && fp[1] == fp_prev[1] && !getenv("NOFP")) break;
+            fp_prev[0] = fp[0];
+            fp_prev[1] = fp[1];
+            have_fp = true;
         }
         reset_tmp();
+    }
+
+    // Content hash of the kernel's IR: blocks (labels, order, terminators),
+    // instructions with their operands (values by id/type/name, constants by
+    // type and Python value) and the next value id.
+    OCB_HD void fingerprint(uint64_t out[2]) {
+        uint64_t h1 = 1469598103934665603ull, h2 = 0x9E3779B97F4A7C15ull;
+        auto mix = [&](uint64_t v) {
+            h1 = (h1 ^ v) * 1099511628211ull;
+            h2 = (h2 + v + (h2 << 6) + (h2 >> 2)) * 0xff51afd7ed558ccdull;
+        };
+        auto mix_str = [&](Str s_) {
+            mix(s_.n);
+            for (uint32_t i = 0; i < s_.n; ++i) mix((uint8_t)s_.p[i]);
+        };
+        auto mix_op = [&](Opnd o) {
+            mix(o.k);
+            if (o.k == O_VAL) {
+                const Value &v = m.vals[o.x];
+                mix(v.id);
+                mix(v.ty);
+                mix_str(v.name);
+            } else if (o.k == O_CONST) {
+                const Const &c = m.consts[o.x];
+                mix(c.ty);
+                mix(c.pyfloat);
+                if (c.pyfloat) {
+                    uint64_t b;
+                    memcpy(&b, &c.f, 8);
+                    mix(b);
+                } else {
+                    mix((uint64_t)c.i);
+                    mix((uint64_t)((unsigned __int128)c.i >> 64));
+                }
+            }
+        };
+        mix(k->next_id);
+        mix(k->blocks.n);
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            const Block &b = B(k->blocks[bi]);
+            mix_str(b.label);
+            mix(b.insts.n);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                mix(in.kind);
+                mix(in.op);
+                if (in.dest >= 0) mix_op(ov((uint32_t)in.dest));
+                else mix(0xFFFF);
+                mix_op(in.a);
+                mix_op(in.b);
+                mix_op(in.c);
+                mix_str(in.func);
+                mix(in.pidx);
+                mix(in.args.n);
+                for (uint32_t q = 0; q < in.args.n; ++q) mix_op(in.args[q]);
+            }
+            mix(b.term.kind);
+            mix_op(b.term.v);
+            mix_str(b.term.t);
+            mix_str(b.term.f);
+        }
+        out[0] = h1;
+        out[1] = h2;
     }
 #undef OCB_PASS
 };

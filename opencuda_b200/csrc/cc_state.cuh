@@ -28,7 +28,22 @@ struct CCArgs {
     uint64_t *out_len;           // n_tu + 1 (last = 0)
     int32_t *status;             // in: earlier stages' verdicts; out: final
     int stage;
+    uint32_t spread;             // TUs per warp (1..32): lane < spread works
+    uint32_t ir_permille;        // share of a TU's slice for the IR (rest: scratch)
+    uint64_t *peak;              // optional: per-TU arena bytes used (tuning)
 };
+
+// TU index of this thread, or n_tu when the lane is idle
+OCB_HD inline uint32_t cc_tu_index(const CCArgs &A) {
+#ifdef __CUDA_ARCH__
+    uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+    uint32_t lane = g & 31, warp = g >> 5;
+    if (lane >= A.spread) return 0xFFFFFFFFu;
+    return warp * A.spread + lane;
+#else
+    return 0xFFFFFFFFu;
+#endif
+}
 
 OCB_HD inline TUState *tu_state(const CCArgs &A, uint32_t i) {
     return (TUState *)(A.arena + A.arena_off[i]);

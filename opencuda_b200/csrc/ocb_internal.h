@@ -112,6 +112,16 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
               cudaStream_t st);
 }  // namespace ocb
 
+// Phase timing for tuning: with OCB_TIMING set in the environment, mark()
+// synchronises the stream and prints the time since the previous mark.
+struct PhaseTimer {
+    bool on;
+    double t0;
+    cudaStream_t st;
+    explicit PhaseTimer(cudaStream_t s);
+    void mark(const char *what);
+};
+
 #define OCB_TRY(what, expr)                                    \
     do {                                                       \
         cudaError_t e_ = (expr);                               \
