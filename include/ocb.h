@@ -142,6 +142,31 @@ int  ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off
 int  ocb_compile_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
                        uint32_t n_tu, ocb_text **out);
 
+/* Device-resident form of ocb_parse_batch / ocb_optimize_batch /
+ * ocb_compile_batch (stage 0, 1, 2): the batch is already in device memory
+ * (d_src, d_tu_off[n_tu+1] as for ocb_lex_device) and the result stays there.
+ * TUs that outgrow their arena are gathered, run again with larger arenas and
+ * merged back on the device.  On return the work is complete and
+ * *d_out / *out_bytes / *d_out_off[n_tu+1] / *d_status[n_tu] describe the
+ * packed outputs; they are owned by the context and stay valid until its next
+ * call. */
+int  ocb_compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
+                        const uint64_t *d_tu_off, uint32_t n_tu, int stage,
+                        const uint8_t **d_out, uint64_t *out_bytes,
+                        const uint64_t **d_out_off, const int32_t **d_status);
+
+/* Per-kernel timing of the compiler's three kernels, for measurement:
+ * ocb_kernel_profile(ctx, 1) zeroes the counters and brackets every later
+ * launch of k_cc_parse, k_cc_opt and k_cc_emit with CUDA events on the
+ * context's stream (0 turns it off).  ocb_kernel_times fills ms[3] with the
+ * summed event durations and launches[3] with the launch counts, in that
+ * kernel order. */
+int  ocb_kernel_profile(ocb_ctx *ctx, int enable);
+/* The context's own CUDA stream (a cudaStream_t), on which every batch call
+ * queues its work; for callers that time or order work around those calls. */
+void *ocb_stream(ocb_ctx *ctx);
+int  ocb_kernel_times(const ocb_ctx *ctx, double *ms, uint64_t *launches);
+
 /* Allocation-free form of ocb_lex_device, for callers that may not allocate
  * device memory when they lex (a framework's memory pool or a fixed arena that
  * forbids cudaMalloc/cudaFree after start-up, or a thread that must not take

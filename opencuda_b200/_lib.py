@@ -40,6 +40,11 @@ SIGNATURES = [
     ("ocb_parse_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_optimize_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_compile_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
+    ("ocb_compile_device", c_int, [c_void_p, c_void_p, c_u64, c_void_p, c_u32, c_int,
+                                   P(c_void_p), P(c_u64), P(c_void_p), P(c_void_p)]),
+    ("ocb_kernel_profile", c_int, [c_void_p, c_int]),
+    ("ocb_stream", c_void_p, [c_void_p]),
+    ("ocb_kernel_times", c_int, [c_void_p, P(ctypes.c_double), P(c_u64)]),
     ("ocb_lex_device_static", c_int, [c_void_p, c_u64, c_void_p, c_u32, c_void_p,
                                       c_void_p, c_void_p, c_u64, c_void_p, c_void_p,
                                       c_void_p, c_void_p, ctypes.c_char_p, ctypes.c_size_t]),

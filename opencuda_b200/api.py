@@ -205,6 +205,39 @@ class Context:
         finally:
             self.lib.ocb_text_free(out)
 
+    def compile_device(self, d_src: int, n_bytes: int, d_tu_off: int, n_tu: int,
+                       stage: int = 2):
+        """Device-pointer form of parse/optimize/compile_batch
+        (``ocb_compile_device``, stage 0/1/2).  Returns
+        ``(d_out, out_bytes, d_out_off, d_status)``: device addresses owned by
+        the context, valid until its next call; the work is complete."""
+        d_out, d_off, d_st = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        nb = ctypes.c_uint64()
+        self._check(self.lib.ocb_compile_device(self.h, d_src, n_bytes, d_tu_off, n_tu, stage,
+                                                ctypes.byref(d_out), ctypes.byref(nb),
+                                                ctypes.byref(d_off), ctypes.byref(d_st)),
+                    "ocb_compile_device")
+        return d_out.value or 0, nb.value, d_off.value or 0, d_st.value or 0
+
+    KERNELS = ("k_cc_parse", "k_cc_opt", "k_cc_emit")
+
+    @property
+    def stream(self) -> int:
+        """The context's CUDA stream handle (every batch call queues work on it)."""
+        return self.lib.ocb_stream(self.h) or 0
+
+    def kernel_profile(self, enable: bool = True) -> None:
+        """Zero the per-kernel event timers and switch them on/off."""
+        self._check(self.lib.ocb_kernel_profile(self.h, 1 if enable else 0),
+                    "ocb_kernel_profile")
+
+    def kernel_times(self) -> dict:
+        """``{kernel: (total_ms, launches)}`` since ``kernel_profile(True)``."""
+        ms = (ctypes.c_double * 3)()
+        n = (ctypes.c_uint64 * 3)()
+        self.lib.ocb_kernel_times(self.h, ms, n)
+        return {k: (ms[i], n[i]) for i, k in enumerate(self.KERNELS)}
+
     def lex_device(self, d_src: int, n_bytes: int, d_tu_off: int, n_tu: int,
                    d_start: int, d_kindlen: int, d_line: int, tok_cap: int,
                    d_tu_tok_off: int, d_status: int, d_n_tok: int, stream: int = 0):

@@ -77,9 +77,17 @@ void ocb_destroy(ocb_ctx *ctx) {
     for (DevBuf *b : {&ctx->lex_scratch, &ctx->cub_tmp, &ctx->d_src, &ctx->d_tu_off,
                       &ctx->d_tok_start, &ctx->d_tok_kl, &ctx->d_tok_line, &ctx->d_tu_tok,
                       &ctx->d_status, &ctx->d_count, &ctx->pp_scratch, &ctx->pp_arena,
-                      &ctx->pp_text, &ctx->pp_off, &ctx->pp_status, &ctx->pp_qinc})
+                      &ctx->pp_text, &ctx->pp_off, &ctx->pp_status, &ctx->pp_qinc,
+                      &ctx->cc_tok, &ctx->cc_scratch, &ctx->cc_arena, &ctx->cc_out,
+                      &ctx->cc_text, &ctx->cc_off, &ctx->cc_status, &ctx->cc_in_status,
+                      &ctx->res_text, &ctx->res_off, &ctx->res_status, &ctx->rt_src,
+                      &ctx->rt_src_off, &ctx->rt_idx, &ctx->rt_map, &ctx->rt_len,
+                      &ctx->rt_in_status, &ctx->rt_text, &ctx->rt_off, &ctx->rt_status,
+                      &ctx->rt_qinc, &ctx->mg_text, &ctx->mg_off, &ctx->mg_status})
         b->release();
     ctx->h_stage.release();
+    for (cudaEvent_t &e : ctx->kev)
+        if (e) cudaEventDestroy(e);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -209,7 +217,9 @@ static int upload_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off
     return 0;
 }
 
-static int download_text(ocb_ctx *ctx, ocb_text *t, uint32_t n_tu, uint64_t total) {
+// Device result (text, offsets, statuses, include flags) -> host ocb_text.
+static int download_text(ocb_ctx *ctx, ocb_text *t, uint32_t n_tu, uint64_t total,
+                         const DevBuf &text, const DevBuf &off, const DevBuf &status) {
     cudaStream_t st = ctx->stream;
     t->n_tu = n_tu;
     t->bytes.resize(total);
@@ -217,10 +227,10 @@ static int download_text(ocb_ctx *ctx, ocb_text *t, uint32_t n_tu, uint64_t tota
     t->status.resize(n_tu);
     t->qinclude.resize(n_tu);
     cudaError_t e = cudaSuccess;
-    if (total) e = cudaMemcpyAsync(t->bytes.data(), ctx->pp_text.p, total, cudaMemcpyDeviceToHost, st);
-    if (!e) e = cudaMemcpyAsync(t->off.data(), ctx->pp_off.p, 8 * ((size_t)n_tu + 1),
+    if (total) e = cudaMemcpyAsync(t->bytes.data(), text.p, total, cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaMemcpyAsync(t->off.data(), off.p, 8 * ((size_t)n_tu + 1),
                                 cudaMemcpyDeviceToHost, st);
-    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->pp_status.p, 4 * (size_t)n_tu,
+    if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), status.p, 4 * (size_t)n_tu,
                                         cudaMemcpyDeviceToHost, st);
     if (!e && n_tu) e = cudaMemcpyAsync(t->qinclude.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu,
                                         cudaMemcpyDeviceToHost, st);
@@ -234,140 +244,21 @@ int ocb_preprocess_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_of
     if (!ctx || !out || !tu_off) return fail(ctx, "ocb_preprocess_batch: null argument");
     *out = nullptr;
     OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
-    cudaStream_t st = ctx->stream;
     uint64_t N = 0;
     int rc = upload_batch(ctx, src, tu_off, n_tu, N);
     if (rc) return rc;
-    OCB_TRY("device offsets", ctx->pp_off.ensure(8 * ((size_t)n_tu + 1)));
-    OCB_TRY("device status", ctx->pp_status.ensure(4 * (size_t)n_tu + 4));
-    OCB_TRY("device flags", ctx->pp_qinc.ensure(4 * (size_t)n_tu + 4));
     uint64_t total = 0;
-    rc = pp_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(), n_tu, 2,
-                   ctx->pp_text, ctx->pp_off.as<uint64_t>(), ctx->pp_status.as<int32_t>(),
-                   ctx->pp_qinc.as<uint32_t>(), &total, st);
+    rc = pp_with_reruns(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(), n_tu,
+                        &total, ctx->stream);
     if (rc) return rc;
     ocb_text *t = new (std::nothrow) ocb_text();
     if (!t) return fail(ctx, "ocb_preprocess_batch: out of host memory");
-    rc = download_text(ctx, t, n_tu, total);
+    rc = download_text(ctx, t, n_tu, total, ctx->pp_text, ctx->pp_off, ctx->pp_status);
     if (rc) {
         delete t;
         return rc;
     }
-    // TUs whose arena was too small (macro growth) run again, alone, with a
-    // larger arena; their output replaces the first attempt's.
-    for (uint32_t scale = 32; scale <= 512; scale *= 16) {
-        std::vector<uint32_t> redo;
-        for (uint32_t i = 0; i < n_tu; ++i)
-            if (t->status[i] == OCB_TU_OVERFLOW) redo.push_back(i);
-        if (redo.empty()) break;
-        std::vector<uint64_t> sub_off(redo.size() + 1, 0);
-        for (size_t k = 0; k < redo.size(); ++k)
-            sub_off[k + 1] = sub_off[k] + (tu_off[redo[k] + 1] - tu_off[redo[k]]);
-        std::vector<uint8_t> sub(sub_off.back() + 1);
-        for (size_t k = 0; k < redo.size(); ++k)
-            memcpy(sub.data() + sub_off[k], src + tu_off[redo[k]], sub_off[k + 1] - sub_off[k]);
-        uint64_t sN = 0;
-        rc = upload_batch(ctx, sub.data(), sub_off.data(), (uint32_t)redo.size(), sN);
-        uint64_t stotal = 0;
-        if (!rc)
-            rc = pp_device(ctx, ctx->d_src.as<uint8_t>(), sN, ctx->d_tu_off.as<uint64_t>(),
-                           (uint32_t)redo.size(), scale, ctx->pp_text, ctx->pp_off.as<uint64_t>(),
-                           ctx->pp_status.as<int32_t>(), ctx->pp_qinc.as<uint32_t>(), &stotal, st);
-        ocb_text r;
-        if (!rc) rc = download_text(ctx, &r, (uint32_t)redo.size(), stotal);
-        if (rc) {
-            delete t;
-            return rc;
-        }
-        // splice the retried TUs into the result
-        ocb_text m;
-        m.n_tu = n_tu;
-        m.off.resize((size_t)n_tu + 1);
-        m.status = t->status;
-        m.qinclude = t->qinclude;
-        size_t k = 0;
-        for (uint32_t i = 0; i < n_tu; ++i) {
-            m.off[i] = m.bytes.size();
-            if (k < redo.size() && redo[k] == i) {
-                m.bytes.insert(m.bytes.end(), r.bytes.begin() + r.off[k], r.bytes.begin() + r.off[k + 1]);
-                m.status[i] = r.status[k];
-                m.qinclude[i] = r.qinclude[k];
-                ++k;
-            } else {
-                m.bytes.insert(m.bytes.end(), t->bytes.begin() + t->off[i], t->bytes.begin() + t->off[i + 1]);
-            }
-        }
-        m.off[n_tu] = m.bytes.size();
-        *t = std::move(m);
-    }
     *out = t;
-    return 0;
-}
-
-// Run the back half (lex + parse) over TUs already preprocessed on the host;
-// TUs that outgrow their arena run again alone with larger arenas.
-static int compile_text(ocb_ctx *ctx, const ocb_text &pp, int stage, ocb_text *out) {
-    cudaStream_t st = ctx->stream;
-    uint32_t n_tu = pp.n_tu;
-    out->n_tu = n_tu;
-    out->status.assign(n_tu, 0);
-    out->qinclude = pp.qinclude;
-    out->off.assign((size_t)n_tu + 1, 0);
-    out->bytes.clear();
-    std::vector<uint32_t> todo(n_tu);
-    for (uint32_t i = 0; i < n_tu; ++i) todo[i] = i;
-    std::vector<std::vector<uint8_t>> res(n_tu);
-    PhaseTimer T(st);
-    for (uint32_t scale = 1; !todo.empty(); scale *= 8) {
-        // sub-batch of the pending TUs
-        std::vector<uint64_t> off(todo.size() + 1, 0);
-        for (size_t k = 0; k < todo.size(); ++k)
-            off[k + 1] = off[k] + (pp.off[todo[k] + 1] - pp.off[todo[k]]);
-        std::vector<uint8_t> text(off.back() + 1);
-        std::vector<int32_t> in_st(todo.size());
-        for (size_t k = 0; k < todo.size(); ++k) {
-            memcpy(text.data() + off[k], pp.bytes.data() + pp.off[todo[k]], off[k + 1] - off[k]);
-            in_st[k] = pp.status[todo[k]];
-        }
-        uint64_t N = 0;
-        int rc = upload_batch(ctx, text.data(), off.data(), (uint32_t)todo.size(), N);
-        if (rc) return rc;
-        size_t nt = todo.size();
-        OCB_TRY("device status", ctx->cc_in_status.ensure(4 * nt + 4));
-        OCB_TRY("device status", ctx->cc_status.ensure(4 * nt + 4));
-        OCB_TRY("device offsets", ctx->cc_off.ensure(8 * (nt + 1)));
-        OCB_TRY("h2d status", cudaMemcpyAsync(ctx->cc_in_status.p, in_st.data(), 4 * nt,
-                                              cudaMemcpyHostToDevice, st));
-        uint64_t total = 0;
-        T.mark(scale == 1 ? "cc: upload" : "cc: upload (retry)");
-        rc = cc_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(),
-                       (uint32_t)nt, ctx->cc_in_status.as<int32_t>(), stage, scale, ctx->cc_text,
-                       ctx->cc_off.as<uint64_t>(), ctx->cc_status.as<int32_t>(), &total, st);
-        if (rc) return rc;
-        std::vector<uint8_t> bytes(total);
-        std::vector<uint64_t> o(nt + 1);
-        std::vector<int32_t> s(nt);
-        cudaError_t e = cudaSuccess;
-        if (total) e = cudaMemcpyAsync(bytes.data(), ctx->cc_text.p, total, cudaMemcpyDeviceToHost, st);
-        if (!e) e = cudaMemcpyAsync(o.data(), ctx->cc_off.p, 8 * (nt + 1), cudaMemcpyDeviceToHost, st);
-        if (!e) e = cudaMemcpyAsync(s.data(), ctx->cc_status.p, 4 * nt, cudaMemcpyDeviceToHost, st);
-        if (!e) e = cudaStreamSynchronize(st);
-        if (e) return fail(ctx, "d2h compile output", e);
-        T.mark("cc: download");
-        std::vector<uint32_t> next;
-        for (size_t k = 0; k < nt; ++k) {
-            uint32_t i = todo[k];
-            out->status[i] = s[k];
-            if (s[k] == OCB_TU_OVERFLOW && scale < 64) next.push_back(i);
-            else res[i].assign(bytes.begin() + o[k], bytes.begin() + o[k + 1]);
-        }
-        todo.swap(next);
-    }
-    for (uint32_t i = 0; i < n_tu; ++i) {
-        out->off[i] = out->bytes.size();
-        out->bytes.insert(out->bytes.end(), res[i].begin(), res[i].end());
-    }
-    out->off[n_tu] = out->bytes.size();
     return 0;
 }
 
@@ -375,18 +266,20 @@ static int stage_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
                        int stage, ocb_text **out) {
     if (!ctx || !out || !tu_off) return fail(ctx, "null argument");
     *out = nullptr;
-    ocb_text *pp = nullptr;
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
     PhaseTimer T(ctx->stream);
-    int rc = ocb_preprocess_batch(ctx, src, tu_off, n_tu, &pp);
+    uint64_t N = 0;
+    int rc = upload_batch(ctx, src, tu_off, n_tu, N);
     if (rc) return rc;
-    T.mark("preprocess (host api)");
+    T.mark("upload");
+    uint64_t total = 0;
+    rc = compile_device(ctx, ctx->d_src.as<uint8_t>(), N, ctx->d_tu_off.as<uint64_t>(), n_tu,
+                        stage, &total);
+    if (rc) return rc;
     ocb_text *t = new (std::nothrow) ocb_text();
-    if (!t) {
-        delete pp;
-        return fail(ctx, "out of host memory");
-    }
-    rc = compile_text(ctx, *pp, stage, t);
-    delete pp;
+    if (!t) return fail(ctx, "out of host memory");
+    rc = download_text(ctx, t, n_tu, total, ctx->res_text, ctx->res_off, ctx->res_status);
+    T.mark("download");
     if (rc) {
         delete t;
         return rc;
@@ -408,6 +301,50 @@ int ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
 int ocb_compile_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
                       ocb_text **out) {
     return stage_batch(ctx, src, tu_off, n_tu, 2, out);
+}
+
+int ocb_compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
+                       const uint64_t *d_tu_off, uint32_t n_tu, int stage,
+                       const uint8_t **d_out, uint64_t *out_bytes, const uint64_t **d_out_off,
+                       const int32_t **d_status) {
+    if (!ctx) return -1;
+    if (stage < 0 || stage > 2) return fail(ctx, "ocb_compile_device: stage must be 0, 1 or 2");
+    if (n_tu && (!d_src || !d_tu_off)) return fail(ctx, "ocb_compile_device: null argument");
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
+    uint64_t total = 0;
+    int rc = compile_device(ctx, d_src, n_bytes, d_tu_off, n_tu, stage, &total);
+    if (rc) return rc;
+    ctx->res_bytes = total;
+    ctx->res_n_tu = n_tu;
+    if (d_out) *d_out = ctx->res_text.as<uint8_t>();
+    if (out_bytes) *out_bytes = total;
+    if (d_out_off) *d_out_off = ctx->res_off.as<uint64_t>();
+    if (d_status) *d_status = ctx->res_status.as<int32_t>();
+    return 0;
+}
+
+void *ocb_stream(ocb_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int ocb_kernel_profile(ocb_ctx *ctx, int enable) {
+    if (!ctx) return -1;
+    OCB_TRY("cudaSetDevice", cudaSetDevice(ctx->device));
+    for (cudaEvent_t &e : ctx->kev)
+        if (!e) OCB_TRY("event create", cudaEventCreate(&e));
+    ctx->kprof_on = enable != 0;
+    for (int k = 0; k < 3; ++k) {
+        ctx->kms[k] = 0;
+        ctx->kn[k] = 0;
+    }
+    return 0;
+}
+
+int ocb_kernel_times(const ocb_ctx *ctx, double *ms, uint64_t *launches) {
+    if (!ctx) return -1;
+    for (int k = 0; k < 3; ++k) {
+        if (ms) ms[k] = ctx->kms[k];
+        if (launches) launches[k] = ctx->kn[k];
+    }
+    return 0;
 }
 
 int ocb_text_view(const ocb_text *t, uint64_t *n_bytes, const uint8_t **bytes,

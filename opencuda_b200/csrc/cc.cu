@@ -138,11 +138,16 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         unsigned warps = (nc + spread - 1) / spread;
         unsigned blocks = (warps + 3) / 4;  // 4 warps (128 threads) per block
         T.mark("cc: chunk setup");
+        bool kp = ctx->kprof_on;
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[0], st));
         OCB_TRY("cc: parse launch", launch_k_cc_parse(A, blocks, 128, st));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[1], st));
         T.mark("cc: k_cc_parse");
         if (stage >= CC_STAGE_OPT) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, blocks, 128, st));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[2], st));
         T.mark("cc: k_cc_opt");
         OCB_TRY("cc: emit launch", launch_k_cc_emit(A, blocks, 128, st));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[3], st));
         T.mark("cc: k_cc_emit");
         size_t t1 = 0;
         cub::DeviceScan::ExclusiveSum(nullptr, t1, out_len, pack_off, (int)(nc + 1), st);
@@ -152,6 +157,15 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         uint64_t tot = 0;
         OCB_TRY("cc: d2h", cudaMemcpyAsync(&tot, pack_off + nc, 8, cudaMemcpyDeviceToHost, st));
         OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+        if (kp) {
+            for (int k = 0; k < 3; ++k) {
+                if (k == 1 && stage < CC_STAGE_OPT) continue;
+                float ms = 0;
+                OCB_TRY("cc: event time", cudaEventElapsedTime(&ms, ctx->kev[k], ctx->kev[k + 1]));
+                ctx->kms[k] += ms;
+                ctx->kn[k] += 1;
+            }
+        }
         if (running + tot + 64 > out_text.cap) {  // grow, keeping what is packed so far
             DevBuf nb;
             size_t want = out_text.cap * 2;

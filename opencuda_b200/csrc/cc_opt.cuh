@@ -2083,7 +2083,7 @@ struct Opt {
             OCB_PASS(merge_linear_chains());
             uint64_t fp[2];
             fingerprint(fp);
-            if (have_fp && fp[0] == fp_prev[0] && fp[1] == fp_prev[1] && !getenv("NOFP")) break;
+            if (have_fp && fp[0] == fp_prev[0] && fp[1] == fp_prev[1]) break;
             fp_prev[0] = fp[0];
             fp_prev[1] = fp[1];
             have_fp = true;

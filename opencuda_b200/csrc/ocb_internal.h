@@ -69,6 +69,18 @@ struct ocb_ctx {
     ocb::DevBuf pp_scratch, pp_arena, pp_text, pp_off, pp_status, pp_qinc;
     // compiler back half (tokens -> IR -> PTX) scratch and outputs
     ocb::DevBuf cc_tok, cc_scratch, cc_arena, cc_out, cc_text, cc_off, cc_status, cc_in_status;
+    // whole-pipeline result (res_*), rerun sub-batches (rt_*) and merge targets (mg_*)
+    ocb::DevBuf res_text, res_off, res_status;
+    ocb::DevBuf rt_src, rt_src_off, rt_idx, rt_map, rt_len, rt_in_status, rt_text, rt_off,
+        rt_status, rt_qinc;
+    ocb::DevBuf mg_text, mg_off, mg_status;
+    uint64_t res_bytes = 0;
+    uint32_t res_n_tu = 0;
+    // per-kernel CUDA-event timing of the compiler kernels (ocb_kernel_profile)
+    bool kprof_on = false;
+    cudaEvent_t kev[4] = {};
+    double kms[3] = {};
+    uint64_t kn[3] = {};
 };
 
 struct ocb_text {
@@ -110,6 +122,15 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
               uint32_t n_tu, const int32_t *d_in_status, int stage, uint32_t scale,
               DevBuf &out_text, uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total,
               cudaStream_t st);
+// Preprocess with reruns of the TUs that outgrew the preprocessor's arena
+// (pipeline.cu).  Result in ctx->pp_text / pp_off / pp_status / pp_qinc.
+int pp_with_reruns(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_tu_off,
+                   uint32_t n_tu, uint64_t *h_total, cudaStream_t st);
+// The whole pipeline on device buffers (pipeline.cu): preprocess, then
+// lex/parse/optimize/emit up to `stage`, with arena reruns on the device.
+// Result in ctx->res_text / res_off / res_status (+ ctx->pp_qinc).
+int compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_tu_off,
+                   uint32_t n_tu, int stage, uint64_t *h_total);
 }  // namespace ocb
 
 // Phase timing for tuning: with OCB_TIMING set in the environment, mark()

@@ -66,3 +66,56 @@ def test_mutations_ptx_against_live_reference(ctx):
     with ref_runner.RefPool() as pool:
         ref = pool.run(srcs, what=("ptx",), chunksize=16)
     check_ptx(tb, srcs, ref, allow_unsupported=0.02)
+
+
+def _device_compile(ctx, srcs, stage=2):
+    """ocb_compile_device on a device-resident batch -> (bytes, offsets, statuses)."""
+    import numpy as np
+    import torch
+    from opencuda_b200.api import pack_sources
+
+    class _Dev:
+        def __init__(self, ptr, n, typestr):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
+                                             "data": (int(ptr), True), "version": 3}
+
+    buf, off = pack_sources(srcs)
+    d_src = torch.from_numpy(buf.copy()).cuda()
+    d_off = torch.from_numpy(off.astype(np.int64)).cuda()
+    n = len(srcs)
+    torch.cuda.synchronize()
+    d_out, nb, d_oo, d_st = ctx.compile_device(d_src.data_ptr(), len(buf), d_off.data_ptr(), n,
+                                               stage)
+    dev = torch.device("cuda", 0)
+    data = (torch.as_tensor(_Dev(d_out, nb, "|u1"), device=dev).cpu().numpy().tobytes()
+            if nb else b"")
+    oo = torch.as_tensor(_Dev(d_oo, n + 1, "<u8"), device=dev).cpu().numpy()
+    st = torch.as_tensor(_Dev(d_st, n, "<i4"), device=dev).cpu().numpy()
+    return data, oo, st
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2])
+def test_device_entry_point_matches_host_api(ctx, stage):
+    srcs = [synth.SGEMM_SRC] + synth.random_batch(300, seed=21) + mutate_sources(100, 5) + [""]
+    data, oo, st = _device_compile(ctx, srcs, stage)
+    fn = {0: ctx.parse_batch, 1: ctx.optimize_batch, 2: ctx.compile_batch}[stage]
+    tb = fn(srcs)
+    assert list(st) == list(tb.status)
+    assert data == tb.data
+    assert list(oo) == list(tb.off)
+
+
+def test_arena_reruns_gathered_and_merged_on_device(ctx, monkeypatch):
+    """A first arena of 300 B/token overflows almost every TU: they are gathered,
+    rerun at x8 and x64 and merged back; the result equals a run without
+    reruns."""
+    srcs = [synth.SGEMM_SRC] + synth.random_batch(200, seed=33) + mutate_sources(60, 9)
+    want = _device_compile(ctx, srcs)
+    monkeypatch.setenv("OCB_CC_ARENA_PER_TOKEN", "300")
+    monkeypatch.setenv("OCB_CC_ARENA_BASE", "4096")
+    got = _device_compile(ctx, srcs)
+    assert list(got[2]) == list(want[2])
+    assert got[0] == want[0]
+    assert list(got[1]) == list(want[1])
+    tb = ctx.compile_batch(srcs)
+    assert tb.data == want[0]
