@@ -200,7 +200,7 @@ class DevArray:
 
     def __init__(self, ptr, n, typestr):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
-                                         "data": (int(ptr), True), "version": 3}
+                                         "data": (int(ptr), False), "version": 3}
 
 
 def count_launches(fn):

@@ -77,7 +77,7 @@ def _device_compile(ctx, srcs, stage=2):
     class _Dev:
         def __init__(self, ptr, n, typestr):
             self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
-                                             "data": (int(ptr), True), "version": 3}
+                                             "data": (int(ptr), False), "version": 3}
 
     buf, off = pack_sources(srcs)
     d_src = torch.from_numpy(buf.copy()).cuda()
