@@ -121,7 +121,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_init():
+def dist_init(backend: str = "nccl"):
+    """Rank, world size and local rank from the torchrun environment; joins
+    the process group when there is more than one rank (NCCL on the GPU box,
+    gloo in the CPU tests of this logic)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -129,8 +132,9 @@ def dist_init():
         import datetime
         import torch
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
     return rank, world, local
 
 
@@ -150,9 +154,10 @@ def allreduce(x, world, device, op="max"):
     return float(t.item())
 
 
-def workload(rank):
+def workload(rank, n=N_KERNELS):
+    """This rank's kernels: its own seed, so ranks compile disjoint TUs."""
     from opencuda_b200 import synth
-    return synth.random_batch(N_KERNELS, seed=SEED + RANK_SEED_STRIDE * rank)
+    return synth.random_batch(n, seed=SEED + RANK_SEED_STRIDE * rank)
 
 
 def cpu_sample_size(cores):
@@ -303,7 +308,7 @@ def main():
     ctx = api.Context(local)
     peak, peak_kind = measured_peak()
 
-    srcs = workload(rank)[:args.kernels]
+    srcs = workload(rank, args.kernels)
     buf, off = api.pack_sources(srcs)
     n_tu = len(srcs)
     nbytes = len(buf)

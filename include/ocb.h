@@ -60,6 +60,12 @@ int  ocb_create(ocb_ctx **out, int device, uint32_t flags);
 void ocb_destroy(ocb_ctx *ctx);
 /* Last error text of this context (valid until the next call on it). */
 const char *ocb_last_error(ocb_ctx *ctx);
+/* Set the `.target` line of the PTX modules that later compiles on this
+ * context write (default "sm_120", 1-31 bytes, no control characters).
+ * Replaces the CLI's --arch option (opencuda/__main__.py:23-24, written as
+ * `.target {arch}` at :64); like the reference, the value is not checked
+ * against a list of architectures. */
+int  ocb_set_target(ocb_ctx *ctx, const char *arch);
 /* Library build string (architecture, version). */
 const char *ocb_version(void);
 

@@ -26,6 +26,7 @@ SIGNATURES = [
     ("ocb_create", c_int, [P(c_void_p), c_int, c_u32]),
     ("ocb_destroy", None, [c_void_p]),
     ("ocb_last_error", ctypes.c_char_p, [c_void_p]),
+    ("ocb_set_target", c_int, [c_void_p, ctypes.c_char_p]),
     ("ocb_lex_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_tokens_view", c_int, [c_void_p, P(c_u64), P(c_void_p), P(c_void_p),
                                 P(c_void_p), P(c_void_p), P(c_void_p)]),

@@ -139,6 +139,13 @@ class Context:
             raise OcbError(f"{what}: {msg.decode() if msg else rc}")
 
     # ---- lexer -----------------------------------------------------------
+    def set_target(self, arch: str) -> None:
+        """``.target`` of the PTX modules later compiles write (``--arch``)."""
+        if getattr(self, "_target", None) == arch:
+            return
+        self._check(self.lib.ocb_set_target(self.h, arch.encode("utf-8")), "ocb_set_target")
+        self._target = arch
+
     def lex_batch(self, srcs=None, *, buf=None, tu_off=None) -> TokenBatch:
         """Lex every TU (``lexer.py:258`` ``lex`` per TU)."""
         if srcs is not None:

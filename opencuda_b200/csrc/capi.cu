@@ -80,6 +80,7 @@ void ocb_destroy(ocb_ctx *ctx) {
                       &ctx->pp_text, &ctx->pp_off, &ctx->pp_status, &ctx->pp_qinc,
                       &ctx->cc_tok, &ctx->cc_scratch, &ctx->cc_arena, &ctx->cc_out,
                       &ctx->cc_text, &ctx->cc_off, &ctx->cc_status, &ctx->cc_in_status,
+                      &ctx->cc_order, &ctx->cc_spill,
                       &ctx->res_text, &ctx->res_off, &ctx->res_status, &ctx->rt_src,
                       &ctx->rt_src_off, &ctx->rt_idx, &ctx->rt_map, &ctx->rt_len,
                       &ctx->rt_in_status, &ctx->rt_text, &ctx->rt_off, &ctx->rt_status,
@@ -94,6 +95,18 @@ void ocb_destroy(ocb_ctx *ctx) {
 
 const char *ocb_last_error(ocb_ctx *ctx) {
     return ctx ? ctx->err.c_str() : "null context";
+}
+
+int ocb_set_target(ocb_ctx *ctx, const char *arch) {
+    if (!ctx || !arch) return fail(ctx, "ocb_set_target: null argument");
+    size_t n = strlen(arch);
+    if (n == 0 || n >= sizeof ctx->target)
+        return fail(ctx, "ocb_set_target: target must be 1 to 31 bytes");
+    for (size_t i = 0; i < n; ++i)
+        if ((unsigned char)arch[i] < 0x20 || (unsigned char)arch[i] == 0x7F)
+            return fail(ctx, "ocb_set_target: control character in target");
+    memcpy(ctx->target, arch, n + 1);
+    return 0;
 }
 
 int ocb_lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes, const uint64_t *d_tu_off,

@@ -58,6 +58,8 @@ struct ocb_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     std::string err;
+    // `.target` of the PTX modules this context writes (ocb_set_target)
+    char target[32] = "sm_120";
     // lexer scratch
     ocb::DevBuf lex_scratch, cub_tmp;
     // staging for host-buffer entry points
@@ -69,6 +71,8 @@ struct ocb_ctx {
     ocb::DevBuf pp_scratch, pp_arena, pp_text, pp_off, pp_status, pp_qinc;
     // compiler back half (tokens -> IR -> PTX) scratch and outputs
     ocb::DevBuf cc_tok, cc_scratch, cc_arena, cc_out, cc_text, cc_off, cc_status, cc_in_status;
+    // compiler: per-chunk TU order (largest first) and the shared spill pool
+    ocb::DevBuf cc_order, cc_spill;
     // whole-pipeline result (res_*), rerun sub-batches (rt_*) and merge targets (mg_*)
     ocb::DevBuf res_text, res_off, res_status;
     ocb::DevBuf rt_src, rt_src_off, rt_idx, rt_map, rt_len, rt_in_status, rt_text, rt_off,

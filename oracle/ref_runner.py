@@ -147,6 +147,29 @@ def _compile_only(src):
     return len(r.get("ptx", ""))
 
 
+def _resolve(args):
+    """The reference's include resolution (``preprocess.py:125-175``)."""
+    src, dirs = args
+    from opencuda.frontend.preprocess import _resolve_includes
+    try:
+        return _resolve_includes(src, [Path(d) for d in dirs], visited=set())
+    except Exception as e:  # noqa: BLE001
+        return ("error", type(e).__name__)
+
+
+def run_cli(argv, cwd=None, timeout=600):
+    """The reference CLI ``python -m opencuda ARGV`` in a fresh interpreter
+    (``PYTHONHASHSEED=0``, only ``oracle/_ref/py`` on the path).  Returns
+    ``(returncode, stdout, stderr)``."""
+    import subprocess
+    if not available():
+        raise RuntimeError("reference oracle not built: run oracle/build_ref.sh")
+    env = dict(os.environ, PYTHONHASHSEED="0", PYTHONPATH=str(REF_DIR))
+    p = subprocess.run([sys.executable, "-m", "opencuda", *map(str, argv)], cwd=cwd, env=env,
+                       capture_output=True, text=True, timeout=timeout)
+    return p.returncode, p.stdout, p.stderr
+
+
 class RefPool:
     """A pool of spawn workers that run the reference."""
 
@@ -162,6 +185,9 @@ class RefPool:
     def run(self, srcs, what=("ptx",), arch="sm_120", chunksize=4):
         return self.pool.map(_job, [(s, tuple(what), arch) for s in srcs],
                              chunksize=chunksize)
+
+    def resolve_includes(self, srcs, dirs):
+        return self.pool.map(_resolve, [(s, [str(d) for d in dirs]) for s in srcs])
 
     def lex_raw(self, srcs, chunksize=16):
         return self.pool.map(_lex_raw, srcs, chunksize=chunksize)
