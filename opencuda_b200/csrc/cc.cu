@@ -3,6 +3,7 @@
 // thread per translation unit.  Each TU gets a private slice of one arena
 // buffer sized from its token count; a TU that outgrows it reports
 // OCB_TU_OVERFLOW and the caller runs it again with a larger slice.
+#include <algorithm>
 #include <cub/cub.cuh>
 #include "ocb_internal.h"
 #include "cc_state.cuh"
@@ -65,7 +66,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     size_t n1 = (size_t)n_tu + 1;
     uint64_t tok_cap = N + n_tu + 16;
     OCB_TRY("cc: tokens", ctx->cc_tok.ensure(12 * tok_cap + 16));
-    OCB_TRY("cc: scratch", ctx->cc_scratch.ensure(8 * n1 * 5 + 8 + 4 * n1 + 64));
+    OCB_TRY("cc: scratch", ctx->cc_scratch.ensure(8 * n1 * 5 + 8 + 4 * n1 + 64 + 16));
     uint32_t *tstart = ctx->cc_tok.as<uint32_t>();
     uint32_t *tkl = tstart + tok_cap;
     uint32_t *tline = tkl + tok_cap;
@@ -76,6 +77,8 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     uint64_t *pack_off = out_len + n1;
     uint64_t *n_tok = pack_off + n1;
     int32_t *lex_status = (int32_t *)(n_tok + 1);
+    unsigned long long *spill_top =
+        (unsigned long long *)(((uintptr_t)(lex_status + n1) + 15) & ~(uintptr_t)15);
     PhaseTimer T(st);
     int rc = lex_device(ctx, d_text, N, d_off, n_tu, tstart, tkl, tline, tok_cap, tu_tok,
                         lex_status, n_tok, st);
@@ -107,6 +110,16 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     uint64_t budget_cap = env_u64("OCB_CC_BUDGET_MB", 24576) << 20;
     if (budget > budget_cap) budget = budget_cap;
     if (budget < (256ull << 20)) budget = 256ull << 20;
+    // One eighth of the budget is the spill pool that TUs outgrowing their
+    // slice draw from (shared by every TU of a chunk, reset per chunk).
+    uint64_t spill_b = env_u64("OCB_CC_SPILL_MB", budget >> 23) << 20;
+    if (spill_b) {
+        OCB_TRY("cc: spill pool", ctx->cc_spill.ensure(spill_b));
+        budget -= spill_b < budget / 2 ? spill_b : budget / 2;
+    }
+    bool order_on = env_u64("OCB_CC_ORDER", 1) != 0;
+    OCB_TRY("cc: order", ctx->cc_order.ensure(4 * (size_t)n_tu + 16));
+    std::vector<uint32_t> h_order;
     std::vector<uint64_t> h_aoff, h_ooff;
     uint64_t running = 0;
     uint32_t a = 0;
@@ -132,9 +145,24 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         OCB_TRY("cc: h2d", cudaMemcpyAsync(out_cap_off, h_ooff.data(), 8 * (size_t)(nc + 1),
                                            cudaMemcpyHostToDevice, st));
         OCB_TRY("cc: zero", cudaMemsetAsync(out_len, 0, 8 * (size_t)(nc + 1), st));
+        OCB_TRY("cc: zero", cudaMemsetAsync(spill_top, 0, 8, st));
+        if (order_on) {
+            // largest TUs (by tokens) first: the longest-running threads start
+            // in the first wave instead of forming the tail
+            h_order.resize(nc);
+            for (uint32_t j = 0; j < nc; ++j) h_order[j] = j;
+            std::stable_sort(h_order.begin(), h_order.end(), [&](uint32_t x, uint32_t y) {
+                return h_tok[a + x + 1] - h_tok[a + x] > h_tok[a + y + 1] - h_tok[a + y];
+            });
+            OCB_TRY("cc: h2d", cudaMemcpyAsync(ctx->cc_order.p, h_order.data(), 4 * (size_t)nc,
+                                               cudaMemcpyHostToDevice, st));
+        }
         CCArgs A{d_text, tstart, tkl, tu_tok + a, nc, ctx->cc_arena.as<uint8_t>(), arena_off,
                  ctx->cc_out.as<uint8_t>(), out_cap_off, out_len, d_status + a, stage, spread,
-                 ir_pm, nullptr};
+                 ir_pm, nullptr, {}, order_on ? ctx->cc_order.as<uint32_t>() : nullptr,
+                 SpillPool{spill_b ? ctx->cc_spill.as<uint8_t>() : nullptr,
+                           spill_b ? spill_top : nullptr, spill_b}};
+        memcpy(A.target, ctx->target, sizeof A.target);
         unsigned warps = (nc + spread - 1) / spread;
         unsigned blocks = (warps + 3) / 4;  // 4 warps (128 threads) per block
         T.mark("cc: chunk setup");

@@ -75,15 +75,41 @@ OCB_HD inline pyint py_shr(pyint a, pyint s) {
 // ---------------------------------------------------------------------------
 // arena + growable vectors
 // ---------------------------------------------------------------------------
+// A TU's slice is a bump allocator.  When an allocation does not fit, it is
+// taken from the launch's shared spill pool (one atomic add; spilled blocks
+// are never reused, resets of `used` only rewind the slice); `oom` is set
+// only when the pool is exhausted too, and the driver then reruns the TU
+// with a larger slice.
+struct SpillPool {
+    uint8_t *base;
+    unsigned long long *top;   // bytes handed out so far (device counter)
+    uint64_t cap;
+};
+
 struct Arena {
     uint8_t *base;
     uint64_t used, cap;
     bool oom;
+    SpillPool spill = {nullptr, nullptr, 0};
+    OCB_HD void *spill_alloc(uint64_t n, uint64_t align) {
+        if (!spill.top) return nullptr;
+        uint64_t want = (n + align + 15) & ~15ull;
+#ifdef __CUDA_ARCH__
+        uint64_t o = atomicAdd(spill.top, (unsigned long long)want);
+#else
+        uint64_t o = *spill.top;
+        *spill.top += want;
+#endif
+        if (o + want > spill.cap) return nullptr;
+        uintptr_t p = ((uintptr_t)(spill.base + o) + align - 1) & ~(uintptr_t)(align - 1);
+        return (void *)p;
+    }
     OCB_HD void *alloc(uint64_t n, uint64_t align = 8) {
         uint64_t a = (used + align - 1) & ~(align - 1);
         if (a + n > cap) {
-            oom = true;
-            return nullptr;
+            void *p = spill_alloc(n, align);
+            if (!p) oom = true;
+            return p;
         }
         used = a + n;
 #ifdef OCB_ARENA_PEAK

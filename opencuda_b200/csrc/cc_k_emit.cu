@@ -9,7 +9,7 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(128) k_cc_emit(CCArgs A) {
+__global__ void __launch_bounds__(128, OCB_CC_MIN_BLOCKS) k_cc_emit(CCArgs A) {
     uint32_t i = cc_tu_index(A);
     if (i >= A.n_tu) return;
     A.out_len[i] = 0;
@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(128) k_cc_emit(CCArgs A) {
     int32_t st = OCB_TU_OK;
     if (A.stage >= CC_STAGE_PTX) {
         S->tmp.used = 0;
-        bool ok = emit_module(m, S->tmp, o, "sm_120");
+        bool ok = emit_module(m, S->tmp, o, A.target);
         if (S->ar.oom || S->tmp.oom || o.full) st = OCB_TU_OVERFLOW;
         else if (m.unsup || (!ok && !m.raises)) st = OCB_TU_UNSUPPORTED;
         else if (!ok) st = m.raises;

@@ -7,7 +7,7 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(128) k_cc_opt(CCArgs A) {
+__global__ void __launch_bounds__(128, OCB_CC_MIN_BLOCKS) k_cc_opt(CCArgs A) {
     uint32_t i = cc_tu_index(A);
     if (i >= A.n_tu) return;
     TUState *S = tu_state(A, i);

@@ -8,7 +8,7 @@
 namespace ocb {
 namespace cc {
 
-__global__ void __launch_bounds__(128) k_cc_parse(CCArgs A) {
+__global__ void __launch_bounds__(128, OCB_CC_MIN_BLOCKS) k_cc_parse(CCArgs A) {
     uint32_t i = cc_tu_index(A);
     if (i >= A.n_tu) return;
     uint64_t sz = A.arena_off[i + 1] - A.arena_off[i];
@@ -22,8 +22,8 @@ __global__ void __launch_bounds__(128) k_cc_parse(CCArgs A) {
     uint8_t *base = A.arena + A.arena_off[i] + ((sizeof(TUState) + 15) & ~(size_t)15);
     uint64_t rest = sz - ((sizeof(TUState) + 15) & ~(size_t)15);
     uint64_t ir_sz = (rest / 1000 * A.ir_permille) & ~15ull;
-    S->ar = Arena{base, 0, ir_sz, false};
-    S->tmp = Arena{base + ir_sz, 0, rest - ir_sz, false};
+    S->ar = Arena{base, 0, ir_sz, false, A.spill};
+    S->tmp = Arena{base + ir_sz, 0, rest - ir_sz, false, A.spill};
     S->m.init(&S->ar);
     Parser *P = (Parser *)S->tmp.alloc(sizeof(Parser), 16);
     if (!P) {

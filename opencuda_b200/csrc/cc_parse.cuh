@@ -519,6 +519,7 @@ struct Parser {
     OCB_HD void pop_loop();
     OCB_HD OCB_NI void parse_while();
     OCB_HD OCB_NI void parse_do();
+    OCB_HD OCB_NI void parse_switch();
     OCB_HD OCB_NI void parse_decl(Ty ty, bool vol);
     OCB_HD OCB_NI void parse_shared(bool vol);
     OCB_HD OCB_NI void parse_if();

@@ -408,6 +408,101 @@ OCB_HD inline void Parser::pop_loop() {
     continue_snaps.n--;
 }
 
+// switch (parser.py:3030-3138): the case bodies are parsed in source order,
+// each from the variables as they were before the switch; the dispatch is a
+// compare chain built after the last case (switch_dispatch, switch_next_*),
+// so its blocks and values come after every case block.  A switch pushes a
+// break target only: `continue` still belongs to the enclosing loop.
+OCB_HD inline void Parser::parse_switch() {
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    Opnd sv = parse_expr();
+    if (bad() || !expect(TK_RPAREN) || !expect(TK_LBRACE)) return;
+    uint32_t pre = cur;
+    VarMap before = vars.copy(ar);
+    uint32_t xb = new_block("switch_exit");
+    break_targets.push(ar, m.blocks[xb].label);
+    break_snaps.push(ar, before);
+    Vec<Opnd> cvals;
+    Vec<uint32_t> cblocks;
+    cvals.init();
+    cblocks.init();
+    int32_t db = -1;       // default block
+    int32_t fall = -1;     // block falling through into the next label
+    while (!match(TK_RBRACE)) {
+        if (bad()) return;
+        uint32_t k = peek();
+        if (bad()) return;
+        if (k == TK_CASE || k == TK_DEFAULT) {
+            if (B().term.kind == T_NONE && cur != pre) {
+                loop_writeback(before);
+                fall = (int32_t)cur;
+            } else {
+                fall = -1;
+            }
+            uint32_t nb;
+            if (k == TK_CASE) {
+                advance();
+                Opnd cv = parse_expr();
+                if (bad() || !expect(TK_COLON)) return;
+                nb = new_block("case");
+                cvals.push(ar, cv);
+                cblocks.push(ar, nb);
+            } else {
+                advance();
+                if (!expect(TK_COLON)) return;
+                nb = new_block("default");
+                db = (int32_t)nb;
+            }
+            if (fall >= 0) {
+                m.blocks[fall].term = Term{T_BR, onone(), m.blocks[nb].label, Str{nullptr, 0}};
+                fall = -1;
+            }
+            vars = before.copy(ar);
+            cur = nb;
+        } else {
+            parse_stmt();
+        }
+        if (bad()) return;
+    }
+    break_targets.n--;
+    break_snaps.n--;
+    Str xl = m.blocks[xb].label;
+    if (B().term.kind == T_NONE) {
+        loop_writeback(before);
+        B().term = Term{T_BR, onone(), xl, Str{nullptr, 0}};
+    }
+    for (uint32_t q = 0; q < cblocks.n; ++q) {
+        if (m.blocks[cblocks[q]].term.kind == T_NONE) {
+            cur = cblocks[q];
+            loop_writeback(before);
+            B().term = Term{T_BR, onone(), xl, Str{nullptr, 0}};
+        }
+    }
+    if (db >= 0 && m.blocks[db].term.kind == T_NONE) {
+        cur = (uint32_t)db;
+        loop_writeback(before);
+        B().term = Term{T_BR, onone(), xl, Str{nullptr, 0}};
+    }
+    uint32_t eb = new_block("switch_dispatch");
+    if (m.blocks[pre].term.kind == T_NONE)
+        m.blocks[pre].term = Term{T_BR, onone(), m.blocks[eb].label, Str{nullptr, 0}};
+    uint32_t c = eb;
+    for (uint32_t q = 0; q < cblocks.n && !bad(); ++q) {
+        uint32_t d = new_val("cmp", S_BOOL);
+        cur = c;
+        emit_cmp(d, CO_EQ, sv, cvals[q]);
+        uint32_t nx = new_block("switch_next");
+        m.blocks[c].term = Term{T_CBR, ov(d), m.blocks[cblocks[q]].label,
+                                m.blocks[nx].label};
+        c = nx;
+    }
+    cur = c;
+    B().term = Term{T_BR, onone(), db >= 0 ? m.blocks[db].label : xl, Str{nullptr, 0}};
+    vars = before.copy(ar);
+    cur = xb;
+}
+
 // for loop (parser.py:2789-2900)
 OCB_HD inline void Parser::parse_for() {
     advance();
@@ -718,7 +813,7 @@ OCB_HD inline void Parser::parse_stmt_inner() {
     case TK_FOR: parse_for(); return;
     case TK_WHILE: parse_while(); return;
     case TK_DO: parse_do(); return;
-    case TK_SWITCH: unsup(); return;
+    case TK_SWITCH: parse_switch(); return;
     case TK_BREAK:
     case TK_CONTINUE: {
         bool brk = k == TK_BREAK;

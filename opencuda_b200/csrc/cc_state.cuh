@@ -8,6 +8,12 @@ namespace cc {
 
 enum { CC_STAGE_IR = 0, CC_STAGE_OPT = 1, CC_STAGE_PTX = 2 };
 
+// Minimum resident 128-thread blocks per SM requested from the compiler for
+// the parse/optimize/emit kernels (caps their registers per thread).
+#ifndef OCB_CC_MIN_BLOCKS
+#define OCB_CC_MIN_BLOCKS 1
+#endif
+
 struct TUState {
     Arena ar;    // the IR (3/4 of the slice after this header)
     Arena tmp;   // per-pass scratch (1/4)
@@ -31,6 +37,9 @@ struct CCArgs {
     uint32_t spread;             // TUs per warp (1..32): lane < spread works
     uint32_t ir_permille;        // share of a TU's slice for the IR (rest: scratch)
     uint64_t *peak;              // optional: per-TU arena bytes used (tuning)
+    char target[32];             // `.target` of the module header (NUL terminated)
+    const uint32_t *order;       // optional: TU of each thread slot (largest first)
+    SpillPool spill;             // shared overflow space of this launch
 };
 
 // TU index of this thread, or n_tu when the lane is idle
@@ -39,7 +48,9 @@ OCB_HD inline uint32_t cc_tu_index(const CCArgs &A) {
     uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
     uint32_t lane = g & 31, warp = g >> 5;
     if (lane >= A.spread) return 0xFFFFFFFFu;
-    return warp * A.spread + lane;
+    uint32_t j = warp * A.spread + lane;
+    if (j >= A.n_tu) return 0xFFFFFFFFu;
+    return A.order ? A.order[j] : j;
 #else
     return 0xFFFFFFFFu;
 #endif

@@ -1,4 +1,5 @@
 // Batch lexer for sm_100a: host driver (kernels in lex_kernels.cuh).
+#include <cstdlib>
 #include <cub/cub.cuh>
 #include <thrust/iterator/reverse_iterator.h>
 #include "ocb_internal.h"
@@ -79,12 +80,23 @@ int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d
             cub::DeviceScan::ExclusiveScan(tmp, t2, nlseg, nlcarry, SegSumOp(), (uint64_t)0, nwi, st));
     OCB_TRY("lex: sync scan", cub::DeviceScan::InclusiveScan(tmp, t3, rin, rout, MinOp(), nwi, st));
     k_set_u64<<<1, 1, 0, st>>>(S + n_win, N);
-    k_lex_tokens<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo, nlcarry,
-                                         counts, nullptr, o);
+    // OCB_LEX_MATCHER=1 selects the sequential matcher (for timing comparisons)
+    const char *mv = getenv("OCB_LEX_MATCHER");
+    bool dfa = !(mv && *mv && *mv != '0');
+    if (dfa)
+        k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                                 nlcarry, counts, nullptr, o);
+    else
+        k_lex_tokens<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                             nlcarry, counts, nullptr, o);
     k_set_u64<<<1, 1, 0, st>>>(counts + n_win, 0);
     OCB_TRY("lex: count scan", cub::DeviceScan::ExclusiveSum(tmp, t4, counts, toff, nwi + 1, st));
-    k_lex_tokens<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo, nlcarry,
-                                         nullptr, toff, o);
+    if (dfa)
+        k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                                 nlcarry, nullptr, toff, o);
+    else
+        k_lex_tokens<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                             nlcarry, nullptr, toff, o);
     k_lex_finish<<<grid_tu, 256, 0, st>>>(n_tu, errkey, unsup, d_status, d_tu_tok_off, total,
                                            d_n_tok);
     OCB_TRY("lex: launch", cudaGetLastError());
@@ -234,12 +246,12 @@ extern "C" int ocb_lex_device_static(const uint8_t *d_src, uint64_t N, const uin
         se = cub::DeviceScan::ExclusiveScan(tmp, t2, nlseg, nlcarry, SegSumOp(), (uint64_t)0, nwi, st);
     if (se == cudaSuccess) se = cub::DeviceScan::InclusiveScan(tmp, t3, rin, rout, MinOp(), nwi, st);
     k_set_u64<<<1, 1, 0, st>>>(S + n_win, N);
-    k_lex_tokens<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo, nlcarry,
-                                         counts, nullptr, o);
+    k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                             nlcarry, counts, nullptr, o);
     k_set_u64<<<1, 1, 0, st>>>(counts + n_win, 0);
     if (se == cudaSuccess) se = cub::DeviceScan::ExclusiveSum(tmp, t4, counts, toff, nwi + 1, st);
-    k_lex_tokens<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo, nlcarry,
-                                         nullptr, toff, o);
+    k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
+                                             nlcarry, nullptr, toff, o);
     k_lex_finish<<<grid_tu, 256, 0, st>>>(n_tu, errkey, unsup, d_status, d_tu_tok_off, total,
                                            d_n_tok);
     if (se != cudaSuccess || cudaGetLastError() != cudaSuccess)

@@ -18,6 +18,7 @@
 #include <string.h>
 #include "../../include/ocb.h"
 #include "lex_dfa.cuh"
+#include "lex_tokdfa.cuh"
 
 namespace ocb {
 namespace lex {
@@ -543,6 +544,180 @@ k_lex_tokens(bool write, const uint8_t *__restrict__ src, uint64_t N,
             n = lex_segment<true>(s, tu_off, n_tu, a, b, line, kw, toff[w], o);
         else
             n = lex_segment<false>(s, tu_off, n_tu, a, b, line, kw, 0, o);
+    }
+    if (!write) counts[w] = n;
+}
+
+// ---------------------------------------------------------------------------
+// token automaton (lex_tokdfa.cuh): one byte per loop iteration, the same
+// instruction stream in every lane
+// ---------------------------------------------------------------------------
+__device__ const TokDfa g_tokdfa = make_tok_dfa();
+
+struct DfaSmem {
+    uint8_t next[NQ * NB];
+    uint8_t acc[NQ];
+    uint8_t cls[256];
+};
+
+__device__ __forceinline__ void load_dfa(DfaSmem &t) {
+    const uint8_t *g = (const uint8_t *)&g_tokdfa;
+    uint8_t *d = (uint8_t *)&t;
+    static_assert(sizeof(DfaSmem) == sizeof(TokDfa), "table layout");
+    for (uint32_t i = threadIdx.x; i < sizeof(TokDfa); i += blockDim.x) d[i] = g[i];
+    __syncthreads();
+}
+
+// Source bytes through a 16-byte register window (one vector load per 16
+// bytes; the buffer is 16-byte aligned, reads stay below N).
+struct ByteWin {
+    const uint8_t *__restrict__ src;
+    uint64_t N;
+    uint64_t base;
+    uint4 w;
+    __device__ __forceinline__ uint32_t at(uint64_t q) {
+        uint64_t b = q & ~15ull;
+        if (b != base) {
+            base = b;
+            if (b + 16 <= N) {
+                w = __ldg(reinterpret_cast<const uint4 *>(src + b));
+            } else {
+                uint32_t x0 = 0, x1 = 0, x2 = 0, x3 = 0;
+                for (uint32_t j = 0; j < 16 && b + j < N; ++j) {
+                    uint32_t v = (uint32_t)__ldg(src + b + j) << (8 * (j & 3));
+                    if (j < 4) x0 |= v;
+                    else if (j < 8) x1 |= v;
+                    else if (j < 12) x2 |= v;
+                    else x3 |= v;
+                }
+                w = make_uint4(x0, x1, x2, x3);
+            }
+        }
+        uint32_t k = (uint32_t)(q >> 2) & 3u;
+        uint32_t v = k == 0 ? w.x : (k == 1 ? w.y : (k == 2 ? w.z : w.w));
+        return (v >> (8u * ((uint32_t)q & 3u))) & 0xFFu;
+    }
+};
+
+// Keyword kind of the identifier [p, p+L) (K_IDENT when it is none).
+__device__ __forceinline__ uint32_t keyword_kind(ByteWin &bw, uint64_t p, uint64_t L,
+                                                 const KwEntry *kw) {
+    if (L < 2 || L > 15) return K_IDENT;
+    uint32_t c0 = bw.at(p), cl = bw.at(p + L - 1), c2 = bw.at(p + (L > 2 ? 2 : L - 1));
+    const KwEntry &k = kw[(3u * (uint32_t)L + 47u * c0 + 16u * cl + c2) & 127u];
+    if (k.len != L) return K_IDENT;
+    for (uint64_t j = 0; j < L; ++j)
+        if ((uint8_t)k.w[j] != bw.at(p + j)) return K_IDENT;
+    return k.kind;
+}
+
+// As lex_segment, with the token automaton: tokens starting in [a, b) (a is
+// a sync point), EOF tokens of every TU that ends in (a, b] (and, for a == 0,
+// of the empty TUs at 0).  Returns the count; WRITE also stores them.
+template <bool WRITE>
+__device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off, uint32_t n_tu,
+                                uint64_t a, uint64_t b, uint32_t line, const KwEntry *kw,
+                                const DfaSmem &T, uint64_t out0, const LexOut &o) {
+    uint64_t n = 0;
+    uint32_t k = upper_bound_u64(tu_off, n_tu, a) - 1;
+    auto emit = [&](uint64_t pos, uint32_t kind, uint64_t len, uint32_t ln) {
+        if (WRITE) {
+            uint64_t i = out0 + n;
+            if (i < o.cap) {
+                o.start[i] = (uint32_t)pos;
+                o.kindlen[i] = (kind << 24) | (uint32_t)(len > 0xFFFFFFu ? 0xFFFFFFu : len);
+                if (o.line) o.line[i] = ln;
+            }
+        }
+        n++;
+    };
+    if (a == 0) {
+        for (uint32_t j = 0; j < k; ++j) {  // empty TUs at the very start
+            emit(0, K_EOF, 0, 1);
+            if (WRITE) o.tu_tok_off[j + 1] = out0 + n;
+        }
+    }
+    uint64_t e = __ldg(tu_off + k + 1);
+    uint64_t tok = a, q = a, last = a;
+    uint32_t st = Q_START, lk = 0, nl = 0, nla = 0;
+    for (;;) {
+        if (st == Q_START) {  // at a token boundary: TU ends and the segment end
+            while (tok == e && e <= b) {  // TU k ends here: its EOF token is ours
+                emit(e, K_EOF, 0, line);
+                if (WRITE) o.tu_tok_off[k + 1] = out0 + n;
+                ++k;
+                line = 1;
+                if (k >= n_tu) break;
+                e = __ldg(tu_off + k + 1);
+            }
+            if (k >= n_tu || tok >= b) break;
+        }
+        uint32_t c = q < e ? bw.at(q) : 0u;
+        uint32_t cls = q < e ? T.cls[c] : (uint32_t)B_EOT;
+        uint32_t ns = T.next[st * NB + cls];
+        if (ns != Q_DEAD) {
+            st = ns;
+            ++q;
+            nl += c == '\n';
+            uint32_t ac = T.acc[st];
+            if (ac) {
+                last = q;
+                lk = ac;
+                nla = nl;
+            }
+            continue;
+        }
+        // the automaton died: commit the longest accepted prefix
+        if (lk == 0) {
+            tok += 1;  // nothing matches here: finditer skips one character
+        } else {
+            if (lk != ACC_SKIP) {
+                uint32_t kind = lk;
+                if (WRITE) {
+                    if (kind == K_IDENT) kind = keyword_kind(bw, tok, last - tok, kw);
+                    if (kind & HEXFLOAT) {
+                        uint32_t v = hexfloat_verdict(Src{bw.src}, tok, last - tok);
+                        if (v) atomicMin(o.errkey + k, (unsigned long long)((tok << 8) | v));
+                    }
+                    if (last - tok > 0xFFFFFFu) o.unsup[k] = 1;
+                }
+                emit(tok, kind, last - tok, line);
+            }
+            if (lk != K_STRING && lk != K_CHAR) line += nla;
+            tok = last;
+        }
+        q = tok;
+        st = Q_START;
+        lk = 0;
+        nl = nla = 0;
+    }
+    return n;
+}
+
+__global__ void __launch_bounds__(BLOCK)
+k_lex_tokens_dfa(bool write, const uint8_t *__restrict__ src, uint64_t N,
+                 const uint64_t *__restrict__ tu_off, uint32_t n_tu, uint64_t n_win,
+                 const uint64_t *__restrict__ S, const uint32_t *__restrict__ sinfo,
+                 const uint64_t *__restrict__ nlcarry, uint64_t *__restrict__ counts,
+                 const uint64_t *__restrict__ toff, LexOut o) {
+    __shared__ DfaSmem T;
+    load_dfa(T);
+    const KwEntry *kw = g_kw;
+    uint64_t w = (uint64_t)blockIdx.x * BLOCK + threadIdx.x;
+    if (w >= n_win) return;
+    uint64_t a = S[w], b = S[w + 1];
+    if (a > N) a = N;
+    if (b > N) b = N;
+    uint64_t n = 0;
+    if (a < b) {
+        uint32_t si = sinfo[w];
+        uint32_t line = (si & 0x80000000u) ? 1u
+                        : 1u + (uint32_t)(nlcarry[w] & ~SEG_FLAG) + (si & 0x7FFFFFFFu);
+        ByteWin bw{src, N, ~0ull, make_uint4(0, 0, 0, 0)};
+        if (write)
+            n = dfa_segment<true>(bw, tu_off, n_tu, a, b, line, kw, T, toff[w], o);
+        else
+            n = dfa_segment<false>(bw, tu_off, n_tu, a, b, line, kw, T, 0, o);
     }
     if (!write) counts[w] = n;
 }

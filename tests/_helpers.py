@@ -302,3 +302,136 @@ def mutate_sources(n: int, seed: int):
                 t[j] = ' ' + r.choice(extra) + ' '
         out.append(''.join(t))
     return out
+
+
+SWITCH_CASES = [
+    # plain cases with breaks, default last
+    """__global__ void s0(int *o, int n) {
+    int t = threadIdx.x; int r = 0;
+    switch (t & 3) {
+    case 0: r = 10; break;
+    case 1: r = n * 2; break;
+    case 2: r = r + 5; break;
+    default: r = -1; break;
+    }
+    o[t] = r;
+}""",
+    # fallthrough chains, default in the middle, empty cases
+    """__global__ void s1(float *o, int k) {
+    int t = threadIdx.x; float a = 1.0f; int c = 0;
+    switch (k) {
+    case 1:
+    case 2: a = a * 2.0f;
+    case 3: a = a + 1.0f; c = c + 1; break;
+    default: a = 0.5f;
+    case 7: c = c + 7;
+    }
+    o[t] = a + c;
+}""",
+    # no default, switch on an expression, an empty switch
+    """__global__ void s2(int *o, int *in) {
+    int t = threadIdx.x; int v = in[t]; int acc = v;
+    switch (v * 3 + 1) { case 4: acc = acc + 1; break; case 7: acc = acc ^ 5; }
+    switch (t) { }
+    o[t] = acc;
+}""",
+    # switch in a loop: break leaves the switch, continue the loop
+    """__global__ void s3(int *o, int n) {
+    int t = threadIdx.x; int s = 0;
+    for (int i = 0; i < n; i++) {
+        switch (i & 3) {
+        case 0: s = s + i; break;
+        case 1: continue;
+        case 2: s = s * 2; if (s > 100) { s = 0; break; } s = s + 1; break;
+        default: s = s - 1;
+        }
+        s = s + 3;
+    }
+    o[t] = s;
+}""",
+    # nested switches and a loop inside a case, constant-folded switch value
+    """__global__ void s4(float *o, int a, int b) {
+    int t = threadIdx.x; float f = 0.0f; int m = 4;
+    switch (a) {
+    case 0:
+        switch (b) { case 0: f = 1.0f; break; case 1: f = 2.0f; break; default: f = 3.0f; }
+        break;
+    case 1:
+        for (int j = 0; j < 4; j++) { f = f + j; }
+        break;
+    default:
+        while (m > 0) { m = m - 1; f = f * 1.5f; }
+    }
+    switch (2) { case 2: f = f + 0.25f; break; default: f = -f; }
+    o[t] = f;
+}""",
+    # declarations inside cases, unsigned and char case labels
+    """__global__ void s5(unsigned *o, unsigned u) {
+    int t = threadIdx.x; unsigned r = 0;
+    switch (u) {
+    case 0u: { unsigned q = u + 9u; r = q * 2u; break; }
+    case 'a': r = 97u;
+    case 0x10: r = r + 16u; break;
+    }
+    o[t] = r;
+}""",
+    # break outside a loop or switch -> ParseError in the reference
+    """__global__ void s6(int *o) { int t = threadIdx.x; switch (t) { case 0: o[t] = 1; } break; }""",
+    # default only, and a return inside a case
+    """__global__ void s7(int *o, int k) {
+    int t = threadIdx.x;
+    switch (k) { default: o[t] = 3; }
+    switch (k) { case 5: return; case 6: o[t] = 6; }
+    o[t] = o[t] + 1;
+}""",
+]
+
+
+def switch_sources(n: int, seed: int):
+    """Seeded random kernels built around switch statements: nested
+    switch/if/for, fallthrough, break/continue, defaults anywhere."""
+    r = random.Random(seed)
+    out = []
+    for i in range(n):
+        ints = ["a", "b", "c"]
+        lines = [f"__global__ void sw{i}(int *o, int *in, int n) {{",
+                 "    int t = threadIdx.x;", "    int a = in[t]; int b = n; int c = 1;"]
+
+        def stmt(depth, in_loop, in_sw):
+            k = r.random()
+            v, w = r.choice(ints), r.choice(ints)
+            if depth < 3 and k < 0.3:
+                lab = r.sample(range(-2, 12), r.randint(0, 4))
+                body = [f"switch ({v} {r.choice(['&', '%', '+'])} {r.randint(1, 5)}) {{"]
+                dpos = r.randint(0, len(lab)) if r.random() < 0.6 else -1
+                for j in range(len(lab) + 1):
+                    if j == dpos:
+                        body.append("default:")
+                    elif j < len(lab):
+                        body.append(f"case {lab[j]}:")
+                    else:
+                        continue
+                    for _ in range(r.randint(0, 2)):
+                        body.extend(stmt(depth + 1, in_loop, True))
+                    if r.random() < 0.6:
+                        body.append("break;")
+                body.append("}")
+                return body
+            if depth < 3 and k < 0.4:
+                return [f"for (int i{depth} = 0; i{depth} < {r.randint(1, 5)}; i{depth}++) {{",
+                        *stmt(depth + 1, True, in_sw), "}"]
+            if depth < 3 and k < 0.5:
+                return [f"if ({v} > {w}) {{", *stmt(depth + 1, in_loop, in_sw), "} else {",
+                        *stmt(depth + 1, in_loop, in_sw), "}"]
+            if in_loop and k < 0.55:
+                return ["continue;"]
+            if (in_loop or in_sw) and k < 0.6:
+                return ["break;"]
+            return [f"{v} = {w} {r.choice(['+', '-', '*', '^'])} {r.randint(0, 9)};"]
+
+        for _ in range(r.randint(1, 4)):
+            lines.extend("    " + s for s in stmt(0, False, False))
+        lines.append("    o[t] = a + b * c;")
+        lines.append("}")
+        out.append("\n".join(lines) + "\n")
+    return out
