@@ -140,6 +140,11 @@ struct SharedInit {  // module-level __shared__ array (name, element type, count
     int64_t count;
 };
 
+struct TypedefEnt {
+    Str name;
+    Ty ty;
+};
+
 struct Parser {
     Arena &ar;
     Module &m;
@@ -155,6 +160,7 @@ struct Parser {
     Vec<uint64_t> copy_chain;  // (dest id << 32 | value index + 1) pairs
     VarMap row_strides;        // name -> Const index holding the row stride
     VarMap global_consts;      // module-level names bound to constants
+    Vec<TypedefEnt> user_typedefs;  // typedef / enum tag names of this TU, in order
     Vec<SharedInit> module_shared;
     Vec<NameSet> scopes;
     NameSet shared_scalars;
@@ -173,6 +179,7 @@ struct Parser {
         copy_chain.init();
         row_strides.init();
         global_consts.init();
+        user_typedefs.init();
         module_shared.init();
         scopes.init();
         shared_scalars.init();
@@ -519,6 +526,19 @@ struct Parser {
     OCB_HD void pop_loop();
     OCB_HD OCB_NI void parse_while();
     OCB_HD OCB_NI void parse_do();
+    OCB_HD OCB_NI void parse_enum_def();
+    OCB_HD OCB_NI void parse_typedef();
+    // a typedef of this TU (the latest binding of the name wins, as a dict
+    // assignment does in the reference)
+    OCB_HD bool user_typedef(Str v, Ty &t) const {
+        for (uint32_t i = user_typedefs.n; i-- > 0;)
+            if (eq(user_typedefs[i].name, v)) {
+                t = user_typedefs[i].ty;
+                return true;
+            }
+        return false;
+    }
+    OCB_HD void add_typedef(Str v, Ty t) { user_typedefs.push(ar, TypedefEnt{v, t}); }
     OCB_HD OCB_NI void parse_switch();
     OCB_HD OCB_NI void parse_decl(Ty ty, bool vol);
     OCB_HD OCB_NI void parse_shared(bool vol);

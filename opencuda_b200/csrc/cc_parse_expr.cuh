@@ -108,7 +108,7 @@ OCB_HD inline bool Parser::parse_type(Ty &out) {
     if (k == TK_IDENT) {
         Str v = peekv();
         Ty t;
-        if (typedef_scalar(v, t)) {
+        if (user_typedef(v, t) || typedef_scalar(v, t)) {
             advance();
             out = t;
             return true;
@@ -891,7 +891,9 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
                           pk == TK_VOLATILE;
         if (!type_ahead && pk == TK_IDENT) {
             Ty t;
-            if (typedef_scalar(peekv(), t) || vector_type_name(peekv())) type_ahead = true;
+            if (user_typedef(peekv(), t) || typedef_scalar(peekv(), t) ||
+                vector_type_name(peekv()))
+                type_ahead = true;
         }
         if (type_ahead) {
             uint32_t saved = pos;

@@ -800,7 +800,8 @@ OCB_HD inline void Parser::parse_stmt_inner() {
     bool decl = is_decl_start_kind(k);
     if (!decl && k == TK_IDENT) {
         Ty t;
-        decl = typedef_scalar(peekv(), t) || vector_type_name(peekv());
+        decl = user_typedef(peekv(), t) || typedef_scalar(peekv(), t) ||
+               vector_type_name(peekv());
     }
     if (decl) {
         Ty ty;
@@ -988,6 +989,115 @@ OCB_HD inline void Parser::parse_kernel() {
     if (B().term.kind == T_NONE) B().term = Term{T_RET, onone(), Str{nullptr, 0}, Str{nullptr, 0}};
 }
 
+// enum (parser.py:3944-3972): enumerators become module-level INT32
+// constants, folded at parse time; the tag names INT32.
+OCB_HD inline void Parser::parse_enum_def() {
+    if (!expect(TK_ENUM)) return;
+    if (at(TK_IDENT)) {
+        add_typedef(peekv(), S_INT32);
+        advance();
+    }
+    if (!expect(TK_LBRACE)) return;
+    pyint counter = 0;
+    while (!at(TK_RBRACE)) {
+        if (bad()) return;
+        if (!at(TK_IDENT)) {
+            perr();
+            return;
+        }
+        Str name = peekv();
+        advance();
+        if (match(TK_ASSIGN)) {
+            Opnd v = parse_assign_expr();
+            if (bad()) return;
+            counter = 0;  // a non-constant initializer counts as 0
+            if (v.k == O_CONST) {
+                const Const &c = m.consts[v.x];
+                if (c.pyfloat) {  // int(float): truncation
+                    if (!(c.f == c.f) || c.f >= 1e30 || c.f <= -1e30) {
+                        unsup();
+                        return;
+                    }
+                    counter = (pyint)c.f;
+                } else {
+                    counter = c.i;
+                }
+            }
+        }
+        global_consts.set(ar, name, m.cint(S_INT32, counter));
+        counter += 1;
+        if (!py_ok(counter)) {
+            unsup();
+            return;
+        }
+        if (!match(TK_COMMA)) break;
+    }
+    if (bad() || !expect(TK_RBRACE)) return;
+    match(TK_SEMI);
+}
+
+// typedef (parser.py:3974-4029): scalar and pointer aliases, enum aliases,
+// function-pointer and array typedefs (the alias names the return / element
+// type); struct and union typedefs are outside the subset.
+OCB_HD inline void Parser::parse_typedef() {
+    if (!expect(TK_TYPEDEF)) return;
+    if (at(TK_ENUM)) {
+        parse_enum_def();
+        if (bad()) return;
+        if (at(TK_IDENT)) {
+            add_typedef(peekv(), S_INT32);
+            advance();
+        }
+        match(TK_SEMI);
+        return;
+    }
+    if (at(TK_STRUCT) || at(TK_UNION)) {
+        unsup();
+        return;
+    }
+    Ty ty;
+    if (!parse_type_with_ptr(ty)) return;
+    if (at(TK_LPAREN)) {  // ret_ty (*alias)(params...)
+        advance();
+        match(TK_STAR);
+        bool named = at(TK_IDENT);
+        Str alias = named ? peekv() : Str{nullptr, 0};
+        if (named) advance();
+        match(TK_RPAREN);
+        if (at(TK_LPAREN)) {
+            int depth = 0;
+            while (!at(TK_EOF)) {
+                uint32_t kk = peek();
+                advance();
+                if (kk == TK_LPAREN) {
+                    depth++;
+                } else if (kk == TK_RPAREN) {
+                    if (--depth == 0) break;
+                }
+            }
+        }
+        match(TK_SEMI);
+        if (named) add_typedef(alias, ty);
+        return;
+    }
+    if (!at(TK_IDENT)) {
+        perr();
+        return;
+    }
+    Str alias = peekv();
+    advance();
+    if (at(TK_LBRACKET)) {  // typedef T name[N]: the dimension is parsed and dropped
+        advance();
+        if (!at(TK_RBRACKET)) {
+            parse_assign_expr();
+            if (bad()) return;
+        }
+        if (!expect(TK_RBRACKET)) return;
+    }
+    if (!expect(TK_SEMI)) return;
+    add_typedef(alias, ty);
+}
+
 // parse_module (parser.py:4194-4437): pass 1 registers module-level names and
 // records kernel positions; pass 2 parses the kernels in order.
 OCB_HD inline void Parser::parse_module() {
@@ -1072,9 +1182,12 @@ OCB_HD inline void Parser::parse_module() {
                     }
                 }
             }
-        } else if (k == TK_DEVICE || k == TK_STRUCT || k == TK_UNION || k == TK_TYPEDEF ||
-                   k == TK_ENUM || k == TK_CONSTANT) {
-            unsup();  // __device__ functions/variables, structs, typedefs, enums, __constant__
+        } else if (k == TK_TYPEDEF) {
+            parse_typedef();
+        } else if (k == TK_ENUM) {
+            parse_enum_def();
+        } else if (k == TK_DEVICE || k == TK_STRUCT || k == TK_UNION || k == TK_CONSTANT) {
+            unsup();  // __device__ functions/variables, structs, __constant__
             return;
         } else if (k == TK_SHARED) {
             advance();

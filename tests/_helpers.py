@@ -435,3 +435,99 @@ def switch_sources(n: int, seed: int):
         lines.append("}")
         out.append("\n".join(lines) + "\n")
     return out
+
+
+TYPEDEF_ENUM_CASES = [
+    # enum constants with implicit and explicit values, a tag used as a type
+    """enum Mode { M_ADD, M_MUL = 4, M_SUB, M_LAST = M_SUB + 10 };
+__global__ void e0(int *o, int k) {
+    int t = threadIdx.x; enum Mode m = M_MUL; Mode q = (Mode)k;
+    int r = (k == M_ADD) ? t + M_LAST : t * M_SUB;
+    o[t] = r + m + q;
+}""",
+    # anonymous enum, trailing comma, float and negative initializers
+    """enum { A0 = -3, A1, A2 = 2.75, A3, };
+__global__ void e1(float *o) { int t = threadIdx.x; o[t] = A0 + A1 * A2 - A3; }""",
+    # scalar and pointer typedefs, typedef of a typedef, unsigned aliases
+    """typedef float real;
+typedef unsigned int u32;
+typedef real *realp;
+typedef u32 word;
+__global__ void e2(realp out, const real *in, word n) {
+    u32 t = threadIdx.x; real s = 0.0f;
+    for (word i = 0; i < 4; i++) { s = s + in[(t + i) & 63]; }
+    if (t < n) out[t] = s * (real)2;
+}""",
+    # typedef enum with an alias, used in a switch; enum defined after the kernel
+    """typedef enum { RED, GREEN = 5, BLUE } Color;
+__global__ void e3(int *o, int k) {
+    int t = threadIdx.x; Color c = (Color)k; int v = 0;
+    switch (c) { case RED: v = LATE_A; break; case GREEN: v = 2; break; case BLUE: v = 3; break; default: v = -1; }
+    o[t] = v + LATE_B;
+}
+enum { LATE_A = 11, LATE_B };""",
+    # array typedef (dimension dropped), function-pointer typedef, redefinition
+    """typedef float vec8[8];
+typedef int (*binop)(int, int);
+typedef int T1;
+typedef double T1;
+__global__ void e4(float *o, T1 d) { int t = threadIdx.x; vec8 x = 1.5f; T1 y = d * 2.0; o[t] = x + y; }""",
+    # a typedef name shadowing a builtin typedef, sizeof of typedefs
+    """typedef long long int64_t;
+typedef unsigned char byte;
+__global__ void e5(unsigned long long *o) {
+    int t = threadIdx.x; int64_t a = t; byte b = 200;
+    o[t] = a * sizeof(int64_t) + sizeof(byte) + b;
+}""",
+    # errors: a typedef without a name, an enumerator that is not an identifier
+    """typedef float;\n__global__ void e6(float *o) { o[0] = 1.0f; }""",
+    """enum { 3, B };\n__global__ void e7(int *o) { o[0] = 1; }""",
+    # an enum that is never closed
+    """enum E { P, Q\n__global__ void e8(int *o) { o[0] = P; }""",
+]
+
+
+def typedef_enum_sources(n: int, seed: int):
+    """Seeded kernels that declare enums (tags, explicit and implicit values)
+    and scalar/pointer typedefs at module scope and use them in declarations,
+    casts and arithmetic."""
+    r = random.Random(seed)
+    scal = ["int", "unsigned int", "float", "double", "long long", "unsigned char", "short"]
+    out = []
+    for i in range(n):
+        lines, consts, types = [], [], []
+        for e in range(r.randint(1, 3)):
+            names = [f"K{i}_{e}_{j}" for j in range(r.randint(1, 5))]
+            parts = []
+            for nm in names:
+                if consts and r.random() < 0.3:
+                    parts.append(f"{nm} = {r.choice(consts)} + {r.randint(0, 9)}")
+                elif r.random() < 0.3:
+                    parts.append(f"{nm} = {r.randint(-20, 40)}")
+                else:
+                    parts.append(nm)
+                consts.append(nm)
+            tag = f"Tag{e}" if r.random() < 0.5 else ""
+            if tag:
+                types.append(f"enum {tag}" if r.random() < 0.5 else tag)
+            lines.append(f"enum {tag} {{ {', '.join(parts)} }};")
+        for d in range(r.randint(1, 3)):
+            base = r.choice(scal + [t for t in types if not t.startswith("enum")])
+            alias = f"ty{d}"
+            lines.append(f"typedef {base} {alias};")
+            types.append(alias)
+        body = ["    int t = threadIdx.x;"]
+        vars_ = ["t"]
+        for s in range(r.randint(2, 8)):
+            ty = r.choice(types + ["int", "float"])
+            e1 = r.choice(consts + vars_)
+            e2 = r.choice(consts + vars_)
+            expr = f"({ty})({e1} {r.choice(['+', '-', '*'])} {e2})"
+            body.append(f"    {ty} v{s} = {expr};")
+            vars_.append(f"v{s}")
+        body.append(f"    o[t] = {' + '.join(vars_[-4:])};")
+        lines.append(f"__global__ void te{i}(float *o) {{")
+        lines.extend(body)
+        lines.append("}")
+        out.append("\n".join(lines) + "\n")
+    return out

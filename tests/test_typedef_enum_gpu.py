@@ -1,0 +1,31 @@
+"""`enum` and `typedef` at module scope (parser.py:3944-4029) on the GPU:
+hand cases (tags as types, explicit / implicit / float / expression values,
+pointer, function-pointer and array typedefs, redefinitions, a typedef enum
+used in a switch, malformed definitions) and seeded random ones, compared
+with the live reference as parsed IR, optimized IR and PTX."""
+import pytest
+
+from oracle import ref_runner
+from opencuda_b200.api import TU_UNSUPPORTED
+from tests._helpers import TYPEDEF_ENUM_CASES, typedef_enum_sources
+
+pytestmark = pytest.mark.gpu
+
+RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError": 4}
+
+
+@pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
+def test_typedef_enum_against_live_reference(ctx, stage):
+    srcs = TYPEDEF_ENUM_CASES + typedef_enum_sources(300, 23)
+    fn = {"ir": ctx.parse_batch, "opt": ctx.optimize_batch, "ptx": ctx.compile_batch}[stage]
+    tb = fn(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=(stage,), chunksize=4)
+    for i, (s, r) in enumerate(zip(srcs, ref)):
+        st = int(tb.status[i])
+        assert st != TU_UNSUPPORTED, (i, s[:300])
+        if stage not in r:
+            assert st == RAISE_STATUS.get(r["error"][0], 6), (i, r["error"], st)
+            continue
+        assert st == 0, (i, st, s[:300])
+        assert tb.text(i) == r[stage], (i, s)
