@@ -145,6 +145,15 @@ struct TypedefEnt {
     Ty ty;
 };
 
+// A __device__ function kept as a token range and expanded at each call
+// (parser.py:4031-4087, _device_funcs).
+struct DevFunc {
+    Str name;
+    Ty ret;
+    Vec<Param> params;
+    uint32_t body_start, body_end;  // the body's '{' ... one past its '}'
+};
+
 struct Parser {
     Arena &ar;
     Module &m;
@@ -161,6 +170,10 @@ struct Parser {
     VarMap row_strides;        // name -> Const index holding the row stride
     VarMap global_consts;      // module-level names bound to constants
     Vec<TypedefEnt> user_typedefs;  // typedef / enum tag names of this TU, in order
+    Vec<DevFunc> dfuncs;            // __device__ functions, in definition order
+    int32_t inline_dest;            // value receiving `return` inside an inlined body, or -1
+    Str inline_merge;               // label that `return` branches to while inlining
+    uint32_t inline_depth;
     Vec<SharedInit> module_shared;
     Vec<NameSet> scopes;
     NameSet shared_scalars;
@@ -180,6 +193,10 @@ struct Parser {
         row_strides.init();
         global_consts.init();
         user_typedefs.init();
+        dfuncs.init();
+        inline_dest = -1;
+        inline_merge = Str{nullptr, 0};
+        inline_depth = 0;
         module_shared.init();
         scopes.init();
         shared_scalars.init();
@@ -267,13 +284,14 @@ struct Parser {
     }
 
     // ---- IR helpers ----------------------------------------------------------
-    OCB_HD uint32_t new_block(const char *prefix) {
+    OCB_HD uint32_t new_block(const char *prefix) { return new_block(S(prefix)); }
+    OCB_HD uint32_t new_block(Str prefix) {
         block_count++;
         if (!kern) {  // outside a kernel: AttributeError
             raise_(R_OTHER);
             return cur;
         }
-        Str lab = cat(ar, S(prefix), S("_"), utoa(ar, block_count));
+        Str lab = cat(ar, prefix, S("_"), utoa(ar, block_count));
         uint32_t b = m.new_block(lab);
         kern->blocks.push(ar, b);
         return b;
@@ -539,6 +557,16 @@ struct Parser {
         return false;
     }
     OCB_HD void add_typedef(Str v, Ty t) { user_typedefs.push(ar, TypedefEnt{v, t}); }
+    OCB_HD OCB_NI void parse_device_func();
+    OCB_HD OCB_NI Opnd inline_call(uint32_t fi, Vec<Opnd> &args, Str name);
+    OCB_HD OCB_NI bool dfunc_cycle();
+    // the definition a call resolves to (a later definition replaces an
+    // earlier one, as a dict assignment does)
+    OCB_HD int32_t find_dfunc(Str v) const {
+        for (uint32_t i = dfuncs.n; i-- > 0;)
+            if (eq(dfuncs[i].name, v)) return (int32_t)i;
+        return -1;
+    }
     OCB_HD OCB_NI void parse_switch();
     OCB_HD OCB_NI void parse_decl(Ty ty, bool vol);
     OCB_HD OCB_NI void parse_shared(bool vol);

@@ -993,8 +993,10 @@ OCB_HD inline Opnd Parser::parse_call(Str name) {
         unsup();  // texture/surface/TMA/mbarrier intrinsics and printf
         return onone();
     }
-    // generic intrinsic call (parser.py:1929-2138); __device__ functions never
-    // reach here because a TU that defines one is outside the subset
+    // __device__ functions: expanded in place (parser.py:1749-1929)
+    int32_t fi = find_dfunc(name);
+    if (fi >= 0) return inline_call((uint32_t)fi, args, name);
+    // generic intrinsic call (parser.py:1929-2138)
     if (in_list(name, kVoidStmts) || eq(name, "__syncwarp")) {
         call(-1, name);
         return m.cint(S_VOID, 0);

@@ -837,6 +837,13 @@ OCB_HD inline void Parser::parse_stmt_inner() {
             rv = parse_expr();
             if (bad() || !expect(TK_SEMI)) return;
         }
+        if (inline_dest >= 0) {  // inside an inlined __device__ body (parser.py:3150-3189)
+            if (rv.k != O_NONE)
+                emit_bin((uint32_t)inline_dest, BO_ADD, rv, m.czero(m.vals[inline_dest].ty));
+            B().term = Term{T_BR, onone(), inline_merge, Str{nullptr, 0}};
+            cur = new_block("after_inline_return");
+            return;
+        }
         B().term = Term{T_RET, rv, Str{nullptr, 0}, Str{nullptr, 0}};
         return;
     }
@@ -1098,6 +1105,149 @@ OCB_HD inline void Parser::parse_typedef() {
     add_typedef(alias, ty);
 }
 
+// __device__ function definition (parser.py:4031-4087): signature, then the
+// body is skipped and kept as a token range for inlining.
+OCB_HD inline void Parser::parse_device_func() {
+    if (!expect(TK_DEVICE)) return;
+    while (at(TK_DEVICE) || at(TK_STATIC) ||
+           (at(TK_IDENT) && in_list(peekv(), " __noinline__ __forceinline__ __inline__ "
+                                             "__attribute__ __cdecl__ __stdcall__ __fastcall__ ")))
+        advance();
+    if (bad()) return;
+    Ty rt;
+    if (!parse_type_with_ptr(rt)) return;
+    if (!at(TK_IDENT)) {
+        perr();
+        return;
+    }
+    Str name = peekv();
+    advance();
+    if (!expect(TK_LPAREN)) return;
+    Vec<Param> params;
+    params.init();
+    if (at(TK_VOID) && kind_at(pos + 1) == TK_RPAREN) advance();
+    if (bad()) return;
+    if (!at(TK_RPAREN)) {
+        for (;;) {
+            Ty pty;
+            if (!parse_type_with_ptr(pty)) return;
+            Str pname;
+            if (!expect_ident(pname)) return;
+            if (at(TK_LBRACKET)) {  // array parameter decaying to a pointer
+                unsup();
+                return;
+            }
+            params.push(ar, Param{pname, pty});
+            if (!match(TK_COMMA)) break;
+        }
+    }
+    if (bad() || !expect(TK_RPAREN)) return;
+    if (match(TK_SEMI)) return;  // a prototype registers nothing
+    uint32_t bs = pos;
+    if (!expect(TK_LBRACE)) return;
+    int depth = 1;
+    while (depth > 0) {
+        uint32_t kk = peek();
+        if (bad()) return;
+        if (kk == TK_EOF) {  // unterminated body: the reference never returns
+            unsup();
+            return;
+        }
+        if (kk == TK_LBRACE) depth++;
+        if (kk == TK_RBRACE) depth--;
+        advance();
+    }
+    dfuncs.push(ar, DevFunc{name, rt, params, bs, pos});
+}
+
+// Recursion (parser.py:4396-4431): a call graph over the identifiers in each
+// body; any cycle means functions the reference compiles as .func, which
+// this engine does not.
+OCB_HD inline bool Parser::dfunc_cycle() {
+    uint32_t n = dfuncs.n;
+    if (!n) return false;
+    // state per function: 0 unvisited, 1 on the path, 2 done (iterative DFS)
+    uint8_t *color = (uint8_t *)ar.alloc(n, 1);
+    uint32_t *stack = (uint32_t *)ar.alloc(4ull * n, 4);
+    uint32_t *scan = (uint32_t *)ar.alloc(4ull * n, 4);
+    if (!color || !stack || !scan) return false;
+    for (uint32_t i = 0; i < n; ++i) color[i] = 0;
+    for (uint32_t root = 0; root < n; ++root) {
+        if (color[root] || find_dfunc(dfuncs[root].name) != (int32_t)root) continue;
+        uint32_t sp = 0;
+        stack[sp] = root;
+        scan[sp] = dfuncs[root].body_start;
+        color[root] = 1;
+        ++sp;
+        while (sp) {
+            uint32_t f = stack[sp - 1];
+            uint32_t &q = scan[sp - 1];
+            int32_t callee = -1;
+            while (q < dfuncs[f].body_end && q < tk.n) {
+                uint32_t t = q++;
+                if (kind_at(t) != TK_IDENT) continue;
+                callee = find_dfunc(val_at(t));
+                if (callee >= 0) break;
+            }
+            if (callee < 0) {
+                color[f] = 2;
+                --sp;
+                continue;
+            }
+            if (color[callee] == 1) return true;
+            if (color[callee] == 0) {
+                color[callee] = 1;
+                stack[sp] = (uint32_t)callee;
+                scan[sp] = dfuncs[callee].body_start;
+                ++sp;
+            }
+        }
+    }
+    return false;
+}
+
+// Call of a __device__ function (parser.py:1749-1929, scalar form): the
+// arguments bind the parameter names, the body is parsed again in place with
+// `return` writing `<name>_ret` and branching to `inline_<name>_merge`, and
+// the caller's variables are restored afterwards.
+OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
+    if (inline_depth >= 16) {
+        unsup();
+        return onone();
+    }
+    DevFunc f = dfuncs[fi];
+    VarMap saved_vars = vars.copy(ar);
+    uint32_t saved_pos = pos;
+    int32_t saved_dest = inline_dest;
+    Str saved_merge = inline_merge;
+    for (uint32_t k = 0; k < f.params.n && k < args.n; ++k) vars.set(ar, f.params[k].name, args[k]);
+    uint32_t rd = new_val(cat(ar, name, S("_ret")), f.ret);
+    uint32_t mb = new_block(cat(ar, S("inline_"), name, S("_merge")));
+    if (bad()) return onone();
+    inline_dest = (int32_t)rd;
+    inline_merge = m.blocks[mb].label;
+    Vec<NameSet> saved_scopes = scopes;
+    scopes.init();
+    ++inline_depth;
+    pos = f.body_start;
+    if (!expect(TK_LBRACE)) return onone();
+    while (!at(TK_RBRACE)) {
+        if (bad()) return onone();
+        parse_stmt();
+        if (bad()) return onone();
+    }
+    advance();
+    --inline_depth;
+    if (B().term.kind == T_NONE) B().term = Term{T_BR, onone(), m.blocks[mb].label, Str{nullptr, 0}};
+    cur = mb;
+    pos = saved_pos;
+    vars = saved_vars;
+    inline_dest = saved_dest;
+    inline_merge = saved_merge;
+    scopes = saved_scopes;
+    return ov(rd);
+}
+
 // parse_module (parser.py:4194-4437): pass 1 registers module-level names and
 // records kernel positions; pass 2 parses the kernels in order.
 OCB_HD inline void Parser::parse_module() {
@@ -1186,8 +1336,24 @@ OCB_HD inline void Parser::parse_module() {
             parse_typedef();
         } else if (k == TK_ENUM) {
             parse_enum_def();
-        } else if (k == TK_DEVICE || k == TK_STRUCT || k == TK_UNION || k == TK_CONSTANT) {
-            unsup();  // __device__ functions/variables, structs, __constant__
+        } else if (k == TK_DEVICE) {
+            // a function when '(' comes before ';' (parser.py:4282-4304)
+            bool is_func = false;
+            for (uint32_t la = pos + 1; la < tk.n; ++la) {
+                uint32_t lk = kind_at(la);
+                if (lk == TK_LPAREN) {
+                    is_func = true;
+                    break;
+                }
+                if (lk == TK_SEMI || lk == TK_EOF) break;
+            }
+            if (!is_func) {
+                unsup();  // __device__ variables
+                return;
+            }
+            parse_device_func();
+        } else if (k == TK_STRUCT || k == TK_UNION || k == TK_CONSTANT) {
+            unsup();  // structs, __constant__
             return;
         } else if (k == TK_SHARED) {
             advance();
@@ -1211,6 +1377,10 @@ OCB_HD inline void Parser::parse_module() {
         }
     }
     if (bad()) return;
+    if (dfunc_cycle()) {  // recursive __device__ functions (.func) are outside the subset
+        unsup();
+        return;
+    }
     for (uint32_t i = 0; i < kpos.n && !bad(); ++i) {
         pos = kpos[i];
         parse_kernel();

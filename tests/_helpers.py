@@ -531,3 +531,107 @@ def typedef_enum_sources(n: int, seed: int):
         lines.append("}")
         out.append("\n".join(lines) + "\n")
     return out
+
+
+DEVFUNC_CASES = [
+    # scalar helper with one return
+    """__device__ float sq(float x) { return x * x; }
+__global__ void d0(float *o, const float *in) { int t = threadIdx.x; o[t] = sq(in[t]) + sq(2.0f); }""",
+    # several returns, called in a loop and in a condition
+    """__device__ int clampi(int v, int lo, int hi) {
+    if (v < lo) return lo;
+    if (v > hi) return hi;
+    return v;
+}
+__global__ void d1(int *o, int n) {
+    int t = threadIdx.x; int s = 0;
+    for (int i = 0; i < 8; i++) { s = s + clampi(t - i, 0, n); }
+    if (clampi(s, 0, 100) > 50) s = s * 2;
+    o[t] = s;
+}""",
+    # void helper writing through a pointer, early `return;`
+    """__device__ void put(float *p, int i, float v) {
+    if (i < 0) return;
+    p[i] = v * 0.5f;
+}
+__global__ void d2(float *o, int n) { int t = threadIdx.x; put(o, t - 3, 1.0f); put(o, n, 2.0f); }""",
+    # nested calls, callee defined after the caller, qualifiers and a prototype
+    """__device__ float g(float x);
+__device__ __forceinline__ float f(float a, float b) { return g(a) * b + g(b); }
+static __device__ float g(float x) { return x + 1.0f; }
+__global__ void d3(float *o, float k) { int t = threadIdx.x; o[t] = f(f(k, 2.0f), g(k)); }""",
+    # locals named like the caller's, a loop inside the helper, threadIdx inside
+    """__device__ int acc(int n) {
+    int s = 0;
+    for (int i = 0; i < n; i++) { s = s + i * threadIdx.x; }
+    return s;
+}
+__global__ void d4(int *o) {
+    int s = 7; int i = 3;
+    int r = acc(4) + acc(i);
+    o[threadIdx.x] = r + s + i;
+}""",
+    # double and unsigned helpers, a helper used in a switch and a ternary
+    """__device__ double lerp(double a, double b, double t) { return a + (b - a) * t; }
+__device__ unsigned mix(unsigned x) { return (x ^ (x >> 3)) * 2654435761u; }
+__global__ void d5(double *o, unsigned k) {
+    int t = threadIdx.x; double v = 0.0;
+    switch (mix(k) & 3u) { case 0: v = lerp(1.0, 2.0, 0.25); break; default: v = lerp(0.0, 8.0, 0.5); }
+    o[t] = (mix(t) > 100u) ? v : -v;
+}""",
+    # a helper that only declares, and one returning a pointer
+    """__device__ void nothing(int x) { int y = x + 1; }
+__device__ float *at(float *p, int i) { return p + i; }
+__global__ void d6(float *o) { int t = threadIdx.x; nothing(t); *at(o, t) = 3.0f; }""",
+]
+
+# recursive __device__ functions: the reference emits .func bodies for them
+DEVFUNC_RECURSIVE_CASES = [
+    """__device__ int fact(int n) { if (n <= 1) return 1; return n * fact(n - 1); }
+__global__ void r0(int *o) { o[threadIdx.x] = fact(threadIdx.x & 7); }""",
+    """__device__ int ping(int n);
+__device__ int pong(int n) { return n <= 0 ? 0 : ping(n - 1) + 1; }
+__device__ int ping(int n) { return n <= 0 ? 0 : pong(n - 1) + 2; }
+__global__ void r1(int *o) { o[threadIdx.x] = ping(5); }""",
+]
+
+
+def devfunc_sources(n: int, seed: int):
+    """Seeded kernels calling chains of small scalar __device__ helpers
+    (several returns, loops, nested calls, helpers defined before or after
+    their callers)."""
+    r = random.Random(seed)
+    out = []
+    for i in range(n):
+        nf = r.randint(1, 4)
+        funcs = []
+        for j in range(nf):
+            ty = r.choice(["int", "float", "unsigned int"])
+            name = f"h{i}_{j}"
+            body = [f"__device__ {ty} {name}({ty} a, {ty} b) {{"]
+            body.append(f"    {ty} c = a {r.choice(['+', '-', '*'])} b;")
+            if r.random() < 0.5:
+                body.append(f"    if (c > ({ty}){r.randint(0, 50)}) return c {r.choice(['+', '*'])} a;")
+            if r.random() < 0.4:
+                body.append(f"    for (int k = 0; k < {r.randint(1, 4)}; k++) {{ c = c + ({ty})k; }}")
+            if j > 0 and r.random() < 0.6:
+                callee = funcs[r.randrange(j)][0]
+                body.append(f"    c = c + ({ty}){callee}(({funcs[r.randrange(j)][1]})a, "
+                            f"({funcs[r.randrange(j)][1]})b);")
+            body.append(f"    return c {r.choice(['+', '-', '^'] if ty != 'float' else ['+', '-'])} b;")
+            body.append("}")
+            funcs.append((name, ty, "\n".join(body)))
+        order = funcs[:]
+        if r.random() < 0.3:  # define callees after callers, with prototypes first
+            protos = [f"__device__ {ty} {nm}({ty} a, {ty} b);" for nm, ty, _ in funcs]
+            text = "\n".join(protos) + "\n" + "\n".join(b for _, _, b in reversed(order))
+        else:
+            text = "\n".join(b for _, _, b in order)
+        calls = []
+        for k in range(r.randint(1, 4)):
+            nm, ty, _ = r.choice(funcs)
+            calls.append(f"    {ty} v{k} = {nm}(({ty})(t + {k}), ({ty})in[t & 63]);")
+        kern = [f"__global__ void dk{i}(float *o, const int *in) {{", "    int t = threadIdx.x;",
+                *calls, f"    o[t] = {' + '.join(f'(float)v{k}' for k in range(len(calls)))};", "}"]
+        out.append(text + "\n" + "\n".join(kern) + "\n")
+    return out
