@@ -715,7 +715,7 @@ OCB_HD inline Opnd Parser::parse_postfix_expr() {
 
 // Correctly rounded decimal -> double for literals the fast path covers
 // (Clinger: <= 15 significant digits... up to 2^53, |exponent| <= 22).
-OCB_HD inline bool parse_decimal(Str s, double &out) {
+OCB_HD inline bool parse_decimal_fast(Str s, double &out) {
     uint64_t mant = 0;
     int digits = 0, exp10 = 0;
     uint32_t i = 0;
@@ -760,6 +760,171 @@ OCB_HD inline bool parse_decimal(Str s, double &out) {
     double v = (double)mant;
     out = exp10 >= 0 ? v * p10[exp10] : v / p10[-exp10];
     return true;
+}
+
+// Exact decimal -> double, round half to even, for every literal the lexer
+// accepts ([0-9]*.?[0-9]*([eE][+-]?[0-9]+)?): the value N * 10^E is formed
+// with big integers (N: the significant digits, at most 60 of them), scaled
+// by 2^s and divided by 10^-E when E < 0, then rounded to 53 bits or to the
+// subnormal grid -- the result Python's float() gives.  Only literals the
+// fast path above cannot take come here.
+struct BigU {
+    static constexpr int W = 56;   // 32-bit words: 1792 bits
+    uint32_t w[W];
+    int n;                         // words in use (no leading zero words)
+    OCB_HD void set(uint32_t v) { n = v ? 1 : 0; w[0] = v; }
+    OCB_HD bool mul_add(uint32_t m, uint32_t a) {
+        uint64_t c = a;
+        for (int i = 0; i < n; ++i) {
+            uint64_t t = (uint64_t)w[i] * m + c;
+            w[i] = (uint32_t)t;
+            c = t >> 32;
+        }
+        if (c) {
+            if (n >= W) return false;
+            w[n++] = (uint32_t)c;
+        }
+        return true;
+    }
+    OCB_HD int bits() const {
+        if (!n) return 0;
+        uint32_t t = w[n - 1];
+        int b = 0;
+        while (t) { ++b; t >>= 1; }
+        return (n - 1) * 32 + b;
+    }
+    OCB_HD bool bit(int i) const { return i >= 0 && i / 32 < n && ((w[i / 32] >> (i % 32)) & 1u); }
+    OCB_HD bool any_below(int i) const {  // a set bit at a position < i
+        for (int k = 0; k < n && k * 32 < i; ++k) {
+            uint32_t m = (i - k * 32 >= 32) ? 0xFFFFFFFFu : ((1u << (i - k * 32)) - 1u);
+            if (w[k] & m) return true;
+        }
+        return false;
+    }
+    OCB_HD uint64_t bits_from(int i, int cnt) const {  // cnt <= 54 bits starting at bit i
+        uint64_t r = 0;
+        for (int j = cnt - 1; j >= 0; --j) r = (r << 1) | (bit(i + j) ? 1u : 0u);
+        return r;
+    }
+    OCB_HD bool shl1_or(uint32_t b) {
+        uint32_t c = b;
+        for (int i = 0; i < n; ++i) {
+            uint32_t nc = w[i] >> 31;
+            w[i] = (w[i] << 1) | c;
+            c = nc;
+        }
+        if (c) {
+            if (n >= W) return false;
+            w[n++] = c;
+        }
+        return true;
+    }
+    OCB_HD int cmp(const BigU &o) const {
+        if (n != o.n) return n < o.n ? -1 : 1;
+        for (int i = n - 1; i >= 0; --i)
+            if (w[i] != o.w[i]) return w[i] < o.w[i] ? -1 : 1;
+        return 0;
+    }
+    OCB_HD void sub(const BigU &o) {  // *this -= o, *this >= o
+        int64_t br = 0;
+        for (int i = 0; i < n; ++i) {
+            int64_t t = (int64_t)w[i] - (i < o.n ? o.w[i] : 0) - br;
+            br = t < 0;
+            w[i] = (uint32_t)(t + (br << 32));
+        }
+        while (n && !w[n - 1]) --n;
+    }
+};
+
+OCB_HD inline bool parse_decimal_exact(Str s, double &out) {
+    BigU N;
+    N.set(0);
+    int nd = 0, exp10 = 0;
+    uint32_t i = 0;
+    bool any = false, dot = false;
+    for (; i < s.n; ++i) {
+        char c = s.p[i];
+        if (c == '.' && !dot) { dot = true; continue; }
+        if (c < '0' || c > '9') break;
+        any = true;
+        if (dot) --exp10;
+        if (nd == 0 && c == '0') continue;
+        if (++nd > 60) return false;
+        if (!N.mul_add(10, (uint32_t)(c - '0'))) return false;
+    }
+    if (!any) return false;
+    if (i < s.n && (s.p[i] == 'e' || s.p[i] == 'E')) {
+        ++i;
+        bool neg = false;
+        if (i < s.n && (s.p[i] == '+' || s.p[i] == '-')) neg = s.p[i++] == '-';
+        int e = 0;
+        bool ed = false;
+        for (; i < s.n && s.p[i] >= '0' && s.p[i] <= '9'; ++i) {
+            ed = true;
+            if (e < 100000) e = e * 10 + (s.p[i] - '0');
+        }
+        if (!ed) return false;
+        exp10 += neg ? -e : e;
+    }
+    if (i != s.n) return false;
+    if (!N.n) { out = 0.0; return true; }
+    if (exp10 + nd > 310) {  // beyond DBL_MAX: inf
+        uint64_t inf_bits = 0x7FF0000000000000ull;
+        memcpy(&out, &inf_bits, 8);
+        return true;
+    }
+    if (exp10 + nd < -326) { out = 0.0; return true; }       // below half the least subnormal
+    BigU Q;  // q = N * 10^E, or floor(N * 2^sh / 10^-E)
+    int sh = 0;
+    bool sticky = false;
+    if (exp10 >= 0) {
+        Q = N;
+        for (int k = 0; k < exp10; ++k)
+            if (!Q.mul_add(10, 0)) return false;
+    } else {
+        BigU D;
+        D.set(1);
+        for (int k = 0; k < -exp10; ++k)
+            if (!D.mul_add(10, 0)) return false;
+        sh = D.bits() - N.bits() + 56;
+        if (sh < 0) sh = 0;
+        // long division of N * 2^sh by D, one quotient bit at a time
+        BigU R;
+        R.set(0);
+        Q.set(0);
+        int nb = N.bits() + sh;
+        for (int b = nb - 1; b >= 0; --b) {
+            uint32_t nbit = (b >= sh && N.bit(b - sh)) ? 1u : 0u;
+            if (!R.shl1_or(nbit)) return false;
+            uint32_t qb = 0;
+            if (R.cmp(D) >= 0) {
+                R.sub(D);
+                qb = 1;
+            }
+            if (!Q.shl1_or(qb)) return false;
+        }
+        sticky = R.n != 0;
+    }
+    // value = Q * 2^-sh (+ sticky); keep 53 bits or stop at 2^-1074
+    int lq = Q.bits();
+    int drop = lq - 53;
+    if (drop < sh - 1074) drop = sh - 1074;
+    uint64_t mant;
+    if (drop <= 0) {
+        mant = Q.bits_from(0, lq);
+        out = ldexp((double)mant, -sh);
+        return true;
+    }
+    mant = Q.bits_from(drop, lq - drop);
+    bool half = Q.bit(drop - 1);
+    bool rest = sticky || Q.any_below(drop - 1);
+    if (half && (rest || (mant & 1))) ++mant;
+    out = ldexp((double)mant, drop - sh);
+    return true;
+}
+
+OCB_HD inline bool parse_decimal(Str s, double &out) {
+    return parse_decimal_fast(s, out) || parse_decimal_exact(s, out);
 }
 
 // _parse_primary_expr (parser.py:1532-2249)
