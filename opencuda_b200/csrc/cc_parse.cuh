@@ -557,6 +557,7 @@ struct Parser {
         return false;
     }
     OCB_HD void add_typedef(Str v, Ty t) { user_typedefs.push(ar, TypedefEnt{v, t}); }
+    OCB_HD OCB_NI Opnd spill_scalar(Str name, Opnd value);
     OCB_HD OCB_NI void parse_device_func();
     OCB_HD OCB_NI Opnd inline_call(uint32_t fi, Vec<Opnd> &args, Str name);
     OCB_HD OCB_NI bool dfunc_cycle();

@@ -456,6 +456,34 @@ OCB_HD inline Opnd Parser::parse_mul_expr() {
     return lhs;
 }
 
+// &x of a scalar (parser.py:1054-1069, 1156-1170): the slot `_spill_<x>` is
+// a .local declaration of one element, made on first use and kept in the
+// variable table; each `&` stores the current value into it.  Later reads of
+// x do not see writes through the pointer, except after an inlined call that
+// received it (inline_call reloads those).
+OCB_HD inline Opnd Parser::spill_scalar(Str name, Opnd value) {
+    Str sn = cat(ar, S("_spill_"), name);
+    Opnd *sp = vars.get(sn);
+    Opnd slot;
+    if (sp) {
+        slot = *sp;
+    } else {
+        Ty vt = tyof(value);
+        bool ok = true;
+        Ty lt = ty_ptr(vt, AS_LOCAL, false, ok);
+        if (!ok) {
+            unsup();
+            return onone();
+        }
+        uint32_t v = new_val(sn, lt);
+        slot = ov(v);
+        vars.set(ar, sn, slot);
+        kern->locals.push(ar, LocalDecl{sn, vt, 1, v});
+    }
+    emit_store(slot, value);
+    return slot;
+}
+
 // _parse_unary_expr (parser.py:972-1287)
 OCB_HD inline Opnd Parser::parse_unary_expr() {
     if (++nest > MAX_NEST) { unsup(); --nest; return onone(); }
@@ -491,8 +519,9 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
                         r = var;
                         goto out;
                     }
-                } else {
-                    unsup();  // &scalar spills to .local
+                } else {  // &scalar: spilled to a one-element .local slot
+                    advance();
+                    r = spill_scalar(name, var);
                     goto out;
                 }
             }
@@ -501,7 +530,10 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
             Opnd o = parse_unary_expr();
             if (bad()) goto out;
             if (o.k == O_VAL && is_ptr(tyof(o))) { r = o; goto out; }
-            if (o.k == O_VAL) { unsup(); goto out; }
+            if (o.k == O_VAL && kern) {  // &expr of a scalar value: spilled too
+                r = spill_scalar(vname(o), o);
+                goto out;
+            }
             r = o;
             goto out;
         }

@@ -1220,6 +1220,28 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
     uint32_t saved_pos = pos;
     int32_t saved_dest = inline_dest;
     Str saved_merge = inline_merge;
+    // caller variables passed as &x: reloaded from their slot afterwards
+    struct Spilled {
+        Str name;
+        Ty ty;
+        Opnd slot;
+    };
+    Vec<Spilled> spilled;
+    spilled.init();
+    for (uint32_t k = 0; k < args.n; ++k) {
+        Opnd a = args[k];
+        if (a.k != O_VAL || !is_ptr(tyof(a)) || ty_as(tyof(a)) != AS_LOCAL) continue;
+        for (uint32_t q = 0; q < saved_vars.e.n; ++q) {
+            const VarEnt &ve = saved_vars.e[q];
+            if (!ve.live || !starts(ve.name, "_spill_") || ve.v.k != O_VAL ||
+                m.vals[ve.v.x].id != m.vals[a.x].id)
+                continue;
+            Str orig = Str{ve.name.p + 7, ve.name.n - 7};
+            Opnd *ov0 = saved_vars.get(orig);
+            if (ov0 && ov0->k == O_VAL) spilled.push(ar, Spilled{orig, tyof(*ov0), a});
+            break;
+        }
+    }
     for (uint32_t k = 0; k < f.params.n && k < args.n; ++k) vars.set(ar, f.params[k].name, args[k]);
     uint32_t rd = new_val(cat(ar, name, S("_ret")), f.ret);
     uint32_t mb = new_block(cat(ar, S("inline_"), name, S("_merge")));
@@ -1242,6 +1264,11 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
     cur = mb;
     pos = saved_pos;
     vars = saved_vars;
+    for (uint32_t k = 0; k < spilled.n && !bad(); ++k) {
+        uint32_t u = new_val(spilled[k].name, spilled[k].ty);
+        emit_load(u, spilled[k].slot);
+        vars.set(ar, spilled[k].name, ov(u));
+    }
     inline_dest = saved_dest;
     inline_merge = saved_merge;
     scopes = saved_scopes;

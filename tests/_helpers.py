@@ -635,3 +635,40 @@ def devfunc_sources(n: int, seed: int):
                 *calls, f"    o[t] = {' + '.join(f'(float)v{k}' for k in range(len(calls)))};", "}"]
         out.append(text + "\n" + "\n".join(kern) + "\n")
     return out
+
+
+ADDR_OF_CASES = [
+    # out-parameters through device helpers, reloaded after the call
+    """__device__ void divmod(int a, int b, int *q, int *r) { *q = a / b; *r = a - (a / b) * b; }
+__global__ void a0(int *o, int n) {
+    int t = threadIdx.x; int q = 0; int r = 0;
+    divmod(t + n, 7, &q, &r);
+    o[t] = q * 10 + r;
+}""",
+    # the same variable spilled twice, read through the pointer, a float slot
+    """__device__ void bump(float *p, float d) { *p = *p + d; }
+__global__ void a1(float *o) {
+    int t = threadIdx.x; float acc = 1.0f;
+    bump(&acc, 2.0f);
+    bump(&acc, (float)t);
+    float *pa = &acc;
+    o[t] = acc + *pa;
+}""",
+    # &x without a call: later reads keep the old value, writes go to the slot
+    """__global__ void a2(int *o) {
+    int t = threadIdx.x; int x = t * 3;
+    int *p = &x;
+    *p = 5;
+    o[t] = x + *p;
+}""",
+    # &(expression) spills the value of the expression
+    """__device__ int twice(int *p) { return *p * 2; }
+__global__ void a3(int *o, int k) { int t = threadIdx.x; o[t] = twice(&k) + twice(&t); }""",
+    # & in a loop and in a branch
+    """__device__ void inc(int *p) { *p = *p + 1; }
+__global__ void a4(int *o, int n) {
+    int t = threadIdx.x; int c = 0;
+    for (int i = 0; i < 4; i++) { if (i < n) inc(&c); }
+    o[t] = c;
+}""",
+]
