@@ -599,24 +599,51 @@ struct ByteWin {
     }
 };
 
-// Keyword kind of the identifier [p, p+L) (K_IDENT when it is none).
-__device__ __forceinline__ uint32_t keyword_kind(ByteWin &bw, uint64_t p, uint64_t L,
-                                                 const KwEntry *kw) {
+// Keyword table packed for register compares: the spelling as two 64-bit
+// little-endian words (bytes past the length are zero).
+struct KwPacked {
+    uint64_t lo, hi;
+    uint32_t len, kind;
+};
+
+__device__ __forceinline__ void load_kw_packed(KwPacked *t, const KwEntry *kw) {
+    for (uint32_t i = threadIdx.x; i < 128; i += blockDim.x) {
+        uint64_t lo = 0, hi = 0;
+        for (uint32_t j = 0; j < 16; ++j) {
+            uint64_t c = j < kw[i].len ? (uint8_t)kw[i].w[j] : 0;
+            if (j < 8) lo |= c << (8 * j);
+            else hi |= c << (8 * (j - 8));
+        }
+        t[i] = KwPacked{lo, hi, kw[i].len, kw[i].kind};
+    }
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint64_t lo, uint64_t hi, uint32_t j) {
+    return (uint32_t)((j < 8 ? lo >> (8 * j) : hi >> (8 * (j - 8))) & 0xFFu);
+}
+
+// Keyword kind of an identifier of length L whose first 16 bytes are packed
+// in (lo, hi), zero beyond L (K_IDENT when it is none).  Same perfect hash as
+// the keyword table: (3L + 47 s[0] + 16 s[L-1] + s[min(2, L-1)]) mod 128.
+__device__ __forceinline__ uint32_t keyword_kind_packed(uint64_t lo, uint64_t hi, uint64_t L,
+                                                        const KwPacked *kw) {
     if (L < 2 || L > 15) return K_IDENT;
-    uint32_t c0 = bw.at(p), cl = bw.at(p + L - 1), c2 = bw.at(p + (L > 2 ? 2 : L - 1));
-    const KwEntry &k = kw[(3u * (uint32_t)L + 47u * c0 + 16u * cl + c2) & 127u];
-    if (k.len != L) return K_IDENT;
-    for (uint64_t j = 0; j < L; ++j)
-        if ((uint8_t)k.w[j] != bw.at(p + j)) return K_IDENT;
-    return k.kind;
+    uint32_t l = (uint32_t)L;
+    uint32_t c0 = (uint32_t)(lo & 0xFFu), cl = byte_of(lo, hi, l - 1),
+             c2 = byte_of(lo, hi, l > 2 ? 2 : l - 1);
+    const KwPacked &k = kw[(3u * l + 47u * c0 + 16u * cl + c2) & 127u];
+    return (k.len == l && k.lo == lo && k.hi == hi) ? k.kind : (uint32_t)K_IDENT;
 }
 
 // As lex_segment, with the token automaton: tokens starting in [a, b) (a is
 // a sync point), EOF tokens of every TU that ends in (a, b] (and, for a == 0,
 // of the empty TUs at 0).  Returns the count; WRITE also stores them.
+// Every iteration reads one byte and computes both outcomes -- the automaton
+// advances, or it died and the longest accepted prefix is committed -- as
+// selects, so the lanes of a warp stay on one instruction stream.
 template <bool WRITE>
 __device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off, uint32_t n_tu,
-                                uint64_t a, uint64_t b, uint32_t line, const KwEntry *kw,
+                                uint64_t a, uint64_t b, uint32_t line, const KwPacked *kw,
                                 const DfaSmem &T, uint64_t out0, const LexOut &o) {
     uint64_t n = 0;
     uint32_t k = upper_bound_u64(tu_off, n_tu, a) - 1;
@@ -640,6 +667,7 @@ __device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off
     uint64_t e = __ldg(tu_off + k + 1);
     uint64_t tok = a, q = a, last = a;
     uint32_t st = Q_START, lk = 0, nl = 0, nla = 0;
+    uint64_t w0 = 0, w1 = 0;  // bytes of the current token, first 16
     for (;;) {
         if (st == Q_START) {  // at a token boundary: TU ends and the segment end
             while (tok == e && e <= b) {  // TU k ends here: its EOF token is ours
@@ -652,44 +680,46 @@ __device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off
             }
             if (k >= n_tu || tok >= b) break;
         }
-        uint32_t c = q < e ? bw.at(q) : 0u;
-        uint32_t cls = q < e ? T.cls[c] : (uint32_t)B_EOT;
+        bool in_tu = q < e;
+        uint32_t c = in_tu ? bw.at(q) : 0u;
+        uint32_t cls = in_tu ? T.cls[c] : (uint32_t)B_EOT;
         uint32_t ns = T.next[st * NB + cls];
-        if (ns != Q_DEAD) {
-            st = ns;
-            ++q;
-            nl += c == '\n';
-            uint32_t ac = T.acc[st];
-            if (ac) {
-                last = q;
-                lk = ac;
-                nla = nl;
-            }
-            continue;
-        }
-        // the automaton died: commit the longest accepted prefix
-        if (lk == 0) {
-            tok += 1;  // nothing matches here: finditer skips one character
-        } else {
-            if (lk != ACC_SKIP) {
-                uint32_t kind = lk;
-                if (WRITE) {
-                    if (kind == K_IDENT) kind = keyword_kind(bw, tok, last - tok, kw);
-                    if (kind & HEXFLOAT) {
-                        uint32_t v = hexfloat_verdict(Src{bw.src}, tok, last - tok);
-                        if (v) atomicMin(o.errkey + k, (unsigned long long)((tok << 8) | v));
-                    }
-                    if (last - tok > 0xFFFFFFu) o.unsup[k] = 1;
+        uint32_t ac = T.acc[ns];
+        bool adv = ns != Q_DEAD;
+        // the commit this byte would cause if the automaton died here
+        bool has = lk != 0;
+        if (!adv && has && lk != ACC_SKIP) {
+            uint32_t kind = lk;
+            if (WRITE) {
+                uint64_t L = last - tok;
+                if (kind == K_IDENT) kind = keyword_kind_packed(w0, w1, L, kw);
+                if (kind & HEXFLOAT) {
+                    uint32_t v = hexfloat_verdict(Src{bw.src}, tok, L);
+                    if (v) atomicMin(o.errkey + k, (unsigned long long)((tok << 8) | v));
                 }
-                emit(tok, kind, last - tok, line);
+                if (L > 0xFFFFFFu) o.unsup[k] = 1;
             }
-            if (lk != K_STRING && lk != K_CHAR) line += nla;
-            tok = last;
+            emit(tok, kind, last - tok, line);
         }
-        q = tok;
-        st = Q_START;
-        lk = 0;
-        nl = nla = 0;
+        line += (!adv && has && lk != K_STRING && lk != K_CHAR) ? nla : 0u;
+        uint64_t ntok = has ? last : tok + 1;
+        // advance
+        uint32_t j = (uint32_t)(q - tok);
+        uint64_t cb = (uint64_t)c;
+        w0 |= (adv && j < 8) ? cb << (8 * j) : 0ull;
+        w1 |= (adv && j >= 8 && j < 16) ? cb << (8 * (j - 8)) : 0ull;
+        uint64_t q1 = q + 1;
+        uint32_t nl1 = nl + (c == '\n' ? 1u : 0u);
+        bool acc_now = adv && ac != 0;
+        last = acc_now ? q1 : (adv ? last : ntok);
+        lk = acc_now ? ac : (adv ? lk : 0u);
+        nla = acc_now ? nl1 : (adv ? nla : 0u);
+        nl = adv ? nl1 : 0u;
+        st = adv ? ns : (uint32_t)Q_START;
+        tok = adv ? tok : ntok;
+        q = adv ? q1 : ntok;
+        w0 = adv ? w0 : 0ull;
+        w1 = adv ? w1 : 0ull;
     }
     return n;
 }
@@ -701,8 +731,10 @@ k_lex_tokens_dfa(bool write, const uint8_t *__restrict__ src, uint64_t N,
                  const uint64_t *__restrict__ nlcarry, uint64_t *__restrict__ counts,
                  const uint64_t *__restrict__ toff, LexOut o) {
     __shared__ DfaSmem T;
-    load_dfa(T);
-    const KwEntry *kw = g_kw;
+    __shared__ KwPacked kwp[128];
+    load_kw_packed(kwp, g_kw);
+    load_dfa(T);  // (its barrier also covers the keyword table)
+    const KwPacked *kw = kwp;
     uint64_t w = (uint64_t)blockIdx.x * BLOCK + threadIdx.x;
     if (w >= n_win) return;
     uint64_t a = S[w], b = S[w + 1];
