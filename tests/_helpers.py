@@ -672,3 +672,20 @@ __global__ void a4(int *o, int n) {
     o[t] = c;
 }""",
 ]
+
+
+# calls the reference's emitter has no case for: no instruction is emitted,
+# only the destination register is taken
+UNKNOWN_CALL_CASES = [
+    """__global__ void u0(float *o, const float *in) {
+    int t = threadIdx.x; float x = in[t];
+    float a = __expf(x); float b = __fdividef(x, 3.0f); float c = __saturatef(x);
+    o[t] = a + b + c + sqrtf(x);
+}""",
+    """__global__ void u1(int *o, int k) {
+    int t = threadIdx.x;
+    int p = __builtin_popcount(k); int q = my_helper(t, k);
+    o[t] = p * q + t;
+}""",
+    """__global__ void u2(double *o, double d) { int t = threadIdx.x; o[t] = __dadd_rn(d, 1.0) + sin(d); }""",
+]

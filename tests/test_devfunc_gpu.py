@@ -1,14 +1,16 @@
 """`__device__` functions on the GPU: definitions kept as token ranges and
 expanded at each call (parser.py:1749-1929, 4031-4087) -- several returns,
 void helpers, nested calls, prototypes and qualifiers, helpers defined after
-their callers, `&x` out-parameters spilled to .local -- compared with the live reference as parsed IR, optimized IR
+their callers, `&x` out-parameters spilled to .local, calls the reference's emitter has no
+case for -- compared with the live reference as parsed IR, optimized IR
 and PTX.  Recursive helpers, which the reference compiles to .func bodies,
 must come back as `unsupported`, never as different output."""
 import pytest
 
 from oracle import ref_runner
 from opencuda_b200.api import TU_UNSUPPORTED
-from tests._helpers import ADDR_OF_CASES, DEVFUNC_CASES, DEVFUNC_RECURSIVE_CASES, devfunc_sources
+from tests._helpers import (ADDR_OF_CASES, DEVFUNC_CASES, DEVFUNC_RECURSIVE_CASES, UNKNOWN_CALL_CASES,
+                            devfunc_sources)
 
 pytestmark = pytest.mark.gpu
 
@@ -17,7 +19,7 @@ RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError"
 
 @pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
 def test_device_functions_against_live_reference(ctx, stage):
-    srcs = DEVFUNC_CASES + ADDR_OF_CASES + devfunc_sources(300, 31)
+    srcs = DEVFUNC_CASES + ADDR_OF_CASES + UNKNOWN_CALL_CASES + devfunc_sources(300, 31)
     fn = {"ir": ctx.parse_batch, "opt": ctx.optimize_batch, "ptx": ctx.compile_batch}[stage]
     tb = fn(srcs)
     with ref_runner.RefPool() as pool:
