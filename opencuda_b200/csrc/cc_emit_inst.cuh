@@ -905,6 +905,53 @@ OCB_HD inline void Emit::emit_math(const Inst &in, Str dest) {
         SB b = sb();
         b.s("    mov.u32 ").s(dest).s(", 32;");
         put(b);
+    } else if (in_list(f, " __mul24 __umul24 __mulhi __umulhi ")) {
+        // integer multiplies (emit.py:2493-2508)
+        const char *op = eq(f, "__mul24") ? "mul24.lo.s32" : eq(f, "__umul24") ? "mul24.lo.u32" :
+                         eq(f, "__mulhi") ? "mul.hi.s32" : "mul.hi.u32";
+        Str a = arg0("0");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0");
+        SB b = sb();
+        b.s("    ").s(op).c(' ').s(dest).s(", ").s(a).s(", ").s(bb).c(';');
+        put(b);
+    } else if (eq(f, "__byte_perm")) {  // prmt (emit.py:2534-2539)
+        Str a = arg0("0");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0");
+        Str sel = na > 2 ? opnd(arg(2)) : S("0");
+        SB b = sb();
+        b.s("    prmt.b32 ").s(dest).s(", ").s(a).s(", ").s(bb).s(", ").s(sel).c(';');
+        put(b);
+    } else if (in_list(f, " powf pow ")) {  // exp2(y * log2(x)) (emit.py:2824-2833)
+        Str x = arg0("0f00000000");
+        Str y = na > 1 ? opnd(arg(1)) : S("0f3F800000");
+        uint32_t lg = new_value(nm("_pow_lg2x_", dn), S_FLOAT);
+        uint32_t yl = new_value(nm("_pow_ylg2x_", dn), S_FLOAT);
+        line1("lg2.approx.f32", reg(lg), x);
+        SB b = sb();
+        b.s("    mul.f32 ").s(reg(yl)).s(", ").s(y).s(", ").s(reg(lg)).c(';');
+        put(b);
+        line1("ex2.approx.f32", dest, reg(yl));
+    } else if (in_list(f, " hypotf hypot ")) {  // sqrt(a*a + b*b) (emit.py:2834-2843)
+        Str a = arg0("0f00000000");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0f00000000");
+        uint32_t a2 = new_value(nm("_hypot_a2_", dn), S_FLOAT);
+        uint32_t ab = new_value(nm("_hypot_ab2_", dn), S_FLOAT);
+        SB b = sb();
+        b.s("    mul.f32 ").s(reg(a2)).s(", ").s(a).s(", ").s(a).c(';');
+        put(b);
+        SB b2 = sb();
+        b2.s("    fma.rn.f32 ").s(reg(ab)).s(", ").s(bb).s(", ").s(bb).s(", ").s(reg(a2)).c(';');
+        put(b2);
+        line1("sqrt.approx.f32", dest, reg(ab));
+    } else if (in_list(f, " cbrtf cbrt ")) {  // exp2(log2(x) / 3) (emit.py:2844-2853)
+        Str x = arg0("0f00000000");
+        uint32_t lg = new_value(nm("_cbrt_lg2x_", dn), S_FLOAT);
+        uint32_t l3 = new_value(nm("_cbrt_lg2x3_", dn), S_FLOAT);
+        line1("lg2.approx.f32", reg(lg), x);
+        SB b = sb();
+        b.s("    mul.f32 ").s(reg(l3)).s(", ").s(reg(lg)).s(", 0f3EAAAAAB;");
+        put(b);
+        line1("ex2.approx.f32", dest, reg(l3));
     } else if (in_list(f, ref_call_names()) || sstarts(f, "atomic") || sstarts(f, "__devfn_")) {
         unsup();  // other intrinsics the reference expands (half, dp4a, warp reductions, atan2, ...)
     }

@@ -689,3 +689,15 @@ UNKNOWN_CALL_CASES = [
 }""",
     """__global__ void u2(double *o, double d) { int t = threadIdx.x; o[t] = __dadd_rn(d, 1.0) + sin(d); }""",
 ]
+
+INTRINSIC_CASES = [
+    """__global__ void i0(float *o, const float *in) {
+    int t = threadIdx.x; float x = in[t]; float y = in[t + 1];
+    o[t] = powf(x, y) + hypotf(x, 2.0f) + cbrtf(y) + powf(x, 2.0f);
+}""",
+    """__global__ void i1(int *o, unsigned *u, int k) {
+    int t = threadIdx.x;
+    o[t] = __mul24(t, k) + __mulhi(t, 123456789) + (int)__umulhi(u[t], 77u) + (int)__umul24(u[t], 3u);
+    u[t] = __byte_perm(u[t], u[t + 1], 0x3210) + __byte_perm(u[t], 0u, 0x0123);
+}""",
+]
