@@ -625,7 +625,7 @@ __device__ __forceinline__ uint32_t byte_of(uint64_t lo, uint64_t hi, uint32_t j
 // Keyword kind of an identifier of length L whose first 16 bytes are packed
 // in (lo, hi), zero beyond L (K_IDENT when it is none).  Same perfect hash as
 // the keyword table: (3L + 47 s[0] + 16 s[L-1] + s[min(2, L-1)]) mod 128.
-__device__ __forceinline__ uint32_t keyword_kind_packed(uint64_t lo, uint64_t hi, uint64_t L,
+__device__ __forceinline__ uint32_t keyword_kind_packed(uint64_t lo, uint64_t hi, uint32_t L,
                                                         const KwPacked *kw) {
     if (L < 2 || L > 15) return K_IDENT;
     uint32_t l = (uint32_t)L;
@@ -664,21 +664,24 @@ __device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off
             if (WRITE) o.tu_tok_off[j + 1] = out0 + n;
         }
     }
-    uint64_t e = __ldg(tu_off + k + 1);
-    uint64_t tok = a, q = a, last = a;
+    // positions are 32-bit (a batch is below 4 GiB); the counting pass
+    // (WRITE = false) tracks neither lines nor identifier bytes
+    uint32_t e = (uint32_t)__ldg(tu_off + k + 1);
+    const uint32_t b32 = (uint32_t)b;
+    uint32_t tok = (uint32_t)a, q = (uint32_t)a, last = (uint32_t)a;
     uint32_t st = Q_START, lk = 0, nl = 0, nla = 0;
-    uint64_t w0 = 0, w1 = 0;  // bytes of the current token, first 16
+    uint64_t w0 = 0, w1 = 0;  // bytes of the current token, first 16 (WRITE)
     for (;;) {
         if (st == Q_START) {  // at a token boundary: TU ends and the segment end
-            while (tok == e && e <= b) {  // TU k ends here: its EOF token is ours
+            while (tok == e && e <= b32) {  // TU k ends here: its EOF token is ours
                 emit(e, K_EOF, 0, line);
                 if (WRITE) o.tu_tok_off[k + 1] = out0 + n;
                 ++k;
                 line = 1;
                 if (k >= n_tu) break;
-                e = __ldg(tu_off + k + 1);
+                e = (uint32_t)__ldg(tu_off + k + 1);
             }
-            if (k >= n_tu || tok >= b) break;
+            if (k >= n_tu || tok >= b32) break;
         }
         bool in_tu = q < e;
         uint32_t c = in_tu ? bw.at(q) : 0u;
@@ -691,35 +694,36 @@ __device__ uint64_t dfa_segment(ByteWin &bw, const uint64_t *__restrict__ tu_off
         if (!adv && has && lk != ACC_SKIP) {
             uint32_t kind = lk;
             if (WRITE) {
-                uint64_t L = last - tok;
+                uint32_t L = last - tok;
                 if (kind == K_IDENT) kind = keyword_kind_packed(w0, w1, L, kw);
                 if (kind & HEXFLOAT) {
                     uint32_t v = hexfloat_verdict(Src{bw.src}, tok, L);
-                    if (v) atomicMin(o.errkey + k, (unsigned long long)((tok << 8) | v));
+                    if (v) atomicMin(o.errkey + k, (unsigned long long)(((uint64_t)tok << 8) | v));
                 }
                 if (L > 0xFFFFFFu) o.unsup[k] = 1;
             }
             emit(tok, kind, last - tok, line);
         }
-        line += (!adv && has && lk != K_STRING && lk != K_CHAR) ? nla : 0u;
-        uint64_t ntok = has ? last : tok + 1;
-        // advance
-        uint32_t j = (uint32_t)(q - tok);
-        uint64_t cb = (uint64_t)c;
-        w0 |= (adv && j < 8) ? cb << (8 * j) : 0ull;
-        w1 |= (adv && j >= 8 && j < 16) ? cb << (8 * (j - 8)) : 0ull;
-        uint64_t q1 = q + 1;
-        uint32_t nl1 = nl + (c == '\n' ? 1u : 0u);
+        uint32_t ntok = has ? last : tok + 1;
+        uint32_t q1 = q + 1;
         bool acc_now = adv && ac != 0;
+        if (WRITE) {
+            line += (!adv && has && lk != K_STRING && lk != K_CHAR) ? nla : 0u;
+            uint32_t j = q - tok;
+            uint64_t cb = (uint64_t)c;
+            w0 |= (adv && j < 8) ? cb << (8 * j) : 0ull;
+            w1 |= (adv && j >= 8 && j < 16) ? cb << (8 * (j - 8)) : 0ull;
+            uint32_t nl1 = nl + (c == '\n' ? 1u : 0u);
+            nla = acc_now ? nl1 : (adv ? nla : 0u);
+            nl = adv ? nl1 : 0u;
+            w0 = adv ? w0 : 0ull;
+            w1 = adv ? w1 : 0ull;
+        }
         last = acc_now ? q1 : (adv ? last : ntok);
         lk = acc_now ? ac : (adv ? lk : 0u);
-        nla = acc_now ? nl1 : (adv ? nla : 0u);
-        nl = adv ? nl1 : 0u;
         st = adv ? ns : (uint32_t)Q_START;
         tok = adv ? tok : ntok;
         q = adv ? q1 : ntok;
-        w0 = adv ? w0 : 0ull;
-        w1 = adv ? w1 : 0ull;
     }
     return n;
 }
