@@ -746,14 +746,15 @@ k_lex_tokens_dfa(bool write, const uint8_t *__restrict__ src, uint64_t N,
     if (b > N) b = N;
     uint64_t n = 0;
     if (a < b) {
-        uint32_t si = sinfo[w];
-        uint32_t line = (si & 0x80000000u) ? 1u
-                        : 1u + (uint32_t)(nlcarry[w] & ~SEG_FLAG) + (si & 0x7FFFFFFFu);
         ByteWin bw{src, N, ~0ull, make_uint4(0, 0, 0, 0)};
-        if (write)
+        if (write) {  // only the writing pass needs the line at the sync point
+            uint32_t si = sinfo[w];
+            uint32_t line = (si & 0x80000000u) ? 1u
+                            : 1u + (uint32_t)(nlcarry[w] & ~SEG_FLAG) + (si & 0x7FFFFFFFu);
             n = dfa_segment<true>(bw, tu_off, n_tu, a, b, line, kw, T, toff[w], o);
-        else
-            n = dfa_segment<false>(bw, tu_off, n_tu, a, b, line, kw, T, 0, o);
+        } else {
+            n = dfa_segment<false>(bw, tu_off, n_tu, a, b, 1u, kw, T, 0, o);
+        }
     }
     if (!write) counts[w] = n;
 }
