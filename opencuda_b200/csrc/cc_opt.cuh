@@ -106,22 +106,10 @@ struct IdArr {
         n = size;
         dflt = d;
         p = (T *)a.alloc(sizeof(T) * (uint64_t)(size ? size : 1), 16);
-        if (!p) {
+        if (p)
+            for (uint32_t i = 0; i < size; ++i) p[i] = d;
+        else
             n = 0;
-            return;
-        }
-        uint32_t i = 0;
-        if (sizeof(T) == 4 || sizeof(T) == 1) {  // 16-byte stores of the fill pattern
-            uint32_t w;
-            if (sizeof(T) == 4) memcpy(&w, &d, 4);
-            else w = 0x01010101u * (uint32_t)*(const uint8_t *)&d;
-            uint4 pat = make_uint4(w, w, w, w);
-            uint32_t per = 16 / (uint32_t)sizeof(T), nv = size / per;
-            uint4 *v = (uint4 *)p;  // the arena returns 16-byte aligned blocks
-            for (uint32_t k = 0; k < nv; ++k) v[k] = pat;
-            i = nv * per;
-        }
-        for (; i < size; ++i) p[i] = d;
     }
     OCB_HD T get(uint32_t id) const { return id < n ? p[id] : dflt; }
     OCB_HD bool set(uint32_t id, T v) {
@@ -328,14 +316,7 @@ struct Seen {
         n = o.n;
         t = (E *)a.alloc(sizeof(E) * (uint64_t)cap, 16);
         if (!t) return false;
-        uint64_t nb = sizeof(E) * (uint64_t)cap;
-        if (nb % 16 == 0 && ((uintptr_t)o.t & 15) == 0) {  // both tables 16-byte aligned
-            const uint4 *s4 = (const uint4 *)o.t;
-            uint4 *d4 = (uint4 *)t;
-            for (uint64_t k = 0; k < nb / 16; ++k) d4[k] = s4[k];
-        } else {
-            for (uint32_t i = 0; i < cap; ++i) t[i] = o.t[i];
-        }
+        for (uint32_t i = 0; i < cap; ++i) t[i] = o.t[i];
         return true;
     }
 };
