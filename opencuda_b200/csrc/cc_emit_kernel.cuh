@@ -263,8 +263,39 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
             ++i;
         }
     }
-    // (4) mov.bNN copy propagation
+    // (4) mov.bNN copy propagation.  Each line's destination register is
+    // parsed once and kept aligned with L (a substitution never changes a
+    // line's destination; an erase removes one entry), and label positions
+    // are cached per branch target (an erased mov line is never a label, so
+    // an erase only moves the labels after it up by one).
     {
+        Vec<Str> dests;  // pat_dest of each line, n = 0 when the line has none
+        dests.init();
+        if (!dests.reserve(tmp, L.n + 1)) { unsup(); return; }
+        for (uint32_t j = 0; j < L.n; ++j) {
+            Str dd;
+            dests.p[j] = pat_dest(L[j], dd) ? dd : Str{nullptr, 0};
+        }
+        dests.n = L.n;
+        struct LabelPos { Str tgt; int64_t pos; };
+        Vec<LabelPos> labels;
+        labels.init();
+        auto label_pos = [&](Str tgt) -> int64_t {
+            for (uint32_t q = 0; q < labels.n; ++q)
+                if (eq(labels[q].tgt, tgt)) return labels[q].pos;
+            // the last "name:" line (not indented) with that name
+            int64_t pos = -1;
+            for (uint32_t q = 0; q < L.n; ++q) {
+                Str ln = L[q];
+                uint32_t e = ln.n;
+                while (e && is_wsc(ln.p[e - 1])) --e;
+                if (e && ln.p[e - 1] == ':' && !(ln.n && ln.p[0] == ' ') && e - 1 == tgt.n &&
+                    mem_eq(ln.p, tgt.p, tgt.n))
+                    pos = q;
+            }
+            labels.push(tmp, LabelPos{tgt, pos});
+            return pos;
+        };
         uint32_t i = 0;
         uint32_t guard = 0;
         while (i < L.n && !bad()) {
@@ -273,8 +304,8 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
             if (pat_movb(L[i], dst, src) && eq(reg_class(dst), reg_class(src))) {
                 int64_t src_redef = -1;
                 for (uint32_t j = i + 1; j < L.n; ++j) {
-                    Str dd;
-                    if (pat_dest(L[j], dd)) {
+                    Str dd = dests[j];
+                    if (dd.n) {
                         if (eq(dd, dst)) break;
                         if (eq(dd, src)) {
                             src_redef = j;
@@ -285,8 +316,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                 bool unsafe = false;
                 if (src_redef >= 0) {
                     for (uint32_t j = (uint32_t)src_redef + 1; j < L.n; ++j) {
-                        Str dd;
-                        if (pat_dest(L[j], dd) && eq(dd, dst)) break;
+                        if (dests[j].n && eq(dests[j], dst)) break;
                         if (str_has(L[j], dst)) {
                             unsafe = true;
                             break;
@@ -298,16 +328,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                     for (uint32_t j = i; j < L.n && !unsafe; ++j) {
                         Str tgt;
                         if (!pat_bra(L[j], tgt)) continue;
-                        // label_pos: the last "name:" line (not indented) with that name
-                        int64_t pos = -1;
-                        for (uint32_t q = 0; q < L.n; ++q) {
-                            Str ln = L[q];
-                            uint32_t e = ln.n;
-                            while (e && is_wsc(ln.p[e - 1])) --e;
-                            if (e && ln.p[e - 1] == ':' && !(ln.n && ln.p[0] == ' ') && e - 1 == tgt.n &&
-                                mem_eq(ln.p, tgt.p, tgt.n))
-                                pos = q;
-                        }
+                        int64_t pos = label_pos(tgt);
                         if (pos >= 0 && pos <= (int64_t)j) unsafe = true;
                     }
                 }
@@ -316,13 +337,20 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                     continue;
                 }
                 L.erase(i);
+                dests.erase(i);
+                for (uint32_t q = 0; q < labels.n; ++q)
+                    if (labels[q].pos > (int64_t)i) labels[q].pos--;
                 for (uint32_t j = i; j < L.n; ++j) {
-                    Str dd;
-                    bool isd = pat_dest(L[j], dd);
+                    Str dd = dests[j];
+                    bool isd = dd.n != 0;
                     if (isd && eq(dd, dst)) break;
                     bool redef_src = isd && eq(dd, src);
                     bool ch;
                     L[j] = sub_reg(ar, L[j], dst, src, ch);
+                    if (ch) {
+                        Str nd;
+                        dests.p[j] = pat_dest(L[j], nd) ? nd : Str{nullptr, 0};
+                    }
                     if (redef_src) break;
                 }
                 continue;
