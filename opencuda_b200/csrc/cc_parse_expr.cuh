@@ -1045,8 +1045,33 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
         if (eq(name, "nullptr")) return m.cint(S_UINT64, 0);
         if ((eq(name, "static_cast") || eq(name, "reinterpret_cast") || eq(name, "const_cast")) &&
             at(TK_LT)) {
-            unsup();
-            return onone();
+            // C++ named casts (parser.py:1610-1630): a type whose parse fails
+            // (any exception) becomes INT32, each '*' wraps it in a global
+            // pointer; a pointer operand in another space keeps its space
+            advance();
+            Ty ct;
+            if (parse_type(ct)) {
+                while (!bad() && match(TK_STAR)) {
+                    bool ok = true;
+                    ct = ty_ptr(ct, AS_GLOBAL, false, ok);
+                    if (!ok) { unsup(); return onone(); }
+                }
+            }
+            if (bad()) {
+                if (!catch_any()) return onone();
+                ct = S_INT32;
+            }
+            if (!expect(TK_GT) || !expect(TK_LPAREN)) return onone();
+            Opnd opd = parse_assign_expr();
+            if (bad() || !expect(TK_RPAREN)) return onone();
+            if (is_ptr(ct) && opd.k == O_VAL && is_ptr(tyof(opd)) && ty_as(tyof(opd)) != AS_GLOBAL) {
+                bool ok = true;
+                ct = ty_ptr(ty_pointee(ct), ty_as(tyof(opd)), false, ok);
+                if (!ok) { unsup(); return onone(); }
+            }
+            uint32_t d = new_val("cast", ct);
+            emit_cvt(d, opd);
+            return ov(d);
         }
         if (match(TK_LPAREN)) return parse_call(name);
         Opnd *vp = vars.get(name);

@@ -701,3 +701,23 @@ INTRINSIC_CASES = [
     u[t] = __byte_perm(u[t], u[t + 1], 0x3210) + __byte_perm(u[t], 0u, 0x0123);
 }""",
 ]
+
+CAST_CASES = [
+    """__global__ void c0(float *o, const int *in, unsigned char *b) {
+    int t = threadIdx.x;
+    float f = static_cast<float>(in[t]);
+    int i = static_cast<int>(f * 2.5f);
+    unsigned u = reinterpret_cast<unsigned>(i);
+    float *p = const_cast<float *>(o);
+    p[t] = f + static_cast<double>(u) + static_cast<float>(b[t]);
+}""",
+    """__global__ void c1(int *o) {
+    __shared__ float s[32];
+    int t = threadIdx.x;
+    float *ps = static_cast<float *>(s);
+    ps[t] = 1.0f;
+    o[t] = static_cast<int>(ps[t]) + static_cast<long long>(t);
+}""",
+    # an unknown type is not consumed: the '>' is missing (ParseError)
+    """__global__ void c2(int *o) { int t = threadIdx.x; o[t] = static_cast<Unknown>(t); }""",
+]
