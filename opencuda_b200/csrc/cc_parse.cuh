@@ -237,9 +237,7 @@ struct Parser {
             raise_(R_OTHER);  // IndexError in the reference
             return TK_EOF;
         }
-        uint32_t k = tk.kindlen[i] >> 24;
-        if (k & 0x80) unsup();  // hex-float literal value
-        return k & 0x7F;
+        return (tk.kindlen[i] >> 24) & 0x7F;  // hex floats: FLOAT_LIT (value in parse_hexfloat)
     }
     OCB_HD Str val_at(uint32_t i) {
         if (i >= tk.n) return Str{"", 0};

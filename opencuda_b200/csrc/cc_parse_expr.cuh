@@ -955,6 +955,69 @@ OCB_HD inline bool parse_decimal_exact(Str s, double &out) {
     return true;
 }
 
+// float.fromhex of a hex-float literal without its [fFlL] suffix
+// (lexer.py:282-284; the parser then reads back str() of it, the same
+// double): 0x <hex digits> [. <hex digits>] p [+-] <decimal digits>, scaled
+// by 2^exp and rounded half to even to 53 bits or to the subnormal grid.
+// Values that overflow never get here (the lexer reports OverflowError).
+OCB_HD inline bool parse_hexfloat(Str s, double &out) {
+    uint32_t i = 0;
+    if (s.n < 3 || s.p[0] != '0' || (s.p[1] | 0x20) != 'x') return false;
+    i = 2;
+    uint64_t m = 0;          // the first significant bits (up to 60)
+    int mbits = 0;           // bits held in m
+    int64_t scale = 0;       // value = m * 2^scale (+ sticky)
+    bool sticky = false, dot = false, any = false;
+    for (; i < s.n; ++i) {
+        char c = s.p[i];
+        if (c == '.' && !dot) { dot = true; continue; }
+        uint32_t d;
+        if (c >= '0' && c <= '9') d = c - '0';
+        else if ((c | 0x20) >= 'a' && (c | 0x20) <= 'f') d = (c | 0x20) - 'a' + 10;
+        else break;
+        any = true;
+        if (dot) scale -= 4;
+        if (mbits + 4 <= 60) {
+            m = (m << 4) | d;
+            if (m) mbits += 4;
+        } else {  // beyond 60 bits: keep the digit's weight, fold it into sticky
+            scale += 4;
+            sticky = sticky || d != 0;
+        }
+    }
+    if (!any || i >= s.n || (s.p[i] | 0x20) != 'p') return false;
+    ++i;
+    bool neg = false;
+    if (i < s.n && (s.p[i] == '+' || s.p[i] == '-')) neg = s.p[i++] == '-';
+    int64_t e = 0;
+    bool ed = false;
+    for (; i < s.n && s.p[i] >= '0' && s.p[i] <= '9'; ++i) {
+        ed = true;
+        if (e < 100000) e = e * 10 + (s.p[i] - '0');
+    }
+    if (!ed || i != s.n) return false;
+    scale += neg ? -e : e;
+    if (m == 0) { out = 0.0; return true; }
+#ifdef __CUDA_ARCH__
+    int lq = 64 - __clzll((long long)m);
+#else
+    int lq = 64 - __builtin_clzll(m);
+#endif
+    int64_t drop = lq - 53;                       // bits below the 53 kept
+    if (drop < -1074 - scale) drop = -1074 - scale;  // subnormal grid 2^-1074
+    if (drop <= 0) {
+        out = ldexp((double)m, (int)scale);
+        return true;
+    }
+    if (drop > 63) { out = 0.0; return true; }    // far below the least subnormal
+    uint64_t mant = m >> drop;
+    bool half = (m >> (drop - 1)) & 1u;
+    bool rest = sticky || (drop > 1 && (m & ((1ull << (drop - 1)) - 1)) != 0);
+    if (half && (rest || (mant & 1))) ++mant;
+    out = ldexp((double)mant, (int)(scale + drop));
+    return true;
+}
+
 OCB_HD inline bool parse_decimal(Str s, double &out) {
     return parse_decimal_fast(s, out) || parse_decimal_exact(s, out);
 }
@@ -1025,9 +1088,15 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
     }
     if (k == TK_FLOAT_LIT) {
         advance();
+        double d;
+        if (v.n > 2 && v.p[0] == '0' && (v.p[1] | 0x20) == 'x') {  // hex float: [fFlL] suffix
+            uint32_t e = v.n;
+            while (e > 0 && ((v.p[e - 1] | 0x20) == 'f' || (v.p[e - 1] | 0x20) == 'l')) --e;
+            if (!parse_hexfloat(Str{v.p, e}, d)) { unsup(); return onone(); }
+            return m.cfloat(S_FLOAT, d);
+        }
         uint32_t e = v.n;
         while (e > 0 && (v.p[e - 1] | 0x20) == 'f') --e;
-        double d;
         if (!parse_decimal(Str{v.p, e}, d)) { unsup(); return onone(); }
         return m.cfloat(S_FLOAT, d);
     }

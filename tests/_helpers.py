@@ -721,3 +721,12 @@ CAST_CASES = [
     # an unknown type is not consumed: the '>' is missing (ParseError)
     """__global__ void c2(int *o) { int t = threadIdx.x; o[t] = static_cast<Unknown>(t); }""",
 ]
+
+HEXFLOAT_CASES = [
+    """__global__ void h0(float *o, double *d) {
+    int t = threadIdx.x;
+    float a = 0x1.8p3f; float b = 0x.8p-2F; float c = 0x10p0;
+    d[t] = 0x1.fffffffffffffp1023 * 0.0 + 0x1p-1074 + 0x1.921fb54442d18p+1L;
+    o[t] = a * b + c + 0xAp-4;
+}""",
+]
