@@ -244,7 +244,9 @@ enum : uint32_t {
     S_VOID = 0, S_BOOL, S_INT8, S_UINT8, S_INT16, S_UINT16, S_INT32, S_UINT32,
     S_INT64, S_UINT64, S_FLOAT, S_DOUBLE, S_HALF
 };
-enum : uint32_t { AS_GENERIC = 0, AS_GLOBAL, AS_SHARED, AS_LOCAL, AS_CONST };
+// AS_INT0: the integer 0 the reference stores as the space of an array
+// parameter's pointer (PtrTy(ty, 0)); it is none of the named spaces.
+enum : uint32_t { AS_GENERIC = 0, AS_GLOBAL, AS_SHARED, AS_LOCAL, AS_CONST, AS_INT0 };
 
 OCB_HD inline Ty ty_s(uint32_t s) { return s; }
 OCB_HD inline uint32_t ty_depth(Ty t) { return (t >> 4) & 3; }
@@ -313,6 +315,7 @@ OCB_HD inline const char *as_name(uint32_t a) {
     case AS_GLOBAL: return "global";
     case AS_SHARED: return "shared";
     case AS_LOCAL: return "local";
+    case AS_INT0: return "0";
     default: return "const";
     }
 }

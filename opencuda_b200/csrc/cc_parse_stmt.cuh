@@ -924,9 +924,19 @@ OCB_HD inline void Parser::parse_kernel() {
             if (!parse_type_with_ptr(pty)) return;
             Str pname;
             if (!expect_ident(pname)) return;
-            if (at(TK_LBRACKET)) {  // array parameter: PtrTy(ty, 0) in the reference
-                unsup();
-                return;
+            if (at(TK_LBRACKET)) {  // array parameter: PtrTy(ty, 0) (parser.py:3768-3774)
+                advance();
+                while (!at(TK_RBRACKET)) {
+                    if (bad()) return;
+                    if (at(TK_EOF)) { unsup(); return; }  // the reference never returns
+                    advance();
+                }
+                advance();
+                if (!is_ptr(pty)) {
+                    bool ok = true;
+                    pty = ty_ptr(pty, AS_INT0, false, ok);
+                    if (!ok) { unsup(); return; }
+                }
             }
             while (at(TK_IDENT) && eq(peekv(), "__attribute__")) {
                 advance();
@@ -1133,9 +1143,19 @@ OCB_HD inline void Parser::parse_device_func() {
             if (!parse_type_with_ptr(pty)) return;
             Str pname;
             if (!expect_ident(pname)) return;
-            if (at(TK_LBRACKET)) {  // array parameter decaying to a pointer
-                unsup();
-                return;
+            if (at(TK_LBRACKET)) {  // array parameter: PtrTy(ty, 0) (parser.py:4051-4059)
+                advance();
+                while (!at(TK_RBRACKET)) {
+                    if (bad()) return;
+                    if (at(TK_EOF)) { unsup(); return; }  // the reference never returns
+                    advance();
+                }
+                advance();
+                if (!is_ptr(pty)) {
+                    bool ok = true;
+                    pty = ty_ptr(pty, AS_INT0, false, ok);
+                    if (!ok) { unsup(); return; }
+                }
             }
             params.push(ar, Param{pname, pty});
             if (!match(TK_COMMA)) break;

@@ -730,3 +730,14 @@ HEXFLOAT_CASES = [
     o[t] = a * b + c + 0xAp-4;
 }""",
 ]
+
+ARRAY_PARAM_CASES = [
+    """__device__ float sum3(float v[3]) { return v[0] + v[1] + v[2]; }
+__global__ void ap0(float out[], const float in[256], int n) {
+    int t = threadIdx.x;
+    float *q = out + 1;
+    out[t] = in[t] * 2.0f + sum3(out);
+    if (t < n) q[t] = in[t & 255];
+}""",
+    """__global__ void ap1(int a[], int *b, int k) { int t = threadIdx.x; a[t] = b[t] + a[t + k]; b[t] = a[0]; }""",
+]
