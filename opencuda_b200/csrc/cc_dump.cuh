@@ -77,6 +77,11 @@ OCB_HD inline void dump_opnd(Out &o, const Module &m, Opnd x) {
         dump_ty(o, v.ty);
         return;
     }
+    if (x.k == O_SYM) {
+        o.put('@');
+        o.put(m.gvars[x.x].name);
+        return;
+    }
     const Const &c = m.consts[x.x];
     o.put('#');
     dump_ty(o, c.ty);
@@ -143,6 +148,13 @@ OCB_HD inline void dump_inst(Out &o, const Module &m, const Inst &i) {
             dump_opnd(o, m, i.args[k]);
         }
         o.put(')');
+        break;
+    case I_GADDR:
+        dest();
+        o.put("gaddr @");
+        o.put(i.func);
+        o.put(' ');
+        o.put(as_name(i.op));
         break;
     case I_PARAM:
         dest();
@@ -229,6 +241,10 @@ OCB_HD inline void dump_module(Out &o, const Module &m) {
             o.put("\n  ");
             dump_term(o, m, b.term);
         }
+    }
+    if (m.gvars.n) {
+        if (m.kernels.n) o.put('\n');
+        o.put("module-extras");
     }
     o.put('\n');
 }

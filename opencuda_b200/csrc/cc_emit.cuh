@@ -423,6 +423,7 @@ struct Emit {
             return reg(o);
         }
         if (o.k == O_CONST) return konst(o, force);
+        if (o.k == O_SYM) return m.gvars[o.x].name;  // the symbol as an address
         unsup();
         return S("?");
     }
@@ -583,7 +584,7 @@ struct Emit {
                 if (in.kind == I_BIN && (in.op == BO_AND || in.op == BO_OR || in.op == BO_XOR) &&
                     in.a.k == O_VAL && is_pred(vid(in.a)) && in.b.k == O_VAL && is_pred(vid(in.b)))
                     add_pred(m.vals[in.dest].id);
-                if (in.kind == I_LOAD || in.kind == I_PARAM) def(in.dest, idx);
+                if (in.kind == I_LOAD || in.kind == I_PARAM || in.kind == I_GADDR) def(in.dest, idx);
                 if (in.kind == I_CALL && in.dest >= 0) def(in.dest, idx);
                 switch (in.kind) {
                 case I_BIN:

@@ -330,6 +330,12 @@ OCB_HD inline void Emit::emit_load(const Inst &in) {
         if (as == AS_SHARED) sp = "shared";
         else if (as == AS_LOCAL) sp = "local";
         else if (as == AS_CONST) nc = true;
+    } else if (in.a.k == O_SYM) {  // [symbol] in the symbol's own state space
+        Ty pt = m.gvars[in.a.x].ptr;
+        if (ty_vol(pt)) vol = true;
+        uint32_t as = ty_as(pt);
+        if (as == AS_CONST) sp = "const";
+        else if (as == AS_SHARED) sp = "shared";
     }
     if (cstr_eq(ptx, "f16")) ptx = "b16";
     SB b = sb();
@@ -914,6 +920,339 @@ OCB_HD inline void Emit::emit_math(const Inst &in, Str dest) {
         SB b = sb();
         b.s("    ").s(op).c(' ').s(dest).s(", ").s(a).s(", ").s(bb).c(';');
         put(b);
+    } else if (sstarts(f, "__reduce_") && in_list(f, " __reduce_add_sync __reduce_min_sync __reduce_max_sync "
+                   "__reduce_and_sync __reduce_or_sync __reduce_xor_sync __reduce_umin_sync __reduce_umax_sync ")) {
+        // redux.sync (emit.py:2447-2479): value first, mask second in the instruction
+        const char *op = eq(f, "__reduce_add_sync") ? "add.s32" : eq(f, "__reduce_min_sync") ? "min.s32" :
+                         eq(f, "__reduce_max_sync") ? "max.s32" : eq(f, "__reduce_and_sync") ? "and.b32" :
+                         eq(f, "__reduce_or_sync") ? "or.b32" : eq(f, "__reduce_xor_sync") ? "xor.b32" :
+                         eq(f, "__reduce_umin_sync") ? "min.u32" : "max.u32";
+        Str mk = arg0("0xffffffff");
+        Str val = na > 1 ? opnd(arg(1)) : S("0");
+        SB b = sb();
+        b.s("    redux.sync.").s(op).c(' ').s(dest).s(", ").s(val).s(", ").s(mk).c(';');
+        put(b);
+    } else if (eq(f, "__match_any_sync") || eq(f, "__match_all_sync")) {  // emit.py:2480-2491
+        Str mk = arg0("0xffffffff");
+        Str val = na > 1 ? opnd(arg(1)) : S("0");
+        SB b = sb();
+        b.s("    match.").s(eq(f, "__match_any_sync") ? "any" : "all").s(".sync.b32 ").s(dest).s(", ").s(val)
+            .s(", ").s(mk).c(';');
+        put(b);
+    } else if (in_list(f, " __hadd __hadd_rn __hadd_sat ")) {  // emit.py:2509-2523
+        Ty dty = in.dest >= 0 ? V((uint32_t)in.dest).ty : (Ty)S_INT32;
+        if (!is_ptr(dty) && ty_scalar(dty) == S_HALF) {  // f16 add
+            Str a = arg0("0h0000");
+            Str bb = na > 1 ? opnd(arg(1)) : S("0h0000");
+            SB b = sb();
+            b.s("    add.rn").s(eq(f, "__hadd_sat") ? ".sat" : "").s(".f16 ").s(dest).s(", ").s(a).s(", ").s(bb).c(';');
+            put(b);
+        } else {  // integer halving add: (a + b) >> 1
+            Str a = arg0("0");
+            Str bb = na > 1 ? opnd(arg(1)) : S("0");
+            uint32_t t = new_value(nm("_hadd_tmp_", dn), S_INT32);
+            SB b1 = sb();
+            b1.s("    add.s32 ").s(reg(t)).s(", ").s(a).s(", ").s(bb).c(';');
+            put(b1);
+            SB b2 = sb();
+            b2.s("    shr.s32 ").s(dest).s(", ").s(reg(t)).s(", 1;");
+            put(b2);
+        }
+    } else if (eq(f, "__rhadd")) {  // (a + b + 1) >> 1 unsigned (emit.py:2524-2532)
+        Str a = arg0("0");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0");
+        uint32_t t = new_value(nm("_rhadd_tmp_", dn), S_UINT32);
+        SB b1 = sb();
+        b1.s("    add.u32 ").s(reg(t)).s(", ").s(a).s(", ").s(bb).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    add.u32 ").s(reg(t)).s(", ").s(reg(t)).s(", 1;");
+        put(b2);
+        SB b3 = sb();
+        b3.s("    shr.u32 ").s(dest).s(", ").s(reg(t)).s(", 1;");
+        put(b3);
+    } else if (eq(f, "__ushort_as_half") || eq(f, "__short_as_half")) {  // emit.py:2554-2569
+        SB b = sb();
+        if (!na) {
+            b.s("    mov.b16 ").s(dest).s(", 0;");
+        } else {
+            Str src = opnd(arg(0));
+            if (sstarts(src, "%r")) {  // low half of a b32 register by vector unpack
+                uint32_t dc = new_value(nm("_half_discard_", dn), S_HALF);
+                b.s("    mov.b32 {").s(dest).s(", ").s(reg(dc)).s("}, ").s(src).c(';');
+            } else {
+                b.s("    mov.b16 ").s(dest).s(", ").s(src).c(';');
+            }
+        }
+        put(b);
+    } else if (eq(f, "__half_as_ushort") || eq(f, "__half_as_short")) {  // emit.py:2570-2585
+        if (!na) {
+            SB b = sb();
+            b.s("    mov.b32 ").s(dest).s(", 0;");
+            put(b);
+        } else {
+            Str src = opnd(arg(0));
+            if (sstarts(src, "%h")) {  // pack with a zero half
+                uint32_t z = new_value(nm("_half_zero_", dn), S_HALF);
+                SB b1 = sb();
+                b1.s("    mov.b16 ").s(reg(z)).s(", 0;");
+                put(b1);
+                SB b2 = sb();
+                b2.s("    mov.b32 ").s(dest).s(", {").s(src).s(", ").s(reg(z)).s("};");
+                put(b2);
+            } else {
+                SB b = sb();
+                b.s("    mov.b16 ").s(dest).s(", ").s(src).c(';');
+                put(b);
+            }
+        }
+    } else if (in_list(f, " __int2half_rn __uint2half_rn __short2half_rn __ushort2half_rn __ll2half_rn __ull2half_rn "
+                          "__int2half_rz __uint2half_rz __ll2half_rz __ull2half_rz ")) {  // emit.py:2586-2600
+        Str src = arg0("0");
+        const char *sp = na && arg(0).k == O_VAL ? ptx_type(V(arg(0).x).ty) : "s32";
+        SB b = sb();
+        b.s("    cvt.").s(ends_with(f, "_rz") ? "rz" : "rn").s(".f16.").s(sp).c(' ').s(dest).s(", ").s(src).c(';');
+        put(b);
+    } else if (in_list(f, " __half2int_rn __half2uint_rn __half2short_rn __half2ushort_rn __half2ll_rn __half2ull_rn "
+                          "__half2int_rz __half2uint_rz __half2short_rz __half2ushort_rz __half2ll_rz __half2ull_rz ")) {
+        // emit.py:2601-2614
+        Str src = arg0("0h0000");
+        const char *dp = in.dest >= 0 ? ptx_type(V((uint32_t)in.dest).ty) : "s32";
+        SB b = sb();
+        b.s("    cvt.").s(ends_with(f, "_rz") ? "rzi." : "rni.").s(dp).s(".f16 ").s(dest).s(", ").s(src).c(';');
+        put(b);
+    } else if (in_list(f, " __float2half __float2half_rn __float2half_rd __float2half_ru __float2half_rz ")) {
+        // emit.py:2615-2626
+        const char *rm = eq(f, "__float2half_rd") ? "rm" : eq(f, "__float2half_ru") ? "rp" :
+                         eq(f, "__float2half_rz") ? "rz" : "rn";
+        Str src = arg0("0f00000000");
+        SB b = sb();
+        b.s("    cvt.").s(rm).s(".f16.f32 ").s(dest).s(", ").s(src).c(';');
+        put(b);
+    } else if (in_list(f, " __half2float __low2float __high2float ")) {  // emit.py:2627-2629
+        line1("cvt.f32.f16", dest, arg0("0h0000"));
+    } else if (in_list(f, " __hmul __hmul_rn __hmul_sat __hsub __hsub_rn __hfmin __hmin __hfmax __hmax ")) {
+        // two-operand f16 arithmetic (emit.py:2630-2641, 2655-2662)
+        const char *op = eq(f, "__hmul_sat") ? "mul.rn.sat.f16" : sstarts(f, "__hmul") ? "mul.rn.f16" :
+                         sstarts(f, "__hsub") ? "sub.rn.f16" : (eq(f, "__hfmin") || eq(f, "__hmin")) ? "min.f16" :
+                         "max.f16";
+        Str a = arg0("0h0000");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0h0000");
+        SB b = sb();
+        b.s("    ").s(op).c(' ').s(dest).s(", ").s(a).s(", ").s(bb).c(';');
+        put(b);
+    } else if (in_list(f, " __hfma __hfma_sat __hfma_relu ")) {  // emit.py:2663-2673
+        Str a = arg0("0h0000");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0h0000");
+        Str c = na > 2 ? opnd(arg(2)) : S("0h0000");
+        SB b = sb();
+        b.s("    fma.rn").s(eq(f, "__hfma_sat") ? ".sat" : eq(f, "__hfma_relu") ? ".relu" : "").s(".f16 ").s(dest)
+            .s(", ").s(a).s(", ").s(bb).s(", ").s(c).c(';');
+        put(b);
+    } else if (eq(f, "__habs") || eq(f, "__hneg")) {  // emit.py:2674-2679
+        line1(eq(f, "__habs") ? "abs.f16" : "neg.f16", dest, arg0("0h0000"));
+    } else if (eq(f, "__hexp2")) {  // emit.py:2722-2725
+        line1("ex2.approx.f16", dest, arg0("0h0000"));
+    } else if (eq(f, "__hdiv")) {  // a * f16(rcp(f32(b))) (emit.py:2642-2654)
+        Str a = arg0("0h0000");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0h3C00");
+        uint32_t fb = new_value(nm("_hdiv_b_", dn), S_FLOAT);
+        uint32_t fr = new_value(nm("_hdiv_r_", dn), S_FLOAT);
+        uint32_t hr = new_value(nm("_hdiv_h_", dn), S_HALF);
+        line1("cvt.f32.f16", reg(fb), bb);
+        line1("rcp.approx.f32", reg(fr), reg(fb));
+        line1("cvt.rn.f16.f32", reg(hr), reg(fr));
+        SB b = sb();
+        b.s("    mul.rn.f16 ").s(dest).s(", ").s(a).s(", ").s(reg(hr)).c(';');
+        put(b);
+    } else if (in_list(f, " __hrcp __hsqrt __hrsqrt __hexp __hlog __hceil __hfloor __hrint __htrunc "
+                          "__hcos __hsin __hlog2 __hlog10 ")) {
+        // through f32 and back (emit.py:2680-2721)
+        Str src = arg0("0h0000");
+        uint32_t fi = new_value(nm("_hf32in_", dn), S_FLOAT);
+        uint32_t fo = new_value(nm("_hf32out_", dn), S_FLOAT);
+        line1("cvt.f32.f16", reg(fi), src);
+        if (eq(f, "__hrcp")) {
+            line1("rcp.approx.f32", reg(fo), reg(fi));
+        } else if (eq(f, "__hsqrt")) {
+            line1("sqrt.approx.f32", reg(fo), reg(fi));
+        } else if (eq(f, "__hrsqrt")) {
+            line1("rsqrt.approx.f32", reg(fo), reg(fi));
+        } else if (eq(f, "__hexp")) {
+            uint32_t sc = new_value(nm("_hscale_", dn), S_FLOAT);
+            SB b = sb();
+            b.s("    mul.f32 ").s(reg(sc)).s(", ").s(reg(fi)).s(", 0f3FB8AA3B;");
+            put(b);
+            line1("ex2.approx.f32", reg(fo), reg(sc));
+        } else if (eq(f, "__hlog") || eq(f, "__hlog10")) {
+            uint32_t lg = new_value(nm("_hlg2_", dn), S_FLOAT);
+            line1("lg2.approx.f32", reg(lg), reg(fi));
+            SB b = sb();
+            b.s("    mul.f32 ").s(reg(fo)).s(", ").s(reg(lg)).s(eq(f, "__hlog") ? ", 0f3F317218;" : ", 0f3E9A209B;");
+            put(b);
+        } else if (eq(f, "__hlog2")) {
+            line1("lg2.approx.f32", reg(fo), reg(fi));
+        } else if (eq(f, "__hcos")) {
+            line1("cos.approx.f32", reg(fo), reg(fi));
+        } else if (eq(f, "__hsin")) {
+            line1("sin.approx.f32", reg(fo), reg(fi));
+        } else {
+            uint32_t it = new_value(nm("_hint_", dn), S_INT32);
+            const char *rm = eq(f, "__hceil") ? "cvt.rpi.s32.f32" : eq(f, "__hfloor") ? "cvt.rmi.s32.f32" :
+                             eq(f, "__hrint") ? "cvt.rni.s32.f32" : "cvt.rzi.s32.f32";
+            line1(rm, reg(it), reg(fi));
+            line1("cvt.rn.f32.s32", reg(fo), reg(it));
+        }
+        line1("cvt.rn.f16.f32", dest, reg(fo));
+    } else if (in_list(f, " __hgt __hlt __hge __hle __heq __hne ")) {  // setp.f16 + selp (emit.py:2726-2738)
+        const char *cmp = eq(f, "__hgt") ? "gt" : eq(f, "__hlt") ? "lt" : eq(f, "__hge") ? "ge" :
+                          eq(f, "__hle") ? "le" : eq(f, "__heq") ? "eq" : "ne";
+        Str a = arg0("0h0000");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0h0000");
+        uint32_t pt = new_value(nm("_hcmp_", dn), S_BOOL);
+        add_pred(V(pt).id);
+        SB b1 = sb();
+        b1.s("    setp.").s(cmp).s(".f16 ").s(reg(pt)).s(", ").s(a).s(", ").s(bb).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    selp.s32 ").s(dest).s(", 1, 0, ").s(reg(pt)).c(';');
+        put(b2);
+    } else if (eq(f, "__hisnan") || eq(f, "__hisinf")) {  // via f32 testp (emit.py:2739-2749)
+        Str src = arg0("0h0000");
+        uint32_t ft = new_value(nm("_h2f_", dn), S_FLOAT);
+        uint32_t pt = new_value(nm("_htest_", dn), S_BOOL);
+        add_pred(V(pt).id);
+        line1("cvt.f32.f16", reg(ft), src);
+        SB b1 = sb();
+        b1.s("    testp.").s(eq(f, "__hisnan") ? "notanumber" : "infinite").s(".f32 ").s(reg(pt)).s(", ")
+            .s(reg(ft)).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    selp.s32 ").s(dest).s(", 1, 0, ").s(reg(pt)).c(';');
+        put(b2);
+    } else if (in_list(f, " asinf asin acosf acos ")) {
+        // asin(x) = atan(x / sqrt(1 - x^2)) with the atan series; acos = pi/2 - asin (emit.py:2772-2829)
+        bool ac = sstarts(f, "acos");
+        const char *pf = ac ? "_acos_" : "_asin_";
+        Str x = arg0("0f00000000");
+        auto val = [&](const char *suffix) {
+            SB b = sb();
+            b.s(pf).s(suffix).i(dn);
+            return new_value(b.str(), S_FLOAT);
+        };
+        uint32_t x2 = val("x2_"), om = val("om_"), sq = val("sq_"), rat = val("r_");
+        uint32_t ax2 = val("ax2_"), ax4 = val("ax4_"), ax6 = val("ax6_"), pp = val("p_"), p2 = val("p2_");
+        uint32_t as = ac ? val("as_") : 0;
+        SB b1 = sb();
+        b1.s("    mul.f32 ").s(reg(x2)).s(", ").s(x).s(", ").s(x).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    fma.rn.f32 ").s(reg(om)).s(", ").s(reg(x2)).s(", 0fBF800000, 0f3F800000;");
+        put(b2);
+        line1("sqrt.approx.f32", reg(sq), reg(om));
+        SB b3 = sb();
+        b3.s("    div.approx.f32 ").s(reg(rat)).s(", ").s(x).s(", ").s(reg(sq)).c(';');
+        put(b3);
+        SB b4 = sb();
+        b4.s("    mul.f32 ").s(reg(ax2)).s(", ").s(reg(rat)).s(", ").s(reg(rat)).c(';');
+        put(b4);
+        SB b5 = sb();
+        b5.s("    mul.f32 ").s(reg(ax4)).s(", ").s(reg(ax2)).s(", ").s(reg(ax2)).c(';');
+        put(b5);
+        SB b6 = sb();
+        b6.s("    mul.f32 ").s(reg(ax6)).s(", ").s(reg(ax4)).s(", ").s(reg(ax2)).c(';');
+        put(b6);
+        SB b7 = sb();
+        b7.s("    fma.rn.f32 ").s(reg(pp)).s(", ").s(reg(ax6)).s(", 0fBE124925, 0f3F800000;");
+        put(b7);
+        SB b8 = sb();
+        b8.s("    fma.rn.f32 ").s(reg(p2)).s(", ").s(reg(ax4)).s(", 0f3E4CCCCD, ").s(reg(pp)).c(';');
+        put(b8);
+        SB b9 = sb();
+        b9.s("    fma.rn.f32 ").s(reg(pp)).s(", ").s(reg(ax2)).s(", 0fBEAAAAAB, ").s(reg(p2)).c(';');
+        put(b9);
+        SB b10 = sb();
+        b10.s("    mul.f32 ").s(ac ? reg(as) : dest).s(", ").s(reg(rat)).s(", ").s(reg(pp)).c(';');
+        put(b10);
+        if (ac) {
+            SB b11 = sb();
+            b11.s("    sub.f32 ").s(dest).s(", 0f3FC90FDB, ").s(reg(as)).c(';');
+            put(b11);
+        }
+    } else if (in_list(f, " __dp4a __dp4a_u __dp4a_su __dp4a_us ")) {  // emit.py:2433-2446
+        const char *op = eq(f, "__dp4a_u") ? "dp4a.u32.u32" : eq(f, "__dp4a_su") ? "dp4a.s32.u32" :
+                         eq(f, "__dp4a_us") ? "dp4a.u32.s32" : "dp4a.s32.s32";
+        Str a = arg0("0");
+        Str bb = na > 1 ? opnd(arg(1)) : S("0");
+        Str c = na > 2 ? opnd(arg(2)) : S("0");
+        SB b = sb();
+        b.s("    ").s(op).c(' ').s(dest).s(", ").s(a).s(", ").s(bb).s(", ").s(c).c(';');
+        put(b);
+    } else if (in_list(f, " __funnelshift_l __funnelshift_lc __funnelshift_r __funnelshift_rc ")) {
+        // shf (emit.py:2540-2553): clamp for the *c forms, wrap otherwise
+        Str lo = arg0("0");
+        Str hi = na > 1 ? opnd(arg(1)) : S("0");
+        Str sh = na > 2 ? opnd(arg(2)) : S("0");
+        bool left = sstarts(f, "__funnelshift_l");
+        bool clamp = f.p[f.n - 1] == 'c';
+        SB b = sb();
+        b.s("    shf.").s(left ? "l" : "r").c('.').s(clamp ? "clamp" : "wrap").s(".b32 ").s(dest)
+            .s(", ").s(lo).s(", ").s(hi).s(", ").s(sh).c(';');
+        put(b);
+    } else if (in_list(f, " atanf atan ")) {  // x * (1 - x^2/3 + x^4/5 - x^6/7) (emit.py:2756-2771)
+        Str x = arg0("0f00000000");
+        uint32_t x2 = new_value(nm("_atan_x2_", dn), S_FLOAT);
+        uint32_t x4 = new_value(nm("_atan_x4_", dn), S_FLOAT);
+        uint32_t x6 = new_value(nm("_atan_x6_", dn), S_FLOAT);
+        uint32_t pp = new_value(nm("_atan_p_", dn), S_FLOAT);
+        uint32_t p2 = new_value(nm("_atan_p2_", dn), S_FLOAT);
+        SB b1 = sb();
+        b1.s("    mul.f32 ").s(reg(x2)).s(", ").s(x).s(", ").s(x).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    mul.f32 ").s(reg(x4)).s(", ").s(reg(x2)).s(", ").s(reg(x2)).c(';');
+        put(b2);
+        SB b3 = sb();
+        b3.s("    mul.f32 ").s(reg(x6)).s(", ").s(reg(x4)).s(", ").s(reg(x2)).c(';');
+        put(b3);
+        SB b4 = sb();
+        b4.s("    fma.rn.f32 ").s(reg(pp)).s(", ").s(reg(x6)).s(", 0fBE124925, 0f3F800000;");
+        put(b4);
+        SB b5 = sb();
+        b5.s("    fma.rn.f32 ").s(reg(p2)).s(", ").s(reg(x4)).s(", 0f3E4CCCCD, ").s(reg(pp)).c(';');
+        put(b5);
+        SB b6 = sb();
+        b6.s("    fma.rn.f32 ").s(reg(pp)).s(", ").s(reg(x2)).s(", 0fBEAAAAAB, ").s(reg(p2)).c(';');
+        put(b6);
+        SB b7 = sb();
+        b7.s("    mul.f32 ").s(dest).s(", ").s(x).s(", ").s(reg(pp)).c(';');
+        put(b7);
+    } else if (in_list(f, " atan2f atan2 ")) {  // y/x through a truncated series (emit.py:2854-2885)
+        Str y = arg0("0f00000000");
+        Str x = na > 1 ? opnd(arg(1)) : S("0f3F800000");
+        uint32_t ratio = new_value(nm("_atan2_r_", dn), S_FLOAT);
+        new_value(nm("_atan2_l_", dn), S_FLOAT);   // allocated but unused, as there
+        new_value(nm("_atan2_e_", dn), S_FLOAT);
+        new_value(nm("_atan2_sv_", dn), S_FLOAT);
+        new_value(nm("_atan2_cv_", dn), S_FLOAT);
+        uint32_t t2 = new_value(nm("_atan2_t2_", dn), S_FLOAT);
+        uint32_t t4 = new_value(nm("_atan2_t4_", dn), S_FLOAT);
+        uint32_t poly = new_value(nm("_atan2_p_", dn), S_FLOAT);
+        SB b1 = sb();
+        b1.s("    div.approx.f32 ").s(reg(ratio)).s(", ").s(y).s(", ").s(x).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    mul.f32 ").s(reg(t2)).s(", ").s(reg(ratio)).s(", ").s(reg(ratio)).c(';');
+        put(b2);
+        SB b3 = sb();
+        b3.s("    mul.f32 ").s(reg(t4)).s(", ").s(reg(t2)).s(", ").s(reg(t2)).c(';');
+        put(b3);
+        SB b4 = sb();
+        b4.s("    fma.rn.f32 ").s(reg(poly)).s(", ").s(reg(t4)).s(", 0f3E4CCCCD, ").s(reg(ratio)).c(';');
+        put(b4);
+        SB b5 = sb();
+        b5.s("    fma.rn.f32 ").s(dest).s(", ").s(reg(t2)).s(", 0fBEAAAAAB, ").s(reg(poly)).c(';');
+        put(b5);
     } else if (eq(f, "__byte_perm")) {  // prmt (emit.py:2534-2539)
         Str a = arg0("0");
         Str bb = na > 1 ? opnd(arg(1)) : S("0");
@@ -968,6 +1307,16 @@ OCB_HD inline void Emit::emit_inst(uint32_t ix) {
         SB b = sb();
         b.s("    ld.param.").s(pt).c(' ').s(reg(in.dest)).s(", [").s(in.func).s("];");
         put(b);
+        break;
+    }
+    case I_GADDR: {  // generic address of the symbol, then into its state space (emit.py:1169-1178)
+        Str d = reg(in.dest);
+        SB b1 = sb();
+        b1.s("    mov.u64 ").s(d).s(", ").s(in.func).c(';');
+        put(b1);
+        SB b2 = sb();
+        b2.s("    cvta.to.").s(in.op == AS_CONST ? "const" : "global").s(".u64 ").s(d).s(", ").s(d).c(';');
+        put(b2);
         break;
     }
     case I_BIN: emit_bin(in); break;

@@ -765,6 +765,22 @@ OCB_HD inline bool emit_module(Module &m, Arena &tmp, Out &o, const char *arch) 
     o.put(arch);
     o.put('\n');
     line(S(".address_size 64"));
+    // module-level variable declarations lead the preamble (emit.py:3164-3190)
+    if (m.gvars.n) {
+        Vec<Str> pre;
+        pre.init();
+        for (uint32_t q = 0; q < m.gvars.n; ++q) {
+            const GVar &g = m.gvars[q];
+            SB b = E.sb();
+            b.s(".visible .").s(g.space == AS_CONST ? "const" : "global").s(" .align ");
+            b.i(is_ptr(g.elem) ? 8 : (pyint)ty_size(g.elem)).s(" .").s(ptx_type(g.elem)).c(' ').s(g.name);
+            if (g.count > 1) b.c('[').i(g.count).c(']');
+            b.c(';');
+            pre.push(*m.ar, b.str());
+        }
+        for (uint32_t q = 0; q < E.preamble.n; ++q) pre.push(*m.ar, E.preamble[q]);
+        E.preamble = pre;
+    }
     // all lines are joined by '\n' without a trailing newline
     Vec<Str> all;
     all.init();

@@ -204,6 +204,11 @@ OCB_HD inline bool starts(Str a, const char *b) {
         if (i >= a.n || a.p[i] != b[i]) return false;
     return true;
 }
+OCB_HD inline bool ends_with(Str a, const char *b) {
+    uint32_t n = 0;
+    while (b[n]) ++n;
+    return n <= a.n && mem_eq(a.p + a.n - n, b, n);
+}
 OCB_HD inline uint32_t hash(Str s) {
     uint32_t h = 2166136261u;
     for (uint32_t i = 0; i < s.n; ++i) h = (h ^ (uint8_t)s.p[i]) * 16777619u;
@@ -334,10 +339,12 @@ struct Const {
     pyint i;
     double f;
 };
-enum : uint8_t { O_NONE = 0, O_VAL = 1, O_CONST = 2 };
+// O_SYM: a module-level __device__ / __constant__ symbol used directly as an
+// address (the reference's SymbolRef); x indexes Module::gvars.
+enum : uint8_t { O_NONE = 0, O_VAL = 1, O_CONST = 2, O_SYM = 3 };
 struct Opnd {
     uint8_t k;
-    uint32_t x;  // index into values / consts
+    uint32_t x;  // index into values / consts / gvars
 };
 OCB_HD inline Opnd ov(uint32_t v) { return Opnd{O_VAL, v}; }
 OCB_HD inline Opnd oc(uint32_t c) { return Opnd{O_CONST, c}; }
@@ -354,7 +361,9 @@ OCB_HD inline const char *cmpop_name(uint8_t o) {
     return n[o];
 }
 
-enum : uint8_t { I_BIN = 0, I_CMP, I_SELECT, I_LOAD, I_STORE, I_CVT, I_CALL, I_PARAM };
+// I_GADDR: the address of a module symbol into a u64 register (GlobalAddrInst,
+// ir/nodes.py:166-178); func = symbol name, op = its address space.
+enum : uint8_t { I_BIN = 0, I_CMP, I_SELECT, I_LOAD, I_STORE, I_CVT, I_CALL, I_PARAM, I_GADDR };
 struct Inst {
     uint8_t kind, op;
     int32_t dest;     // value index, -1 = none
@@ -405,6 +414,16 @@ struct Kernel {
     bool has_locals;           // the reference created _local_decls
 };
 
+// A module-level variable (Module.global_vars, ir/nodes.py:289): element
+// type, element count, address space (AS_GLOBAL or AS_CONST), and the
+// pointer type its symbol carries.
+struct GVar {
+    Str name;
+    Ty elem, ptr;
+    uint32_t count;
+    uint32_t space;
+};
+
 // All IR objects of one TU.
 struct Module {
     Arena *ar;
@@ -413,6 +432,7 @@ struct Module {
     Vec<Inst> insts;
     Vec<Block> blocks;
     Vec<Kernel> kernels;
+    Vec<GVar> gvars;          // in declaration order
     bool unsup;               // the engine cannot reproduce this TU
     int raises;               // reference exception (OCB_TU_RAISES_*) or 0
 
@@ -423,6 +443,7 @@ struct Module {
         insts.init();
         blocks.init();
         kernels.init();
+        gvars.init();
         unsup = false;
         raises = 0;
         // Reserved up front so the tables are never empty-and-unallocated: a
@@ -453,6 +474,7 @@ struct Module {
     OCB_HD Ty opty(Opnd o) const {
         if (o.k == O_VAL) return vals[o.x].ty;
         if (o.k == O_CONST) return consts[o.x].ty;
+        if (o.k == O_SYM) return gvars[o.x].ptr;
         return S_VOID;
     }
     OCB_HD uint32_t new_block(Str label) {

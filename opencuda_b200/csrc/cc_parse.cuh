@@ -574,6 +574,8 @@ struct Parser {
     OCB_HD OCB_NI void parse_expr_stmt();
     OCB_HD OCB_NI void parse_kernel();
     OCB_HD OCB_NI void parse_module();
+    OCB_HD OCB_NI void parse_gvar(bool constant_form);
+    OCB_HD Opnd gaddr(uint32_t g);
 };
 
 }  // namespace cc

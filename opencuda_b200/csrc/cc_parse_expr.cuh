@@ -492,6 +492,29 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
         bool generic = true;
         if (at(TK_IDENT)) {
             Str name = peekv();
+            Opnd *gs = global_consts.get(name);
+            if (gs && gs->k == O_SYM) {  // &global, &global[idx] (parser.py:978-1016)
+                uint32_t gi = gs->x;
+                advance();
+                Opnd addr = gaddr(gi);
+                if (match(TK_LBRACKET)) {
+                    Opnd index = parse_expr();
+                    if (bad() || !expect(TK_RBRACKET)) { --nest; return onone(); }
+                    Ty gp = m.gvars[gi].ptr;
+                    uint32_t es = ty_size(ty_pointee(gp));
+                    if (es != 1) {
+                        Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                        uint32_t sc = new_val("scale", it);
+                        emit_bin(sc, BO_MUL, index, m.cint(it, es));
+                        index = ov(sc);
+                    }
+                    uint32_t ea = new_val("elem_addr", gp);
+                    emit_bin(ea, BO_ADD, addr, index);
+                    addr = ov(ea);
+                }
+                --nest;
+                return addr;
+            }
             Opnd *vp = vars.get(name);
             if (vp) {
                 Opnd var = *vp;
@@ -1154,7 +1177,16 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
             }
             return var;
         }
-        if (Opnd *g = global_consts.get(name)) return *g;
+        if (Opnd *g = global_consts.get(name)) {
+            if (g->k != O_SYM) return *g;
+            // module variable (parser.py:2164-2185): its address before '[' and
+            // for a non-scalar, else a load of the scalar through the symbol
+            uint32_t gi = g->x;
+            if (at(TK_LBRACKET) || is_ptr(m.gvars[gi].elem)) return gaddr(gi);
+            uint32_t d = new_val(m.gvars[gi].name, m.gvars[gi].elem);
+            emit_load(d, Opnd{O_SYM, gi});
+            return ov(d);
+        }
         if (eq(name, "true")) return m.cint(S_INT32, 1);
         if (eq(name, "false")) return m.cint(S_INT32, 0);
         if (eq(name, "NULL")) return m.cint(S_UINT64, 0);

@@ -52,6 +52,37 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
     if (k == TK_IDENT) {
         Str name = peekv();
         Opnd *vp = vars.get(name);
+        Opnd *gs = vp ? nullptr : global_consts.get(name);
+        if (gs && gs->k == O_SYM && pos + 1 < tk.n) {
+            // module variable as an lvalue: its address, or its element's
+            // (parser.py:3433-3522)
+            uint32_t nk = kind_at(pos + 1);
+            if (nk == TK_ASSIGN || nk == TK_PLUS_EQ || nk == TK_MINUS_EQ || nk == TK_STAR_EQ ||
+                nk == TK_SLASH_EQ || nk == TK_PERCENT_EQ || nk == TK_AMP_EQ || nk == TK_PIPE_EQ ||
+                nk == TK_CARET_EQ || nk == TK_LSHIFT_EQ || nk == TK_RSHIFT_EQ || nk == TK_LBRACKET ||
+                nk == TK_DOT) {
+                uint32_t gi = gs->x;
+                advance();
+                Opnd addr = gaddr(gi);
+                if (at(TK_LBRACKET)) {
+                    advance();
+                    Opnd index = parse_expr();
+                    if (bad() || !expect(TK_RBRACKET)) return onone();
+                    Ty gp = m.gvars[gi].ptr;
+                    uint32_t es = ty_size(ty_pointee(gp));
+                    if (es != 1) {
+                        Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                        uint32_t sc = new_val("scale", it);
+                        emit_bin(sc, BO_MUL, index, m.cint(it, es));
+                        index = ov(sc);
+                    }
+                    uint32_t ea = new_val("addr", gp);
+                    emit_bin(ea, BO_ADD, addr, index);
+                    return ov(ea);
+                }
+                return addr;
+            }
+        }
         if (vp && is_ptr(tyof(*vp))) {
             Opnd var = *vp;
             Ty vt = tyof(var);
@@ -1297,6 +1328,85 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
 
 // parse_module (parser.py:4194-4437): pass 1 registers module-level names and
 // records kernel positions; pass 2 parses the kernels in order.
+// A module-level variable: `__device__ [static] [__constant__] [volatile] T
+// name[N] [= init];` (parser.py:4305-4366) or `__constant__ [const|static|
+// __device__]* T name[N] [= init];` (parser.py:4155-4191).  The initializer is
+// skipped, as there; the name is bound to a symbol in the same table as the
+// module's enum constants, and the variable joins the module's declarations.
+OCB_HD inline void Parser::parse_gvar(bool constant_form) {
+    bool is_const = constant_form, is_vol = false;
+    if (constant_form) {
+        advance();  // __constant__
+        while (at(TK_CONST) || at(TK_STATIC) || at(TK_DEVICE)) advance();
+    } else {
+        while (at(TK_DEVICE) || at(TK_STATIC)) advance();
+        if (at(TK_CONSTANT)) {
+            is_const = true;
+            advance();
+        }
+        if (at(TK_VOLATILE)) {
+            is_vol = true;
+            advance();
+        }
+    }
+    Ty t;
+    if (!parse_type_with_ptr(t)) return;
+    if (!constant_form && is_ptr(t) && ty_vol(t)) is_vol = true;
+    if (!at(TK_IDENT)) { perr(); return; }
+    Str name = peekv();
+    advance();
+    int64_t count = 1;
+    if (match(TK_LBRACKET)) {
+        Opnd so = parse_assign_expr();
+        if (bad()) return;
+        if (!const_dim(*this, so, count)) return;
+        if (!expect(TK_RBRACKET)) return;
+        if (at(TK_LBRACKET)) {  // row strides of multi-dimensional globals are outside the subset
+            unsup();
+            return;
+        }
+    }
+    if (count > 0x7fffffff || count < -0x7fffffff) { unsup(); return; }
+    if (match(TK_ASSIGN)) {  // skip the initializer
+        int depth = 0;
+        while (!at(TK_EOF) && !bad()) {
+            uint32_t kk = peek();
+            if (kk == TK_LBRACE) {
+                depth++;
+                advance();
+            } else if (kk == TK_RBRACE) {
+                depth--;
+                advance();
+                if (depth == 0) break;
+            } else if (depth == 0 && kk == TK_SEMI) {
+                break;
+            } else {
+                advance();
+            }
+        }
+    }
+    match(TK_SEMI);
+    uint32_t sp = is_const ? AS_CONST : AS_GLOBAL;
+    bool ok = true;
+    Ty pt = ty_ptr(t, sp, is_vol, ok);
+    if (!ok) { unsup(); return; }
+    if (!m.gvars.push(ar, GVar{name, t, pt, (uint32_t)(int32_t)count, sp})) { unsup(); return; }
+    global_consts.set(ar, name, Opnd{O_SYM, m.gvars.n - 1});
+}
+
+// GlobalAddrInst(Value(f"{sym}_ptr", sym.ty), sym, space)
+OCB_HD inline Opnd Parser::gaddr(uint32_t g) {
+    const GVar &gv = m.gvars[g];
+    uint32_t d = new_val(cat(ar, gv.name, S("_ptr")), gv.ptr);
+    Inst in{};
+    in.kind = I_GADDR;
+    in.op = (uint8_t)gv.space;
+    in.dest = (int32_t)d;
+    in.func = gv.name;
+    emit(in);
+    return ov(d);
+}
+
 OCB_HD inline void Parser::parse_module() {
     if (bad() || !m.vals.cap || !m.blocks.cap || !m.insts.cap || !m.consts.cap) {
         ar.oom = true;
@@ -1395,12 +1505,14 @@ OCB_HD inline void Parser::parse_module() {
                 if (lk == TK_SEMI || lk == TK_EOF) break;
             }
             if (!is_func) {
-                unsup();  // __device__ variables
-                return;
+                parse_gvar(false);
+                continue;
             }
             parse_device_func();
-        } else if (k == TK_STRUCT || k == TK_UNION || k == TK_CONSTANT) {
-            unsup();  // structs, __constant__
+        } else if (k == TK_CONSTANT) {
+            parse_gvar(true);
+        } else if (k == TK_STRUCT || k == TK_UNION) {
+            unsup();  // structs
             return;
         } else if (k == TK_SHARED) {
             advance();

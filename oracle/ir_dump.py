@@ -76,6 +76,9 @@ def inst_str(i) -> str:
         return f"{op_str(i.dest)} = cvt {op_str(i.src)}"
     if isinstance(i, N.CallInst):
         return f"{op_str(i.dest)} = call {i.func}({', '.join(op_str(a) for a in i.args)})"
+    if isinstance(i, N.GlobalAddrInst):
+        asp = i.addr_space.value if hasattr(i.addr_space, "value") else str(i.addr_space)
+        return f"{op_str(i.dest)} = gaddr @{i.sym_name} {asp}"
     if isinstance(i, N.ParamInst):
         return f"{op_str(i.dest)} = param {i.param_index} {i.param_name}"
     return f"?{type(i).__name__}"
