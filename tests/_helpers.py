@@ -741,3 +741,103 @@ __global__ void ap0(float out[], const float in[256], int n) {
 }""",
     """__global__ void ap1(int a[], int *b, int k) { int t = threadIdx.x; a[t] = b[t] + a[t + k]; b[t] = a[0]; }""",
 ]
+
+MORE_INTRINSIC_CASES = [
+    """__global__ void m0(float *o, const float *in, int *io, unsigned *u) {
+    int t = threadIdx.x; float x = in[t]; float y = in[t + 1];
+    o[t] = atan2f(y, x) + atanf(x) + atan2f(1.0f, y);
+    io[t] = __dp4a(io[t], io[t + 1], 7) + (int)__dp4a_u(u[t], 3u, 1u);
+    u[t] = __funnelshift_l(u[t], u[t + 1], 5) + __funnelshift_rc(u[t], 0u, (unsigned)t);
+}""",
+]
+
+HALF_REDUCE_CASES = [
+    """__global__ void h0(__half *o, const __half *a, const __half *b, float *f, int n) {
+    int t = threadIdx.x;
+    __half x = a[t]; __half y = b[t];
+    __half s = __hadd(x, y); __half m = __hmul(s, y); __half d = __hsub(m, x);
+    __half q = __hdiv(d, y); __half r = __hfma(x, y, q);
+    o[t] = __hmax(__habs(r), __hneg(__hmin(x, y)));
+    f[t] = __half2float(r) + __low2float(__hsqrt(x)) + __half2float(__hexp(y)) + __half2float(__hlog10(x));
+    f[t + n] = (float)(__hlt(x, y) + __hisnan(r) + __heq(s, m));
+    o[t + n] = __float2half(f[t]) ;
+    o[t + 2 * n] = __float2half_rz(f[t + n]);
+}""",
+    """__global__ void h1(unsigned short *u, __half *o, int *io) {
+    int t = threadIdx.x;
+    __half h = __ushort_as_half(u[t]);
+    u[t + 1] = __half_as_ushort(h);
+    o[t] = __int2half_rn(io[t]);
+    io[t] = __half2int_rz(h) + __hadd(io[t], t) + __rhadd(t, 3);
+    o[t + 1] = __hceil(h);
+}""",
+    """__global__ void r0(int *o, const int *a, unsigned *u, float *f) {
+    int t = threadIdx.x;
+    int v = a[t];
+    o[t] = __reduce_add_sync(0xffffffff, v) + __reduce_min_sync(0xffffffff, v) + __reduce_max_sync(0xffffffff, v);
+    u[t] = __reduce_and_sync(0xffffffffu, u[t]) ^ __reduce_or_sync(0xffffffffu, u[t]) ^ __reduce_xor_sync(0xffffffffu, u[t])
+         ^ __reduce_umin_sync(0xffffffffu, u[t]) ^ __reduce_umax_sync(0xffffffffu, u[t]);
+    o[t + 32] = __match_any_sync(0xffffffff, v);
+    f[t] = asinf(f[t]) + acosf(f[t + 1]);
+}""",
+]
+
+GLOBAL_VAR_CASES = [
+    """__device__ int g_counter;
+__device__ float g_scale = 2.0f;
+__device__ int g_table[16];
+__global__ void k(int *out, float *f, const int *idx, int n) {
+    int t = threadIdx.x;
+    if (t < n) {
+        out[t] = atomicAdd(&g_counter, 1);
+        f[t] = f[t] * g_scale;
+        int i = idx[t] & 15;
+        out[t + n] = g_table[i] + atomicAdd(&g_table[i], 2);
+    }
+}""",
+    """__device__ __constant__ int dc_int = 100;
+__constant__ __device__ float cd_float = 2.5f;
+__constant__ float c_only = 1.5f;
+__constant__ __device__ int cd_table[8] = {1, 2, 3, 4, 5, 6, 7, 8};
+__constant__ double c_d[4] = {1.0, 2.0, 3.0, 4.0};
+__global__ void c(float *out, int *io, double *d, int n) {
+    int tid = threadIdx.x;
+    if (tid < n) {
+        out[tid] = (float)dc_int * cd_float + c_only * (float)tid;
+        io[tid] = cd_table[io[tid] & 7] * tid;
+        d[tid] = c_d[tid & 3] + c_d[0];
+    }
+}""",
+    """__device__ float g_acc;
+__device__ int g_hist[32];
+__device__ volatile int g_flag;
+__device__ unsigned long long g_big;
+__device__ char g_c[7];
+__device__ short g_s;
+__global__ void w(const float *in, int n) {
+    int t = threadIdx.x + blockIdx.x * blockDim.x;
+    g_acc = in[t];
+    g_acc += 1.0f;
+    g_hist[t & 31] = t;
+    g_hist[t & 31] += n;
+    g_hist[(t + 1) & 31] -= g_hist[t & 31];
+    g_flag = 1;
+    while (g_flag == 0) { }
+    g_big = (unsigned long long)t * 3ull;
+    g_c[t & 3] = (char)t;
+    g_s = (short)n;
+    for (int i = 0; i < 4; ++i) g_hist[i] = g_hist[i] + i;
+}""",
+    """__global__ void after(float *o, int n) {
+    int t = threadIdx.x;
+    if (t < n) o[t] = late_w[t & 3] * late_s;
+}
+__device__ float late_w[4] = {0.25f, 0.25f, 0.25f, 0.25f};
+__constant__ float late_s = 3.0f;
+__device__ float *g_ptr;
+__global__ void ptrs(float *o) {
+    int t = threadIdx.x;
+    g_ptr = o;
+    o[t] = (float)t;
+}""",
+]

@@ -11,7 +11,8 @@ from oracle import ref_runner
 from opencuda_b200.api import TU_UNSUPPORTED
 from tests._helpers import (ADDR_OF_CASES, CAST_CASES, DEVFUNC_CASES, DEVFUNC_RECURSIVE_CASES,
                             ARRAY_PARAM_CASES, HEXFLOAT_CASES, INTRINSIC_CASES,
-                            UNKNOWN_CALL_CASES, devfunc_sources)
+                            HALF_REDUCE_CASES, MORE_INTRINSIC_CASES, UNKNOWN_CALL_CASES,
+                            devfunc_sources)
 
 pytestmark = pytest.mark.gpu
 
@@ -21,7 +22,8 @@ RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError"
 @pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
 def test_device_functions_against_live_reference(ctx, stage):
     srcs = (DEVFUNC_CASES + ADDR_OF_CASES + UNKNOWN_CALL_CASES + INTRINSIC_CASES + CAST_CASES +
-            HEXFLOAT_CASES + ARRAY_PARAM_CASES + devfunc_sources(300, 31))
+            HEXFLOAT_CASES + ARRAY_PARAM_CASES + MORE_INTRINSIC_CASES + HALF_REDUCE_CASES +
+            devfunc_sources(300, 31))
     fn = {"ir": ctx.parse_batch, "opt": ctx.optimize_batch, "ptx": ctx.compile_batch}[stage]
     tb = fn(srcs)
     with ref_runner.RefPool() as pool:
