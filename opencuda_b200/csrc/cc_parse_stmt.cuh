@@ -69,6 +69,28 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                     Opnd index = parse_expr();
                     if (bad() || !expect(TK_RBRACKET)) return onone();
                     Ty gp = m.gvars[gi].ptr;
+                    Opnd *rs = row_strides.get(m.gvars[gi].name);
+                    if (rs && at(TK_LBRACKET)) {  // g[i][j]: row stride, then the element
+                        Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                        uint32_t sc = new_val("scale", it);
+                        emit_bin(sc, BO_MUL, index, m.cint(it, m.consts[rs->x].i));
+                        uint32_t ra = new_val("raddr", gp);
+                        emit_bin(ra, BO_ADD, addr, ov(sc));
+                        advance();
+                        Opnd col = parse_expr();
+                        if (bad() || !expect(TK_RBRACKET)) return onone();
+                        Ty et = ty_pointee(gp);
+                        uint32_t ces = is_ptr(et) ? 8 : ty_size(et);
+                        if (ces != 1) {
+                            Ty ct = isval(col) ? tyof(col) : (Ty)S_INT32;
+                            uint32_t s2 = new_val("scale", ct);
+                            emit_bin(s2, BO_MUL, col, m.cint(ct, ces));
+                            col = ov(s2);
+                        }
+                        uint32_t ea = new_val("addr", gp);
+                        emit_bin(ea, BO_ADD, ov(ra), col);
+                        return ov(ea);
+                    }
                     uint32_t es = ty_size(ty_pointee(gp));
                     if (es != 1) {
                         Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
@@ -1361,9 +1383,24 @@ OCB_HD inline void Parser::parse_gvar(bool constant_form) {
         if (bad()) return;
         if (!const_dim(*this, so, count)) return;
         if (!expect(TK_RBRACKET)) return;
-        if (at(TK_LBRACKET)) {  // row strides of multi-dimensional globals are outside the subset
-            unsup();
-            return;
+        // further dimensions of a __device__ array multiply the count and give
+        // the row stride its element-address lvalues use (parser.py:4334-4348);
+        // the __constant__ form reads one dimension and leaves the rest to the
+        // module loop, which skips it token by token
+        if (!constant_form && at(TK_LBRACKET)) {
+            int64_t inner = 1;
+            while (at(TK_LBRACKET) && !bad()) {
+                advance();
+                Opnd dop = parse_assign_expr();
+                if (bad()) return;
+                int64_t dim;
+                if (!const_dim(*this, dop, dim)) return;
+                if (!mul_dim(*this, count, dim) || !mul_dim(*this, inner, dim)) return;
+                if (!expect(TK_RBRACKET)) return;
+            }
+            int64_t es = is_ptr(t) ? 8 : (int64_t)ty_size(t);
+            if (!mul_dim(*this, inner, es)) return;
+            row_strides.set(ar, name, m.cint(S_INT32, inner));
         }
     }
     if (count > 0x7fffffff || count < -0x7fffffff) { unsup(); return; }

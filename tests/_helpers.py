@@ -841,3 +841,30 @@ __global__ void ptrs(float *o) {
     o[t] = (float)t;
 }""",
 ]
+
+GLOBAL_2D_CASES = [
+    """__device__ float g_m[4][8];
+__device__ double g_d[3][5];
+__global__ void m1(float *o, int n) {
+    int t = threadIdx.x;
+    g_m[t & 3][t & 7] = (float)t;
+    g_m[1][2] += 1.0f;
+    g_d[n][t] = 0.5;
+    o[t] = (float)t;
+}""",
+    """__device__ float g_m[4][8];
+__device__ int g_c[2][3][4];
+__global__ void m2(float *o, int n) {
+    int t = threadIdx.x;
+    g_m[t & 3][t & 7] = (float)t;
+    g_m[1][2] += 1.0f;
+    g_c[1][t & 3][0] = n;
+    o[t] = g_m[t & 3][0] + (float)g_c[0][1][2];
+}""",
+    """__constant__ float c_k[3][3] = {{1, 2, 1}, {2, 4, 2}, {1, 2, 1}};
+__constant__ int c_after = 5;
+__global__ void cv(float *o, const float *in, int w) {
+    int t = threadIdx.x;
+    o[t] = in[t] * c_k[1][1] + (float)c_after;
+}""",
+]

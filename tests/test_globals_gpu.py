@@ -10,9 +10,11 @@ import pytest
 
 import opencuda_b200 as oc
 from oracle import ref_runner
-from tests._helpers import GLOBAL_VAR_CASES
+from tests._helpers import GLOBAL_2D_CASES, GLOBAL_VAR_CASES
 
 pytestmark = pytest.mark.gpu
+
+RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError": 4}
 
 
 @pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
@@ -35,3 +37,24 @@ def test_module_variable_declarations_through_compile():
         ptx = oc.compile(src)
         assert ptx == r["ptx"]
         assert ptx.split("\n")[4].startswith(".visible .")
+
+
+@pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
+def test_multi_dimensional_module_arrays_against_live_reference(ctx, stage):
+    """`__device__ T g[R][C]` carries a row stride that only the element
+    lvalue `g[i][j] = v` uses (the rvalue path looks the stride up under the
+    address value's name, as the reference does); a `__constant__` array reads
+    one dimension and the module loop skips the rest.  Where the reference
+    raises, the engine must report the same exception class."""
+    srcs = GLOBAL_2D_CASES
+    fn = {"ir": ctx.parse_batch, "opt": ctx.optimize_batch, "ptx": ctx.compile_batch}[stage]
+    tb = fn(srcs)
+    with ref_runner.RefPool() as pool:
+        ref = pool.run(srcs, what=(stage,))
+    for i, r in enumerate(ref):
+        st = int(tb.status[i])
+        if stage not in r:
+            assert st == RAISE_STATUS.get(r["error"][0], 6), (i, r["error"], st)
+            continue
+        assert st == 0, (i, st)
+        assert tb.text(i) == r[stage], (i, srcs[i])
