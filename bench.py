@@ -3,29 +3,42 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (one "step"): compile 4,096 seeded random kernels (50-200 statements
-each, ~4.6 KB, ~19 MB of CUDA C per GPU; 60% s32 / 40% f32 arithmetic,
-if/else depth <= 3, unrollable for loops of trip 2-16, atomics and
-__shfl_sync) to PTX: preprocess -> lex -> parse -> optimize -> register
-allocation -> PTX text, with the arena reruns for TUs that outgrow their first
-slice.  Each GPU compiles its own 4,096 kernels (another seed per rank: weak
-scaling, TUs shard with no collective).  The working set of a step (arenas of
-~13 GB) is far larger than L2, so no flush is needed between steps.
+Workload: the 262,144 seeded lognormal-size kernels (median 3 KB, sigma 1,
+1.20 GiB of CUDA C; the statement mix of the random kernels: 60% s32 / 40%
+f32 arithmetic, if/else depth <= 3, unrollable for loops of trip 2-16,
+atomics and __shfl_sync), compiled to PTX: preprocess -> lex -> parse ->
+optimize -> register allocation -> PTX text.  The batch is split into
+``--slices`` interleaved slices (slice j = kernels i with i % S == j, so
+every slice has the batch's size distribution); one step compiles one slice,
+step k slice k % S, so K >= S timed steps compile the whole batch.  With N
+ranks (one per GPU) every slice is split across the ranks by bytes with
+greedy LPT (strong scaling: the job's total work does not depend on N).
+The working set of a step (GBs of compiler arenas) is far larger than L2, so
+no flush is needed between steps.
 
-* ``value``      -- source MB/s over all GPUs with the batch resident in HBM
-                    (``ocb_compile_device``), timed with CUDA events on the
-                    context's stream, max over ranks.
-* ``e2e``        -- the same metric through the public host API
-                    (``Context.compile_batch``: pinned source -> device -> PTX
-                    text, offsets and statuses back on the host).
-* ``roofline``   -- the dominant kernel: end-to-end compile bytes (source +
-                    PTX of the TUs of one launch) / its mean launch time,
-                    against the measured HBM copy peak.
-* ``cpu_baseline`` -- the reference compiler (pure Python, oracle/_ref/py) on
-                    all host cores over a bounded sample of the same kernels.
-* ``lexer``      -- the batch lexer over 1 GiB of lexer stress text per GPU
-                    (GB/s of source and its HBM roofline fraction).
-* ``latency_sgemm`` -- batch-1 latency of the tiled SGEMM kernel, end to end.
+Every timed step is bracketed by a barrier and a device synchronisation and
+timed with CUDA events on the context's stream; the step time is the max
+over ranks.  After each step, outside the timed region, every TU's PTX is
+compared with the reference compiler's output (sha256 digests made once by
+``python -m oracle.goldens c5``); ``value`` counts only the source bytes of
+TUs whose PTX is byte-identical.
+
+* ``value``   -- byte-identical source MB/s over all GPUs with the batch
+                 resident in HBM (``ocb_compile_device``).
+* ``e2e``     -- the same through the public host API
+                 (``Context.compile_batch``: pinned source -> device -> PTX
+                 text, offsets and statuses back on the host), every step.
+* ``parity``  -- per-TU verdicts of all timed steps (identical,
+                 reference_raises, unsupported, mismatched).
+* ``roofline``-- the dominant kernel: compile bytes (source + PTX of the TUs
+                 of one launch) / mean launch time, against the measured HBM
+                 copy peak; ``traffic`` from an ncu capture, per TU.
+* ``cpu_baseline`` -- the reference compiler (pure Python) on all host cores
+                 over an evenly spaced sample of the batch.
+* ``lexer``   -- the batch lexer over 1 GiB of lexer stress text per GPU.
+* ``configs`` -- single-GPU extras: the 4,096 random kernels, the 256
+                 register-pressure kernels (both parity-checked) and the
+                 batch-1 latency of the tiled SGEMM kernel.
 
 ``--impl reference`` times only the reference compiler (rank 0; other ranks
 exit without work).
@@ -33,12 +46,14 @@ exit without work).
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import subprocess
 import sys
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -48,18 +63,20 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "source MB/s compiled to byte-identical PTX at 1/2/4/8 B200; lexer GB/s vs HBM"
 UNIT = "MB/s source"
-N_KERNELS = 4096
-SEED = 1234
-RANK_SEED_STRIDE = 1_000_000
-TOKEN_RECORD_BYTES = 12     # start u32 + kind<<24|len u32 + line u32
+C5_N = 262144
+C5_SEED = 5678
+C2_N, C2_SEED = 4096, 1234
+C4_N, C4_SEED = 256, 4242
+TOKEN_RECORD_BYTES = 8      # start u32 + kind<<24|len u32 (line derived)
 LEX_BYTES = 1 << 30
 LEX_TU_BYTES = 16384
-WORKLOAD = ("4,096 seeded random kernels (50-200 stmts, ~4.6 KB each) compiled to PTX "
-            "per GPU")
+WORKLOAD = ("262,144 seeded lognormal-size kernels (median 3 KB, sigma 1, 1.20 GiB) "
+            "compiled to PTX")
+CACHE = ROOT / "baseline" / "_ref" / "cache"
 
 # DRAM bytes (read + write) per TU of k_cc_opt from an ncu capture of one
-# launch over the first 256 kernels of this workload (370.5 MB read + 760.2 MB
-# written); the full 4,096-kernel launch is too large to capture under ncu,
+# launch over the first 256 kernels of the random-kernel workload (370.5 MB
+# read + 760.2 MB written); a full launch is too large to capture under ncu,
 # so the figure is scaled by the TUs of one launch.
 NCU_OPT_DRAM_BYTES_PER_TU = (370.5e6 + 760.2e6) / 256
 
@@ -122,6 +139,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ---------------------------------------------------------------------------
+# ranks
+# ---------------------------------------------------------------------------
 def dist_init(backend: str = "nccl"):
     """Rank, world size and local rank from the torchrun environment; joins
     the process group when there is more than one rank (NCCL on the GPU box,
@@ -135,7 +155,7 @@ def dist_init(backend: str = "nccl"):
         import torch.distributed as dist
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
     return rank, world, local
 
 
@@ -155,15 +175,131 @@ def allreduce(x, world, device, op="max"):
     return float(t.item())
 
 
-def workload(rank, n=N_KERNELS):
-    """This rank's kernels: its own seed, so ranks compile disjoint TUs."""
-    from opencuda_b200 import synth
-    return synth.random_batch(n, seed=SEED + RANK_SEED_STRIDE * rank)
+def host_procs(world: int) -> int:
+    return max(1, len(os.sched_getaffinity(0)) // max(1, world))
 
 
-def cpu_sample_size(cores):
-    # ~32 kernels per core: a few seconds of wall time, tens of CPU-seconds
-    return min(N_KERNELS, 32 * cores)
+# ---------------------------------------------------------------------------
+# the workload
+# ---------------------------------------------------------------------------
+def c5_batch(rank: int, world: int, n: int = C5_N):
+    """The lognormal batch as (uint8 buffer, uint64 tu_off[n+1]).  Rank 0
+    generates it (all host cores) into a cache file the other ranks then
+    read, so the ranks of one job do not each generate it."""
+    from opencuda import synth
+    f = CACHE / f"c5_g{synth.GEN_VERSION}_{n}.npz"
+    if rank == 0 and not f.is_file():
+        srcs = synth.lognormal_batch(n, seed=C5_SEED,
+                                     procs=len(os.sched_getaffinity(0)))
+        buf, off = synth_pack(srcs)
+        CACHE.mkdir(parents=True, exist_ok=True)
+        tmp = f.with_name(f.name + f".{os.getpid()}.tmp.npz")
+        np.savez(tmp, buf=buf, off=off)
+        os.replace(tmp, f)
+    barrier(world)
+    z = np.load(f)
+    return z["buf"], z["off"]
+
+
+def synth_pack(srcs):
+    from opencuda import api
+    return api.pack_sources(srcs)
+
+
+def slice_plan(sizes, n_slices: int, world: int):
+    """Per slice, per rank: the TU indices that rank compiles.  Slice j holds
+    TUs i with i % n_slices == j; each slice is split across ranks by bytes
+    with greedy LPT (``opencuda.partition_lpt``), largest TUs first."""
+    from opencuda import partition_lpt
+    sizes = np.asarray(sizes, dtype=np.int64)
+    plan = []
+    for j in range(n_slices):
+        idx = np.arange(j, len(sizes), n_slices, dtype=np.int64)
+        parts = partition_lpt(sizes[idx].tolist(), world)
+        plan.append([idx[np.asarray(p, dtype=np.int64)] if p else np.zeros(0, np.int64)
+                     for p in parts])
+    return plan
+
+
+def gather(buf, off, idx):
+    """The TUs ``idx`` of a packed batch as a new packed batch."""
+    idx = np.asarray(idx, dtype=np.int64)
+    lens = (off[idx + 1] - off[idx]).astype(np.uint64)
+    noff = np.zeros(len(idx) + 1, np.uint64)
+    np.cumsum(lens, out=noff[1:])
+    out = np.empty(int(noff[-1]), np.uint8)
+    for j, i in enumerate(idx.tolist()):
+        out[int(noff[j]):int(noff[j + 1])] = buf[int(off[i]):int(off[i + 1])]
+    return out, noff
+
+
+# ---------------------------------------------------------------------------
+# parity against the reference's golden digests
+# ---------------------------------------------------------------------------
+def load_goldens(name: str):
+    try:
+        from oracle import goldens
+    except ImportError:
+        return None
+    return goldens.load(name)
+
+
+class Parity:
+    """Per-TU verdicts against the golden record of one workload."""
+
+    def __init__(self, gold):
+        self.gold = gold
+        self.c = {"identical": 0, "reference_raises": 0, "unsupported": 0, "mismatched": 0}
+        self.identical_bytes = 0
+        self.first_mismatch = None
+        self.pool = ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4))
+
+    def check(self, idx, data, out_off, status, src_lens):
+        """``idx``: global TU indices; ``data``/``out_off``: their packed PTX;
+        ``status``: their statuses; ``src_lens``: their source bytes."""
+        from opencuda import api
+        mv = memoryview(data)
+        ok = [j for j in range(len(idx)) if int(status[j]) == 0]
+        digs = dict(zip(ok, self.pool.map(
+            lambda j: hashlib.sha256(mv[int(out_off[j]):int(out_off[j + 1])]).digest(), ok)))
+        for j, i in enumerate(np.asarray(idx).tolist()):
+            st = int(status[j])
+            gs = int(self.gold["status"][i]) if self.gold is not None else None
+            if st == api.TU_UNSUPPORTED:
+                v = "unsupported"
+            elif self.gold is None:
+                v = "identical" if st == 0 else "mismatched"
+            elif st == 0 and gs == 0 and digs[j] == bytes(self.gold["digest"][i]):
+                v = "identical"
+            elif st != 0 and gs != 0 and st == gs:
+                v = "reference_raises"
+            else:
+                v = "mismatched"
+                if self.first_mismatch is None:
+                    self.first_mismatch = {"tu": i, "status": st, "golden_status": gs}
+            self.c[v] += 1
+            if v == "identical":
+                self.identical_bytes += int(src_lens[j])
+
+    def summary(self, world, dev):
+        out = {k: int(allreduce(float(v), world, dev, "sum")) for k, v in self.c.items()}
+        out["checked_against"] = ("reference golden digests (sha256 of the PTX module text)"
+                                  if self.gold is not None else "unchecked: no golden record")
+        if self.first_mismatch is not None:
+            out["first_mismatch_rank_local"] = self.first_mismatch
+        return out
+
+
+# ---------------------------------------------------------------------------
+# the reference arm / CPU baseline
+# ---------------------------------------------------------------------------
+def cpu_sample(buf, off, n_tus: int):
+    """An evenly spaced sample of ``n_tus`` TUs of the batch (the batch's size
+    distribution, deterministic)."""
+    n = len(off) - 1
+    idx = np.linspace(0, n - 1, num=min(n, n_tus)).astype(np.int64)
+    srcs = [bytes(buf[int(off[i]):int(off[i + 1])]).decode("utf-8") for i in idx]
+    return idx, srcs
 
 
 def time_reference(srcs, cores, steps, warmup):
@@ -175,38 +311,50 @@ def time_reference(srcs, cores, steps, warmup):
         return [pool.time_compile(srcs)[0] for _ in range(steps)]
 
 
+REF_SAMPLE_TUS = 1024
+
+
 def run_reference(args, rank, world):
-    """The reference's own compiler (pure Python) on all host cores."""
+    """The reference's own compiler (pure Python) on all host cores, over an
+    evenly spaced sample of the batch per step."""
     if rank != 0:
         return
-    srcs_all = workload(0)
+    buf, off = c5_batch(0, 1)
     cores = len(os.sched_getaffinity(0))
-    k = cpu_sample_size(cores)
-    srcs = srcs_all[:k]
+    idx, srcs = cpu_sample(buf, off, REF_SAMPLE_TUS)
     nbytes = sum(len(s.encode()) for s in srcs)
     ts = time_reference(srcs, cores, args.steps, args.warmup)
     t = float(np.mean(ts))
     v = nbytes / t / 1e6
-    sample = (f"first {k} of the {N_KERNELS} kernels ({nbytes} bytes) per step, "
+    sample = (f"{len(srcs)} evenly spaced kernels of the 262,144 ({nbytes} bytes) per step, "
               f"reference preprocess->parse->optimize->ir_to_ptx in {cores} processes")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "n_kernels": N_KERNELS, "seed": SEED},
+        "config": {"workload": WORKLOAD, "n_kernels": C5_N, "seed": C5_SEED},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# GPU helpers
+# ---------------------------------------------------------------------------
 class DevArray:
     """A device address as a CUDA-array-interface object (for torch.as_tensor)."""
 
     def __init__(self, ptr, n, typestr):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
                                          "data": (int(ptr), False), "version": 3}
+
+
+def d2h(torch, dev, ptr, n, typestr):
+    if n == 0:
+        return np.zeros(0, np.dtype(typestr))
+    return torch.as_tensor(DevArray(ptr, n, typestr), device=dev).cpu().numpy()
 
 
 def count_launches(fn):
@@ -229,7 +377,7 @@ def count_launches(fn):
     return sum(names.values()), names
 
 
-def lexer_measure(ctx, api, synth, dev, rank, steps, warmup, peak, nbytes_req):
+def lexer_measure(ctx, synth, dev, rank, steps, warmup, peak, nbytes_req):
     """Lexer GB/s over the lexer stress text (resident in HBM)."""
     import torch
     buf, off = synth.lexstress_batch(total_bytes=nbytes_req, tu_bytes=LEX_TU_BYTES,
@@ -241,15 +389,15 @@ def lexer_measure(ctx, api, synth, dev, rank, steps, warmup, peak, nbytes_req):
     cap = nbytes // 2 + n_tu + 1   # > 2x the measured token density of this text
     d_start = torch.empty(cap, dtype=torch.int32, device=dev)
     d_kl = torch.empty(cap, dtype=torch.int32, device=dev)
-    d_line = torch.empty(cap, dtype=torch.int32, device=dev)
     d_tto = torch.empty(n_tu + 1, dtype=torch.int64, device=dev)
     d_status = torch.empty(n_tu, dtype=torch.int32, device=dev)
     d_n = torch.zeros(1, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        # token records only (start, kind|len): the line is derived on request
         ctx.lex_device(d_src.data_ptr(), nbytes, d_off.data_ptr(), n_tu, d_start.data_ptr(),
-                       d_kl.data_ptr(), d_line.data_ptr(), cap, d_tto.data_ptr(),
+                       d_kl.data_ptr(), 0, cap, d_tto.data_ptr(),
                        d_status.data_ptr(), d_n.data_ptr(), stream.cuda_stream)
 
     for _ in range(warmup):
@@ -266,7 +414,7 @@ def lexer_measure(ctx, api, synth, dev, rank, steps, warmup, peak, nbytes_req):
     torch.cuda.synchronize()
     t = e0.elapsed_time(e1) / 1e3 / steps
     alg = nbytes + TOKEN_RECORD_BYTES * n_tok
-    del d_src, d_start, d_kl, d_line
+    del d_src, d_start, d_kl
     torch.cuda.empty_cache()
     return {"value": nbytes / t / 1e9, "unit": "GB/s source", "bytes": nbytes,
             "tokens": n_tok, "ms_per_step": t * 1e3,
@@ -274,20 +422,55 @@ def lexer_measure(ctx, api, synth, dev, rank, steps, warmup, peak, nbytes_req):
             "roofline": {"bound": "hbm", "achieved": alg / t / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": alg / t / 1e9 / peak,
                          "algorithmic_bytes": alg,
-                         "scope": "whole lexer step (source + 12 B per token record)"}}
+                         "scope": "whole lexer step (source + 8 B per token record)"}}
 
 
+def compile_config(ctx, torch, dev, stream, srcs, gold_name, reps=1):
+    """One extra workload: device-resident compile timed over ``reps`` calls
+    after one warm-up, every TU checked against its golden record."""
+    from opencuda import api
+    buf, off = api.pack_sources(srcs)
+    n = len(srcs)
+    d_src = torch.from_numpy(buf.copy()).to(dev)
+    d_off = torch.from_numpy(off.astype(np.int64)).to(dev)
+    torch.cuda.synchronize()
+    ctx.compile_device(d_src.data_ptr(), len(buf), d_off.data_ptr(), n, 2)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        r = ctx.compile_device(d_src.data_ptr(), len(buf), d_off.data_ptr(), n, 2)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / reps
+    d_out, nb, d_oo, d_st = r
+    data = d2h(torch, dev, d_out, nb, "|u1").tobytes()
+    oo = d2h(torch, dev, d_oo, n + 1, "<u8")
+    st = d2h(torch, dev, d_st, n, "<i4")
+    par = Parity(load_goldens(gold_name))
+    par.check(np.arange(n), data, oo, st, np.diff(off))
+    return {"value": par.identical_bytes / t / 1e6, "unit": UNIT, "ms": t * 1e3,
+            "source_bytes": int(len(buf)), "ptx_bytes": int(nb),
+            "parity": par.summary(1, dev)}
+
+
+# ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--kernels", type=int, default=N_KERNELS,
-                    help="kernels per GPU (default 4096; smaller only for profiling)")
+    ap.add_argument("--slices", type=int, default=16,
+                    help="interleaved slices of the batch; one step compiles one slice")
+    ap.add_argument("--tus", type=int, default=C5_N,
+                    help="first TUs of the batch to use (smaller only for profiling)")
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="steps of the end-to-end leg (default: min(steps, slices))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-lexer", action="store_true")
+    ap.add_argument("--no-configs", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true",
                     help="skip the CUPTI launch count (for runs under ncu)")
     ap.add_argument("--lexer-bytes", type=int, default=LEX_BYTES)
@@ -303,102 +486,136 @@ def main():
         return
 
     import torch
-    from opencuda_b200 import api, synth
+    from opencuda import api, synth
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    ctx = api.Context(local)
     peak, peak_kind = measured_peak()
 
-    srcs = workload(rank, args.kernels)
-    buf, off = api.pack_sources(srcs)
-    n_tu = len(srcs)
-    nbytes = len(buf)
-    host_src = torch.from_numpy(buf.copy()).pin_memory()
-    d_src = host_src.to(dev)
-    d_off = torch.from_numpy(off.astype(np.int64)).to(dev)
+    # the batch, this rank's share of every slice (resident in HBM)
+    buf_all, off_all = c5_batch(rank, world)
+    n_all = min(args.tus, len(off_all) - 1)
+    sizes = np.diff(off_all[:n_all + 1]).astype(np.int64)
+    S = max(1, min(args.slices, n_all))
+    plan = slice_plan(sizes, S, world)
+    mine = [plan[j][rank] for j in range(S)]
+    ctx = api.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
-    torch.cuda.synchronize()   # the batch is on the device before the context's stream reads it
+    shards = []
+    for j in range(S):
+        b, o = gather(buf_all, off_all, mine[j])
+        host = torch.from_numpy(b).pin_memory() if len(b) else torch.zeros(0, dtype=torch.uint8)
+        shards.append({"idx": mine[j], "buf": b, "off": o, "host": host,
+                       "d_src": host.to(dev), "d_off": torch.from_numpy(o.astype(np.int64)).to(dev),
+                       "n": len(mine[j]), "bytes": int(len(b))})
+    del buf_all
+    torch.cuda.synchronize()
+    gold = load_goldens("c5")
 
-    def step():
-        return ctx.compile_device(d_src.data_ptr(), nbytes, d_off.data_ptr(), n_tu, 2)
+    def step(j):
+        sh = shards[j]
+        return ctx.compile_device(sh["d_src"].data_ptr(), sh["bytes"], sh["d_off"].data_ptr(),
+                                  sh["n"], 2)
 
-    for _ in range(args.warmup):
-        step()
+    for w in range(args.warmup):
+        step(w % S)
     torch.cuda.synchronize()
     launches, launch_names = None, None
     if not args.no_launch_count:
         try:
-            launches, launch_names = count_launches(step)
+            launches, launch_names = count_launches(lambda: step(0))
         except Exception as ex:  # noqa: BLE001
             launch_names = {"error": f"{type(ex).__name__}: {ex}"}
 
+    # timed steps: each bracketed by a barrier and a synchronisation, CUDA
+    # events on the context's stream; PTX checked after each, untimed
+    par = Parity(gold)
     ctx.kernel_profile(True)
     clocks = ClockSampler(local)
-    barrier(world)
-    torch.cuda.synchronize()
     clocks.start()
+    t_sum, t_sum_local, src_bytes, ptx_bytes = 0.0, 0.0, 0, 0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        d_out, out_bytes, d_out_off, d_status = step()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    for k in range(args.steps):
+        j = k % S
+        sh = shards[j]
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        d_out, nb, d_oo, d_st = step(j)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3
+        t_sum_local += t
+        t_sum += allreduce(t, world, dev, "max")
+        src_bytes += sh["bytes"]
+        ptx_bytes += nb
+        data = d2h(torch, dev, d_out, nb, "|u1").tobytes()
+        oo = d2h(torch, dev, d_oo, sh["n"] + 1, "<u8")
+        st = d2h(torch, dev, d_st, sh["n"], "<i4")
+        par.check(sh["idx"], data, oo, st, np.diff(sh["off"]))
     clk = clocks.stop()
     ktimes = ctx.kernel_times()
     ctx.kernel_profile(False)
     barrier(world)
-    t_step = e0.elapsed_time(e1) / 1e3 / args.steps
-    t_max = allreduce(t_step, world, dev, "max")
-    total_bytes = allreduce(float(nbytes), world, dev, "sum")
-    value = total_bytes / t_max / 1e6
-
-    # statuses of the device result (a view of the context's buffer)
-    st_host = (torch.as_tensor(DevArray(d_status, n_tu, "<i4"), device=dev).cpu().numpy()
-               if n_tu else np.zeros(0, np.int32))
-    n_ok = int((st_host == 0).sum())
-    n_unsup = int((st_host == api.TU_UNSUPPORTED).sum())
-    n_over = int((st_host == api.TU_OVERFLOW).sum())
-    n_raise = int(((st_host > 0) & (st_host < 0x100)).sum())
-    ok_bytes = int(sum(int(off[i + 1] - off[i]) for i in range(n_tu) if st_host[i] == 0))
+    total_src = allreduce(float(src_bytes), world, dev, "sum")
+    ident = allreduce(float(par.identical_bytes), world, dev, "sum")
+    value = ident / t_sum / 1e6
+    parity = par.summary(world, dev)
+    distinct = len({k % S for k in range(args.steps)})
+    per_rank_bytes = [int(sum(int(sizes[i]) for i in plan[j][r]) for j in range(S))
+                      for r in range(world)]
 
     # roofline of the dominant kernel: source + PTX bytes of the TUs it processed
-    dom = max(ktimes, key=lambda k: ktimes[k][0])
+    dom = max(ktimes, key=lambda x: ktimes[x][0])
     dom_ms, dom_n = ktimes[dom]
-    tus_per_launch = n_tu * args.steps / max(dom_n, 1)
-    alg_per_launch = (nbytes + out_bytes) * args.steps / max(dom_n, 1)
+    n_tus_timed = sum(shards[k % S]["n"] for k in range(args.steps))
+    tus_per_launch = n_tus_timed / max(dom_n, 1)
+    alg_per_launch = (src_bytes + ptx_bytes) / max(dom_n, 1)
     t_launch = dom_ms / 1e3 / max(dom_n, 1)
-    achieved = alg_per_launch / t_launch / 1e9
-    traffic = (NCU_OPT_DRAM_BYTES_PER_TU * tus_per_launch
-               if (NCU_OPT_DRAM_BYTES_PER_TU is not None and dom == "k_cc_opt") else None)
+    achieved = alg_per_launch / t_launch / 1e9 if t_launch > 0 else 0.0
+    traffic = (NCU_OPT_DRAM_BYTES_PER_TU * tus_per_launch if dom == "k_cc_opt" else None)
     ktot = sum(v[0] for v in ktimes.values())
-    kernels = {k: {"ms_total": v[0], "launches": v[1],
+    kernels = {x: {"ms_total": v[0], "launches": v[1],
                    "share_of_compile_kernels": (v[0] / ktot if ktot else None),
-                   "share_of_step": v[0] / 1e3 / (t_step * args.steps)}
-               for k, v in ktimes.items()}
+                   "share_of_step": v[0] / 1e3 / t_sum_local if t_sum_local else None}
+               for x, v in ktimes.items()}
 
     # end to end through the public host API (pinned source, PTX back on the host)
     e2e = None
     if not args.no_e2e:
-        src_np = host_src.numpy()
-        tb = ctx.compile_batch(buf=src_np, tu_off=off)
-        barrier(world)
-        torch.cuda.synchronize()
+        ke = args.e2e_steps if args.e2e_steps is not None else min(args.steps, S)
+        te, h2d, d2h_b = 0.0, 0, 0
+        epar = Parity(gold)
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(args.steps):
-            tb = ctx.compile_batch(buf=src_np, tu_off=off)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        t_e2e = f0.elapsed_time(f1) / 1e3 / args.steps
-        t_e2e = allreduce(t_e2e, world, dev, "max")
-        e2e = {"value": total_bytes / t_e2e / 1e6, "unit": UNIT,
-               "ms_per_step": t_e2e * 1e3,
-               "h2d_bytes_per_step": int(nbytes + 8 * (n_tu + 1)),
-               "d2h_bytes_per_step": int(len(tb.data) + 8 * (n_tu + 1) + 4 * n_tu + 4 * n_tu)}
+        ctx.compile_batch(buf=shards[0]["host"].numpy(), tu_off=shards[0]["off"])
+        for k in range(ke):
+            sh = shards[k % S]
+            src_np = sh["host"].numpy()
+            barrier(world)
+            torch.cuda.synchronize()
+            f0.record(stream)
+            tb = ctx.compile_batch(buf=src_np, tu_off=sh["off"])
+            f1.record(stream)
+            torch.cuda.synchronize()
+            te += allreduce(f0.elapsed_time(f1) / 1e3, world, dev, "max")
+            h2d += sh["bytes"] + 8 * (sh["n"] + 1)
+            d2h_b += len(tb.data) + 8 * (sh["n"] + 1) + 8 * sh["n"]
+            epar.check(sh["idx"], tb.data, tb.off, tb.status, np.diff(sh["off"]))
+        e_ident = allreduce(float(epar.identical_bytes), world, dev, "sum")
+        e2e = {"value": e_ident / te / 1e6, "unit": UNIT, "steps": ke,
+               "ms_per_step": te / ke * 1e3,
+               "h2d_bytes_per_step": int(h2d / ke), "d2h_bytes_per_step": int(d2h_b / ke),
+               "parity": epar.summary(world, dev)}
 
-    # batch-1 latency of the tiled SGEMM kernel (public API, end to end)
-    lat = None
-    if rank == 0:
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = {}
+        configs["random_4096"] = compile_config(
+            ctx, torch, dev, stream, synth.random_batch(C2_N, seed=C2_SEED), "c2")
+        configs["random_4096"]["workload"] = "4,096 random kernels, 50-200 stmts (~4.6 KB)"
+        configs["regpressure_256"] = compile_config(
+            ctx, torch, dev, stream, synth.regpressure_batch(C4_N, seed=C4_SEED), "c4")
+        configs["regpressure_256"]["workload"] = ("256 register-pressure kernels, ~6,000 "
+                                                  "statements / ~20k SSA values each")
         for _ in range(3):
             ctx.compile_batch([synth.SGEMM_SRC])
         ts = []
@@ -406,11 +623,14 @@ def main():
             t0 = time.perf_counter()
             ctx.compile_batch([synth.SGEMM_SRC])
             ts.append(time.perf_counter() - t0)
-        lat = {"ms": float(np.median(ts)) * 1e3, "source_bytes": len(synth.SGEMM_SRC)}
+        configs["latency_sgemm"] = {"ms": float(np.median(ts)) * 1e3,
+                                    "source_bytes": len(synth.SGEMM_SRC),
+                                    "what": "batch-1 latency, source on the host to PTX "
+                                            "text on the host (Context.compile_batch)"}
 
     lexer = None
     if not args.no_lexer:
-        lexer = lexer_measure(ctx, api, synth, dev, rank, args.steps, args.warmup, peak,
+        lexer = lexer_measure(ctx, synth, dev, rank, min(args.steps, 5), args.warmup, peak,
                               args.lexer_bytes)
         lexer["value"] = allreduce(lexer["bytes"], world, dev, "sum") / \
             allreduce(lexer["ms_per_step"] / 1e3, world, dev, "max") / 1e9
@@ -419,18 +639,21 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cores = len(os.sched_getaffinity(0))
-            k = cpu_sample_size(cores)
-            sb = sum(len(s.encode()) for s in srcs[:k])
-            tcpu = time_reference(srcs[:k], cores, 1, 1)[0]
+            buf_all, off_all = c5_batch(0, 1)
+            sidx, ssrc = cpu_sample(buf_all, off_all, REF_SAMPLE_TUS)
+            del buf_all
+            sb = sum(len(s.encode()) for s in ssrc)
+            tcpu = time_reference(ssrc, cores, 1, 1)[0]
             cpu = {"value": sb / tcpu / 1e6, "unit": UNIT, "cores": cores, "kind": "reference",
-                   "sample": f"first {k} of the {n_tu} kernels ({sb} bytes), reference "
-                             f"preprocess->parse->optimize->ir_to_ptx in {cores} processes"}
-            if lat is not None:
+                   "sample": f"{len(ssrc)} evenly spaced kernels of the 262,144 ({sb} bytes), "
+                             f"reference preprocess->parse->optimize->ir_to_ptx in "
+                             f"{cores} processes"}
+            if configs is not None:
                 from oracle import ref_runner
                 with ref_runner.RefPool(1) as pool:
                     pool.time_compile([synth.SGEMM_SRC])
                     tl = [pool.time_compile([synth.SGEMM_SRC])[0] for _ in range(5)]
-                lat["reference_ms"] = float(np.median(tl)) * 1e3
+                configs["latency_sgemm"]["reference_ms"] = float(np.median(tl)) * 1e3
         except Exception as ex:  # noqa: BLE001
             cpu = {"value": None, "error": f"{type(ex).__name__}: {ex}"}
 
@@ -438,17 +661,18 @@ def main():
         print(json.dumps({
             "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": t_max * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "config": {"workload": WORKLOAD if n_tu == N_KERNELS
-                       else f"{n_tu} of the {N_KERNELS} seeded random kernels",
-                       "n_kernels": n_tu, "source_bytes_per_gpu": nbytes,
-                       "ptx_bytes_per_gpu": int(out_bytes), "seed": SEED,
-                       "tu_status": {"ok": n_ok, "reference_raises": n_raise,
-                                     "unsupported": n_unsup, "overflow": n_over},
-                       "ok_source_bytes": ok_bytes,
-                       "l2": "working set (~13 GB of arenas) larger than L2, no flush",
-                       "parallelism": f"tu-shard x{world}"},
+            "ms_per_step": t_sum / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": WORKLOAD if n_all == C5_N
+                       else f"first {n_all} of the 262,144 lognormal-size kernels",
+                       "n_kernels": n_all, "seed": C5_SEED, "slices": S,
+                       "slices_timed": distinct, "tus_timed": int(
+                           allreduce(float(n_tus_timed), world, dev, "sum")),
+                       "source_bytes_timed": int(total_src),
+                       "source_bytes_per_rank": per_rank_bytes,
+                       "l2": "working set (GBs of compiler arenas) larger than L2, no flush",
+                       "parallelism": f"each slice LPT-split by bytes over {world} GPU(s)"},
+            "parity": parity,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": traffic,
@@ -460,7 +684,7 @@ def main():
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": (launches * args.steps if launches is not None else None),
             "gpu_launches_per_step": launch_names,
-            "latency_sgemm": lat,
+            "configs": configs,
             "lexer": lexer,
             "clocks": clk,
         }), flush=True)

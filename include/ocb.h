@@ -182,9 +182,10 @@ int  ocb_kernel_times(const ocb_ctx *ctx, double *ms, uint64_t *launches);
  * larger batches are rejected with -2 before any work is queued.  Arguments
  * and outputs are those of ocb_lex_device (device pointers, work queued on
  * `stream`, no synchronisation); `err` (may be NULL) receives a message of at
- * most err_len-1 bytes on failure.  The first call on a device does a one-time
- * set-up with that device current (the array's device address and the keyword
- * table); make that first call before any stream capture.  Every call shares
+ * most err_len-1 bytes on failure.  The first call on a device (and the first
+ * after a device reset) does a set-up with that device current: it uploads the
+ * keyword table; every call looks up the array's device address, which does not
+ * allocate.  Make that first call before any stream capture.  Every call shares
  * the one array, so calls whose work overlaps on the GPU (other streams, other
  * host threads) race: serialise them.  No counterpart in the reference. */
 int  ocb_lex_device_static(const uint8_t *d_src, uint64_t n_bytes,

@@ -1,4 +1,4 @@
-"""opencuda_b200: a B200-native batch compiler for OpenCUDA's CUDA-C subset.
+"""opencuda: a B200-native batch compiler for OpenCUDA's CUDA-C subset.
 
 The data-parallel phases of the reference pipeline (garrick247/opencuda:
 preprocess -> lex -> parse -> optimize -> emit) run as sm_100a kernels over
@@ -6,9 +6,9 @@ whole batches of translation units; ``include/ocb.h`` is the C ABI.
 
 Drop-in surface: ``compile(src) -> ptx`` (the bytes of the reference CLI's
 ``--emit-ptx`` file), ``compile_batch(srcs, devices=...)`` and the CLI
-``python -m opencuda_b200 X.cu --emit-ptx``.  The per-stage batch calls
+``python -m opencuda X.cu --emit-ptx``.  The per-stage batch calls
 (``lex_batch``, ``preprocess_batch``, ``parse_batch``, ``optimize_batch``)
-live on ``Context`` and in ``opencuda_b200.api``.
+live on ``Context`` and in ``opencuda.api``.
 """
 from .api import (Context, OcbError, TokenBatch, TextBatch, context, lex_batch,  # noqa: F401
                   preprocess_batch, parse_batch, optimize_batch,

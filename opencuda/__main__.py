@@ -1,4 +1,4 @@
-"""Command line: ``python -m opencuda_b200 SRC [SRC ...] --emit-ptx``.
+"""Command line: ``python -m opencuda SRC [SRC ...] --emit-ptx``.
 
 The flags and stdout lines of the reference CLI (``opencuda/__main__.py:13-102``):
 ``--out``, ``--emit-ptx``, ``--arch`` (default sm_120), ``-I/--include DIR``
@@ -21,7 +21,7 @@ from pathlib import Path
 
 def _parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(
-        prog="opencuda_b200",
+        prog="opencuda",
         description="B200 batch compiler for OpenCUDA's CUDA-C subset (C to PTX)")
     ap.add_argument("source", nargs="*", help="input .cu file(s)")
     ap.add_argument("--out", default=None, help="output file (one source only)")
@@ -44,7 +44,7 @@ def main(argv: list[str] | None = None) -> int:
     if args.out and len(args.source) > 1:
         ap.error("--out takes one source")
     if not args.emit_ptx:
-        print("opencuda_b200: cubin output needs OpenPTXas, which is not part of this "
+        print("opencuda: cubin output needs OpenPTXas, which is not part of this "
               "package; use --emit-ptx", file=sys.stderr)
         return 1
 
@@ -62,7 +62,7 @@ def main(argv: list[str] | None = None) -> int:
     for src, p, r in zip(args.source, paths, results):
         print(f"[opencuda] Parsing {src}...")
         if not r.ok:
-            print(f"opencuda_b200: {src}: {r.exc_type}", file=sys.stderr)
+            print(f"opencuda: {src}: {r.exc_type}", file=sys.stderr)
             rc = 1
             continue
         n = compiler.kernel_count(r.ptx)

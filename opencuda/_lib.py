@@ -65,7 +65,7 @@ def load() -> ctypes.CDLL:
         return _lib
     if not LIB_PATH.is_file():
         raise LibraryMissing(
-            f"{LIB_PATH} is missing: build it with `python -m opencuda_b200.build`")
+            f"{LIB_PATH} is missing: build it with `python -m opencuda.build`")
     lib = ctypes.CDLL(str(LIB_PATH))
     for name, res, args in SIGNATURES:
         fn = getattr(lib, name)

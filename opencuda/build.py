@@ -1,8 +1,8 @@
 """Builds the package's CUDA library (``libocb.so``) for sm_100a, in-tree.
 
-``python -m opencuda_b200.build [--force]`` or ``build()``; nvcc
+``python -m opencuda.build [--force]`` or ``build()``; nvcc
 cross-compiles, so no GPU is needed.  Each ``csrc/*.cu`` compiles to its own
-object under ``opencuda_b200/_build/`` (in parallel), with nvcc's dependency
+object under ``opencuda/_build/`` (in parallel), with nvcc's dependency
 files deciding which objects are stale; the objects then link into
 ``libocb.so``.
 """

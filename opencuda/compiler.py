@@ -177,41 +177,58 @@ def compile_batch(srcs: Sequence[str | bytes], *, arch: str = DEFAULT_ARCH,
     ``devices``: CUDA device ordinals to shard over (default: device 0).  The
     TUs are split by bytes with greedy LPT, each device compiles its share in
     its own host thread (one context per listed device; the library releases
-    the GIL while the GPU works) and the results come back in input order."""
+    the GIL while the GPU works) and the results come back in input order.
+
+    A device whose call fails (a CUDA error, or the library's watchdog giving
+    up on a stream that stops making progress) is dropped for the rest of the
+    call and its share is split again, by LPT, over the devices that
+    succeeded; only when every device has failed does the first error
+    propagate."""
     texts = list(srcs)
     if include_paths:
         texts = [resolve_includes(s if isinstance(s, str) else bytes(s).decode("utf-8"),
                                   include_paths) for s in texts]
     blobs = _encode(texts)
     devs = list(devices) if devices else [0]
-    parts = partition_lpt([len(b) for b in blobs], len(devs))
     out: list[Result | None] = [None] * len(blobs)
     errors: list[BaseException] = []
+    live = list(range(len(devs)))          # slots still trusted
+    pending = list(range(len(blobs)))      # TUs without a result
 
-    def work(slot: int, dev: int, idx: list[int]):
+    def work(slot: int, idx: list[int], failed: list):
         try:
             if not idx:
                 return
-            data, off, st = _compile_on(dev, slot, [blobs[i] for i in idx], arch)
+            data, off, st = _compile_on(devs[slot], slot, [blobs[i] for i in idx], arch)
             for j, i in enumerate(idx):
                 s = int(st[j])
                 ptx = (data[int(off[j]):int(off[j + 1])].decode("utf-8", "surrogateescape")
                        if s == api.TU_OK else None)
                 out[i] = Result(ptx=ptx, status=s, exc_type=status_name(s))
-        except BaseException as ex:  # noqa: BLE001 -- re-raised on the caller's thread
-            errors.append(ex)
+        except BaseException as ex:  # noqa: BLE001 -- handled on the caller's thread
+            failed.append((slot, ex))
+            with _ctx_lock:  # a later call starts this slot on a fresh context
+                _contexts.pop((devs[slot], slot), None)
 
-    if len(devs) == 1:
-        work(0, devs[0], parts[0])
-    else:
-        threads = [threading.Thread(target=work, args=(k, d, p), daemon=True)
-                   for k, (d, p) in enumerate(zip(devs, parts))]
-        for t in threads:
-            t.start()
-        for t in threads:
-            t.join()
-    if errors:
-        raise errors[0]
+    while pending:
+        parts = partition_lpt([len(blobs[i]) for i in pending], len(live))
+        shares = [(slot, [pending[k] for k in part]) for slot, part in zip(live, parts)]
+        failed: list = []
+        if len(shares) == 1:
+            work(shares[0][0], shares[0][1], failed)
+        else:
+            threads = [threading.Thread(target=work, args=(slot, idx, failed), daemon=True)
+                       for slot, idx in shares]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join()
+        errors.extend(ex for _, ex in failed)
+        dead = {slot for slot, _ in failed}
+        live = [s for s in live if s not in dead]
+        pending = [i for i in pending if out[i] is None]
+        if pending and not live:
+            raise errors[0]
     return out  # type: ignore[return-value]
 
 

@@ -5,6 +5,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <thread>
 #include "ocb_internal.h"
 
 PhaseTimer::PhaseTimer(cudaStream_t s) : st(s) {
@@ -36,6 +37,23 @@ int fail(ocb_ctx *ctx, const char *what, cudaError_t e) {
 int fail(ocb_ctx *ctx, const std::string &msg) {
     if (ctx) ctx->err = msg;
     return -1;
+}
+
+cudaError_t stream_wait(cudaStream_t st) {
+    static const double limit_s = [] {
+        const char *v = getenv("OCB_WATCHDOG_S");
+        double x = v && *v ? atof(v) : 0.0;
+        return x > 0 ? x : 1800.0;
+    }();
+    auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t it = 0;; ++it) {
+        cudaError_t e = cudaStreamQuery(st);
+        if (e != cudaErrorNotReady) return e;
+        double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (dt > limit_s) return cudaErrorTimeout;
+        if (dt < 0.002) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
 }
 
 }  // namespace ocb
@@ -73,7 +91,7 @@ int ocb_create(ocb_ctx **out, int device, uint32_t flags) {
 void ocb_destroy(ocb_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
-    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->stream) stream_wait(ctx->stream);
     for (DevBuf *b : {&ctx->lex_scratch, &ctx->cub_tmp, &ctx->d_src, &ctx->d_tu_off,
                       &ctx->d_tok_start, &ctx->d_tok_kl, &ctx->d_tok_line, &ctx->d_tu_tok,
                       &ctx->d_status, &ctx->d_count, &ctx->pp_scratch, &ctx->pp_arena,
@@ -159,7 +177,7 @@ int ocb_lex_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint
     if (rc) return rc;
     uint64_t n_tok = 0;
     OCB_TRY("d2h count", cudaMemcpyAsync(&n_tok, ctx->d_count.p, 8, cudaMemcpyDeviceToHost, st));
-    OCB_TRY("lex sync", cudaStreamSynchronize(st));
+    OCB_TRY("lex sync", stream_wait(st));
     if (n_tok > cap) return fail(ctx, "ocb_lex_batch: token capacity exceeded");
     ocb_tokens *t = new (std::nothrow) ocb_tokens();
     if (!t) return fail(ctx, "ocb_lex_batch: out of host memory");
@@ -180,7 +198,7 @@ int ocb_lex_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint
                                 cudaMemcpyDeviceToHost, st);
     if (!e && n_tu) e = cudaMemcpyAsync(t->status.data(), ctx->d_status.p, 4 * (size_t)n_tu,
                                         cudaMemcpyDeviceToHost, st);
-    if (!e) e = cudaStreamSynchronize(st);
+    if (!e) e = stream_wait(st);
     if (e) {
         delete t;
         return fail(ctx, "d2h tokens", e);
@@ -247,7 +265,7 @@ static int download_text(ocb_ctx *ctx, ocb_text *t, uint32_t n_tu, uint64_t tota
                                         cudaMemcpyDeviceToHost, st);
     if (!e && n_tu) e = cudaMemcpyAsync(t->qinclude.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu,
                                         cudaMemcpyDeviceToHost, st);
-    if (!e) e = cudaStreamSynchronize(st);
+    if (!e) e = stream_wait(st);
     if (e) return fail(ctx, "d2h text", e);
     return 0;
 }

@@ -90,7 +90,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     merge_status<<<grid, 256, 0, st>>>(d_status, lex_status, n_tu);
     std::vector<uint64_t> h_tok(n1);
     OCB_TRY("cc: d2h", cudaMemcpyAsync(h_tok.data(), tu_tok, 8 * n1, cudaMemcpyDeviceToHost, st));
-    OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+    OCB_TRY("cc: sync", stream_wait(st));
     size_t cur_stack = 0;
     OCB_TRY("cc: stack limit", cudaDeviceGetLimit(&cur_stack, cudaLimitStackSize));
     if (cur_stack < kCCStack) OCB_TRY("cc: stack limit", cudaDeviceSetLimit(cudaLimitStackSize, kCCStack));
@@ -184,7 +184,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
                 cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, out_len, pack_off, (int)(nc + 1), st));
         uint64_t tot = 0;
         OCB_TRY("cc: d2h", cudaMemcpyAsync(&tot, pack_off + nc, 8, cudaMemcpyDeviceToHost, st));
-        OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+        OCB_TRY("cc: sync", stream_wait(st));
         if (kp) {
             for (int k = 0; k < 3; ++k) {
                 if (k == 1 && stage < CC_STAGE_OPT) continue;
@@ -201,7 +201,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
             OCB_TRY("cc: output", nb.ensure(want));
             if (running) OCB_TRY("cc: d2d", cudaMemcpyAsync(nb.p, out_text.p, running,
                                                            cudaMemcpyDeviceToDevice, st));
-            OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+            OCB_TRY("cc: sync", stream_wait(st));
             out_text.release();
             out_text = nb;
             nb.p = nullptr;
@@ -215,7 +215,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         a = b;
         T.mark("cc: pack");
     }
-    OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+    OCB_TRY("cc: sync", stream_wait(st));
     *h_total = running;
     return 0;
 }

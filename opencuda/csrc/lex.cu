@@ -130,6 +130,14 @@ constexpr size_t kStaticScratchBytes = 8ull << 20; // size of the array below
 // symbol); the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_lex_static_scratch[kStaticScratchBytes];
 
+// The fixed part of the layout (per-window and per-TU arrays) at the limits
+// must leave room for the scan scratch that follows it.
+constexpr size_t kStaticFixedMax =
+    ((sizeof(uint64_t) * (6 * (kStaticMaxBytes / lex::WIN + 2) + 2 * (uint64_t)kStaticMaxTus + 4) +
+      sizeof(uint32_t) * (kStaticMaxBytes / lex::WIN + 2)) + 255) & ~(size_t)255;
+static_assert(kStaticFixedMax + (1u << 20) <= kStaticScratchBytes,
+              "static lexer scratch: the fixed layout at the limits leaves under 1 MiB for scans");
+
 constexpr int kMaxDevices = 128;
 std::mutex g_static_mu;
 void *g_static_ptr[kMaxDevices];  // device address of the array, per device
@@ -169,14 +177,17 @@ extern "C" int ocb_lex_device_static(const uint8_t *d_src, uint64_t N, const uin
         return static_fail(err, err_len, -1, "ocb_lex_device_static: no current CUDA device");
     void *base = nullptr;
     {
-        // One-time set-up on this device (the current one): the array's device
-        // address and the keyword table.  Neither allocates.
+        // Set-up on this device (the current one): the array's device address
+        // and the keyword table.  Neither allocates.  The address is looked up
+        // on every call: after a device reset (a new primary context) it can
+        // change and the keyword table is gone, so a changed address redoes
+        // the upload.
         std::lock_guard<std::mutex> lock(g_static_mu);
-        if (!g_static_ptr[dev]) {
-            void *p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_lex_static_scratch) != cudaSuccess || !p)
-                return static_fail(err, err_len, -1,
-                                   "ocb_lex_device_static: cudaGetSymbolAddress failed");
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_lex_static_scratch) != cudaSuccess || !p)
+            return static_fail(err, err_len, -1,
+                               "ocb_lex_device_static: cudaGetSymbolAddress failed");
+        if (g_static_ptr[dev] != p) {
             KwEntry t[128];
             build_kw_table(t);
             if (cudaMemcpyToSymbol(g_kw, t, sizeof(t)) != cudaSuccess)
@@ -207,6 +218,8 @@ extern "C" int ocb_lex_device_static(const uint8_t *d_src, uint64_t N, const uin
     uint64_t *toff = mapscan;
     uint64_t *total = toff + n_win;
     uint64_t *fsync = counts;
+    if (fixed > kStaticScratchBytes)
+        return static_fail(err, err_len, -2, "ocb_lex_device_static: layout exceeds the array");
     void *tmp = (unsigned char *)base + fixed;
     size_t tmp_cap = kStaticScratchBytes - fixed;
 
@@ -239,22 +252,31 @@ extern "C" int ocb_lex_device_static(const uint8_t *d_src, uint64_t N, const uin
     if (tmax > tmp_cap)
         return static_fail(err, err_len, -2, "ocb_lex_device_static: scan scratch does not fit");
 
+    // Each step is queued only when everything before it was queued: a
+    // failed scan must not leave later kernels reading what an earlier call
+    // left in the array and writing it to the caller's outputs.
+    const char *failed = "ocb_lex_device_static: launch failed";
     k_lex_map<<<grid, BLOCK, 0, st>>>(d_src, N, d_tu_off, n_tu, n_win, maps);
-    cudaError_t se = cub::DeviceScan::InclusiveScan(tmp, t1, maps, mapscan, ComposeOp(), nwi, st);
+    if (cudaGetLastError() != cudaSuccess ||
+        cub::DeviceScan::InclusiveScan(tmp, t1, maps, mapscan, ComposeOp(), nwi, st) != cudaSuccess)
+        return static_fail(err, err_len, -1, failed);
     k_lex_sync<<<grid, BLOCK, 0, st>>>(d_src, N, d_tu_off, n_tu, n_win, mapscan, nlseg, fsync, sinfo);
-    if (se == cudaSuccess)
-        se = cub::DeviceScan::ExclusiveScan(tmp, t2, nlseg, nlcarry, SegSumOp(), (uint64_t)0, nwi, st);
-    if (se == cudaSuccess) se = cub::DeviceScan::InclusiveScan(tmp, t3, rin, rout, MinOp(), nwi, st);
+    if (cudaGetLastError() != cudaSuccess ||
+        cub::DeviceScan::ExclusiveScan(tmp, t2, nlseg, nlcarry, SegSumOp(), (uint64_t)0, nwi,
+                                       st) != cudaSuccess ||
+        cub::DeviceScan::InclusiveScan(tmp, t3, rin, rout, MinOp(), nwi, st) != cudaSuccess)
+        return static_fail(err, err_len, -1, failed);
     k_set_u64<<<1, 1, 0, st>>>(S + n_win, N);
     k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(false, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
                                              nlcarry, counts, nullptr, o);
     k_set_u64<<<1, 1, 0, st>>>(counts + n_win, 0);
-    if (se == cudaSuccess) se = cub::DeviceScan::ExclusiveSum(tmp, t4, counts, toff, nwi + 1, st);
+    if (cudaGetLastError() != cudaSuccess ||
+        cub::DeviceScan::ExclusiveSum(tmp, t4, counts, toff, nwi + 1, st) != cudaSuccess)
+        return static_fail(err, err_len, -1, failed);
     k_lex_tokens_dfa<<<grid, BLOCK, 0, st>>>(true, d_src, N, d_tu_off, n_tu, n_win, S, sinfo,
                                              nlcarry, nullptr, toff, o);
     k_lex_finish<<<grid_tu, 256, 0, st>>>(n_tu, errkey, unsup, d_status, d_tu_tok_off, total,
                                            d_n_tok);
-    if (se != cudaSuccess || cudaGetLastError() != cudaSuccess)
-        return static_fail(err, err_len, -1, "ocb_lex_device_static: launch failed");
+    if (cudaGetLastError() != cudaSuccess) return static_fail(err, err_len, -1, failed);
     return 0;
 }

@@ -137,6 +137,15 @@ int compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_
                    uint32_t n_tu, int stage, uint64_t *h_total);
 }  // namespace ocb
 
+// Waits until the work queued on `st` is done, like cudaStreamSynchronize,
+// but gives up after the watchdog limit (OCB_WATCHDOG_S seconds in the
+// environment, default 1800) and returns cudaErrorTimeout: a host thread
+// never blocks forever on a device that stopped making progress.  Polls
+// cudaStreamQuery (yielding for the first 2 ms, then sleeping 100 us).
+namespace ocb {
+cudaError_t stream_wait(cudaStream_t st);
+}  // namespace ocb
+
 // Phase timing for tuning: with OCB_TIMING set in the environment, mark()
 // synchronises the stream and prints the time since the previous mark.
 struct PhaseTimer {

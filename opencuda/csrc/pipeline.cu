@@ -106,7 +106,7 @@ int merge_parts(ocb_ctx *ctx, uint32_t n_tu, Part A, Part B, Part C,
     uint64_t total = 0;
     OCB_TRY("merge: d2h", cudaMemcpyAsync(&total, C.off->as<uint64_t>() + n_tu, 8,
                                           cudaMemcpyDeviceToHost, st));
-    OCB_TRY("merge: sync", cudaStreamSynchronize(st));
+    OCB_TRY("merge: sync", stream_wait(st));
     OCB_TRY("merge: text", C.text->ensure(total + 64));
     k_merge_copy<<<n_tu, 128, 0, st>>>(A.text->as<uint8_t>(), A.off->as<uint64_t>(),
                                        B.text->as<uint8_t>(), B.off->as<uint64_t>(),
@@ -145,7 +145,7 @@ static int cc_with_reruns(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const
     for (uint32_t scale = 8; scale <= 64; scale *= 8) {
         if (n_tu) OCB_TRY("cc: d2h", cudaMemcpyAsync(hs.data(), ctx->res_status.p, 4 * (size_t)n_tu,
                                                      cudaMemcpyDeviceToHost, st));
-        OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+        OCB_TRY("cc: sync", stream_wait(st));
         std::vector<uint32_t> redo;
         for (uint32_t i = 0; i < n_tu; ++i)
             if (hs[i] == OCB_TU_OVERFLOW && hin[i] == 0) redo.push_back(i);
@@ -153,7 +153,7 @@ static int cc_with_reruns(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const
         if (h_off.empty()) {
             h_off.resize(n1);
             OCB_TRY("cc: d2h", cudaMemcpyAsync(h_off.data(), d_off, 8 * n1, cudaMemcpyDeviceToHost, st));
-            OCB_TRY("cc: sync", cudaStreamSynchronize(st));
+            OCB_TRY("cc: sync", stream_wait(st));
         }
         uint64_t sub_bytes = 0;
         rc = gather_sub(ctx, d_text, d_off, h_off, redo, &sub_bytes, st);
@@ -198,7 +198,7 @@ int pp_with_reruns(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_
     for (uint32_t scale = 32; scale <= 512; scale *= 16) {
         if (n_tu) OCB_TRY("pp: d2h", cudaMemcpyAsync(hs.data(), ctx->pp_status.p, 4 * (size_t)n_tu,
                                                      cudaMemcpyDeviceToHost, st));
-        OCB_TRY("pp: sync", cudaStreamSynchronize(st));
+        OCB_TRY("pp: sync", stream_wait(st));
         std::vector<uint32_t> redo;
         for (uint32_t i = 0; i < n_tu; ++i)
             if (hs[i] == OCB_TU_OVERFLOW) redo.push_back(i);
@@ -206,7 +206,7 @@ int pp_with_reruns(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_
         if (h_off.empty()) {
             h_off.resize(n1);
             OCB_TRY("pp: d2h", cudaMemcpyAsync(h_off.data(), d_tu_off, 8 * n1, cudaMemcpyDeviceToHost, st));
-            OCB_TRY("pp: sync", cudaStreamSynchronize(st));
+            OCB_TRY("pp: sync", stream_wait(st));
         }
         uint64_t sub_bytes = 0;
         rc = gather_sub(ctx, d_src, d_tu_off, h_off, redo, &sub_bytes, st);
@@ -232,7 +232,7 @@ int pp_with_reruns(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_
         std::vector<uint32_t> qa(n_tu), qb(nr);
         OCB_TRY("pp: d2h", cudaMemcpyAsync(qa.data(), ctx->pp_qinc.p, 4 * (size_t)n_tu, cudaMemcpyDeviceToHost, st));
         OCB_TRY("pp: d2h", cudaMemcpyAsync(qb.data(), ctx->rt_qinc.p, 4 * (size_t)nr, cudaMemcpyDeviceToHost, st));
-        OCB_TRY("pp: sync", cudaStreamSynchronize(st));
+        OCB_TRY("pp: sync", stream_wait(st));
         for (uint32_t k = 0; k < nr; ++k) qa[redo[k]] = qb[k];
         OCB_TRY("pp: h2d", cudaMemcpyAsync(ctx->pp_qinc.p, qa.data(), 4 * (size_t)n_tu, cudaMemcpyHostToDevice, st));
     }
@@ -250,7 +250,7 @@ int compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_
         OCB_TRY("pipeline: offsets", ctx->pp_off.ensure(8));
         OCB_TRY("pipeline: status", ctx->res_status.ensure(4));
         OCB_TRY("pipeline: h2d", cudaMemcpyAsync(ctx->res_off.p, &z, 8, cudaMemcpyHostToDevice, st));
-        OCB_TRY("pipeline: sync", cudaStreamSynchronize(st));
+        OCB_TRY("pipeline: sync", stream_wait(st));
         *h_total = 0;
         return 0;
     }

@@ -32,7 +32,7 @@ int pp_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_
             cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, sizes, arena_off, (int)n1, st));
     uint64_t arena_total = 0;
     OCB_TRY("pp: d2h", cudaMemcpyAsync(&arena_total, arena_off + n_tu, 8, cudaMemcpyDeviceToHost, st));
-    OCB_TRY("pp: sync", cudaStreamSynchronize(st));
+    OCB_TRY("pp: sync", stream_wait(st));
     OCB_TRY("pp: arena", ctx->pp_arena.ensure(arena_total));
     OCB_TRY("pp: memset", cudaMemsetAsync(d_qinc, 0, 4 * (size_t)n_tu, st));
     PPArgs A{d_src, d_tu_off, n_tu, ctx->pp_arena.as<uint8_t>(), arena_off,
@@ -44,7 +44,7 @@ int pp_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_
             cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t2, len64, d_out_off, (int)n1, st));
     uint64_t total = 0;
     OCB_TRY("pp: d2h", cudaMemcpyAsync(&total, d_out_off + n_tu, 8, cudaMemcpyDeviceToHost, st));
-    OCB_TRY("pp: sync", cudaStreamSynchronize(st));
+    OCB_TRY("pp: sync", stream_wait(st));
     OCB_TRY("pp: output", out_text.ensure(total + 64));
     k_pp_pack<<<n_tu, 128, 0, st>>>(ctx->pp_arena.as<uint8_t>(), arena_off, d_out_off,
                                     out_text.as<uint8_t>(), n_tu);

@@ -26,7 +26,9 @@ from __future__ import annotations
 import random
 import numpy as np
 
-GEN_VERSION = 1
+# 2: lognormal statement counts calibrated so the byte sizes have the stated
+#    median (head and tail ~408 bytes, ~34 bytes per statement)
+GEN_VERSION = 2
 
 SGEMM_SRC = r"""// Tiled single-precision GEMM: C = alpha * A * B + beta * C
 // A is MxK, B is KxN, C is MxN, all row-major; one 16x16 tile of C per block.
@@ -213,17 +215,36 @@ def random_batch(n: int = 4096, seed: int = 1234) -> list[str]:
     return [random_kernel(seed + i, i) for i in range(n)]
 
 
+def lognormal_kernel(seed: int, idx: int, median: int = 3000, sigma: float = 1.0) -> str:
+    """One kernel of the lognormal workload, its size drawn from
+    lognormal(median, sigma) bytes."""
+    r = random.Random(seed)
+    target = median * float(np.exp(sigma * r.gauss(0.0, 1.0)))
+    # ~408 bytes of kernel head and tail plus ~34 bytes per statement
+    n_stmts = int(min(max(round((target - 408.0) / 34.0), 4), 4000))
+    return _KernelGen(r, idx).kernel(n_stmts)
+
+
+def _lognormal_range(args):
+    lo, hi, seed, median, sigma = args
+    return [lognormal_kernel(seed + i, i, median, sigma) for i in range(lo, hi)]
+
+
 def lognormal_batch(n: int = 262144, seed: int = 5678, median: int = 3000,
-                    sigma: float = 1.0) -> list[str]:
-    """Random kernels with byte sizes ~ lognormal(median, sigma)."""
-    out = []
-    for i in range(n):
-        r = random.Random(seed + i)
-        target = median * np.exp(sigma * r.gauss(0.0, 1.0))
-        # ~27 bytes of source per statement in this mix.
-        n_stmts = int(min(max(target / 27.0, 4), 4000))
-        out.append(_KernelGen(r, i).kernel(n_stmts))
-    return out
+                    sigma: float = 1.0, procs: int = 1) -> list[str]:
+    """Random kernels with byte sizes ~ lognormal(median, sigma).
+
+    ``procs`` > 1 generates in that many ``spawn`` worker processes (the
+    262,144-kernel batch takes minutes in one process); the output does not
+    depend on it."""
+    if procs <= 1 or n < 4096:
+        return _lognormal_range((0, n, seed, median, sigma))
+    import multiprocessing as mp
+    step = (n + 4 * procs - 1) // (4 * procs)
+    jobs = [(lo, min(n, lo + step), seed, median, sigma) for lo in range(0, n, step)]
+    with mp.get_context("spawn").Pool(procs) as pool:
+        parts = pool.map(_lognormal_range, jobs)
+    return [k for part in parts for k in part]
 
 
 # --------------------------------------------------------------------------

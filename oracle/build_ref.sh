@@ -5,9 +5,12 @@
 # checkout.  The reference is read-only, so setuptools builds from a copy in
 # a temporary directory.  Output goes only to oracle/_ref (git-ignored).
 #
-# usage: oracle/build_ref.sh [REFERENCE_DIR]   (default /root/reference)
+# usage: oracle/build_ref.sh [REFERENCE_DIR]
+#   REFERENCE_DIR defaults to $OCB_REFERENCE_DIR, else /root/reference (the
+#   read-only checkout on the build machine).  Without a checkout there it
+#   keeps the existing install and exits 0.
 set -euo pipefail
-REF="${1:-/root/reference}"
+REF="${1:-${OCB_REFERENCE_DIR:-/root/reference}}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
 OUT="$HERE/_ref/py"
 if [ ! -f "$REF/opencuda/frontend/lexer.py" ]; then

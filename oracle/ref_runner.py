@@ -142,6 +142,26 @@ def _lex_only(src):
         return 0
 
 
+# exception class of the reference -> per-TU status code of include/ocb.h
+RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError": 4,
+                "error": 5}
+
+
+def _digest_job(args):
+    """One TU through the reference CLI path, reduced to what a parity check
+    of many TUs needs: (status code, sha256 of the PTX module text, its byte
+    length).  The status is 0 when the reference writes PTX, else the
+    ``include/ocb.h`` code of the exception class it raises (6 for others)."""
+    import hashlib
+    src, what, arch = args
+    r = _job((src, what, arch))
+    key = "ptx" if "ptx" in what else "pp"
+    if key in r:
+        b = r[key].encode("utf-8", "surrogateescape")
+        return 0, hashlib.sha256(b).digest(), len(b)
+    return RAISE_STATUS.get(r["error"][0], 6), b"", 0
+
+
 def _compile_only(src):
     r = _job((src, ("ptx",), "sm_120"))
     return len(r.get("ptx", ""))
@@ -184,6 +204,11 @@ class RefPool:
 
     def run(self, srcs, what=("ptx",), arch="sm_120", chunksize=4):
         return self.pool.map(_job, [(s, tuple(what), arch) for s in srcs],
+                             chunksize=chunksize)
+
+    def digests(self, srcs, what="ptx", arch="sm_120", chunksize=16):
+        """``_digest_job`` over ``srcs`` (``what``: "ptx" or "pp")."""
+        return self.pool.map(_digest_job, [(s, (what,), arch) for s in srcs],
                              chunksize=chunksize)
 
     def resolve_includes(self, srcs, dirs):

@@ -19,6 +19,28 @@ def golden(name: str):
 RAISE_CODE = {"ValueError": 1, "OverflowError": 2}
 
 
+def check_digests(gold, idx, texts, statuses):
+    """Compare engine results with a golden digest record
+    (``oracle/goldens.py``): TU ``idx[j]`` of the workload gave status
+    ``statuses[j]`` and text ``texts[j]`` (bytes or str; ignored unless the
+    status is 0).  Every TU must be byte-identical, or raise where the
+    reference raises (same exception class); returns the count of each."""
+    import hashlib
+    n_ok = n_raise = 0
+    for j, i in enumerate(idx):
+        st, gs = int(statuses[j]), int(gold["status"][i])
+        if gs != 0:
+            assert st == gs, (i, "reference raises", gs, "engine status", st)
+            n_raise += 1
+            continue
+        assert st == 0, (i, "engine status", st)
+        t = texts[j]
+        b = t.encode("utf-8", "surrogateescape") if isinstance(t, str) else bytes(t)
+        assert hashlib.sha256(b).digest() == bytes(gold["digest"][i]), (i, "PTX differs")
+        n_ok += 1
+    return n_ok, n_raise
+
+
 def fuzz_sources(n: int, seed: int, maxlen: int = 80):
     r = random.Random(seed)
     alpha = list("\"'/*\\\n \t\r.0123456789xXeEpP+-fFuUlLabz_=<>&|!;#@\x0c") + [
@@ -279,7 +301,7 @@ def mutate_sources(n: int, seed: int):
     """Seeded token-level mutations (delete / insert / replace) of the hand
     cases and of generated kernels: inputs for the parser's error paths."""
     import re
-    from opencuda_b200 import synth
+    from opencuda import synth
     r = random.Random(seed)
     base = PARSE_CASES + synth.random_batch(50, seed=seed)
     toks_re = re.compile(r"\s+|[A-Za-z_]\w*|\d+\.?\d*[fFuUlL]*|\S")

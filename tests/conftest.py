@@ -15,7 +15,7 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def ctx():
     """A libocb context on cuda:0 (GPU tests only)."""
-    from opencuda_b200 import api
+    from opencuda import api
     c = api.Context(0)
     yield c
     c.close()

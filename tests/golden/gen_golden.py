@@ -22,7 +22,7 @@ ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 
 from oracle import ref_runner  # noqa: E402
-from opencuda_b200 import synth  # noqa: E402
+from opencuda import synth  # noqa: E402
 
 LEX_EDGE = [
     "", "a", "\n", "\n\n\n", "/", "//", "/*", "/**/", "/*/", "/*/*/", "/* */x",

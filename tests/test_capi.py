@@ -6,7 +6,7 @@ from pathlib import Path
 
 import pytest
 
-from opencuda_b200 import _lib
+from opencuda import _lib
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -25,7 +25,7 @@ def test_header_declares_entry_points():
 
 def test_library_exports_every_declared_symbol():
     if not _lib.LIB_PATH.is_file():
-        pytest.fail("libocb.so not built: python -m opencuda_b200.build")
+        pytest.fail("libocb.so not built: python -m opencuda.build")
     lib = ctypes.CDLL(str(_lib.LIB_PATH))
     missing = [n for n in declared_functions() if not hasattr(lib, n)]
     assert not missing, missing

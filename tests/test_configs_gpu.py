@@ -1,15 +1,17 @@
-"""PTX parity on the workload shapes beyond the 4,096-kernel batch: the
-register-pressure kernels (~6,000 statements, ~20k SSA values, peak live
-~4k: the allocator's interval hulls, back-edge extension and FIFO reuse at
-scale, ``emit.py:115-342``) and a sample of the lognormal-size batch (median
-3 KB, sigma 1, the tail up to ~100 KB TUs).  Every TU is compared byte for
-byte with the live reference compiler; TUs where it raises must report the
-same exception class."""
+"""PTX parity on the benchmark workloads: the register-pressure kernels
+(~6,000 statements, ~20k SSA values, peak live ~4k: the allocator's interval
+hulls, back-edge extension and FIFO reuse at scale, ``emit.py:115-342``), the
+4,096 random kernels and the lognormal-size batch (median 3 KB, sigma 1, the
+tail up to ~140 KB TUs).  Every TU is compared byte for byte with the
+reference compiler -- live, or through the golden digests of the whole
+workload (``python -m oracle.goldens``); TUs where it raises must report the
+same exception class, and no TU of these workloads may be ``unsupported``."""
 import pytest
 
-from oracle import ref_runner
-from opencuda_b200 import synth
-from opencuda_b200.api import TU_UNSUPPORTED
+from oracle import goldens, ref_runner
+from opencuda import synth
+from opencuda.api import TU_UNSUPPORTED
+from tests._helpers import check_digests
 
 pytestmark = pytest.mark.gpu
 
@@ -51,3 +53,33 @@ def test_lognormal_sample(ctx):
     with ref_runner.RefPool() as pool:
         ref = pool.run(srcs, what=("ptx",), chunksize=4)
     _check(tb, srcs, ref)
+
+
+def _against_goldens(ctx, name, idx, srcs):
+    gold = goldens.load(name)
+    if gold is None:
+        pytest.skip(f"golden record {name} not made (python -m oracle.goldens {name})")
+    tb = ctx.compile_batch(srcs)
+    assert not any(int(s) == TU_UNSUPPORTED for s in tb.status)
+    texts = [tb.data[int(tb.off[j]):int(tb.off[j + 1])] for j in range(len(srcs))]
+    n_ok, n_raise = check_digests(gold, idx, texts, tb.status)
+    assert n_ok + n_raise == len(srcs)
+    return n_ok, n_raise
+
+
+def test_register_pressure_all_256(ctx):
+    srcs = synth.regpressure_batch(256, seed=4242)
+    n_ok, _ = _against_goldens(ctx, "c4", range(256), srcs)
+    assert n_ok == 256
+
+
+def test_random_4096_all(ctx):
+    srcs = synth.random_batch(4096, seed=1234)
+    _against_goldens(ctx, "c2", range(4096), srcs)
+
+
+def test_lognormal_every_16th(ctx):
+    """16,384 TUs spread over the whole 262,144-kernel batch (every 16th)."""
+    idx = list(range(0, 262144, 16))
+    srcs = [synth.lognormal_kernel(5678 + i, i) for i in idx]
+    _against_goldens(ctx, "c5", idx, srcs)

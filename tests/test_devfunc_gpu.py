@@ -8,7 +8,7 @@ must come back as `unsupported`, never as different output."""
 import pytest
 
 from oracle import ref_runner
-from opencuda_b200.api import TU_UNSUPPORTED
+from opencuda.api import TU_UNSUPPORTED
 from tests._helpers import (ADDR_OF_CASES, CAST_CASES, DEVFUNC_CASES, DEVFUNC_RECURSIVE_CASES,
                             ARRAY_PARAM_CASES, HEXFLOAT_CASES, INTRINSIC_CASES,
                             HALF_REDUCE_CASES, MORE_INTRINSIC_CASES, UNKNOWN_CALL_CASES,

@@ -11,7 +11,7 @@ from pathlib import Path
 import pytest
 
 from oracle import ref_runner
-from opencuda_b200 import compiler
+from opencuda import compiler
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -105,7 +105,7 @@ def test_status_names():
 
 def _cli(*args, cwd=None):
     env = dict(os.environ, PYTHONPATH=str(ROOT))
-    return subprocess.run([sys.executable, "-m", "opencuda_b200", *map(str, args)],
+    return subprocess.run([sys.executable, "-m", "opencuda", *map(str, args)],
                           capture_output=True, text=True, cwd=cwd, env=env, timeout=300)
 
 
@@ -125,6 +125,6 @@ def test_product_path_fails_loudly_without_gpu():
     import torch
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
-    from opencuda_b200 import OcbError
+    from opencuda import OcbError
     with pytest.raises(OcbError):
         compiler.compile("__global__ void k() {}")

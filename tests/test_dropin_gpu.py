@@ -1,5 +1,5 @@
 """The drop-in surface on the GPU: ``compile()``, ``compile_batch()`` and the
-CLI ``python -m opencuda_b200 X.cu --emit-ptx`` against the reference's own
+CLI ``python -m opencuda X.cu --emit-ptx`` against the reference's own
 CLI ``python -m opencuda X.cu --emit-ptx`` (``opencuda/__main__.py:13-102``),
 run unmodified from oracle/_ref/py: same file bytes, same stdout lines."""
 import os
@@ -10,7 +10,7 @@ from pathlib import Path
 import pytest
 
 from oracle import ref_runner
-from opencuda_b200 import compiler, synth
+from opencuda import compiler, synth
 from tests._helpers import golden
 
 pytestmark = pytest.mark.gpu
@@ -49,7 +49,7 @@ def _project(tmp: Path):
 
 def _ours(args, cwd):
     env = dict(os.environ, PYTHONPATH=str(ROOT))
-    return subprocess.run([sys.executable, "-m", "opencuda_b200", *map(str, args)], cwd=cwd,
+    return subprocess.run([sys.executable, "-m", "opencuda", *map(str, args)], cwd=cwd,
                           env=env, capture_output=True, text=True, timeout=600)
 
 

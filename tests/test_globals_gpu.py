@@ -8,7 +8,7 @@ declarations that lead the module text.  Compared with the live reference as
 parsed IR, optimized IR and PTX, and through the drop-in `compile()` call."""
 import pytest
 
-import opencuda_b200 as oc
+import opencuda as oc
 from oracle import ref_runner
 from tests._helpers import GLOBAL_2D_CASES, GLOBAL_VAR_CASES
 

@@ -1,8 +1,9 @@
 """The N>1 path of bench.py on CPU: two gloo ranks (world_size 2) join the
-process group the way torchrun launches them, compile disjoint TU shards
-(weak scaling: each rank its own seed), and combine bytes (sum) and step
-times (max) with the same helpers the GPU run uses.  The data path has no
-collective; these two reductions are the only cross-rank traffic."""
+process group the way torchrun launches them, split every slice of a batch
+across the ranks by bytes (greedy LPT: strong scaling, each TU on exactly one
+rank), and combine bytes (sum) and step times (max) with the same helpers the
+GPU run uses.  The data path has no collective; these reductions are the only
+cross-rank traffic."""
 import multiprocessing as mp
 import os
 import socket
@@ -22,16 +23,26 @@ def _rank_main(rank, world, port, q):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
                       MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     sys.path.insert(0, str(ROOT))
+    import numpy as np
     import torch.distributed as dist
 
     import bench
+    from opencuda import synth
     r, w, _ = bench.dist_init("gloo")
-    srcs = bench.workload(r, 6)
-    nbytes = float(sum(len(s.encode()) for s in srcs))
+    srcs = synth.lognormal_batch(64, seed=5678)
+    buf, off = bench.c5_batch(r, w, n=64)   # rank 0 generates, rank 1 reads its file
+    assert buf.tobytes() == "".join(srcs).encode()
+    plan = bench.slice_plan(np.diff(off), 4, w)
+    mine = [plan[j][r] for j in range(4)]
+    shards = [bench.gather(buf, off, m) for m in mine]
+    for m, (b, o) in zip(mine, shards):
+        assert [bytes(b[int(o[k]):int(o[k + 1])]).decode() for k in range(len(m))] == \
+            [srcs[i] for i in m]
+    nbytes = float(sum(len(b) for b, _ in shards))
     total = bench.allreduce(nbytes, w, "cpu", "sum")
     slowest = bench.allreduce(1.0 + r, w, "cpu", "max")
     bench.barrier(w)
-    q.put((r, w, srcs[0], nbytes, total, slowest))
+    q.put((r, w, [m.tolist() for m in mine], nbytes, total, slowest, len(buf)))
     dist.destroy_process_group()
 
 
@@ -46,8 +57,11 @@ def test_two_gloo_ranks_shard_and_reduce():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    (r0, w0, s0, b0, t0, m0), (r1, w1, s1, b1, t1, m1) = out
+    (r0, w0, p0, b0, t0, m0, n0), (r1, w1, p1, b1, t1, m1, n1) = out
     assert (r0, r1, w0, w1) == (0, 1, 2, 2)
-    assert s0 != s1                       # disjoint shards
-    assert t0 == t1 == b0 + b1            # whole-job bytes
+    for j in range(4):                    # every TU of a slice on exactly one rank
+        assert sorted(p0[j] + p1[j]) == list(range(j, 64, 4))
+        assert not set(p0[j]) & set(p1[j])
+    assert t0 == t1 == b0 + b1 == n0      # whole-job bytes
+    assert abs(b0 - b1) < 0.25 * n0       # balanced by bytes
     assert m0 == m1 == 2.0                # max over ranks

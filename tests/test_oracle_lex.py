@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from oracle import lex_oracle
-from opencuda_b200 import synth
+from opencuda import synth
 from tests._helpers import golden, RAISE_CODE
 
 

@@ -5,7 +5,7 @@ live reference at every stage: parsed IR, optimized IR and PTX."""
 import pytest
 
 from oracle import ref_runner
-from opencuda_b200.api import TU_UNSUPPORTED
+from opencuda.api import TU_UNSUPPORTED
 from tests._helpers import SWITCH_CASES, switch_sources
 
 pytestmark = pytest.mark.gpu

@@ -6,7 +6,7 @@ with the live reference as parsed IR, optimized IR and PTX."""
 import pytest
 
 from oracle import ref_runner
-from opencuda_b200.api import TU_UNSUPPORTED
+from opencuda.api import TU_UNSUPPORTED
 from tests._helpers import TYPEDEF_ENUM_CASES, typedef_enum_sources
 
 pytestmark = pytest.mark.gpu

@@ -15,8 +15,8 @@ import ctypes
 import numpy as np
 import pytest
 
-from opencuda_b200 import _lib, synth
-from opencuda_b200.api import pack_sources
+from opencuda import _lib, synth
+from opencuda.api import pack_sources
 from tests._helpers import fuzz_sources
 
 pytestmark = pytest.mark.gpu
