@@ -7,12 +7,13 @@ Workload: the 262,144 seeded lognormal-size kernels (median 3 KB, sigma 1,
 1.20 GiB of CUDA C; the statement mix of the random kernels: 60% s32 / 40%
 f32 arithmetic, if/else depth <= 3, unrollable for loops of trip 2-16,
 atomics and __shfl_sync), compiled to PTX: preprocess -> lex -> parse ->
-optimize -> register allocation -> PTX text.  The batch is split into
-``--slices`` interleaved slices (slice j = kernels i with i % S == j, so
-every slice has the batch's size distribution); one step compiles one slice,
-step k slice k % S, so K >= S timed steps compile the whole batch.  With N
-ranks (one per GPU) every slice is split across the ranks by bytes with
-greedy LPT (strong scaling: the job's total work does not depend on N).
+optimize -> register allocation -> PTX text.  The batch, ordered by size
+(largest first), is cut into ``--slices`` consecutive slices of about equal
+bytes; one step compiles one slice, step k slice k % S, so K >= S timed
+steps compile the whole batch once (``value`` is then the whole job's
+throughput).  With N ranks (one per GPU) every slice is split across the
+ranks by bytes with greedy LPT (strong scaling: the job's total work does
+not depend on N).
 The working set of a step (GBs of compiler arenas) is far larger than L2, so
 no flush is needed between steps.
 
@@ -207,14 +208,22 @@ def synth_pack(srcs):
 
 
 def slice_plan(sizes, n_slices: int, world: int):
-    """Per slice, per rank: the TU indices that rank compiles.  Slice j holds
-    TUs i with i % n_slices == j; each slice is split across ranks by bytes
-    with greedy LPT (``opencuda.partition_lpt``), largest TUs first."""
+    """Per slice, per rank: the TU indices that rank compiles.  The batch is
+    ordered by size, largest first, and cut into ``n_slices`` consecutive
+    slices of about equal bytes (so one slice holds the largest kernels and
+    the last the smallest); each slice is split across ranks by bytes with
+    greedy LPT (``opencuda.partition_lpt``), largest TUs first."""
     from opencuda import partition_lpt
     sizes = np.asarray(sizes, dtype=np.int64)
+    order = np.argsort(-sizes, kind="stable")
+    cum = np.cumsum(sizes[order])
+    total = int(cum[-1]) if len(cum) else 0
+    # slice of each position: by the bytes before it
+    before = cum - sizes[order]
+    sl = np.minimum((before * n_slices) // max(total, 1), n_slices - 1)
     plan = []
     for j in range(n_slices):
-        idx = np.arange(j, len(sizes), n_slices, dtype=np.int64)
+        idx = order[sl == j]
         parts = partition_lpt(sizes[idx].tolist(), world)
         plan.append([idx[np.asarray(p, dtype=np.int64)] if p else np.zeros(0, np.int64)
                      for p in parts])
@@ -462,7 +471,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--slices", type=int, default=16,
-                    help="interleaved slices of the batch; one step compiles one slice")
+                    help="slices of the size-ordered batch; one step compiles one slice")
     ap.add_argument("--tus", type=int, default=C5_N,
                     help="first TUs of the batch to use (smaller only for profiling)")
     ap.add_argument("--e2e-steps", type=int, default=None,

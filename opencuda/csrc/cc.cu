@@ -80,7 +80,9 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     unsigned long long *spill_top =
         (unsigned long long *)(((uintptr_t)(lex_status + n1) + 15) & ~(uintptr_t)15);
     PhaseTimer T(st);
-    int rc = lex_device(ctx, d_text, N, d_off, n_tu, tstart, tkl, tline, tok_cap, tu_tok,
+    // the parser reads token starts and kinds only: no per-token lines
+    (void)tline;
+    int rc = lex_device(ctx, d_text, N, d_off, n_tu, tstart, tkl, nullptr, tok_cap, tu_tok,
                         lex_status, n_tok, st);
     if (rc) return rc;
     T.mark("cc: lex");

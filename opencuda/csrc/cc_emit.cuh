@@ -6,7 +6,7 @@
 // rewrites them with regular-expression peepholes; this code keeps the same
 // line-level representation and restates each peephole's pattern by hand.
 #pragma once
-#include "cc_opt.cuh"
+#include "cc_opt_base.cuh"
 
 namespace ocb {
 namespace cc {

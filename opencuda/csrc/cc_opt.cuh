@@ -7,319 +7,10 @@
 // Constants carry Python semantics: an int (pyint) or a float, whatever the
 // IR type says; folds follow Python's int/float arithmetic.
 #pragma once
-#include "cc_ir.cuh"
+#include "cc_opt_base.cuh"
 
 namespace ocb {
 namespace cc {
-
-// ---------------------------------------------------------------------------
-// Python value helpers for Const
-// ---------------------------------------------------------------------------
-struct PyVal {
-    uint8_t isf;  // 1 = float
-    pyint i;
-    double f;
-};
-OCB_HD inline PyVal pv_int(pyint i) { return PyVal{0, i, 0.0}; }
-OCB_HD inline PyVal pv_float(double f) { return PyVal{1, 0, f}; }
-OCB_HD inline PyVal pv_of(const Const &c) { return PyVal{c.pyfloat, c.i, c.f}; }
-OCB_HD inline bool is_finite(double f) { return f == f && f - f == 0.0; }
-
-// exact comparison of an int with a float (Python int/float ordering)
-// returns -1, 0, 1; 2 when b is NaN (unordered)
-OCB_HD inline int cmp_int_float(pyint a, double b) {
-    if (b != b) return 2;
-    if (b >= 1.7e38) return -1;   // beyond any kept pyint
-    if (b <= -1.7e38) return 1;
-    double fb = floor(b);
-    pyint ib = (pyint)fb;
-    if (a < ib) return -1;
-    if (a > ib) return 1;
-    return b == fb ? 0 : -1;
-}
-// Python ==
-OCB_HD inline bool pv_eq(const PyVal &a, const PyVal &b) {
-    if (!a.isf && !b.isf) return a.i == b.i;
-    if (a.isf && b.isf) return a.f == b.f;
-    if (a.isf) return cmp_int_float(b.i, a.f) == 0;
-    return cmp_int_float(a.i, b.f) == 0;
-}
-// Python a > b (False when unordered)
-OCB_HD inline bool pv_gt(const PyVal &a, const PyVal &b) {
-    if (!a.isf && !b.isf) return a.i > b.i;
-    if (a.isf && b.isf) return a.f > b.f;
-    if (a.isf) {
-        int c = cmp_int_float(b.i, a.f);
-        return c == -1;
-    }
-    int c = cmp_int_float(a.i, b.f);
-    return c == 1;
-}
-OCB_HD inline bool pv_eq_int(const PyVal &a, pyint v) { return pv_eq(a, pv_int(v)); }
-OCB_HD inline bool pv_truthy(const PyVal &a) { return a.isf ? a.f != 0.0 : a.i != 0; }
-// int(value): false when Python raises (NaN/inf) or leaves the kept range
-OCB_HD inline bool pv_to_int(const PyVal &a, pyint &out) {
-    if (!a.isf) {
-        out = a.i;
-        return true;
-    }
-    if (!is_finite(a.f) || a.f >= 1.3e36 || a.f <= -1.3e36) return false;
-    out = (pyint)trunc(a.f);
-    return true;
-}
-OCB_HD inline double pv_to_float(const PyVal &a) { return a.isf ? a.f : (double)a.i; }
-
-// Python float % (CPython float_rem: fmod, then the sign of the divisor)
-OCB_HD inline double py_fmod(double vx, double wx) {
-    double mod = fmod(vx, wx);
-    if (mod != 0.0) {
-        if ((wx < 0) != (mod < 0)) mod += wx;
-    } else {
-        mod = copysign(0.0, wx);
-    }
-    return mod;
-}
-
-// _mask_int (optimize.py:53-70): wrap to the type's width with its sign.
-// `ok` is false where the reference would keep an unbounded value we cannot.
-OCB_HD inline pyint mask_int_wrapped(pyint wrapped_low, Ty ty) {
-    uint32_t bits = ty_size(ty) * 8;
-    unsigned __int128 mask = bits >= 128 ? ~(unsigned __int128)0
-                                         : (((unsigned __int128)1) << bits) - 1;
-    unsigned __int128 v = (unsigned __int128)wrapped_low & mask;
-    if (ty_is_signed(ty) && bits && ((v >> (bits - 1)) & 1)) {
-        return (pyint)v - (pyint)(((unsigned __int128)1) << bits);
-    }
-    return (pyint)v;
-}
-OCB_HD inline bool masks(Ty ty) { return !is_ptr(ty) && !ty_is_float(ty); }
-
-// ---------------------------------------------------------------------------
-// per-pass scratch: id-indexed arrays and a label -> block map
-// ---------------------------------------------------------------------------
-template <class T>
-struct IdArr {
-    T *p;
-    uint32_t n;
-    T dflt;
-    OCB_HD void init(Arena &a, uint32_t size, T d) {
-        n = size;
-        dflt = d;
-        p = (T *)a.alloc(sizeof(T) * (uint64_t)(size ? size : 1), 16);
-        if (p)
-            for (uint32_t i = 0; i < size; ++i) p[i] = d;
-        else
-            n = 0;
-    }
-    OCB_HD T get(uint32_t id) const { return id < n ? p[id] : dflt; }
-    OCB_HD bool set(uint32_t id, T v) {
-        if (id >= n) return false;
-        p[id] = v;
-        return true;
-    }
-};
-
-struct LabelMap {
-    int32_t *ht;
-    uint32_t cap;
-    const Module *m;
-    OCB_HD void build(Arena &a, const Module &mod, const Vec<uint32_t> &blocks) {
-        m = &mod;
-        cap = 16;
-        while (cap < 2 * blocks.n + 2) cap *= 2;
-        ht = (int32_t *)a.alloc(4ull * cap, 16);
-        if (!ht) {
-            cap = 0;
-            return;
-        }
-        for (uint32_t i = 0; i < cap; ++i) ht[i] = -1;
-        for (uint32_t i = 0; i < blocks.n; ++i) put(blocks[i]);
-    }
-    OCB_HD void put(uint32_t b) {  // last wins, like a dict comprehension
-        Str l = m->blocks[b].label;
-        uint32_t h = hash(l) & (cap - 1);
-        while (ht[h] >= 0) {
-            if (eq(m->blocks[ht[h]].label, l)) {
-                ht[h] = (int32_t)b;
-                return;
-            }
-            h = (h + 1) & (cap - 1);
-        }
-        ht[h] = (int32_t)b;
-    }
-    OCB_HD int32_t get(Str l) const {
-        if (!cap) return -1;
-        uint32_t h = hash(l) & (cap - 1);
-        while (ht[h] >= 0) {
-            if (eq(m->blocks[ht[h]].label, l)) return ht[h];
-            h = (h + 1) & (cap - 1);
-        }
-        return -1;
-    }
-};
-
-// A set of labels (open addressing over Str).
-struct LabelSet {
-    Str *ht;
-    uint32_t cap, n;
-    OCB_HD void init(Arena &a, uint32_t want) {
-        cap = 16;
-        while (cap < 2 * want + 2) cap *= 2;
-        n = 0;
-        ht = (Str *)a.alloc(sizeof(Str) * (uint64_t)cap, 16);
-        if (!ht) {
-            cap = 0;
-            return;
-        }
-        for (uint32_t i = 0; i < cap; ++i) ht[i] = Str{nullptr, 0};
-    }
-    OCB_HD bool has(Str l) const {
-        if (!cap) return false;
-        uint32_t h = hash(l) & (cap - 1);
-        while (ht[h].p) {
-            if (eq(ht[h], l)) return true;
-            h = (h + 1) & (cap - 1);
-        }
-        return false;
-    }
-    OCB_HD bool add(Str l) {  // true when newly added
-        if (!cap) return false;
-        uint32_t h = hash(l) & (cap - 1);
-        while (ht[h].p) {
-            if (eq(ht[h], l)) return false;
-            h = (h + 1) & (cap - 1);
-        }
-        if (2 * (n + 1) > cap) return false;  // sized by the caller
-        ht[h] = l;
-        ++n;
-        return true;
-    }
-};
-
-// CSE keys (optimize.py:397-640)
-struct OKey {
-    uint8_t tag;  // 0 'const', 1 'val'
-    PyVal c;
-    uint32_t id;
-};
-struct CKey {
-    uint8_t kind;  // 0 bin, 1 cvt, 2 cmp, 3 pure call
-    uint8_t op;
-    OKey l, r;
-    uint32_t t1, t2;  // str(type) keys
-    Str func;
-};
-OCB_HD inline bool okey_eq(const OKey &a, const OKey &b) {
-    if (a.tag != b.tag) return false;
-    if (a.tag == 1) return a.id == b.id;
-    return pv_eq(a.c, b.c);
-}
-// tuple a > tuple b for ('const', v) / ('val', id)
-OCB_HD inline bool okey_gt(const OKey &a, const OKey &b) {
-    if (a.tag != b.tag) return a.tag > b.tag;
-    if (a.tag == 1) return a.id > b.id;
-    if (pv_eq(a.c, b.c)) return false;
-    return pv_gt(a.c, b.c);
-}
-OCB_HD inline uint32_t okey_hash(const OKey &k) {
-    if (k.tag == 1) return k.id * 2654435761u + 7;
-    // numeric hash: integral floats hash like ints
-    pyint iv;
-    if (k.c.isf) {
-        double f = k.c.f;
-        if (is_finite(f) && f == trunc(f) && f < 1e30 && f > -1e30) iv = (pyint)f;
-        else {
-            uint64_t b;
-            memcpy(&b, &f, 8);
-            return (uint32_t)(b ^ (b >> 29)) * 0x9E3779B1u;
-        }
-    } else {
-        iv = k.c.i;
-    }
-    uint64_t lo = (uint64_t)iv, hi = (uint64_t)((unsigned __int128)iv >> 64);
-    return (uint32_t)((lo ^ (lo >> 31) ^ (hi * 31)) * 0x9E3779B1u);
-}
-OCB_HD inline bool ckey_eq(const CKey &a, const CKey &b) {
-    if (a.kind != b.kind) return false;
-    if (a.kind == 3) return eq(a.func, b.func);
-    if (a.kind != 1 && a.op != b.op) return false;
-    if (!okey_eq(a.l, b.l)) return false;
-    if (a.kind == 1) return a.t1 == b.t1 && a.t2 == b.t2;
-    if (!okey_eq(a.r, b.r)) return false;
-    return a.kind == 2 || a.t1 == b.t1;
-}
-OCB_HD inline uint32_t ckey_hash(const CKey &k) {
-    if (k.kind == 3) return hash(k.func) ^ 0x55u;
-    uint32_t h = k.kind * 31u + (k.kind == 1 ? 0 : k.op);
-    h = h * 1000003u ^ okey_hash(k.l);
-    if (k.kind != 1) h = h * 1000003u ^ okey_hash(k.r);
-    if (k.kind != 2) h = h * 1000003u ^ k.t1;
-    if (k.kind == 1) h = h * 1000003u ^ k.t2;
-    return h;
-}
-
-// The `seen` dict of one block: key -> value index.
-struct Seen {
-    struct E {
-        CKey k;
-        uint32_t v;
-        uint8_t used;
-    };
-    E *t;
-    uint32_t cap, n;
-    OCB_HD bool init(Arena &a, uint32_t c) {
-        cap = 16;
-        while (cap < c) cap *= 2;
-        n = 0;
-        t = (E *)a.alloc(sizeof(E) * (uint64_t)cap, 16);
-        if (!t) return false;
-        for (uint32_t i = 0; i < cap; ++i) t[i].used = 0;
-        return true;
-    }
-    OCB_HD int32_t find(const CKey &k) const {
-        uint32_t h = ckey_hash(k) & (cap - 1);
-        while (t[h].used) {
-            if (ckey_eq(t[h].k, k)) return (int32_t)t[h].v;
-            h = (h + 1) & (cap - 1);
-        }
-        return -1;
-    }
-    OCB_HD bool grow(Arena &a) {
-        Seen s2;
-        if (!s2.init(a, cap * 2)) return false;
-        for (uint32_t i = 0; i < cap; ++i)
-            if (t[i].used) s2.put_new(t[i].k, t[i].v);
-        *this = s2;
-        return true;
-    }
-    OCB_HD void put_new(const CKey &k, uint32_t v) {
-        uint32_t h = ckey_hash(k) & (cap - 1);
-        while (t[h].used) {
-            if (ckey_eq(t[h].k, k)) {
-                t[h].v = v;
-                return;
-            }
-            h = (h + 1) & (cap - 1);
-        }
-        t[h].k = k;
-        t[h].v = v;
-        t[h].used = 1;
-        n++;
-    }
-    OCB_HD bool put(Arena &a, const CKey &k, uint32_t v) {
-        if (2 * (n + 1) > cap && !grow(a)) return false;
-        put_new(k, v);
-        return true;
-    }
-    OCB_HD bool copy_from(Arena &a, const Seen &o) {
-        cap = o.cap;
-        n = o.n;
-        t = (E *)a.alloc(sizeof(E) * (uint64_t)cap, 16);
-        if (!t) return false;
-        for (uint32_t i = 0; i < cap; ++i) t[i] = o.t[i];
-        return true;
-    }
-};
 
 // ---------------------------------------------------------------------------
 // the optimizer of one kernel
@@ -760,7 +451,7 @@ struct Opt {
             if (np == 1 && p0 >= 0 && has_final[lab_ord(B(k->blocks[p0]).label)]) {
                 if (!seen.copy_from(tmp, final_seen[lab_ord(B(k->blocks[p0]).label)])) return eliminated;
             } else {
-                if (!seen.init(tmp, 64)) return eliminated;
+                if (!seen.init(tmp, 64, m.consts.p)) return eliminated;
             }
             auto in_rep = [&](uint32_t id) { return rstamp.get(id) == bi; };
             auto rep1 = [&](Opnd o) -> Opnd {  // single-step replacement
@@ -777,14 +468,13 @@ struct Opt {
                         if (++guard > 1000000) { unsup(); break; }
                     }
                     r.tag = 1;
-                    r.id = m.vals[v].id;
-                    r.c = PyVal{};
+                    r.x = m.vals[v].id;
                     return r;
                 }
                 r.tag = 0;
-                r.id = 0;
-                r.c = cv(o);
-                if (r.c.isf && r.c.f != r.c.f) unsup();
+                r.x = o.x;
+                const Const &c = m.consts[o.x];
+                if (c.pyfloat && c.f != c.f) unsup();
                 return r;
             };
             auto written = [&](uint32_t id) { return wstamp.get(id) == bi; };
@@ -817,12 +507,11 @@ struct Opt {
                         OKey lk = key(in.a), rk = key(in.b);
                         bool comm = in.op == BO_ADD || in.op == BO_MUL || in.op == BO_AND ||
                                     in.op == BO_OR || in.op == BO_XOR;
-                        if (comm && okey_gt(lk, rk)) { OKey t = lk; lk = rk; rk = t; }
+                        if (comm && okey_gt(lk, rk, m.consts.p)) { OKey t = lk; lk = rk; rk = t; }
                         ck.l = lk;
                         ck.r = rk;
                         ck.t1 = ty_strkey(dty(in));
                         ck.t2 = 0;
-                        ck.func = Str{nullptr, 0};
                         int32_t f = seen.find(ck);
                         if (f >= 0) {
                             add_rep(d, (uint32_t)f);
@@ -841,10 +530,9 @@ struct Opt {
                         ck.kind = 1;
                         ck.op = 0;
                         ck.l = key(in.a);
-                        ck.r = OKey{};
+                        ck.r = OKey{0, 0};
                         ck.t1 = ty_strkey(dty(in));
                         ck.t2 = ty_strkey(m.opty(in.a));
-                        ck.func = Str{nullptr, 0};
                         int32_t f = seen.find(ck);
                         if (f >= 0) {
                             add_rep(d, (uint32_t)f);
@@ -862,10 +550,10 @@ struct Opt {
                     if (!written(d) && gdc.get(d) < 2) {
                         OKey lk = key(in.a), rk = key(in.b);
                         uint8_t op = in.op;
-                        if ((op == CO_EQ || op == CO_NE) && okey_gt(lk, rk)) {
+                        if ((op == CO_EQ || op == CO_NE) && okey_gt(lk, rk, m.consts.p)) {
                             OKey t = lk; lk = rk; rk = t;
                         } else if ((op == CO_LT || op == CO_GT || op == CO_LE || op == CO_GE) &&
-                                   okey_gt(lk, rk)) {
+                                   okey_gt(lk, rk, m.consts.p)) {
                             OKey t = lk; lk = rk; rk = t;
                             op = op == CO_LT ? CO_GT : op == CO_GT ? CO_LT : op == CO_LE ? CO_GE : CO_LE;
                         }
@@ -875,7 +563,6 @@ struct Opt {
                         ck.l = lk;
                         ck.r = rk;
                         ck.t1 = ck.t2 = 0;
-                        ck.func = Str{nullptr, 0};
                         int32_t f = seen.find(ck);
                         if (f >= 0) {
                             add_rep(d, (uint32_t)f);
@@ -887,15 +574,15 @@ struct Opt {
                         }
                     }
                 } else if (in.kind == I_CALL) {
-                    if (in.dest >= 0 && is_pure_builtin(in.func)) {
+                    uint32_t pb = in.dest >= 0 ? pure_builtin_code(in.func) : 0;
+                    if (pb) {
                         uint32_t d = did(in);
                         if (!written(d) && gdc.get(d) < 2) {
                             CKey ck;
                             ck.kind = 3;
-                            ck.op = 0;
-                            ck.l = ck.r = OKey{};
+                            ck.op = (uint8_t)pb;
+                            ck.l = ck.r = OKey{0, 0};
                             ck.t1 = ck.t2 = 0;
-                            ck.func = in.func;
                             int32_t f = seen.find(ck);
                             if (f >= 0) {
                                 add_rep(d, (uint32_t)f);
@@ -966,11 +653,17 @@ struct Opt {
         }
         return eliminated;
     }
-    OCB_HD static bool is_pure_builtin(Str f) {
-        return eq(f, "threadIdx.x") || eq(f, "threadIdx.y") || eq(f, "threadIdx.z") ||
-               eq(f, "blockIdx.x") || eq(f, "blockIdx.y") || eq(f, "blockIdx.z") ||
-               eq(f, "blockDim.x") || eq(f, "blockDim.y") || eq(f, "blockDim.z") ||
-               eq(f, "gridDim.x") || eq(f, "gridDim.y") || eq(f, "gridDim.z");
+    // 1..12 for the builtins CSE treats as pure (optimize.py:555-575:
+    // thread/block index and dimension reads), 0 for any other call
+    OCB_HD static uint32_t pure_builtin_code(Str f) {
+        const char *names[12] = {"threadIdx.x", "threadIdx.y", "threadIdx.z",
+                                 "blockIdx.x",  "blockIdx.y",  "blockIdx.z",
+                                 "blockDim.x",  "blockDim.y",  "blockDim.z",
+                                 "gridDim.x",   "gridDim.y",   "gridDim.z"};
+        if (f.n < 10 || f.n > 11) return 0;
+        for (uint32_t i = 0; i < 12; ++i)
+            if (eq(f, names[i])) return i + 1;
+        return 0;
     }
 
     // ---- dead_block_elim (optimize.py:643-675) ---------------------------------
@@ -1694,24 +1387,43 @@ struct Opt {
         sat_seen = true;
         return true;
     }
-    // _resolve_const_value (unroll.py:21-45)
-    OCB_HD bool resolve_const_value(uint32_t id, pyint &out) {
+    // The constant operand a definition of _resolve_const_value's patterns
+    // reads (unroll.py:30-45), or onone(): CvtInst of a Const, or
+    // BinInst ADD of a Const and a zero Const (in that order of checks).
+    OCB_HD Opnd const_def_operand(const Inst &in) const {
+        if (in.kind == I_CVT && in.a.k == O_CONST) return in.a;
+        if (in.kind == I_BIN && in.op == BO_ADD) {
+            if (in.b.k == O_CONST && cis(in.b, 0)) {
+                if (in.a.k == O_CONST) return in.a;
+            } else if (in.a.k == O_CONST && cis(in.a, 0)) {
+                if (in.b.k == O_CONST) return in.b;
+            }
+        }
+        return onone();
+    }
+    // id -> index + 1 of the first instruction (block order) that defines the
+    // id with one of those patterns; built once per find_unrollable call, so
+    // each lookup is O(1) instead of a scan of the kernel
+    IdArr<uint32_t> const_def;
+    OCB_HD void build_const_defs() {
+        const_def.init(tmp, nid(), 0);
         for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
             Block &b = B(k->blocks[bi]);
             for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
                 const Inst &in = I(b.insts[ii]);
-                if (in.dest < 0 || did(in) != id) continue;
-                if (in.kind == I_CVT && in.a.k == O_CONST) return opnd_int(in.a, out);
-                if (in.kind == I_BIN && in.op == BO_ADD) {
-                    if (in.b.k == O_CONST && cis(in.b, 0)) {
-                        if (in.a.k == O_CONST) return opnd_int(in.a, out);
-                    } else if (in.a.k == O_CONST && cis(in.a, 0)) {
-                        if (in.b.k == O_CONST) return opnd_int(in.b, out);
-                    }
-                }
+                if (in.dest < 0) continue;
+                uint32_t d = did(in);
+                if (const_def.get(d) == 0 && const_def_operand(in).k == O_CONST)
+                    const_def.set(d, b.insts[ii] + 1);
             }
         }
-        return false;
+    }
+    // _resolve_const_value (unroll.py:21-45): the first definition of `id`
+    // that matches a pattern decides
+    OCB_HD bool resolve_const_value(uint32_t id, pyint &out) {
+        uint32_t ix = const_def.get(id);
+        if (!ix) return false;
+        return opnd_int(const_def_operand(I(ix - 1)), out);
     }
     OCB_HD void carried_put(Vec<Carried> &c, uint32_t cid, uint32_t cval, Opnd nval) {
         for (uint32_t i = 0; i < c.n; ++i)
@@ -1726,6 +1438,7 @@ struct Opt {
         out.init();
         LabelMap lm;
         lm.build(tmp, m, k->blocks);
+        build_const_defs();
         for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
             uint32_t cb = k->blocks[bi];
             sat_seen = false;
@@ -1928,42 +1641,61 @@ struct Opt {
         Vec<ULoop> loops;
         if (!find_unrollable(loops)) return 0;
         uint32_t count = 0;
+        // Id-indexed tables shared by every loop of this call, sized for the
+        // values all of them can add, filled once and told apart by stamps:
+        // remap entries by iteration (gen), carried remaps by loop, the
+        // iteration's new dests by iteration.
+        uint64_t cap64 = (uint64_t)nid() + 1024;
+        for (uint32_t li = 0; li < loops.n; ++li)
+            if (loops[li].trip <= (pyint)max_unroll)
+                cap64 += (uint64_t)loops[li].trip * (B(loops[li].body_b).insts.n + 2) + 8;
+        if (cap64 > 0x7FFFFFFFull) { unsup(); return 0; }
+        uint32_t cap = (uint32_t)cap64;
+        IdArr<uint32_t> st;     // iteration stamp of rm[id]
+        st.init(tmp, cap, 0xFFFFFFFFu);
+        Opnd *rm = (Opnd *)tmp.alloc(sizeof(Opnd) * (uint64_t)cap, 16);
+        IdArr<uint32_t> cstamp;  // loop stamp of cval[id]
+        cstamp.init(tmp, cap, 0xFFFFFFFFu);
+        uint32_t *cval = (uint32_t *)tmp.alloc(4ull * cap, 16);
+        IdArr<uint32_t> nstamp;  // iteration stamp of nval[id]
+        nstamp.init(tmp, cap, 0xFFFFFFFFu);
+        uint32_t *nval = (uint32_t *)tmp.alloc(4ull * cap, 16);
+        if (!rm || !cval || !nval || bad()) return 0;
+        uint32_t gen = 0;
         for (uint32_t li = 0; li < loops.n && !bad(); ++li) {
             ULoop &L = loops[li];
             if (L.trip > (pyint)max_unroll) continue;
-            // id-indexed remap: stamp per iteration
-            uint32_t cap = nid() + (uint32_t)L.trip * (B(L.body_b).insts.n + 2) + 8;
-            IdArr<uint32_t> st;
-            st.init(tmp, cap, 0xFFFFFFFFu);
-            Opnd *rm = (Opnd *)tmp.alloc(sizeof(Opnd) * (uint64_t)cap, 16);
-            IdArr<uint32_t> cst;  // carried_remap: id -> value index + 1
-            cst.init(tmp, cap, 0);
-            if (!rm || bad()) return count;
+            // carried_remap: id -> value index + 1 (0: none)
+            auto cst_get = [&](uint32_t id) -> uint32_t { return cstamp.get(id) == li ? cval[id] : 0u; };
+            auto cst_set = [&](uint32_t id, uint32_t v) {
+                if (!cstamp.set(id, li)) { unsup(); return; }
+                cval[id] = v;
+            };
             Vec<uint32_t> all;
             all.init();
             Ty ind_ty = m.vals[L.ind].ty;
             uint32_t ind_id = m.vals[L.ind].id;
             for (pyint it = 0; it < L.trip; ++it) {
                 uint32_t itn = (uint32_t)it;
+                const uint32_t g = gen++;
                 auto rset = [&](uint32_t id, Opnd o) {
-                    if (!st.set(id, itn)) { unsup(); return; }
+                    if (!st.set(id, g)) { unsup(); return; }
                     rm[id] = o;
                 };
                 // remap = dict(carried_remap)
                 for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
-                    uint32_t v = cst.get(L.carried[ci].cid);
+                    uint32_t v = cst_get(L.carried[ci].cid);
                     if (v) rset(L.carried[ci].cid, ov(v - 1));
                 }
                 rset(ind_id, cint(ind_ty, L.init + L.step * it));
                 for (uint32_t q = 0; q < L.sec.n; ++q)
                     rset(L.sec[q].cid, cint(m.vals[L.sec[q].cval].ty, L.sec[q].init + L.sec[q].step * it));
                 auto R = [&](Opnd o) -> Opnd {
-                    if (o.k == O_VAL && st.get(vid(o)) == itn) return rm[vid(o)];
+                    if (o.k == O_VAL && st.get(vid(o)) == g) return rm[vid(o)];
                     return o;
                 };
                 // iter_new_vals: body dest id -> new dest (value index + 1)
-                IdArr<uint32_t> inv_new;
-                inv_new.init(tmp, nid(), 0);
+                auto inv_get = [&](uint32_t id) -> uint32_t { return nstamp.get(id) == g ? nval[id] : 0u; };
                 Block &bb = B(L.body_b);
                 for (uint32_t ii = 0; ii < bb.insts.n; ++ii) {
                     const Inst in = I(bb.insts[ii]);
@@ -1999,18 +1731,19 @@ struct Opt {
                         uint32_t nd = new_value(nm, ov_.ty);
                         ni.dest = (int32_t)nd;
                         rset(ov_.id, ov(nd));
-                        if (!inv_new.set(ov_.id, nd + 1)) { unsup(); return count; }
+                        if (!nstamp.set(ov_.id, g)) { unsup(); return count; }
+                        nval[ov_.id] = nd + 1;
                     }
                     all.push(ar, add_inst(ni));
                 }
                 for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
-                    uint32_t v = inv_new.get(L.carried[ci].cid);
-                    if (v) cst.set(L.carried[ci].cid, v);
+                    uint32_t v = inv_get(L.carried[ci].cid);
+                    if (v) cst_set(L.carried[ci].cid, v);
                 }
                 if (bad()) return count;
             }
             for (uint32_t ci = 0; ci < L.carried.n; ++ci) {
-                uint32_t v = cst.get(L.carried[ci].cid);
+                uint32_t v = cst_get(L.carried[ci].cid);
                 if (!v) continue;
                 Ty cty = m.vals[L.carried[ci].cval].ty;
                 Opnd z = ty_is_float(cty) ? cflt(cty, 0.0) : cint(cty, 0);

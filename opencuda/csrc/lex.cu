@@ -4,8 +4,48 @@
 #include <thrust/iterator/reverse_iterator.h>
 #include "ocb_internal.h"
 #include "lex_kernels.cuh"
+#include "lex_fused.cuh"
 
 namespace ocb {
+
+// The single-pass lexer (lex_fused.cuh): token records without lines.
+static int lex_device_fused(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N,
+                            const uint64_t *d_tu_off, uint32_t n_tu, uint32_t *d_start,
+                            uint32_t *d_kindlen, uint64_t tok_cap, uint64_t *d_tu_tok_off,
+                            int32_t *d_status, uint64_t *d_n_tok, cudaStream_t st) {
+    using namespace lex;
+    uint64_t n_win = (N + WIN - 1) / WIN;
+    uint64_t n_tiles = (n_win + FT - 1) / FT;
+    // scratch: errkey[n_tu] | unsup[n_tu] | ticket, err | mstat[n_tiles] | cstat[n_tiles]
+    size_t a_err = (8 * (size_t)n_tu + 4 * (size_t)n_tu + 15) & ~(size_t)15;
+    size_t zero_bytes = 16 + 16 * (size_t)n_tiles;
+    OCB_TRY("lex: scratch", ctx->lex_scratch.ensure(a_err + zero_bytes));
+    uint8_t *base = ctx->lex_scratch.as<uint8_t>();
+    unsigned long long *errkey = (unsigned long long *)base;
+    uint32_t *unsup = (uint32_t *)(errkey + n_tu);
+    unsigned long long *ticket = (unsigned long long *)(base + a_err);
+    unsigned int *err = (unsigned int *)(ticket + 1);
+    unsigned long long *mstat = ticket + 2;
+    unsigned long long *cstat = mstat + n_tiles;
+    unsigned grid_tu = (n_tu + 255) / 256;
+    k_fill_u64<<<grid_tu, 256, 0, st>>>((uint64_t *)errkey, n_tu, ~0ull);
+    OCB_TRY("lex: memset", cudaMemsetAsync(unsup, 0, sizeof(uint32_t) * n_tu, st));
+    OCB_TRY("lex: memset", cudaMemsetAsync(ticket, 0, zero_bytes, st));
+    int dev = 0, n_sm = 0, per_sm = 0;
+    OCB_TRY("lex: device", cudaGetDevice(&dev));
+    OCB_TRY("lex: device", cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    OCB_TRY("lex: occupancy",
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_lex_fused, FT, 0));
+    if (per_sm < 1) per_sm = 1;
+    uint64_t grid = (uint64_t)n_sm * per_sm;
+    if (grid > n_tiles) grid = n_tiles;
+    LexOut o{d_start, d_kindlen, nullptr, tok_cap, d_tu_tok_off, errkey, unsup};
+    FusedArgs A{d_src, N, d_tu_off, n_tu, n_win, n_tiles, ticket, mstat, cstat, err, o, d_n_tok};
+    k_lex_fused<<<(unsigned)grid, FT, 0, st>>>(A);
+    k_lex_fused_finish<<<grid_tu, 256, 0, st>>>(n_tu, errkey, unsup, err, d_status);
+    OCB_TRY("lex: launch", cudaGetLastError());
+    return 0;
+}
 
 int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d_tu_off,
                uint32_t n_tu, uint32_t *d_start, uint32_t *d_kindlen, uint32_t *d_line,
@@ -25,6 +65,12 @@ int lex_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t N, const uint64_t *d
         OCB_TRY("lex: keyword table", cudaMemcpyToSymbol(g_kw, t, sizeof(t)));
         ctx->kw_ready = true;
     }
+    // Without per-token lines the single-pass kernel does the whole job
+    // (OCB_LEX_FUSED=0 selects the multi-pass pipeline, for comparisons).
+    const char *fv = getenv("OCB_LEX_FUSED");
+    if (!d_line && N > 0 && !(fv && *fv == '0'))
+        return lex_device_fused(ctx, d_src, N, d_tu_off, n_tu, d_start, d_kindlen, tok_cap,
+                                d_tu_tok_off, d_status, d_n_tok, st);
     uint64_t n_win = (N + WIN - 1) / WIN;
     // scratch layout
     uint64_t nw1 = n_win + 1;

@@ -141,3 +141,65 @@ def test_device_entry_point(ctx):
     assert np.array_equal(d_kl[:n].cpu().numpy().view(np.uint32), ref.kindlen)
     assert np.array_equal(d_line[:n].cpu().numpy().view(np.uint32), ref.line)
     assert np.array_equal(d_tto.cpu().numpy().view(np.uint64), ref.tu_tok_off)
+
+
+def _fused(ctx, buf, off):
+    """ocb_lex_device without the line array: the single-pass lexer."""
+    import torch
+    dev = torch.device("cuda:0")
+    n_tu = len(off) - 1
+    d_src = torch.from_numpy(np.ascontiguousarray(buf, np.uint8).copy() if len(buf)
+                             else np.zeros(16, np.uint8)).to(dev)
+    d_off = torch.from_numpy(np.asarray(off, np.uint64).view(np.int64).copy()).to(dev)
+    cap = len(buf) + n_tu + 1
+    d_start = torch.empty(cap, dtype=torch.int32, device=dev)
+    d_kl = torch.empty(cap, dtype=torch.int32, device=dev)
+    d_tto = torch.empty(n_tu + 1, dtype=torch.int64, device=dev)
+    d_status = torch.empty(max(n_tu, 1), dtype=torch.int32, device=dev)
+    d_n = torch.zeros(1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ctx.lex_device(d_src.data_ptr(), len(buf), d_off.data_ptr(), n_tu, d_start.data_ptr(),
+                   d_kl.data_ptr(), 0, cap, d_tto.data_ptr(), d_status.data_ptr(),
+                   d_n.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize()
+    n = int(d_n.item())
+    return (d_start[:n].cpu().numpy().view(np.uint32), d_kl[:n].cpu().numpy().view(np.uint32),
+            d_tto.cpu().numpy().view(np.uint64), d_status[:n_tu].cpu().numpy())
+
+
+def _edge_batches():
+    """TU layouts and texts the single-pass lexer's tiles must get right:
+    empty TUs at the start, middle and end, one-byte TUs, a comment and a
+    string far longer than a tile, runs of tokens with no whitespace (more
+    records than a thread buffers), unterminated comments and strings, hex
+    floats the reference rejects, CRLF text, and TUs cut mid-token."""
+    long_run = "+".join(f"v{i}" for i in range(6000))
+    yield ["", "", "a b", "", "x"]
+    yield ["x"] * 3000
+    yield ["", "/*" + "c" * 40000 + "*/ int a;", "", '"' + "s" * 30000 + '" b', ""]
+    yield [long_run, "y" + long_run, "// " + "q" * 20000 + "\nz = 1;"]
+    yield ["a /* open", '"open', "'x", "0x1.p4 0x.p1 0x1p99999 1.5e3f", "a\r\nb\r\n"]
+    yield ["int a;\n" * 3000, "\n" * 9000, " " * 9000 + "k"]
+    rnd = fuzz_sources(400, 21)
+    yield rnd
+    yield [s[: len(s) // 2] for s in rnd]
+
+
+def test_single_pass_equals_multi_pass(ctx):
+    """The single-pass lexer (no per-token lines) gives the same token
+    records, per-TU offsets and statuses as the multi-pass pipeline, which
+    the other tests pin to the oracle."""
+    batches = list(_edge_batches())
+    buf, off = synth.lexstress_batch(total_bytes=24 << 20, tu_bytes=16384, seed=17,
+                                     pool_lines=50_000)
+    big = [buf[int(off[i]):int(off[i + 1])].decode() for i in range(len(off) - 1)]
+    batches.append(big)
+    batches.append([synth.SGEMM_SRC] + synth.random_batch(300, seed=9) + [""])
+    for srcs in batches:
+        b, o = pack_sources(srcs)
+        ref = ctx.lex_batch(buf=b, tu_off=o)
+        st, kl, tto, status = _fused(ctx, b, o)
+        assert np.array_equal(status, ref.status)
+        assert np.array_equal(tto, ref.tu_tok_off)
+        assert np.array_equal(st, ref.start)
+        assert np.array_equal(kl, ref.kindlen)

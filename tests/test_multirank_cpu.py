@@ -59,8 +59,9 @@ def test_two_gloo_ranks_shard_and_reduce():
         assert p.exitcode == 0
     (r0, w0, p0, b0, t0, m0, n0), (r1, w1, p1, b1, t1, m1, n1) = out
     assert (r0, r1, w0, w1) == (0, 1, 2, 2)
-    for j in range(4):                    # every TU of a slice on exactly one rank
-        assert sorted(p0[j] + p1[j]) == list(range(j, 64, 4))
+    every = sorted(i for j in range(4) for i in p0[j] + p1[j])
+    assert every == list(range(64))       # every TU in one slice, on one rank
+    for j in range(4):
         assert not set(p0[j]) & set(p1[j])
     assert t0 == t1 == b0 + b1 == n0      # whole-job bytes
     assert abs(b0 - b1) < 0.25 * n0       # balanced by bytes
