@@ -561,6 +561,9 @@ def main():
         oo = d2h(torch, dev, d_oo, sh["n"] + 1, "<u8")
         st = d2h(torch, dev, d_st, sh["n"], "<i4")
         par.check(sh["idx"], data, oo, st, np.diff(sh["off"]))
+        if rank == 0:
+            print(f"step {k}: slice {j}, {sh['n']} TUs, {sh['bytes']} bytes, {t * 1e3:.1f} ms",
+                  file=sys.stderr, flush=True)
     clk = clocks.stop()
     ktimes = ctx.kernel_times()
     ctx.kernel_profile(False)
@@ -570,7 +573,7 @@ def main():
     value = ident / t_sum / 1e6
     parity = par.summary(world, dev)
     distinct = len({k % S for k in range(args.steps)})
-    per_rank_bytes = [int(sum(int(sizes[i]) for i in plan[j][r]) for j in range(S))
+    per_rank_bytes = [int(sum(int(sizes[i]) for j in range(S) for i in plan[j][r]))
                       for r in range(world)]
 
     # roofline of the dominant kernel: source + PTX bytes of the TUs it processed

@@ -136,6 +136,20 @@ int  ocb_parse_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
 int  ocb_optimize_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
                         uint32_t n_tu, ocb_text **out);
 
+/* Preprocess, lex, parse (and, with `optimized`, optimize) every TU, then
+ * check its IR with the reference's verifier.  Replaces
+ * opencuda/ir/verify_ir.py:302 verify_module(module, check_reachability)
+ * (verify_kernel :86-247, dominators of ir/dominator.py:44-112) applied to
+ * parse(source) or optimize(parse(source)).  Each TU's text: for every kernel
+ * with violations, in module order, a line `kernel <name>` and then one line
+ * per error string, in the reference's order and wording; empty when the IR
+ * is clean.  Status per TU as for ocb_parse_batch; OCB_TU_UNSUPPORTED also
+ * where two or more non-natural-loop errors of one back edge would come out
+ * in a Python set's order.  Free the result with ocb_text_free. */
+int  ocb_verify_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off,
+                      uint32_t n_tu, int optimized, int check_reachability,
+                      ocb_text **out);
+
 /* ---- compiler ------------------------------------------------------------ */
 /* Compile every TU of a host batch to PTX: preprocess, lex, parse, optimize,
  * allocate registers and emit.  Replaces the CLI path

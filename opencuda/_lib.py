@@ -41,6 +41,8 @@ SIGNATURES = [
     ("ocb_parse_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_optimize_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
     ("ocb_compile_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, P(c_void_p)]),
+    ("ocb_verify_batch", c_int, [c_void_p, c_void_p, c_void_p, c_u32, c_int, c_int,
+                                 P(c_void_p)]),
     ("ocb_compile_device", c_int, [c_void_p, c_void_p, c_u64, c_void_p, c_u32, c_int,
                                    P(c_void_p), P(c_u64), P(c_void_p), P(c_void_p)]),
     ("ocb_kernel_profile", c_int, [c_void_p, c_int]),

@@ -191,7 +191,16 @@ class Context:
         ``--emit-ptx`` output, ``__main__.py:36-85``)."""
         return self._text_call("ocb_compile_batch", srcs, buf, tu_off)
 
-    def _text_call(self, fn, srcs, buf, tu_off) -> TextBatch:
+    def verify_batch(self, srcs=None, *, buf=None, tu_off=None, optimized: bool = False,
+                     check_reachability: bool = True) -> TextBatch:
+        """Preprocess, lex, parse (and optionally optimize) every TU and check
+        its IR with the reference's verifier (``opencuda/ir/verify_ir.py:302``
+        ``verify_module``); each TU's text lists the violations per kernel
+        (empty when the IR is clean)."""
+        return self._text_call("ocb_verify_batch", srcs, buf, tu_off,
+                               1 if optimized else 0, 1 if check_reachability else 0)
+
+    def _text_call(self, fn, srcs, buf, tu_off, *extra) -> TextBatch:
         if srcs is not None:
             buf, tu_off = pack_sources(srcs)
         buf = np.ascontiguousarray(buf, dtype=np.uint8)
@@ -199,7 +208,7 @@ class Context:
         n_tu = len(tu_off) - 1
         out = ctypes.c_void_p()
         src_ptr = buf.ctypes.data if len(buf) else None
-        self._check(getattr(self.lib, fn)(self.h, src_ptr, tu_off.ctypes.data, n_tu,
+        self._check(getattr(self.lib, fn)(self.h, src_ptr, tu_off.ctypes.data, n_tu, *extra,
                                           ctypes.byref(out)), fn)
         try:
             n = ctypes.c_uint64()

@@ -334,6 +334,12 @@ int ocb_compile_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, 
     return stage_batch(ctx, src, tu_off, n_tu, 2, out);
 }
 
+int ocb_verify_batch(ocb_ctx *ctx, const uint8_t *src, const uint64_t *tu_off, uint32_t n_tu,
+                     int optimized, int check_reachability, ocb_text **out) {
+    return stage_batch(ctx, src, tu_off, n_tu, 3 + (optimized ? 1 : 0) + (check_reachability ? 2 : 0),
+                       out);
+}
+
 int ocb_compile_device(ocb_ctx *ctx, const uint8_t *d_src, uint64_t n_bytes,
                        const uint64_t *d_tu_off, uint32_t n_tu, int stage,
                        const uint8_t **d_out, uint64_t *out_bytes, const uint64_t **d_out_off,

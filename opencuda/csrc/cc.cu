@@ -14,6 +14,17 @@ namespace cc {
 cudaError_t launch_k_cc_parse(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
 cudaError_t launch_k_cc_opt(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
 cudaError_t launch_k_cc_emit(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
+cudaError_t launch_k_cc_verify(const CCArgs &A, int check_reach, unsigned grid, unsigned block,
+                               cudaStream_t st);
+
+// Stages beyond CC_STAGE_PTX: the IR verifier's error text after parse (3)
+// or after optimize (4); 5 and 6 are the same with check_reachability.
+enum { CC_STAGE_VERIFY_IR = 3, CC_STAGE_VERIFY_OPT = 4, CC_STAGE_VERIFY_IR_REACH = 5,
+       CC_STAGE_VERIFY_OPT_REACH = 6 };
+inline bool stage_runs_opt(int stage) {
+    return stage == CC_STAGE_OPT || stage == CC_STAGE_PTX || stage == CC_STAGE_VERIFY_OPT ||
+           stage == CC_STAGE_VERIFY_OPT_REACH;
+}
 
 __global__ void merge_status(int32_t *st, const int32_t *lex_st, uint32_t n_tu) {
     uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -101,7 +112,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     // optimizer's per-pass scratch near 650-1300 B/token (p50-p99); PTX text is
     // 11-16 B/token.  A TU beyond these reruns with every size times 8.
     uint64_t a0 = env_u64("OCB_CC_ARENA_BASE", 32768), a1 = env_u64("OCB_CC_ARENA_PER_TOKEN", 2400);
-    uint64_t o0 = 4096, o1 = env_u64("OCB_CC_OUT_PER_TOKEN", stage >= CC_STAGE_PTX ? 40 : 200);
+    uint64_t o0 = 4096, o1 = env_u64("OCB_CC_OUT_PER_TOKEN", stage == CC_STAGE_PTX ? 40 : 200);
     uint32_t ir_pm = (uint32_t)env_u64("OCB_CC_IR_PERMILLE", 400);
     uint32_t spread = (uint32_t)env_u64("OCB_CC_SPREAD", 1);
     if (spread < 1) spread = 1;
@@ -173,10 +184,14 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         OCB_TRY("cc: parse launch", launch_k_cc_parse(A, blocks, 128, st));
         if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[1], st));
         T.mark("cc: k_cc_parse");
-        if (stage >= CC_STAGE_OPT) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, blocks, 128, st));
+        if (stage_runs_opt(stage)) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, blocks, 128, st));
         if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[2], st));
         T.mark("cc: k_cc_opt");
-        OCB_TRY("cc: emit launch", launch_k_cc_emit(A, blocks, 128, st));
+        if (stage <= CC_STAGE_PTX)
+            OCB_TRY("cc: emit launch", launch_k_cc_emit(A, blocks, 128, st));
+        else
+            OCB_TRY("cc: verify launch",
+                    launch_k_cc_verify(A, stage >= CC_STAGE_VERIFY_IR_REACH, blocks, 128, st));
         if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[3], st));
         T.mark("cc: k_cc_emit");
         size_t t1 = 0;
@@ -189,7 +204,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         OCB_TRY("cc: sync", stream_wait(st));
         if (kp) {
             for (int k = 0; k < 3; ++k) {
-                if (k == 1 && stage < CC_STAGE_OPT) continue;
+                if (k == 1 && !stage_runs_opt(stage)) continue;
                 float ms = 0;
                 OCB_TRY("cc: event time", cudaEventElapsedTime(&ms, ctx->kev[k], ctx->kev[k + 1]));
                 ctx->kms[k] += ms;

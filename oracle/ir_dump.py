@@ -121,3 +121,15 @@ def dump_module(m) -> str:
     if m.device_functions or m.global_vars:
         parts.append("module-extras")
     return "\n".join(parts) + "\n"
+
+
+def verify_text(module, check_reachability: bool) -> str:
+    """verify_module(module, check_reachability) (opencuda/ir/verify_ir.py:302)
+    as text: per kernel with violations, `kernel <name>` then its error
+    strings, one per line -- the GPU verifier's output format."""
+    from opencuda.ir.verify_ir import verify_module
+    out = []
+    for name, errs in verify_module(module, check_reachability=check_reachability).items():
+        out.append(f"kernel {name}\n")
+        out.extend(e + "\n" for e in errs)
+    return "".join(out)

@@ -112,6 +112,21 @@ def _job(args):
         except Exception as e:  # noqa: BLE001
             res["error"] = [type(e).__name__, str(e)[:200], "parse"]
             return res
+    vkeys = [w for w in what if w.startswith("verify")]
+    if vkeys:
+        # verify_ir / verify_opt (+ "_reach": check_reachability=True)
+        from opencuda.frontend.parser import parse
+        from opencuda.ir.optimize import optimize
+        from oracle_ir_dump import verify_text
+        try:
+            for w in vkeys:
+                module = parse(pp)
+                if w.startswith("verify_opt"):
+                    module = optimize(module)
+                res[w] = verify_text(module, w.endswith("_reach"))
+        except Exception as e:  # noqa: BLE001
+            res["error"] = [type(e).__name__, str(e)[:200], "verify"]
+            return res
     if "ptx" in what:
         from opencuda.frontend.parser import parse
         from opencuda.ir.optimize import optimize
