@@ -261,6 +261,7 @@ class Parity:
         self.c = {"identical": 0, "reference_raises": 0, "unsupported": 0, "mismatched": 0}
         self.identical_bytes = 0
         self.first_mismatch = None
+        self.unsupported_tus = []   # (TU, golden status) of the first few
         self.pool = ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 4))
 
     def check(self, idx, data, out_off, status, src_lens):
@@ -276,6 +277,8 @@ class Parity:
             gs = int(self.gold["status"][i]) if self.gold is not None else None
             if st == api.TU_UNSUPPORTED:
                 v = "unsupported"
+                if len(self.unsupported_tus) < 32:
+                    self.unsupported_tus.append((int(i), gs))
             elif self.gold is None:
                 v = "identical" if st == 0 else "mismatched"
             elif st == 0 and gs == 0 and digs[j] == bytes(self.gold["digest"][i]):
@@ -296,6 +299,8 @@ class Parity:
                                   if self.gold is not None else "unchecked: no golden record")
         if self.first_mismatch is not None:
             out["first_mismatch_rank_local"] = self.first_mismatch
+        if self.unsupported_tus:
+            out["unsupported_tus_rank_local"] = self.unsupported_tus
         return out
 
 

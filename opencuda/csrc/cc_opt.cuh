@@ -471,10 +471,12 @@ struct Opt {
                     r.x = m.vals[v].id;
                     return r;
                 }
+                // A NaN constant: Python compares ('const', nan) keys by object
+                // identity (equal only to itself); the constant index plays the
+                // object's part (a propagated constant keeps its index, every
+                // fold makes a new one), and okey_eq compares indices first.
                 r.tag = 0;
                 r.x = o.x;
-                const Const &c = m.consts[o.x];
-                if (c.pyfloat && c.f != c.f) unsup();
                 return r;
             };
             auto written = [&](uint32_t id) { return wstamp.get(id) == bi; };
@@ -783,56 +785,105 @@ struct Opt {
     }
 
     // ---- dead_inst_elim (optimize.py:779-832) ----------------------------------
+    // The reference repeats rounds (mark every used id, drop the BinInst /
+    // CmpInst / CvtInst whose dest id is unused) until a round drops nothing.
+    // Dropping an instruction only ever removes uses, so the instructions that
+    // go are exactly those reached by repeatedly dropping one whose dest id has
+    // no remaining use: counted uses and a worklist give the same survivors,
+    // in the same order, and the same total count, in one pass.
     OCB_HD uint32_t dead_inst_elim() {
-        uint32_t eliminated = 0;
-        bool changed = true;
-        while (changed && !bad()) {
-            changed = false;
-            size_t mark = tmp.used;
-            IdArr<uint8_t> used;
-            used.init(tmp, nid(), 0);
-            if (bad()) return eliminated;
-            auto use = [&](Opnd o) {
-                if (o.k == O_VAL) used.set(vid(o), 1);
-            };
-            for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
-                Block &b = B(k->blocks[bi]);
-                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
-                    const Inst &in = I(b.insts[ii]);
-                    switch (in.kind) {
-                    case I_BIN:
-                    case I_CMP:
-                    case I_STORE:
-                        use(in.a);
-                        use(in.b);
-                        break;
-                    case I_CVT:
-                    case I_LOAD: use(in.a); break;
-                    default: break;
-                    }
-                    for (uint32_t q = 0; q < in.args.n; ++q) use(in.args[q]);
-                }
-                const Term &t = b.term;
-                if (t.kind == T_CBR || t.kind == T_RET) use(t.v);
+        uint32_t n0 = nid();
+        IdArr<uint32_t> uses;   // remaining uses per id
+        uses.init(tmp, n0, 0);
+        IdArr<uint32_t> ndefs;  // removable definitions per id (candidates)
+        ndefs.init(tmp, n0, 0);
+        if (bad()) return 0;
+        auto use = [&](Opnd o) {
+            if (o.k == O_VAL) {
+                uint32_t id = vid(o);
+                uses.set(id, uses.get(id) + 1);
             }
+        };
+        auto removable = [&](const Inst &in) {
+            return in.kind == I_BIN || in.kind == I_CMP || in.kind == I_CVT;
+        };
+        auto each_operand = [&](const Inst &in, auto f) {
+            switch (in.kind) {
+            case I_BIN:
+            case I_CMP:
+            case I_STORE:
+                f(in.a);
+                f(in.b);
+                break;
+            case I_CVT:
+            case I_LOAD: f(in.a); break;
+            default: break;
+            }
+            for (uint32_t q = 0; q < in.args.n; ++q) f(in.args[q]);
+        };
+        uint32_t total = 0;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            total += b.insts.n;
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                each_operand(in, use);
+                if (removable(in)) {
+                    uint32_t d = did(in);
+                    ndefs.set(d, ndefs.get(d) + 1);
+                }
+            }
+            const Term &t = b.term;
+            if (t.kind == T_CBR || t.kind == T_RET) use(t.v);
+        }
+        // dead[inst index] marks; the worklist holds ids whose uses reached 0
+        uint8_t *dead = (uint8_t *)tmp.alloc((uint64_t)m.insts.n + 1, 16);
+        uint32_t *work = (uint32_t *)tmp.alloc(4ull * (n0 + 1), 16);
+        // removable instructions grouped by dest id (CSR over ids)
+        uint32_t *start = (uint32_t *)tmp.alloc(4ull * (n0 + 2), 16);
+        uint32_t *list = (uint32_t *)tmp.alloc(4ull * (total + 1), 16);
+        if (!dead || !work || !start || !list || bad()) return 0;
+        for (uint32_t i = 0; i < m.insts.n; ++i) dead[i] = 0;
+        start[0] = 0;
+        for (uint32_t id = 0; id < n0; ++id) start[id + 1] = start[id] + ndefs.get(id);
+        for (uint32_t id = 0; id < n0; ++id) ndefs.set(id, start[id]);  // fill cursor
+        uint32_t nw = 0;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (!removable(in)) continue;
+                uint32_t d = did(in), c = ndefs.get(d);
+                list[c] = b.insts[ii];
+                ndefs.set(d, c + 1);
+            }
+        }
+        for (uint32_t id = 0; id < n0; ++id)
+            if (start[id + 1] > start[id] && uses.get(id) == 0) work[nw++] = id;
+        uint32_t eliminated = 0;
+        while (nw) {
+            uint32_t id = work[--nw];
+            for (uint32_t q = start[id]; q < start[id + 1]; ++q) {
+                uint32_t ix = list[q];
+                if (dead[ix]) continue;
+                dead[ix] = 1;
+                eliminated++;
+                each_operand(I(ix), [&](Opnd o) {
+                    if (o.k != O_VAL) return;
+                    uint32_t u = vid(o), c = uses.get(u);
+                    uses.set(u, c - 1);
+                    if (c == 1 && start[u + 1] > start[u]) work[nw++] = u;
+                });
+            }
+        }
+        if (eliminated)
             for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
                 Block &b = B(k->blocks[bi]);
                 uint32_t w = 0;
-                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
-                    uint32_t ix = b.insts[ii];
-                    const Inst &in = I(ix);
-                    if ((in.kind == I_BIN || in.kind == I_CMP || in.kind == I_CVT) &&
-                        !used.get(did(in))) {
-                        eliminated++;
-                        changed = true;
-                        continue;
-                    }
-                    b.insts[w++] = ix;
-                }
+                for (uint32_t ii = 0; ii < b.insts.n; ++ii)
+                    if (!dead[b.insts[ii]]) b.insts[w++] = b.insts[ii];
                 b.insts.n = w;
             }
-            tmp.used = mark;
-        }
         return eliminated;
     }
 
@@ -1799,8 +1850,11 @@ struct Opt {
         // rounds.  Every pass is a function of the IR's content (and the next
         // value id), so a round that leaves the content unchanged is a fixed
         // point: the remaining rounds cannot change anything and are skipped.
+        // The content before the first round counts too: when the first round
+        // leaves it unchanged, every later round repeats it.
         uint64_t fp_prev[2] = {0, 0};
-        bool have_fp = false;
+        fingerprint(fp_prev);
+        bool have_fp = true;
         for (int r = 0; r < 8 && !bad(); ++r) {
             uint32_t n = 0;
             n += OCB_PASS(unroll_loops(16));

@@ -85,63 +85,90 @@ __device__ __forceinline__ void lb_store(unsigned long long *p, uint64_t v) {
     *(volatile unsigned long long *)p = v;
 }
 
-// Waits (bounded) until tile j has published; returns its word (LB_ERR when
-// the wait gave up, after recording the error).
-__device__ __forceinline__ uint64_t lb_wait(unsigned long long *stat, uint64_t j,
-                                            unsigned int *err) {
-    uint64_t v;
+// Warp-wide look-back window: lane L holds the status word of tile
+// base - L (tiles before tile 0 read as an inclusive word with payload 0).
+// Re-reads until every lane up to the closest inclusive word has published;
+// returns that lane (32 when the window holds none).  Bounded: after
+// LB_SPIN_LIMIT polls it records the error and returns -1.
+__device__ __forceinline__ int lb_window(unsigned long long *stat, int64_t base, uint32_t lane,
+                                         unsigned int *err, uint64_t &v) {
     uint32_t spins = 0;
-    while (((v = lb_load(stat + j)) >> 62) == 0) {
+    for (;;) {
+        int64_t j = base - (int64_t)lane;
+        v = j >= 0 ? lb_load(stat + j) : LB_INC;
+        uint32_t f = (uint32_t)(v >> 62);
+        unsigned inc = __ballot_sync(0xFFFFFFFFu, f >= 2);   // inclusive or error
+        unsigned zero = __ballot_sync(0xFFFFFFFFu, f == 0);
+        int first = inc ? __ffs(inc) - 1 : 32;
+        unsigned need = first == 32 ? 0xFFFFFFFFu : ((2u << first) - 1u);
+        if (!(zero & need)) return first;
         if (++spins > LB_SPIN_LIMIT) {
-            atomicExch(err, 1u);
-            return LB_ERR;
+            if (lane == 0) atomicExch(err, 1u);
+            return -1;
         }
-        __nanosleep(32);
+        __nanosleep(64);
     }
-    return v;
 }
 
 // Mode state at the start of `tile` (whose own map is `agg`): publishes the
-// aggregate, looks back, publishes the inclusive end state.  One thread.
-__device__ uint32_t lookback_mode(const FusedArgs &A, uint64_t tile, uint32_t agg) {
+// aggregate, looks back 32 tiles at a time, publishes the inclusive end
+// state.  Called by all lanes of one warp.
+__device__ uint32_t lookback_mode(const FusedArgs &A, uint64_t tile, uint32_t agg,
+                                  uint32_t lane) {
     if (tile == 0) {
-        lb_store(A.mstat, LB_INC | pmap_apply(agg, S_CODE));
+        if (lane == 0) lb_store(A.mstat, LB_INC | pmap_apply(agg, S_CODE));
         return S_CODE;
     }
-    lb_store(A.mstat + tile, LB_AGG | agg);
-    __threadfence();
-    uint32_t acc = PMAP_IDENTITY;  // maps of tiles (j, tile) composed in order
+    if (lane == 0) lb_store(A.mstat + tile, LB_AGG | agg);
+    __syncwarp();
+    uint32_t acc = PMAP_IDENTITY;  // maps of the tiles after the inclusive one
     uint32_t s_in = S_CODE;
     bool bad = false;
-    for (uint64_t j = tile; j-- > 0;) {
-        uint64_t v = lb_wait(A.mstat, j, A.err);
-        uint64_t f = v & ~LB_PAY;
-        if (f == LB_ERR) { bad = true; break; }
-        if (f == LB_INC) { s_in = pmap_apply(acc, (uint32_t)(v & 7u)); break; }
-        acc = pmap_compose((uint32_t)(v & 0xFFFFFFu), acc);
+    for (int64_t base = (int64_t)tile - 1;; base -= 32) {
+        uint64_t v;
+        int first = lb_window(A.mstat, base, lane, A.err, v);
+        if (first < 0) { bad = true; break; }
+        // apply the window's maps, oldest first: lanes first-1 .. 0 (or 31 .. 0)
+        uint32_t win = PMAP_IDENTITY;
+        for (int L = (first == 32 ? 31 : first - 1); L >= 0; --L)
+            win = pmap_compose(win, (uint32_t)__shfl_sync(0xFFFFFFFFu, (uint32_t)(v & 0xFFFFFFu), L));
+        acc = pmap_compose(win, acc);
+        if (first < 32) {
+            uint64_t vf = __shfl_sync(0xFFFFFFFFu, v, first);
+            if ((vf >> 62) == 3) bad = true;
+            else s_in = pmap_apply(acc, (uint32_t)(vf & 7u));
+            break;
+        }
     }
-    lb_store(A.mstat + tile, bad ? LB_ERR : (LB_INC | pmap_apply(agg, s_in)));
+    if (lane == 0) lb_store(A.mstat + tile, bad ? LB_ERR : (LB_INC | pmap_apply(agg, s_in)));
     return s_in;
 }
 
-// First output index of `tile` (whose own count is `cnt`); one thread.
-__device__ uint64_t lookback_count(const FusedArgs &A, uint64_t tile, uint64_t cnt) {
+// First output index of `tile` (whose own count is `cnt`); all lanes of one
+// warp, 32 predecessors per probe.
+__device__ uint64_t lookback_count(const FusedArgs &A, uint64_t tile, uint64_t cnt, uint32_t lane) {
     if (tile == 0) {
-        lb_store(A.cstat, LB_INC | cnt);
+        if (lane == 0) lb_store(A.cstat, LB_INC | cnt);
         return 0;
     }
-    lb_store(A.cstat + tile, LB_AGG | cnt);
-    __threadfence();
+    if (lane == 0) lb_store(A.cstat + tile, LB_AGG | cnt);
+    __syncwarp();
     uint64_t acc = 0;
     bool bad = false;
-    for (uint64_t j = tile; j-- > 0;) {
-        uint64_t v = lb_wait(A.cstat, j, A.err);
-        uint64_t f = v & ~LB_PAY;
-        if (f == LB_ERR) { bad = true; break; }
-        acc += v & LB_PAY;
-        if (f == LB_INC) break;
+    for (int64_t base = (int64_t)tile - 1;; base -= 32) {
+        uint64_t v;
+        int first = lb_window(A.cstat, base, lane, A.err, v);
+        if (first < 0) { bad = true; break; }
+        uint64_t x = (first == 32 || (int)lane <= first) ? (v & LB_PAY) : 0;
+#pragma unroll
+        for (int d = 16; d >= 1; d >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, d);
+        acc += x;
+        if (first < 32) {
+            if ((__shfl_sync(0xFFFFFFFFu, v, first) >> 62) == 3) bad = true;
+            break;
+        }
     }
-    lb_store(A.cstat + tile, bad ? LB_ERR : (LB_INC | (acc + cnt)));
+    if (lane == 0) lb_store(A.cstat + tile, bad ? LB_ERR : (LB_INC | (acc + cnt)));
     return acc;
 }
 
@@ -289,7 +316,7 @@ __global__ void __launch_bounds__(FT, FMIN_BLOCKS) k_lex_fused(FusedArgs A) {
     __shared__ uint32_t s_wcnt[FT / 32 + 1];
     __shared__ uint32_t s_excl[FT + 1];
     __shared__ uint64_t s_tile, s_tile_off;
-    __shared__ uint32_t s_klo, s_khi, s_state_in;
+    __shared__ uint32_t s_klo, s_khi, s_state_in, s_agg;
     load_kw_packed(kwp, g_kw);
     load_dfa(T);
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -331,7 +358,12 @@ __global__ void __launch_bounds__(FT, FMIN_BLOCKS) k_lex_fused(FusedArgs A) {
         m = map_compose(wpre, m);                      // inclusive map of window tid
         uint64_t mx = __shfl_up_sync(0xFFFFFFFFu, m, 1);
         if (lane == 0) mx = wpre;                      // exclusive map
-        if (tid == FT - 1) s_state_in = lookback_mode(A, tile, map_pack(m));
+        if (tid == FT - 1) s_agg = map_pack(m);
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t si = lookback_mode(A, tile, s_agg, lane);
+            if (lane == 0) s_state_in = si;
+        }
         __syncthreads();
         const uint32_t s_in = s_state_in;
         uint32_t st0 = (uint32_t)((mx >> (8 * s_in)) & 0xFFu);   // mode at my window start
@@ -399,7 +431,11 @@ __global__ void __launch_bounds__(FT, FMIN_BLOCKS) k_lex_fused(FusedArgs A) {
         const uint32_t excl = s_wcnt[warp] + x - n;
         s_excl[tid] = excl;
         if (tid == FT - 1) s_excl[FT] = s_wcnt[FT / 32];
-        if (tid == 0) s_tile_off = lookback_count(A, tile, s_wcnt[FT / 32]);
+        __syncthreads();
+        if (warp == 0) {
+            uint64_t off = lookback_count(A, tile, s_wcnt[FT / 32], lane);
+            if (lane == 0) s_tile_off = off;
+        }
         __syncthreads();
         const uint64_t out0 = s_tile_off;
         // coalesced copy of the buffered records, warp by warp
