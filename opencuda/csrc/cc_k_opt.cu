@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(128, OCB_CC_MIN_BLOCKS) k_cc_opt(CCArgs A) {
     int32_t st = 0;
     if (S->ar.oom || S->tmp.oom) st = OCB_TU_OVERFLOW;
     else if (S->m.unsup) st = OCB_TU_UNSUPPORTED;
+    else if (S->m.raises) st = S->m.raises;
     S->status = st;
     A.status[i] = st;
 }

@@ -23,7 +23,8 @@ struct Opt {
 
     OCB_HD Opt(Module &mod, Arena &tmp_) : m(mod), ar(*mod.ar), tmp(tmp_), k(nullptr) {}
 
-    OCB_HD bool bad() const { return m.unsup || ar.oom || tmp.oom; }
+    // m.raises: a Python exception the reference raises inside optimize()
+    OCB_HD bool bad() const { return m.unsup || m.raises || ar.oom || tmp.oom; }
 #ifdef OCB_TRAP_UNSUP
     void unsup(int line = __builtin_LINE()) {
         fprintf(stderr, "opt unsupported at cc_opt.cuh:%d\n", line);
@@ -662,7 +663,7 @@ struct Opt {
                                  "blockIdx.x",  "blockIdx.y",  "blockIdx.z",
                                  "blockDim.x",  "blockDim.y",  "blockDim.z",
                                  "gridDim.x",   "gridDim.y",   "gridDim.z"};
-        if (f.n < 10 || f.n > 11) return 0;
+        if (f.n < 9 || f.n > 11) return 0;  // gridDim.x .. threadIdx.x
         for (uint32_t i = 0; i < 12; ++i)
             if (eq(f, names[i])) return i + 1;
         return 0;
@@ -1425,13 +1426,14 @@ struct Opt {
     // int(const.value) for the unroller's bound/init/step reads.  Floats
     // beyond the kept range saturate (they only ever fail the trip-count
     // checks); `sat_seen` records it so a loop that would still be unrolled
-    // with such a value is declined.  NaN/inf raise in the reference.
+    // with such a value is declined.  int() of NaN raises ValueError and of
+    // an infinity OverflowError (unroll.py:84-109), ending the compile.
     bool sat_seen = false;
     OCB_HD bool opnd_int(Opnd o, pyint &out) {
         PyVal v = cv(o);
         if (pv_to_int(v, out)) return true;
         if (!is_finite(v.f)) {
-            unsup();
+            m.raises = v.f != v.f ? 1 : 2;  // OCB_TU_RAISES_VALUEERROR / _OVERFLOW
             return false;
         }
         out = v.f > 0 ? PYINT_LIM : -PYINT_LIM;
