@@ -590,15 +590,41 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
         NameSet seen;
         seen.init();
         bool first = true;
+        // struct parameters flatten to one .param per leaf field named
+        // `<param>_<field>`; a name seen before is skipped (emit.py:975-989)
+        struct Leaf {
+            Str name;
+            Ty ty;
+            uint32_t f;    // next field to visit (struct frames)
+        };
+        Leaf stack[24];
         for (uint32_t i = 0; i < k->params.n; ++i) {
-            Str pn = k->params[i].name;
-            if (seen.has(pn)) continue;
-            seen.add(tmp, pn);
-            const char *t = ptx_type(k->params[i].ty);
-            if (cstr_eq(t, "f16")) t = "b16";
-            if (!first) pl.s(", ");
-            first = false;
-            pl.s(".param .").s(t).c(' ').s(pn);
+            uint32_t sp = 0;
+            stack[sp++] = Leaf{k->params[i].name, k->params[i].ty, 0};
+            while (sp) {
+                Leaf &top = stack[sp - 1];
+                if (ty_is_struct(top.ty)) {
+                    if (top.f >= m.nfields(top.ty)) {
+                        --sp;
+                        continue;
+                    }
+                    const SField &fd = m.field(top.ty, top.f++);
+                    if (sp >= 24) { unsup(); return false; }
+                    Str nm = cat(tmp, top.name, S("_"), fd.name);
+                    stack[sp++] = Leaf{nm, fd.ty, 0};
+                    continue;
+                }
+                Str pn = top.name;
+                Ty pty = top.ty;
+                --sp;
+                if (seen.has(pn)) continue;
+                seen.add(tmp, pn);
+                const char *t = ptx_type(pty);
+                if (cstr_eq(t, "f16")) t = "b16";
+                if (!first) pl.s(", ");
+                first = false;
+                pl.s(".param .").s(t).c(' ').s(pn);
+            }
         }
     }
     SB ve = sb();
@@ -622,20 +648,24 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
         const SharedDecl &d = k->shared[s];
         if (d.count == 0) {
             SB b = sb();
-            uint32_t al = is_ptr(d.ty) ? 4 : ty_size(d.ty);
+            uint32_t al = ty_is_scalar(d.ty) ? ty_size(d.ty) : 4;
             b.s(".extern .shared .align ").i(al).s(" .b8 ").s(d.name).s("[];");
             bool dup = false;
             for (uint32_t q = 0; q < preamble.n && !dup; ++q) dup = eq(preamble[q], b.str());
             if (!dup) preamble.push(ar, b.str());
         } else {
             SB b = sb();
-            b.s("    .shared .").s(ptx_type(d.ty)).c(' ').s(d.name).c('[').i(d.count).s("];");
+            if (ty_is_struct(d.ty))  // raw bytes with the fields' alignment
+                b.s("    .shared .align ").i(m.struct_align(d.ty)).s(" .b8 ").s(d.name).c('[')
+                    .i((pyint)m.tsize(d.ty) * d.count).s("];");
+            else
+                b.s("    .shared .").s(ptx_type(d.ty)).c(' ').s(d.name).c('[').i(d.count).s("];");
             out.push(ar, b.str());
         }
     }
     for (uint32_t q = 0; q < k->locals.n; ++q) {
         const LocalDecl &d = k->locals[q];
-        int64_t eb = ty_size(d.ty);
+        int64_t eb = m.tsize(d.ty);
         int64_t al = 1;
         while (al < eb) al <<= 1;
         if (al > 16) al = 16;
@@ -773,9 +803,14 @@ OCB_HD inline bool emit_module(Module &m, Arena &tmp, Out &o, const char *arch) 
             const GVar &g = m.gvars[q];
             SB b = E.sb();
             b.s(".visible .").s(g.space == AS_CONST ? "const" : "global").s(" .align ");
-            b.i(is_ptr(g.elem) ? 8 : (pyint)ty_size(g.elem)).s(" .").s(ptx_type(g.elem)).c(' ').s(g.name);
-            if (g.count > 1) b.c('[').i(g.count).c(']');
-            b.c(';');
+            if (ty_is_struct(g.elem)) {  // raw bytes for the whole struct (x count)
+                b.i(m.struct_align(g.elem)).s(" .b8 ").s(g.name).c('[')
+                    .i((pyint)m.tsize(g.elem) * g.count).s("];");
+            } else {
+                b.i(is_ptr(g.elem) ? 8 : (pyint)ty_size(g.elem)).s(" .").s(ptx_type(g.elem)).c(' ').s(g.name);
+                if (g.count > 1) b.c('[').i(g.count).c(']');
+                b.c(';');
+            }
             pre.push(*m.ar, b.str());
         }
         for (uint32_t q = 0; q < E.preamble.n; ++q) pre.push(*m.ar, E.preamble[q]);

@@ -247,7 +247,8 @@ OCB_HD inline Str utoa(Arena &a, uint64_t v) {
 typedef uint32_t Ty;
 enum : uint32_t {
     S_VOID = 0, S_BOOL, S_INT8, S_UINT8, S_INT16, S_UINT16, S_INT32, S_UINT32,
-    S_INT64, S_UINT64, S_FLOAT, S_DOUBLE, S_HALF
+    S_INT64, S_UINT64, S_FLOAT, S_DOUBLE, S_HALF,
+    S_STRUCT  // StructTy (ir/types.py:107-142): bits 16-31 index Module::structs
 };
 // AS_INT0: the integer 0 the reference stores as the space of an array
 // parameter's pointer (PtrTy(ty, 0)); it is none of the named spaces.
@@ -274,12 +275,19 @@ OCB_HD inline Ty ty_ptr(Ty pointee, uint32_t as, bool vol, bool &ok) {
 }
 OCB_HD inline Ty ty_pointee(Ty t) {
     uint32_t d = ty_depth(t);
-    if (d <= 1) return t & 15;
+    if (d <= 1) return t & (15u | 0xFFFF0000u);
     return (t & ~((3u << 4) | (7u << 6) | (1u << 10))) | (1u << 4) | (AS_GLOBAL << 6);
 }
+OCB_HD inline Ty ty_struct(uint32_t idx) { return S_STRUCT | (idx << 16); }
+OCB_HD inline bool ty_is_struct(Ty t) { return !is_ptr(t) && (t & 15) == S_STRUCT; }
+OCB_HD inline uint32_t ty_sidx(Ty t) { return t >> 16; }
+// a ScalarTy (not a pointer, not a struct)
+OCB_HD inline bool ty_is_scalar(Ty t) { return !is_ptr(t) && (t & 15) != S_STRUCT; }
+// size of a scalar or pointer type (a struct's size is Module::tsize)
 OCB_HD inline uint32_t ty_size(Ty t) {
     if (is_ptr(t)) return 8;
     switch (ty_scalar(t)) {
+    case S_STRUCT: return 0;
     case S_VOID: return 0;
     case S_BOOL: case S_INT8: case S_UINT8: return 1;
     case S_INT16: case S_UINT16: case S_HALF: return 2;
@@ -424,6 +432,18 @@ struct GVar {
     uint32_t space;
 };
 
+// A struct or union type (StructTy: name and ordered fields; a union is laid
+// out as a struct, as there).  Array members `T a[N]` are N fields a_0..a_N-1.
+struct SField {
+    Str name;
+    Ty ty;
+};
+struct StructDef {
+    Str name;
+    uint32_t f0, nf;  // fields: Module::sfields[f0, f0 + nf)
+    uint32_t size;    // StructTy.size
+};
+
 // All IR objects of one TU.
 struct Module {
     Arena *ar;
@@ -433,6 +453,8 @@ struct Module {
     Vec<Block> blocks;
     Vec<Kernel> kernels;
     Vec<GVar> gvars;          // in declaration order
+    Vec<StructDef> structs;   // every StructTy of the TU (Ty bits 16-31 index it)
+    Vec<SField> sfields;
     bool unsup;               // the engine cannot reproduce this TU
     int raises;               // reference exception (OCB_TU_RAISES_*) or 0
 
@@ -444,6 +466,8 @@ struct Module {
         blocks.init();
         kernels.init();
         gvars.init();
+        structs.init();
+        sfields.init();
         unsup = false;
         raises = 0;
         // Reserved up front so the tables are never empty-and-unallocated: a
@@ -454,6 +478,62 @@ struct Module {
         insts.reserve(*a, 64);
         blocks.reserve(*a, 16);
         kernels.reserve(*a, 4);
+    }
+    // Type.size of any type (StructTy.size for structs, types.py:113-124:
+    // each field aligned to its own size, no tail padding)
+    OCB_HD uint32_t tsize(Ty t) const {
+        if (ty_is_struct(t)) return structs[ty_sidx(t)].size;
+        return ty_size(t);
+    }
+    // a new StructTy from its fields; returns its type
+    OCB_HD Ty add_struct(Str name, const SField *f, uint32_t nf) {
+        StructDef d{name, sfields.n, nf, 0};
+        uint64_t total = 0;
+        for (uint32_t i = 0; i < nf; ++i) {
+            sfields.push(*ar, f[i]);
+            uint32_t sz = tsize(f[i].ty);
+            if (sz) total = (total + sz - 1) / sz * sz;
+            total += sz;
+        }
+        d.size = total > 0x7FFFFFFFu ? 0x7FFFFFFFu : (uint32_t)total;
+        if (total > 0x7FFFFFFFu) unsup = true;
+        structs.push(*ar, d);
+        return ty_struct(structs.n - 1);
+    }
+    // index of a field of struct type t, or -1 (KeyError in the reference)
+    OCB_HD int32_t field_index(Ty t, Str fname) const {
+        const StructDef &d = structs[ty_sidx(t)];
+        for (uint32_t i = 0; i < d.nf; ++i)
+            if (eq(sfields[d.f0 + i].name, fname)) return (int32_t)i;
+        return -1;
+    }
+    OCB_HD const SField &field(Ty t, uint32_t i) const { return sfields[structs[ty_sidx(t)].f0 + i]; }
+    // .align of a struct array in PTX: the largest field size (4 without
+    // fields) rounded up to a power of two, at most 16 (codegen/emit.py:1013-1022)
+    OCB_HD uint32_t struct_align(Ty t) const {
+        const StructDef &d = structs[ty_sidx(t)];
+        uint32_t mx = 0;
+        for (uint32_t i = 0; i < d.nf; ++i) {
+            uint32_t z = tsize(sfields[d.f0 + i].ty);
+            if (i == 0 || z > mx) mx = z;
+        }
+        if (!d.nf) mx = 4;
+        uint32_t sa = 1;
+        while (sa < mx && sa < 16) sa <<= 1;
+        return sa;
+    }
+    OCB_HD uint32_t nfields(Ty t) const { return structs[ty_sidx(t)].nf; }
+    // StructTy.field_offset (types.py:126-136) of field i
+    OCB_HD uint32_t field_offset(Ty t, uint32_t fi) const {
+        const StructDef &d = structs[ty_sidx(t)];
+        uint64_t off = 0;
+        for (uint32_t i = 0; i < d.nf; ++i) {
+            uint32_t sz = tsize(sfields[d.f0 + i].ty);
+            if (sz) off = (off + sz - 1) / sz * sz;
+            if (i == fi) break;
+            off += sz;
+        }
+        return (uint32_t)off;
     }
     OCB_HD uint32_t add_val(uint32_t id, Ty ty, Str name) {
         if (!vals.push(*ar, Value{id, ty, name}) && vals.n == 0) return 0;

@@ -132,7 +132,7 @@ namespace cc {
 
 enum : int { E_NONE = 0, E_PARSE = 1, E_OTHER = 2 };
 // Python exception types, reported as the TU status (OCB_TU_RAISES_*)
-enum : int { R_VALUE = 1, R_PARSE = 3, R_OTHER = 6 };
+enum : int { R_VALUE = 1, R_PARSE = 3, R_KEY = 4, R_OTHER = 6 };
 
 struct SharedInit {  // module-level __shared__ array (name, element type, count)
     Str name;
@@ -143,6 +143,27 @@ struct SharedInit {  // module-level __shared__ array (name, element type, count
 struct TypedefEnt {
     Str name;
     Ty ty;
+};
+
+// A struct name visible to the parser (_struct_types: the latest definition
+// of a name wins).
+struct StructName {
+    Str name;
+    Ty ty;
+};
+// Array members of the struct named `sname` (_struct_field_arrays): base
+// name -> element count, for the latest definition that had any.
+struct FieldArr {
+    Str sname, base;
+    uint32_t count;
+    uint32_t group;  // entries of one definition share a group number
+};
+// _inline_struct_return_fields: value id -> {field name -> operand}, kept in
+// insertion order per id (dict order decides later bindings).
+struct ISRF {
+    uint32_t vid;
+    Str fname;
+    Opnd v;
 };
 
 // A __device__ function kept as a token range and expanded at each call
@@ -179,6 +200,11 @@ struct Parser {
     NameSet shared_scalars;
     Vec<Str> break_targets, continue_targets;
     Vec<VarMap> break_snaps, continue_snaps;
+    Vec<StructName> snames;        // user struct/union definitions, in order
+    Ty vec_types[20];              // built-in vector StructTys, made on first use
+    Vec<FieldArr> farrs;
+    uint32_t farr_groups;
+    Vec<ISRF> isrf;
 
     OCB_HD Parser(Arena &a, Module &mod, Tokens t) : ar(a), m(mod), tk(t) {
         pos = 0;
@@ -204,6 +230,11 @@ struct Parser {
         continue_targets.init();
         break_snaps.init();
         continue_snaps.init();
+        snames.init();
+        for (int i = 0; i < 20; ++i) vec_types[i] = 0;
+        farrs.init();
+        farr_groups = 0;
+        isrf.init();
     }
 
     // ---- status ----------------------------------------------------------
@@ -435,7 +466,7 @@ struct Parser {
 
     // _scale_ptr_arith_offset (parser.py:237-254)
     OCB_HD Opnd scale_ptr_off(Ty ptr_ty, Opnd v) {
-        uint32_t es = ty_size(ty_pointee(ptr_ty));
+        uint32_t es = m.tsize(ty_pointee(ptr_ty));
         if (es == 1) return v;
         Ty it = (isval(v) || iscon(v)) ? tyof(v) : (Ty)S_INT32;
         if (iscon(v)) {
@@ -448,6 +479,34 @@ struct Parser {
         uint32_t s = new_val("ptr_off", it);
         emit_bin(s, BO_MUL, v, m.cint(it, es));
         return ov(s);
+    }
+
+    // int(const.value) of an array dimension (1 for a non-constant); float
+    // dimensions are outside the subset
+    OCB_HD bool const_dim_of(Opnd o, int64_t &out) {
+        if (o.k != O_CONST) {
+            out = 1;
+            return true;
+        }
+        const Const &c = m.consts[o.x];
+        if (c.pyfloat || c.i > INT64_MAX / 2 || c.i < INT64_MIN / 2) {
+            unsup();
+            return false;
+        }
+        out = (int64_t)c.i;
+        return true;
+    }
+    // int(const.value) % n (Python modulo, n > 0)
+    OCB_HD bool const_mod(Opnd o, uint32_t n, int64_t &k) {
+        const Const &c = m.consts[o.x];
+        if (c.pyfloat) {
+            unsup();
+            return false;
+        }
+        pyint r = c.i % (pyint)n;
+        if (r < 0) r += n;
+        k = (int64_t)r;
+        return true;
     }
 
     // _loop_writeback (parser.py:256-364)
@@ -478,12 +537,21 @@ struct Parser {
         Vec<P> pending, ordered;
         pending.init();
         ordered.init();
+        // pass 1: struct sentinels get their entry binding back, nothing emitted
+        for (uint32_t i = 0; i < entry.e.n; ++i) {
+            const VarEnt &en = entry.e[i];
+            if (!en.live || en.v.k != O_VAL || !ty_is_struct(m.vals[en.v.x].ty)) continue;
+            Opnd *c = vars.get(en.name);
+            if (!c || c->k != O_VAL || c->x != en.v.x) vars.set(ar, en.name, en.v);
+        }
         for (uint32_t i = 0; i < entry.e.n; ++i) {
             const VarEnt &en = entry.e[i];
             if (!en.live || en.v.k != O_VAL) continue;
+            if (ty_is_struct(m.vals[en.v.x].ty)) continue;
             Opnd *c = vars.get(en.name);
             if (!c) continue;
             if (c->k == O_VAL && c->x == en.v.x) continue;  // `is`
+            if (c->k == O_VAL && ty_is_struct(m.vals[c->x].ty)) continue;
             if (c->k == O_VAL || c->k == O_CONST) pending.push(ar, P{en.name, en.v.x, *c});
         }
         // sequence the copies so no copy clobbers another's source
@@ -555,6 +623,70 @@ struct Parser {
         return false;
     }
     OCB_HD void add_typedef(Str v, Ty t) { user_typedefs.push(ar, TypedefEnt{v, t}); }
+    // ---- structs (cc_parse_struct.cuh) ----
+    OCB_HD OCB_NI bool vector_type(Str v, Ty &t);
+    OCB_HD bool user_struct(Str v, Ty &t) const {
+        for (uint32_t i = snames.n; i-- > 0;)
+            if (eq(snames[i].name, v)) {
+                t = snames[i].ty;
+                return true;
+            }
+        return false;
+    }
+    // name in self._struct_types (user definitions, then the vector types)
+    OCB_HD bool find_struct(Str v, Ty &t) { return user_struct(v, t) || vector_type(v, t); }
+    // name in self._typedefs or name in self._struct_types
+    OCB_HD bool is_type_name(Str v);
+    OCB_HD OCB_NI bool parse_struct_def(Ty &out);
+    // _struct_field_arrays.get(sty.name, {}).get(member): element count or 0
+    OCB_HD uint32_t field_array(Ty st, Str member);
+    OCB_HD bool isstruct(Opnd o) { return o.k == O_VAL && ty_is_struct(tyof(o)); }
+    OCB_HD bool isptr_struct(Opnd o) {
+        return o.k == O_VAL && is_ptr(tyof(o)) && ty_is_struct(ty_pointee(tyof(o)));
+    }
+    // ScalarTy instance test (not a pointer, not a struct)
+    OCB_HD static bool is_scalar_ty(Ty t) { return !is_ptr(t) && !ty_is_struct(t); }
+    OCB_HD int32_t isrf_find(uint32_t vid, Str f) const {
+        for (uint32_t i = 0; i < isrf.n; ++i)
+            if (isrf[i].vid == vid && eq(isrf[i].fname, f)) return (int32_t)i;
+        return -1;
+    }
+    OCB_HD bool isrf_has(uint32_t vid) const {
+        for (uint32_t i = 0; i < isrf.n; ++i)
+            if (isrf[i].vid == vid) return true;
+        return false;
+    }
+    OCB_HD void isrf_set(uint32_t vid, Str f, Opnd v) {
+        int32_t i = isrf_find(vid, f);
+        if (i >= 0) isrf[i].v = v;
+        else isrf.push(ar, ISRF{vid, f, v});
+    }
+    // the field's value of a struct value: the per-field map of its id, else
+    // the variable `<name>_<field>` (or onone())
+    OCB_HD Opnd struct_field_src(uint32_t sval, Str f) {
+        int32_t i = isrf_find(m.vals[sval].id, f);
+        if (i >= 0) return isrf[i].v;
+        Opnd *o = vars.get(cat(ar, m.vals[sval].name, S("_"), f));
+        return o ? *o : onone();
+    }
+    // field index of `member` in struct type st, raising KeyError when absent
+    OCB_HD int32_t field_or_raise(Ty st, Str member) {
+        int32_t fi = m.field_index(st, member);
+        if (fi < 0) raise_(R_KEY);
+        return fi;
+    }
+    OCB_HD OCB_NI void zero_init_fields(Str prefix, Ty st);
+    OCB_HD OCB_NI void load_struct_fields(Opnd base, Ty st, Str prefix, uint32_t abs_off,
+                                          uint32_t as, bool ptr_fields, bool declare_nested);
+    OCB_HD OCB_NI void copy_struct_fields(uint32_t rhs, Str update_name);
+    OCB_HD OCB_NI Opnd member_of_ptr(Opnd lhs, Str member);
+    OCB_HD OCB_NI Opnd member_of_struct(Opnd lhs, Str member, Str &src_name);
+    OCB_HD OCB_NI Opnd parse_compound_literal(Ty st);
+    OCB_HD OCB_NI Opnd field_addr(Opnd addr, Str member);
+    OCB_HD OCB_NI Opnd field_chain(Opnd addr, Ty cur_ty, uint32_t as);
+    OCB_HD OCB_NI Opnd member_lvalue(Opnd var);
+    OCB_HD OCB_NI void flat_struct_params(Str prefix, Ty st, uint32_t slot, NameSet &seen,
+                                          uint32_t &next);
     OCB_HD OCB_NI Opnd spill_scalar(Str name, Opnd value);
     OCB_HD OCB_NI void parse_device_func();
     OCB_HD OCB_NI Opnd inline_call(uint32_t fi, Vec<Opnd> &args, Str name);

@@ -26,15 +26,6 @@ OCB_HD inline bool typedef_scalar(Str v, Ty &t) {
     if (eq(v, "uint8_t") || eq(v, "uint16_t") || eq(v, "uint32_t")) { t = S_UINT32; return true; }
     return false;
 }
-// CUDA vector types registered as structs (parser.py:98-128)
-OCB_HD inline bool vector_type_name(Str v) {
-    const char *n[] = {"float2", "float3", "float4", "double2", "int2", "int3", "int4",
-                       "uint2", "uint3", "uint4", "short2", "ushort2", "char2", "uchar2",
-                       "char4", "uchar4", "long2", "ulong2", "longlong2", "ulonglong2"};
-    for (auto s : n)
-        if (eq(v, s)) return true;
-    return false;
-}
 
 
 // _parse_type (parser.py:368-472)
@@ -95,8 +86,16 @@ OCB_HD inline bool Parser::parse_type(Ty &out) {
     case TK_BOOL: advance(); out = S_INT32; return true;
     default: break;
     }
-    if (k == TK_STRUCT || k == TK_UNION) {
-        unsup();  // struct types are outside the subset
+    if (k == TK_STRUCT || k == TK_UNION) {  // a defined struct or union
+        advance();
+        if (!at(TK_IDENT)) {
+            perr();
+            return false;
+        }
+        Str sn = peekv();
+        advance();
+        if (find_struct(sn, out)) return true;
+        perr();
         return false;
     }
     if (k == TK_ENUM) {
@@ -108,14 +107,11 @@ OCB_HD inline bool Parser::parse_type(Ty &out) {
     if (k == TK_IDENT) {
         Str v = peekv();
         Ty t;
-        if (user_typedef(v, t) || typedef_scalar(v, t)) {
+        if (user_typedef(v, t) || typedef_scalar(v, t) || vector_type(v, t) ||
+            user_struct(v, t)) {  // _typedefs, then a bare struct name
             advance();
             out = t;
             return true;
-        }
-        if (vector_type_name(v)) {
-            unsup();
-            return false;
         }
         if (v.n <= 2 && py_isupper(v)) {
             advance();
@@ -166,7 +162,18 @@ OCB_HD inline Opnd Parser::parse_assign_expr() {
     if (at(TK_IDENT)) {
         Str cand = peekv();
         uint32_t np = pos + 1;
-        if (np < tk.n && is_assign_op(kind_at(np)) && vars.has(cand)) lhs_orig = cand;
+        if (np < tk.n && is_assign_op(kind_at(np)) && vars.has(cand)) {
+            lhs_orig = cand;
+        } else if (np < tk.n && kind_at(np) == TK_DOT && vars.has(cand) &&
+                   isstruct(*vars.get(cand))) {
+            // struct.field = val: the per-field variable is the target
+            uint32_t fp = np + 1;
+            if (fp < tk.n && kind_at(fp) == TK_IDENT && fp + 1 < tk.n &&
+                is_assign_op(kind_at(fp + 1))) {
+                Str cn = cat(ar, cand, S("_"), val_at(fp));
+                if (vars.has(cn)) lhs_orig = cn;
+            }
+        }
     }
     Opnd lhs = parse_or_expr();
     Opnd result = lhs;
@@ -203,11 +210,11 @@ OCB_HD inline Opnd Parser::parse_assign_expr() {
             }
             Ty pt = ty_pointee(tyof(lhs));
             Ty rt = tyof(rhs);
-            if (isval(rhs) && !is_ptr(rt) && !is_ptr(pt) && rt != pt) {
+            if (isval(rhs) && is_scalar_ty(rt) && is_scalar_ty(pt) && rt != pt) {
                 uint32_t co = new_val("coerce", pt);
                 emit_cvt(co, rhs);
                 rhs = ov(co);
-            } else if (iscon(rhs) && !is_ptr(pt) && !is_ptr(rt) && rt != pt && !ty_is_float(rt) &&
+            } else if (iscon(rhs) && is_scalar_ty(pt) && !is_ptr(rt) && rt != pt && !ty_is_float(rt) &&
                        !ty_is_float(pt)) {
                 Const c = m.consts[rhs.x];
                 c.ty = pt;
@@ -221,8 +228,8 @@ OCB_HD inline Opnd Parser::parse_assign_expr() {
         Str un = lhs_orig.p ? lhs_orig : (isval(lhs) ? vname(lhs) : Str{nullptr, 0});
         if (un.p && vars.has(un)) {
             Opnd prev = *vars.get(un);
-            if (prev.k == O_VAL && !is_ptr(tyof(prev)) && (rhs.k == O_VAL || rhs.k == O_CONST) &&
-                !is_ptr(tyof(rhs))) {
+            if (prev.k == O_VAL && is_scalar_ty(tyof(prev)) && (rhs.k == O_VAL || rhs.k == O_CONST) &&
+                is_scalar_ty(tyof(rhs))) {
                 if (iscon(rhs) || (isval(rhs) && !eq(vname(rhs), un))) {
                     Ty pt = tyof(prev);
                     uint32_t mat = new_val(un, pt);
@@ -231,6 +238,7 @@ OCB_HD inline Opnd Parser::parse_assign_expr() {
                 }
             }
             vars.set(ar, un, rhs);
+            if (isstruct(rhs)) copy_struct_fields(rhs.x, un);
         }
         result = rhs;
         goto out;
@@ -501,7 +509,7 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
                     Opnd index = parse_expr();
                     if (bad() || !expect(TK_RBRACKET)) { --nest; return onone(); }
                     Ty gp = m.gvars[gi].ptr;
-                    uint32_t es = ty_size(ty_pointee(gp));
+                    uint32_t es = m.tsize(ty_pointee(gp));
                     if (es != 1) {
                         Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
                         uint32_t sc = new_val("scale", it);
@@ -510,7 +518,7 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
                     }
                     uint32_t ea = new_val("elem_addr", gp);
                     emit_bin(ea, BO_ADD, addr, index);
-                    addr = ov(ea);
+                    addr = field_chain(ov(ea), ty_pointee(gp), ty_as(gp));  // &g[i].f
                 }
                 --nest;
                 return addr;
@@ -524,7 +532,7 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
                     if (match(TK_LBRACKET)) {
                         Opnd index = parse_expr();
                         if (bad() || !expect(TK_RBRACKET)) goto out;
-                        uint32_t es = ty_size(ty_pointee(vt));
+                        uint32_t es = m.tsize(ty_pointee(vt));
                         if (es != 1) {
                             Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
                             uint32_t s = new_val("scale", it);
@@ -533,13 +541,70 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
                         }
                         uint32_t a = new_val("addr", vt);
                         emit_bin(a, BO_ADD, var, index);
-                        r = ov(a);
+                        r = field_chain(ov(a), ty_pointee(vt), ty_as(vt));  // &a[i].f.g
                         goto out;
                     }
                     if (at(TK_ARROW) || at(TK_DOT)) {
                         pos -= 1;  // fall through to the generic handler
                     } else {
                         r = var;
+                        goto out;
+                    }
+                } else if (ty_is_struct(vt)) {  // &s / &s.f[i] (parser.py:1074-1151)
+                    uint32_t nk = pos + 1 < tk.n ? kind_at(pos + 1) : TK_EOF;
+                    bool member = nk == TK_DOT || nk == TK_ARROW;
+                    if (nk == TK_DOT && pos + 3 < tk.n && kind_at(pos + 2) == TK_IDENT &&
+                        kind_at(pos + 3) == TK_LBRACKET) {
+                        Opnd *fl = vars.get(cat(ar, name, S("_"), val_at(pos + 2)));
+                        if (fl && fl->k == O_VAL && is_ptr(tyof(*fl))) {
+                            Opnd flat = *fl;
+                            pos += 4;
+                            Opnd index = parse_expr();
+                            if (bad() || !expect(TK_RBRACKET)) goto out;
+                            uint32_t es = m.tsize(ty_pointee(tyof(flat)));
+                            if (es != 1) {
+                                Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
+                                uint32_t sc = new_val("scale", it);
+                                emit_bin(sc, BO_MUL, index, m.cint(it, es));
+                                index = ov(sc);
+                            }
+                            uint32_t a = new_val("addr", tyof(flat));
+                            emit_bin(a, BO_ADD, flat, index);
+                            r = ov(a);
+                            goto out;
+                        }
+                    }
+                    if (!member) {  // the struct spilled field by field to a .local slot
+                        advance();
+                        Str sn = cat(ar, S("_spill_"), name);
+                        Opnd *sp = vars.get(sn);
+                        Opnd slot;
+                        if (sp) {
+                            slot = *sp;
+                        } else {
+                            bool ok = true;
+                            Ty lt = ty_ptr(vt, AS_LOCAL, false, ok);
+                            if (!ok) { unsup(); goto out; }
+                            uint32_t v = new_val(sn, lt);
+                            slot = ov(v);
+                            vars.set(ar, sn, slot);
+                            kern->locals.push(ar, LocalDecl{sn, vt, 1, v});
+                        }
+                        uint32_t nf = m.nfields(vt);
+                        for (uint32_t q = 0; q < nf && !bad(); ++q) {
+                            SField fd = m.field(vt, q);
+                            if (ty_is_struct(fd.ty)) continue;
+                            Opnd *fv = vars.get(cat(ar, name, S("_"), fd.name));
+                            if (!fv) continue;
+                            Opnd fval = *fv;
+                            bool ok = true;
+                            Ty fp = ty_ptr(fd.ty, AS_LOCAL, false, ok);
+                            if (!ok) { unsup(); goto out; }
+                            uint32_t fa = new_val("faddr", fp);
+                            emit_bin(fa, BO_ADD, slot, m.cint(S_INT32, m.field_offset(vt, q)));
+                            emit_store(ov(fa), fval);
+                        }
+                        r = slot;
                         goto out;
                     }
                 } else {  // &scalar: spilled to a one-element .local slot
@@ -553,7 +618,7 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
             Opnd o = parse_unary_expr();
             if (bad()) goto out;
             if (o.k == O_VAL && is_ptr(tyof(o))) { r = o; goto out; }
-            if (o.k == O_VAL && kern) {  // &expr of a scalar value: spilled too
+            if (o.k == O_VAL && is_scalar_ty(tyof(o)) && kern) {  // &expr of a scalar: spilled too
                 r = spill_scalar(vname(o), o);
                 goto out;
             }
@@ -579,13 +644,13 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
         Ty st;
         int64_t size;
         if (parse_type_with_ptr(st)) {
-            size = ty_size(st);
+            size = m.tsize(st);
         } else {
             if (!catch_any()) goto out;
             pos = saved;
             Opnd e = parse_expr();
             if (bad()) goto out;
-            size = ty_size((isval(e) || iscon(e)) ? tyof(e) : (Ty)S_INT32);
+            size = m.tsize((isval(e) || iscon(e)) ? tyof(e) : (Ty)S_INT32);
         }
         if (!expect(TK_RPAREN)) goto out;
         r = m.cint(S_INT32, size);
@@ -663,6 +728,7 @@ OCB_HD inline Opnd Parser::parse_unary_expr() {
         }
         if (ok && expect(TK_RPAREN)) {
             Opnd o = parse_unary_expr();
+            if (!bad() && ty_is_struct(ct)) { unsup(); goto out; }  // CvtInst to a struct
             if (!bad()) {
                 if (is_ptr(ct) && o.k == O_VAL && is_ptr(tyof(o)) && ty_as(tyof(o)) != AS_GLOBAL) {
                     bool pok = true;
@@ -721,7 +787,7 @@ OCB_HD inline Opnd Parser::parse_postfix_expr() {
                     continue;
                 }
                 Ty pt = ty_pointee(lt);
-                uint32_t es = ty_size(pt);
+                uint32_t es = m.tsize(pt);
                 if (es != 1) {
                     Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
                     uint32_t s = new_val("scale", it);
@@ -730,7 +796,7 @@ OCB_HD inline Opnd Parser::parse_postfix_expr() {
                 }
                 uint32_t a = new_val("addr", lt);
                 emit_bin(a, BO_ADD, lhs, index);
-                if (is_assign_op(peek())) {
+                if (ty_is_struct(pt) || is_assign_op(peek())) {  // struct element: an address
                     lhs = ov(a);
                 } else {
                     uint32_t d = new_val("elem", pt);
@@ -754,13 +820,19 @@ OCB_HD inline Opnd Parser::parse_postfix_expr() {
                     c.func = bi;
                     emit(c);
                     lhs = ov(d);
+                } else if (isstruct(lhs)) {
+                    lhs = member_of_struct(lhs, member, src_name);
+                } else if (isptr_struct(lhs)) {
+                    lhs = member_of_ptr(lhs, member);
                 }
             }
             continue;
         }
         if (match(TK_ARROW)) {
             if (!at(TK_IDENT)) { perr(); return lhs; }
+            Str member = peekv();
             advance();
+            if (isptr_struct(lhs)) lhs = member_of_ptr(lhs, member);
             continue;
         }
         break;
@@ -1171,6 +1243,10 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
             Opnd var = *vp;
             if (shared_scalars.has(name) && var.k == O_VAL && is_ptr(tyof(var)) &&
                 !at(TK_LBRACKET) && !at(TK_DOT)) {
+                if (ty_is_struct(ty_pointee(tyof(var)))) {  // a whole-struct load
+                    unsup();
+                    return onone();
+                }
                 uint32_t d = new_val(name, ty_pointee(tyof(var)));
                 emit_load(d, var);
                 return ov(d);
@@ -1182,7 +1258,7 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
             // module variable (parser.py:2164-2185): its address before '[' and
             // for a non-scalar, else a load of the scalar through the symbol
             uint32_t gi = g->x;
-            if (at(TK_LBRACKET) || is_ptr(m.gvars[gi].elem)) return gaddr(gi);
+            if (at(TK_LBRACKET) || !is_scalar_ty(m.gvars[gi].elem)) return gaddr(gi);
             uint32_t d = new_val(m.gvars[gi].name, m.gvars[gi].elem);
             emit_load(d, Opnd{O_SYM, gi});
             return ov(d);
@@ -1212,18 +1288,15 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
                           pk == TK_LONG || pk == TK_SIGNED || pk == TK_UNSIGNED ||
                           pk == TK_STRUCT || pk == TK_UNION || pk == TK_ENUM || pk == TK_CONST ||
                           pk == TK_VOLATILE;
-        if (!type_ahead && pk == TK_IDENT) {
-            Ty t;
-            if (user_typedef(peekv(), t) || typedef_scalar(peekv(), t) ||
-                vector_type_name(peekv()))
-                type_ahead = true;
-        }
+        if (!type_ahead && pk == TK_IDENT && is_type_name(peekv())) type_ahead = true;
         if (type_ahead) {
             uint32_t saved = pos;
             Ty ct;
             bool ok = parse_type_with_ptr(ct);
             if (ok && at(TK_RPAREN)) {
                 advance();
+                if (at(TK_LBRACE) && ty_is_struct(ct)) return parse_compound_literal(ct);
+                if (ty_is_struct(ct)) { unsup(); return onone(); }  // CvtInst to a struct
                 Opnd o = parse_unary_expr();
                 if (!bad()) {
                     uint32_t d = new_val("cast", ct);

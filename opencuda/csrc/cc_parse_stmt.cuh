@@ -2,7 +2,7 @@
 // _parse_lvalue_or_expr, _parse_stmt_or_block), :3701-3874 (_parse_kernel)
 // and :4194-4443 (parse_module), restated for the supported subset.
 #pragma once
-#include "cc_parse_expr.cuh"
+#include "cc_parse_struct.cuh"
 
 namespace ocb {
 namespace cc {
@@ -80,7 +80,7 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                         Opnd col = parse_expr();
                         if (bad() || !expect(TK_RBRACKET)) return onone();
                         Ty et = ty_pointee(gp);
-                        uint32_t ces = is_ptr(et) ? 8 : ty_size(et);
+                        uint32_t ces = is_scalar_ty(et) ? ty_size(et) : 8;
                         if (ces != 1) {
                             Ty ct = isval(col) ? tyof(col) : (Ty)S_INT32;
                             uint32_t s2 = new_val("scale", ct);
@@ -89,9 +89,9 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                         }
                         uint32_t ea = new_val("addr", gp);
                         emit_bin(ea, BO_ADD, ov(ra), col);
-                        return ov(ea);
+                        return field_chain(ov(ea), et, ty_as(gp));
                     }
-                    uint32_t es = ty_size(ty_pointee(gp));
+                    uint32_t es = m.tsize(ty_pointee(gp));
                     if (es != 1) {
                         Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
                         uint32_t sc = new_val("scale", it);
@@ -100,8 +100,11 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                     }
                     uint32_t ea = new_val("addr", gp);
                     emit_bin(ea, BO_ADD, addr, index);
-                    return ov(ea);
+                    return field_chain(ov(ea), ty_pointee(gp), ty_as(gp));
                 }
+                Ty gp = m.gvars[gi].ptr;
+                if (at(TK_DOT) && ty_is_struct(ty_pointee(gp)))  // g_struct.field = ...
+                    return field_chain(addr, ty_pointee(gp), ty_as(gp));
                 return addr;
             }
         }
@@ -109,6 +112,8 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
             Opnd var = *vp;
             Ty vt = tyof(var);
             advance();
+            if ((at(TK_ARROW) || at(TK_DOT)) && ty_is_struct(ty_pointee(vt)))
+                return member_lvalue(var);
             if (match(TK_LBRACKET)) {
                 Opnd index = parse_expr();
                 if (bad() || !expect(TK_RBRACKET)) return onone();
@@ -123,7 +128,7 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                     advance();
                     Opnd index2 = parse_expr();
                     if (bad() || !expect(TK_RBRACKET)) return onone();
-                    uint32_t es = ty_size(ty_pointee(vt));
+                    uint32_t es = m.tsize(ty_pointee(vt));
                     if (es != 1) {
                         Ty it2 = isval(index2) ? tyof(index2) : (Ty)S_INT32;
                         uint32_t s2 = new_val("scale", it2);
@@ -134,7 +139,7 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                     emit_bin(f, BO_ADD, ov(a), index2);
                     addr = ov(f);
                 } else {
-                    uint32_t es = ty_size(ty_pointee(vt));
+                    uint32_t es = m.tsize(ty_pointee(vt));
                     if (es != 1) {
                         Ty it = isval(index) ? tyof(index) : (Ty)S_INT32;
                         uint32_t s = new_val("scale", it);
@@ -151,7 +156,7 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                         advance();
                         Opnd index2 = parse_expr();
                         if (bad() || !expect(TK_RBRACKET)) return onone();
-                        uint32_t es2 = ty_size(ty_pointee(pt));
+                        uint32_t es2 = m.tsize(ty_pointee(pt));
                         if (es2 != 1) {
                             Ty it2 = isval(index2) ? tyof(index2) : (Ty)S_INT32;
                             uint32_t s2 = new_val("scale", it2);
@@ -162,6 +167,14 @@ OCB_HD inline Opnd Parser::parse_lvalue_or_expr() {
                         emit_bin(f, BO_ADD, ov(rp), index2);
                         addr = ov(f);
                     }
+                }
+                // p[i].pos.x = ...: chained fields stay addresses (parser.py:3645-3658)
+                while (!bad() && at(TK_DOT) && isptr_struct(addr)) {
+                    advance();
+                    if (!at(TK_IDENT)) { perr(); return onone(); }
+                    Str member = peekv();
+                    advance();
+                    addr = field_addr(addr, member);
                 }
                 return addr;
             }
@@ -273,7 +286,7 @@ OCB_HD inline void Parser::parse_shared(bool vol) {
         if (bad()) return false;
         if (has_inner) {
             int64_t st = inner;
-            if (!mul_dim(*this, st, ty_size(ty))) return false;
+            if (!mul_dim(*this, st, is_scalar_ty(ty) ? ty_size(ty) : 8)) return false;
             row_strides.set(ar, n, m.cint(S_INT32, st));
         }
         uint32_t v = new_val(n, smem);
@@ -314,6 +327,85 @@ OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
             }
         }
         if (bad()) return;
+        if (ty_is_struct(dty)) {  // struct / vector variable (parser.py:2502-2603)
+            if (at(TK_LBRACKET)) {  // Foo arr[N]: .local, exposed as PtrTy(Foo, LOCAL)
+                advance();
+                Opnd so = parse_assign_expr();
+                if (bad() || !expect(TK_RBRACKET)) return;
+                int64_t count;
+                if (!const_dim(*this, so, count)) return;
+                bool ok = true;
+                Ty aty = ty_ptr(dty, AS_LOCAL, false, ok);
+                if (!ok) { unsup(); return; }
+                uint32_t v = new_val(name, aty);
+                vars.set(ar, name, ov(v));
+                declare_local(name);
+                kern->locals.push(ar, LocalDecl{name, dty, count, v});
+                if (!match(TK_COMMA)) break;
+                continue;
+            }
+            uint32_t sent = new_val(name, dty);
+            vars.set(ar, name, ov(sent));
+            declare_local(name);
+            zero_init_fields(name, dty);
+            if (bad()) return;
+            if (match(TK_ASSIGN)) {
+                if (at(TK_LBRACE)) {  // { e0, e1, ... } over the scalar fields
+                    advance();
+                    uint32_t nf = m.nfields(dty), fi = 0, i = 0;
+                    while (!at(TK_RBRACE) && !at(TK_EOF)) {
+                        if (bad()) return;
+                        Opnd ve = parse_assign_expr();
+                        if (bad()) return;
+                        // the i-th scalar field
+                        while (fi < nf && !is_scalar_ty(m.field(dty, fi).ty)) fi++;
+                        if (fi < nf) {
+                            SField f = m.field(dty, fi);
+                            Str key = cat(ar, name, S("_"), f.name);
+                            uint32_t fv = new_val(key, f.ty);
+                            if (ve.k == O_CONST && m.consts[ve.x].ty != f.ty) {
+                                Const c = m.consts[ve.x];
+                                c.ty = f.ty;
+                                m.consts.push(ar, c);
+                                uint32_t fv2 = new_val(key, f.ty);
+                                emit_bin(fv2, BO_ADD, oc(m.consts.n - 1), m.czero(f.ty));
+                                vars.set(ar, key, ov(fv2));
+                            } else {
+                                emit_bin(fv, BO_ADD, ve, m.czero(f.ty));
+                                vars.set(ar, key, ov(fv));
+                            }
+                            fi++;
+                        }
+                        i++;
+                        if (!match(TK_COMMA)) break;
+                    }
+                    (void)i;
+                    if (bad() || !expect(TK_RBRACE)) return;
+                } else {
+                    Opnd rhs = parse_assign_expr();
+                    if (bad()) return;
+                    if (isptr_struct(rhs)) {  // Foo v = p[i]: load every field
+                        load_struct_fields(rhs, ty_pointee(tyof(rhs)), name, 0,
+                                           ty_as(tyof(rhs)), false, true);
+                    } else if (isstruct(rhs)) {  // a struct value: copy its fields
+                        uint32_t nf = m.nfields(dty);
+                        for (uint32_t i = 0; i < nf && !bad(); ++i) {
+                            SField f = m.field(dty, i);
+                            if (!is_scalar_ty(f.ty)) continue;
+                            Opnd src = struct_field_src(rhs.x, f.name);
+                            if (src.k == O_NONE) continue;
+                            Str key = cat(ar, name, S("_"), f.name);
+                            uint32_t fv = new_val(key, f.ty);
+                            emit_bin(fv, BO_ADD, src, m.czero(f.ty));
+                            vars.set(ar, key, ov(fv));
+                        }
+                    }
+                }
+            }
+            if (bad()) return;
+            if (!match(TK_COMMA)) break;
+            continue;
+        }
         if (at(TK_LBRACKET)) {  // local array in .local
             advance();
             Opnd so = parse_assign_expr();
@@ -335,7 +427,7 @@ OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
             if (bad()) return;
             if (has_inner) {
                 int64_t st = inner;
-                if (!mul_dim(*this, st, is_ptr(dty) ? 8 : ty_size(dty))) return;
+                if (!mul_dim(*this, st, is_scalar_ty(dty) ? ty_size(dty) : 8)) return;
                 row_strides.set(ar, name, m.cint(S_INT32, st));
             }
             bool ok = true;
@@ -347,7 +439,7 @@ OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
             kern->locals.push(ar, LocalDecl{name, dty, size, v});
             if (match(TK_ASSIGN) && at(TK_LBRACE)) {
                 advance();
-                int64_t esz = is_ptr(dty) ? 8 : ty_size(dty);
+                int64_t esz = is_scalar_ty(dty) ? ty_size(dty) : 8;
                 int64_t idx = 0;
                 // _emit_flat_elems: nested braces flatten into one element list.
                 // State machine of the recursive walk; `depth` = open inner braces.
@@ -406,7 +498,7 @@ OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
                 vars.set(ar, name, ov(v));
             } else if (rhs.k == O_VAL && !val_eq(rhs.x, v)) {
                 Ty rt = tyof(rhs);
-                if (!is_ptr(dty) && !is_ptr(rt) && dty != rt) {
+                if (is_scalar_ty(dty) && is_scalar_ty(rt) && dty != rt) {
                     emit_cvt(v, rhs);
                 } else {
                     emit_bin(v, BO_ADD, rhs, m.cint(dty, 0));
@@ -705,9 +797,26 @@ OCB_HD inline void Parser::parse_expr_stmt() {
             Str un = stmt_lhs.p ? stmt_lhs : vname(lhs);
             if (stmt_lhs.p && vars.has(un)) {
                 vars.set(ar, un, rhs);
+            } else if (isstruct(rhs) && ty_is_struct(ty_pointee(tyof(lhs)))) {
+                // *p = s / a[i] = s: one store per scalar field (parser.py:3258-3274)
+                Ty st = ty_pointee(tyof(lhs));
+                uint32_t as = ty_as(tyof(lhs));
+                uint32_t nf = m.nfields(st);
+                for (uint32_t i = 0; i < nf && !bad(); ++i) {
+                    SField f = m.field(st, i);
+                    if (!is_scalar_ty(f.ty)) continue;
+                    Opnd fv = struct_field_src(rhs.x, f.name);
+                    if (fv.k == O_NONE) continue;
+                    bool ok = true;
+                    Ty fp = ty_ptr(f.ty, as, false, ok);
+                    if (!ok) { unsup(); return; }
+                    uint32_t fa = new_val("faddr", fp);
+                    emit_bin(fa, BO_ADD, lhs, m.cint(S_INT32, m.field_offset(st, i)));
+                    emit_store(ov(fa), fv);
+                }
             } else {
                 Ty pt = ty_pointee(tyof(lhs));
-                if (isval(rhs) && !is_ptr(tyof(rhs)) && !is_ptr(pt) && tyof(rhs) != pt) {
+                if (isval(rhs) && is_scalar_ty(tyof(rhs)) && is_scalar_ty(pt) && tyof(rhs) != pt) {
                     uint32_t co = new_val("coerce", pt);
                     emit_cvt(co, rhs);
                     rhs = ov(co);
@@ -719,14 +828,15 @@ OCB_HD inline void Parser::parse_expr_stmt() {
             Opnd *pp = vars.get(un);
             if (pp) {
                 Opnd prev = *pp;
-                if (isval(rhs) && prev.k == O_VAL && !is_ptr(tyof(prev)) && !is_ptr(tyof(rhs)) &&
-                    !eq(vname(rhs), un)) {
+                if (isval(rhs) && prev.k == O_VAL && is_scalar_ty(tyof(prev)) &&
+                    is_scalar_ty(tyof(rhs)) && !eq(vname(rhs), un)) {
                     Ty pt = tyof(prev);
                     uint32_t mat = new_val(un, pt);
                     emit_bin(mat, BO_ADD, rhs, m.czero(pt));
                     rhs = ov(mat);
                 }
                 vars.set(ar, un, rhs);
+                if (isstruct(rhs)) copy_struct_fields(rhs.x, un);
             }
         }
         while (!bad() && match(TK_COMMA)) {
@@ -791,7 +901,7 @@ OCB_HD inline void Parser::parse_expr_stmt() {
                 bool is_ptr_var = vars.has(un) && !shared_scalars.has(un);
                 if (is_ptr_var) {
                     Ty pt = ty_pointee(lt);
-                    int64_t step = is_ptr(pt) ? 1 : ty_size(pt);
+                    int64_t step = is_scalar_ty(pt) ? ty_size(pt) : 1;
                     uint32_t np = new_val(cat(ar, vname(lhs), S("_inc")), lt);
                     emit_bin(np, op, lhs, m.cint(S_UINT64, step));
                     vars.set(ar, un, ov(np));
@@ -851,11 +961,7 @@ OCB_HD inline void Parser::parse_stmt_inner() {
     }
     if (k == TK_SHARED) { parse_shared(vol); return; }
     bool decl = is_decl_start_kind(k);
-    if (!decl && k == TK_IDENT) {
-        Ty t;
-        decl = user_typedef(peekv(), t) || typedef_scalar(peekv(), t) ||
-               vector_type_name(peekv());
-    }
+    if (!decl && k == TK_IDENT) decl = is_type_name(peekv());
     if (decl) {
         Ty ty;
         if (!parse_type_with_ptr(ty)) return;
@@ -891,7 +997,30 @@ OCB_HD inline void Parser::parse_stmt_inner() {
             if (bad() || !expect(TK_SEMI)) return;
         }
         if (inline_dest >= 0) {  // inside an inlined __device__ body (parser.py:3150-3189)
-            if (rv.k != O_NONE)
+            Ty dt = m.vals[inline_dest].ty;
+            if (rv.k != O_NONE && ty_is_struct(dt) && isstruct(rv)) {
+                // struct result: copies into the canonical field values
+                uint32_t rid = m.vals[inline_dest].id;
+                uint32_t nf = m.nfields(dt);
+                for (uint32_t q = 0; q < nf && !bad(); ++q) {
+                    SField fd = m.field(dt, q);
+                    if (!is_scalar_ty(fd.ty)) continue;
+                    Opnd src = struct_field_src(rv.x, fd.name);
+                    if (src.k == O_NONE) continue;
+                    int32_t e = isrf_find(rid, fd.name);
+                    uint32_t df;
+                    if (e >= 0) {
+                        df = isrf[e].v.x;
+                    } else {
+                        df = new_val(cat(ar, m.vals[inline_dest].name, S("_"), fd.name), fd.ty);
+                        isrf_set(rid, fd.name, ov(df));
+                    }
+                    emit_bin(df, BO_ADD, src, m.czero(fd.ty));
+                }
+            } else if (rv.k != O_NONE && (ty_is_struct(dt) || isstruct(rv))) {
+                unsup();  // a struct copied as one value: no PTX for it
+                return;
+            } else if (rv.k != O_NONE)
                 emit_bin((uint32_t)inline_dest, BO_ADD, rv, m.czero(m.vals[inline_dest].ty));
             B().term = Term{T_BR, onone(), inline_merge, Str{nullptr, 0}};
             cur = new_block("after_inline_return");
@@ -1029,12 +1158,23 @@ OCB_HD inline void Parser::parse_kernel() {
     kidx = m.kernels.n - 1;
     vars.init();
     block_count = 0;
+    isrf.init();
     copy_chain.init();
     uint32_t entry = new_block("entry");
     cur = entry;
     NameSet seen;
     seen.init();
     for (uint32_t i = 0; i < params.n; ++i) {
+        if (ty_is_struct(params[i].ty)) {  // flattened to one ParamInst per leaf field
+            if (!vars.has(params[i].name)) {
+                uint32_t sv = new_val(params[i].name, params[i].ty);
+                vars.set(ar, params[i].name, ov(sv));
+            }
+            uint32_t next;
+            flat_struct_params(params[i].name, params[i].ty, i, seen, next);
+            if (bad()) return;
+            continue;
+        }
         if (seen.has(params[i].name)) continue;
         uint32_t v = new_val(params[i].name, params[i].ty);
         Inst pi = mk_inst(I_PARAM, 0, (int32_t)v, onone(), onone());
@@ -1106,9 +1246,9 @@ OCB_HD inline void Parser::parse_enum_def() {
     match(TK_SEMI);
 }
 
-// typedef (parser.py:3974-4029): scalar and pointer aliases, enum aliases,
-// function-pointer and array typedefs (the alias names the return / element
-// type); struct and union typedefs are outside the subset.
+// typedef (parser.py:3974-4029): scalar, pointer, struct and union aliases,
+// enum aliases, function-pointer and array typedefs (the alias names the
+// return / element type).
 OCB_HD inline void Parser::parse_typedef() {
     if (!expect(TK_TYPEDEF)) return;
     if (at(TK_ENUM)) {
@@ -1121,8 +1261,16 @@ OCB_HD inline void Parser::parse_typedef() {
         match(TK_SEMI);
         return;
     }
-    if (at(TK_STRUCT) || at(TK_UNION)) {
-        unsup();
+    if (at(TK_STRUCT) || at(TK_UNION)) {  // typedef struct [Tag] { ... } Alias;
+        Ty st;
+        if (!parse_struct_def(st)) return;
+        if (at(TK_IDENT)) {
+            add_typedef(peekv(), st);
+            advance();
+            match(TK_SEMI);
+        } else {
+            add_typedef(m.structs[ty_sidx(st)].name, st);
+        }
         return;
     }
     Ty ty;
@@ -1315,12 +1463,48 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
             break;
         }
     }
-    for (uint32_t k = 0; k < f.params.n && k < args.n; ++k) vars.set(ar, f.params[k].name, args[k]);
+    for (uint32_t k = 0; k < f.params.n && k < args.n && !bad(); ++k) {
+        Str pn = f.params[k].name;
+        Ty pty = f.params[k].ty;
+        Opnd a = args[k];
+        if (ty_is_struct(pty) && a.k == O_VAL) {
+            // a fresh sentinel named after the parameter; its fields are the
+            // argument's (loaded through a struct pointer, or the caller's
+            // `<arg>_<field>` values) (parser.py:1790-1853)
+            uint32_t ps = new_val(pn, pty);
+            vars.set(ar, pn, ov(ps));
+            if (isptr_struct(a)) {
+                load_struct_fields(a, ty_pointee(tyof(a)), pn, 0, ty_as(tyof(a)), true, true);
+            } else {
+                uint32_t nf = m.nfields(pty);
+                for (uint32_t q = 0; q < nf; ++q) {
+                    SField fd = m.field(pty, q);
+                    if (ty_is_struct(fd.ty)) continue;
+                    Opnd *cf = vars.get(cat(ar, vname(a), S("_"), fd.name));
+                    if (cf) {
+                        Opnd cv = *cf;
+                        vars.set(ar, cat(ar, pn, S("_"), fd.name), cv);
+                    }
+                }
+            }
+        } else {
+            vars.set(ar, pn, a);
+        }
+    }
     uint32_t rd = new_val(cat(ar, name, S("_ret")), f.ret);
     uint32_t mb = new_block(cat(ar, S("inline_"), name, S("_merge")));
     if (bad()) return onone();
     inline_dest = (int32_t)rd;
     inline_merge = m.blocks[mb].label;
+    if (ty_is_struct(f.ret)) {  // one canonical value per scalar field of the result
+        uint32_t nf = m.nfields(f.ret);
+        for (uint32_t q = 0; q < nf && !bad(); ++q) {
+            SField fd = m.field(f.ret, q);
+            if (!is_scalar_ty(fd.ty)) continue;
+            uint32_t fv = new_val(cat(ar, m.vals[rd].name, S("_"), fd.name), fd.ty);
+            isrf_set(m.vals[rd].id, fd.name, ov(fv));
+        }
+    }
     Vec<NameSet> saved_scopes = scopes;
     scopes.init();
     ++inline_depth;
@@ -1338,6 +1522,24 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
     pos = saved_pos;
     vars = saved_vars;
     for (uint32_t k = 0; k < spilled.n && !bad(); ++k) {
+        Ty sty = spilled[k].ty;
+        if (ty_is_struct(sty)) {  // reload every scalar / pointer field of the slot
+            uint32_t nf = m.nfields(sty);
+            for (uint32_t q = 0; q < nf && !bad(); ++q) {
+                SField fd = m.field(sty, q);
+                if (ty_is_struct(fd.ty)) continue;
+                bool ok = true;
+                Ty fp = ty_ptr(fd.ty, AS_LOCAL, false, ok);
+                if (!ok) { unsup(); return onone(); }
+                uint32_t fa = new_val("faddr", fp);
+                emit_bin(fa, BO_ADD, spilled[k].slot, m.cint(S_INT32, m.field_offset(sty, q)));
+                Str key = cat(ar, spilled[k].name, S("_"), fd.name);
+                uint32_t u = new_val(key, fd.ty);
+                emit_load(u, ov(fa));
+                vars.set(ar, key, ov(u));
+            }
+            continue;
+        }
         uint32_t u = new_val(spilled[k].name, spilled[k].ty);
         emit_load(u, spilled[k].slot);
         vars.set(ar, spilled[k].name, ov(u));
@@ -1345,6 +1547,13 @@ OCB_HD inline Opnd Parser::inline_call(uint32_t fi, Vec<Opnd> &args, Str name) {
     inline_dest = saved_dest;
     inline_merge = saved_merge;
     scopes = saved_scopes;
+    // the result's field values, visible as `<name>_ret_<field>`
+    uint32_t rid = m.vals[rd].id;
+    for (uint32_t q = 0; q < isrf.n && !bad(); ++q)
+        if (isrf[q].vid == rid) {
+            Opnd fv = isrf[q].v;
+            vars.set(ar, cat(ar, m.vals[rd].name, S("_"), isrf[q].fname), fv);
+        }
     return ov(rd);
 }
 
@@ -1398,7 +1607,7 @@ OCB_HD inline void Parser::parse_gvar(bool constant_form) {
                 if (!mul_dim(*this, count, dim) || !mul_dim(*this, inner, dim)) return;
                 if (!expect(TK_RBRACKET)) return;
             }
-            int64_t es = is_ptr(t) ? 8 : (int64_t)ty_size(t);
+            int64_t es = is_scalar_ty(t) ? (int64_t)ty_size(t) : 8;
             if (!mul_dim(*this, inner, es)) return;
             row_strides.set(ar, name, m.cint(S_INT32, inner));
         }
@@ -1549,8 +1758,8 @@ OCB_HD inline void Parser::parse_module() {
         } else if (k == TK_CONSTANT) {
             parse_gvar(true);
         } else if (k == TK_STRUCT || k == TK_UNION) {
-            unsup();  // structs
-            return;
+            Ty st;
+            parse_struct_def(st);
         } else if (k == TK_SHARED) {
             advance();
             Ty t;
