@@ -367,8 +367,9 @@ OCB_HD inline void Parser::parse_decl(Ty ty, bool) {
                                 Const c = m.consts[ve.x];
                                 c.ty = f.ty;
                                 m.consts.push(ar, c);
+                                Opnd rc = oc(m.consts.n - 1);
                                 uint32_t fv2 = new_val(key, f.ty);
-                                emit_bin(fv2, BO_ADD, oc(m.consts.n - 1), m.czero(f.ty));
+                                emit_bin(fv2, BO_ADD, rc, m.czero(f.ty));
                                 vars.set(ar, key, ov(fv2));
                             } else {
                                 emit_bin(fv, BO_ADD, ve, m.czero(f.ty));

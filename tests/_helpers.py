@@ -890,3 +890,220 @@ __global__ void cv(float *o, const float *in, int w) {
     o[t] = in[t] * c_k[1][1] + (float)c_after;
 }""",
 ]
+
+
+# struct / union / vector-type kernels (parser.py:98-128, :3876-3942 and the
+# StructTy paths of the expression, statement and kernel parsers)
+STRUCT_CASES = [
+    # local struct: zero-initialized fields, field stores and reads
+    """struct Acc { float sum; int count; };
+__global__ void s0(float *o, const float *in, int n) {
+    struct Acc a;
+    a.sum = 0.5f; a.count = n;
+    a.sum = a.sum + in[threadIdx.x];
+    a.count += 2;
+    o[threadIdx.x] = a.sum * (float)a.count;
+}""",
+    # aggregate initializer (an int literal into a float field is retyped)
+    """typedef struct { float x, y, z; } P3;
+__global__ void s1(float *o) {
+    P3 p = {1, 2.5f, threadIdx.x};
+    o[threadIdx.x] = p.x + p.y * p.z;
+}""",
+    # pointer to struct: element fields loaded, stored, through -> and [i].
+    """struct Particle { float px, py; float vx, vy; int alive; };
+__global__ void s2(struct Particle *ps, float dt, int n) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        if (ps[i].alive) {
+            ps[i].px = ps[i].px + ps[i].vx * dt;
+            ps[i].py += ps[i].vy * dt;
+        }
+        struct Particle *q = &ps[i];
+        q->vy = q->vy - 9.8f * dt;
+    }
+}""",
+    # struct by value as a kernel parameter (one .param per field)
+    """struct Cfg { int n; float scale; float *dst; };
+__global__ void s3(struct Cfg c, const float *src) {
+    int i = threadIdx.x;
+    if (i < c.n) c.dst[i] = src[i] * c.scale;
+}""",
+    # device functions taking and returning structs, several returns
+    """struct V2 { float x; float y; };
+__device__ struct V2 add2(struct V2 a, struct V2 b) { struct V2 r; r.x = a.x + b.x; r.y = a.y + b.y; return r; }
+__device__ struct V2 pick(struct V2 a, struct V2 b, int k) { if (k > 0) return a; return b; }
+__global__ void s4(float *o, int k) {
+    struct V2 a = {1.0f, 2.0f};
+    struct V2 b; b.x = (float)threadIdx.x; b.y = 3.0f;
+    struct V2 c = add2(a, b);
+    struct V2 d = pick(c, a, k);
+    o[threadIdx.x] = c.x * d.y + d.x;
+}""",
+    # struct fields carried around a loop (write-back of the field values)
+    """struct St { int lo; int hi; float w; };
+__global__ void s5(float *o, const int *in, int n) {
+    struct St s; s.lo = 0; s.hi = 0; s.w = 1.0f;
+    for (int i = 0; i < n; i++) {
+        if (in[i] < 0) s.lo = s.lo + 1; else s.hi = s.hi + in[i];
+        s.w = s.w * 0.5f;
+    }
+    o[threadIdx.x] = (float)(s.hi - s.lo) * s.w;
+}""",
+    # CUDA vector types
+    """__global__ void s6(float *o, int *oi) {
+    float3 a; a.x = 1.0f; a.y = 2.0f; a.z = (float)threadIdx.x;
+    float4 b = {a.x, a.y, a.z, 4.0f};
+    int2 c; c.x = threadIdx.x; c.y = c.x * 2;
+    double2 d; d.x = 1.5; d.y = (double)b.w;
+    uint4 u; u.w = 7u;
+    o[threadIdx.x] = a.x + b.y * b.w + (float)d.y;
+    oi[threadIdx.x] = c.x + c.y + (int)u.w;
+}""",
+    # union, anonymous typedef'd struct, nested struct fields
+    """union Bits { float f; unsigned int u; };
+struct Inner { int a; int b; };
+typedef struct { float m; struct Inner in; } Outer;
+struct Box { float lo[3]; float hi[3]; };
+__global__ void s7(float *o, Outer *po, struct Box *bx) {
+    union Bits v; v.f = 2.0f; v.u = v.u + 1u;
+    Outer q = po[threadIdx.x];
+    float e = bx[0].hi[1] - bx[0].lo[1];
+    o[threadIdx.x] = v.f + q.m + (float)(q.in.a) + e;
+}""",
+    # array members: constant and run-time indices, through pointer and value
+    """struct Hist { int bins[4]; float total; };
+__global__ void s8(struct Hist *h, int *o, int k) {
+    struct Hist l;
+    l.bins[2] = 5; l.total = 1.0f;
+    h->bins[k & 3] = l.bins[2];
+    o[threadIdx.x] = h->bins[1] + l.bins[6];
+}""",
+    # an array member through an element lvalue: KeyError in the reference
+    """struct Hist { int bins[4]; };
+__global__ void s8b(struct Hist *h) { h[1].bins[2] = 9; }""",
+    # module variables of struct type, a __constant__ struct array
+    """struct Par { float a; float b; int n; };
+__device__ struct Par g_par;
+__constant__ struct Par c_tab[4];
+__global__ void s9(float *o) {
+    int t = threadIdx.x;
+    g_par.a = 3.0f;
+    o[t] = c_tab[t & 3].b + (float)c_tab[1].n;
+}""",
+    # __shared__ and local arrays of structs
+    """struct Cell { float v; int id; };
+__global__ void s10(float *o, int n) {
+    __shared__ struct Cell tile[64];
+    struct Cell loc[4];
+    int t = threadIdx.x;
+    tile[t].v = (float)t; tile[t].id = t;
+    loc[t & 3].v = 2.0f;
+    __syncthreads();
+    o[t] = tile[(t + 1) & 63].v + loc[1].v + (float)tile[t].id;
+}""",
+    # &struct passed to a helper that writes through the pointer
+    """struct Pair { int a; int b; };
+__device__ void swap_pair(struct Pair *p) { int t = p->a; p->a = p->b; p->b = t; }
+__global__ void s11(int *o) {
+    struct Pair p; p.a = threadIdx.x; p.b = 7;
+    swap_pair(&p);
+    o[threadIdx.x] = p.a * 10 + p.b;
+}""",
+    # compound literals, struct copies, struct stores through a pointer
+    """typedef struct { float x; float y; } Vec2;
+__device__ Vec2 mk(float a, float b) { return (Vec2){a, b}; }
+__global__ void s12(Vec2 *out, float s) {
+    Vec2 a = mk(s, 2.0f);
+    Vec2 b;
+    b = a;
+    b.y = b.y * s;
+    out[threadIdx.x] = b;
+    *out = a;
+}""",
+    # sizeof of struct types, pointer arithmetic over structs
+    """struct Rec { double d; int i; char c; };
+__global__ void s13(int *o, struct Rec *r) {
+    struct Rec *p = r + 2;
+    p++;
+    o[threadIdx.x] = sizeof(struct Rec) + sizeof(float4) + (int)p->i;
+}""",
+    # a field the struct does not have: KeyError in the reference
+    """struct A { int x; };
+__global__ void s14(int *o) { struct A a; a.x = 1; o[0] = a.y; }""",
+    # an undefined struct: ParseError
+    """__global__ void s15(int *o) { struct Missing m; o[0] = 1; }""",
+    # struct defined after the kernel that uses it (module pass 1)
+    """__global__ void s16(float *o) { struct Late l; l.v = 2.0f; o[threadIdx.x] = l.v; }
+struct Late { float v; };""",
+]
+
+
+def struct_sources(n: int, seed: int):
+    """Seeded kernels over random struct types: mixed scalar, pointer, array
+    and nested fields; locals with and without initializers, field updates in
+    branches and loops, element access through struct pointers, structs passed
+    to and returned from device helpers, and vector types."""
+    r = random.Random(seed)
+    scal = ["int", "float", "unsigned int", "double", "long long"]
+    out = []
+    for i in range(n):
+        nf = r.randint(2, 5)
+        fields = []
+        for j in range(nf):
+            k = r.random()
+            if k < 0.7:
+                fields.append((r.choice(scal), f"f{j}", 0))
+            elif k < 0.85:
+                fields.append((r.choice(["int", "float"]), f"a{j}", r.randint(2, 4)))
+            else:
+                fields.append(("float *", f"p{j}", 0))
+        sname = f"S{i}"
+        decl = " ".join(f"{t} {nm}[{c}];" if c else f"{t} {nm};" for t, nm, c in fields)
+        text = [f"struct {sname} {{ {decl} }};"]
+        scal_f = [(t, nm) for t, nm, c in fields if not c and "*" not in t]
+        arr_f = [(t, nm, c) for t, nm, c in fields if c]
+        if not scal_f:
+            scal_f = [("int", "fz")]
+            text[0] = f"struct {sname} {{ {decl} int fz; }};"
+        use_fn = r.random() < 0.5
+        if use_fn:
+            t0, n0 = r.choice(scal_f)
+            text.append(f"__device__ struct {sname} upd{i}(struct {sname} s, {t0} v) {{")
+            text.append(f"    s.{n0} = s.{n0} + v;")
+            if r.random() < 0.5:
+                text.append(f"    if (v > ({t0})3) return s;")
+            text.append(f"    s.{n0} = s.{n0} * ({t0})2;")
+            text.append("    return s;")
+            text.append("}")
+        vec = r.choice(["float2", "float3", "float4", "int2", "int4", "uint2", "double2"])
+        body = [f"__global__ void st{i}(struct {sname} *ps, float *o, int n) {{",
+                "    int t = threadIdx.x;",
+                f"    struct {sname} a;"]
+        for t, nm in scal_f:
+            if r.random() < 0.7:
+                body.append(f"    a.{nm} = ({t})(t + {r.randint(0, 9)});")
+        if r.random() < 0.5:
+            body.append(f"    struct {sname} b = ps[t & 15];")
+        else:
+            body.append(f"    struct {sname} b; b = a;")
+        t0, n0 = r.choice(scal_f)
+        if r.random() < 0.6:
+            body.append(f"    for (int k = 0; k < {r.randint(2, 8)}; k++) {{")
+            body.append(f"        if (k < n) a.{n0} = a.{n0} + ({t0})k; else b.{n0} = b.{n0} - ({t0})1;")
+            body.append("    }")
+        if arr_f:
+            t1, n1, c1 = r.choice(arr_f)
+            body.append(f"    a.{n1}[{r.randint(0, c1 - 1)}] = ({t1})t;")
+            body.append(f"    ps[t].{n1}[n & {c1 - 1 if c1 in (2, 4) else 1}] = a.{n1}[{r.randint(0, c1 - 1)}];")
+        if use_fn:
+            body.append(f"    struct {sname} c = upd{i}(a, ({t0})n);")
+        else:
+            body.append(f"    struct {sname} c = a;")
+        body.append(f"    ps[t].{n0} = c.{n0} + b.{n0};")
+        body.append(f"    {vec} v; v.x = ({ 'double' if vec == 'double2' else 'float' })c.{n0}; v.y = v.x + 1;")
+        terms = [f"(float)c.{nm}" for _, nm in scal_f] + ["(float)v.y", f"(float)ps[n].{n0}"]
+        body.append(f"    o[t] = {' + '.join(terms)};")
+        body.append("}")
+        out.append("\n".join(text + body) + "\n")
+    return out
