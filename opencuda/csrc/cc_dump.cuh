@@ -50,13 +50,19 @@ struct Out {  // bounded text sink
     }
 };
 
-OCB_HD inline void dump_ty(Out &o, Ty t) {
+OCB_HD inline void dump_ty(Out &o, const Module &m, Ty t) {
+    if (ty_is_struct(t)) {
+        o.put("struct(");
+        o.put(m.structs[ty_sidx(t)].name);
+        o.put(')');
+        return;
+    }
     if (!is_ptr(t)) {
         o.put(scalar_name(ty_scalar(t)));
         return;
     }
     o.put("ptr(");
-    dump_ty(o, ty_pointee(t));
+    dump_ty(o, m, ty_pointee(t));
     o.put(',');
     o.put(as_name(ty_as(t)));
     o.put(ty_vol(t) ? ",1)" : ",0)");
@@ -74,7 +80,7 @@ OCB_HD inline void dump_opnd(Out &o, const Module &m, Opnd x) {
         o.put(':');
         o.put(v.name);
         o.put(':');
-        dump_ty(o, v.ty);
+        dump_ty(o, m, v.ty);
         return;
     }
     if (x.k == O_SYM) {
@@ -84,7 +90,7 @@ OCB_HD inline void dump_opnd(Out &o, const Module &m, Opnd x) {
     }
     const Const &c = m.consts[x.x];
     o.put('#');
-    dump_ty(o, c.ty);
+    dump_ty(o, m, c.ty);
     if (c.pyfloat) {
         uint64_t bits;
         memcpy(&bits, &c.f, 8);
@@ -149,6 +155,24 @@ OCB_HD inline void dump_inst(Out &o, const Module &m, const Inst &i) {
         }
         o.put(')');
         break;
+    case I_PRINTF:
+    case I_ASM: {
+        const char *h = "0123456789abcdef";
+        o.put(i.kind == I_PRINTF ? "printf " : "asm ");
+        for (uint32_t k = 0; k < i.func.n; ++k) {
+            o.put(h[(uint8_t)i.func.p[k] >> 4]);
+            o.put(h[(uint8_t)i.func.p[k] & 15]);
+        }
+        o.put('(');
+        for (uint32_t k = 0; k < i.args.n; ++k) {
+            if (i.kind == I_ASM && k == i.pidx) o.put("; ");
+            else if (k) o.put(", ");
+            dump_opnd(o, m, i.args[k]);
+        }
+        if (i.kind == I_ASM && i.pidx == i.args.n) o.put("; ");
+        o.put(')');
+        break;
+    }
     case I_GADDR:
         dest();
         o.put("gaddr @");
@@ -210,13 +234,13 @@ OCB_HD inline void dump_module(Out &o, const Module &m) {
             o.put("\n param ");
             o.put(k.params[i].name);
             o.put(' ');
-            dump_ty(o, k.params[i].ty);
+            dump_ty(o, m, k.params[i].ty);
         }
         for (uint32_t i = 0; i < k.shared.n; ++i) {
             o.put("\n shared ");
             o.put(k.shared[i].name);
             o.put(' ');
-            dump_ty(o, k.shared[i].ty);
+            dump_ty(o, m, k.shared[i].ty);
             o.put(' ');
             o.put_i64(k.shared[i].count);
         }
@@ -224,7 +248,7 @@ OCB_HD inline void dump_module(Out &o, const Module &m) {
             o.put("\n local ");
             o.put(k.locals[i].name);
             o.put(' ');
-            dump_ty(o, k.locals[i].ty);
+            dump_ty(o, m, k.locals[i].ty);
             o.put(' ');
             o.put_i64(k.locals[i].count);
             o.put(' ');

@@ -277,10 +277,23 @@ struct Emit {
     LabelSet skip;
     Vec<Str> preamble;    // module preamble (ir_to_ptx)
     int term_depth;       // nesting of _emit_term through inlined merge blocks
+    // printf (emit.py:681-694, :1110-1125, :1661-1740)
+    struct PFmt {
+        Str label, fmt;
+    };
+    Vec<PFmt> pfs;        // this kernel's format strings, in block order
+    uint32_t pf_idx;      // the next one an emitted printf takes
+    uint32_t pf_count;    // printf calls emitted in this kernel
+    bool vprintf_decl;    // the module preamble declares vprintf
+    Vec<Str> fmt_done;    // format labels already in the module preamble
 
     OCB_HD Emit(Module &mod, Arena &tmp_) : m(mod), ar(*mod.ar), tmp(tmp_), k(nullptr), fail(false) {
         preamble.init();
         term_depth = 0;
+        pfs.init();
+        pf_idx = pf_count = 0;
+        vprintf_decl = false;
+        fmt_done.init();
     }
 #ifdef OCB_TRAP_UNSUP
     void unsup(int line = __builtin_LINE()) {
@@ -604,6 +617,14 @@ struct Emit {
                     for (uint32_t q = 0; q < in.args.n; ++q) use(in.args[q], idx);
                     if (in.dest >= 0) def(in.dest, idx);
                     break;
+                case I_PRINTF:
+                    for (uint32_t q = 0; q < in.args.n; ++q) use(in.args[q], idx);
+                    break;
+                case I_ASM:  // inputs used, then outputs defined (emit.py:225-231)
+                    for (uint32_t q = in.pidx; q < in.args.n; ++q) use(in.args[q], idx);
+                    for (uint32_t q = 0; q < in.pidx; ++q)
+                        if (in.args[q].k == O_VAL) def((int32_t)in.args[q].x, idx);
+                    break;
                 default: break;
                 }
             }
@@ -718,6 +739,8 @@ struct Emit {
     OCB_HD OCB_NI void emit_load(const Inst &in);
     OCB_HD OCB_NI void emit_store(const Inst &in);
     OCB_HD OCB_NI void emit_call(const Inst &in);
+    OCB_HD OCB_NI void emit_printf(const Inst &in);
+    OCB_HD OCB_NI void emit_asm(const Inst &in);
     OCB_HD OCB_NI void emit_math(const Inst &in, Str dest);
     OCB_HD OCB_NI void emit_term(const Term &t);
     OCB_HD OCB_NI void emit_block(uint32_t b);

@@ -379,6 +379,72 @@ OCB_HD inline void Emit::emit_call(const Inst &in) {
     uint32_t na = in.args.n;
     auto arg = [&](uint32_t i) { return in.args[i]; };
     if (sstarts(f, "__devfn_")) { unsup(); return; }
+    if (eq(f, "tex1Dfetch") || eq(f, "tex2D") || eq(f, "tex3D")) {
+        // texture fetch: a v4 read, the first component into dest (emit.py:1919-1952)
+        Str dest = in.dest >= 0 ? reg(in.dest) : S("%f0");
+        Str tex = na ? opnd(arg(0)) : S("%rd0");
+        int dim = eq(f, "tex1Dfetch") ? 1 : eq(f, "tex2D") ? 2 : 3;
+        Str c[3];
+        if (dim == 1) {
+            c[0] = na > 1 ? opnd(arg(1)) : S("0");
+        } else {
+            for (int q = 0; q < dim; ++q) c[q] = na > (uint32_t)q + 1 ? opnd(arg(q + 1)) : S("0f00000000");
+        }
+        uint32_t n = in.dest >= 0 ? V((uint32_t)in.dest).id : 0;
+        uint32_t f1 = new_value(nm("_tex_g_", n), S_FLOAT), f2 = new_value(nm("_tex_b_", n), S_FLOAT),
+                 f3 = new_value(nm("_tex_a_", n), S_FLOAT);
+        Str r1 = reg(f1), r2 = reg(f2), r3 = reg(f3);
+        SB b = sb();
+        b.s(dim == 1 ? "    tex.1d.v4.f32.s32 {" : dim == 2 ? "    tex.2d.v4.f32.f32 {" : "    tex.3d.v4.f32.f32 {")
+            .s(dest).s(", ").s(r1).s(", ").s(r2).s(", ").s(r3).s("}, [").s(tex).s(", {").s(c[0]);
+        if (dim == 2) b.s(", ").s(c[1]);
+        if (dim == 3) b.s(", ").s(c[1]).s(", ").s(c[2]).s(", ").s(c[2]);
+        b.s("}];");
+        put(b);
+        return;
+    }
+    if (eq(f, "surf1Dread")) {  // (emit.py:1953-1958)
+        Str dest = in.dest >= 0 ? reg(in.dest) : S("%r0");
+        Str surf = na ? opnd(arg(0)) : S("%rd0");
+        Str c = na > 1 ? opnd(arg(1)) : S("0");
+        SB b = sb();
+        b.s("    suld.b.1d.b32.trap {").s(dest).s("}, [").s(surf).s(", {").s(c).s("}];");
+        put(b);
+        return;
+    }
+    if (eq(f, "surf1Dwrite")) {  // (emit.py:1959-1964)
+        Str v = na ? opnd(arg(0)) : S("0");
+        Str surf = na > 1 ? opnd(arg(1)) : S("%rd0");
+        Str c = na > 2 ? opnd(arg(2)) : S("0");
+        SB b = sb();
+        b.s("    sust.b.1d.b32.trap [").s(surf).s(", {").s(c).s("}], {").s(v).s("};");
+        put(b);
+        return;
+    }
+    if (eq(f, "__mbarrier_init")) {  // (emit.py:1985-1989)
+        Str mb = na ? opnd(arg(0)) : S("%rd0");
+        Str cnt = na > 1 ? opnd(arg(1)) : S("1");
+        SB b = sb();
+        b.s("    mbarrier.init.shared::cta.b64 [").s(mb).s("], ").s(cnt).c(';');
+        put(b);
+        return;
+    }
+    if (eq(f, "__mbarrier_try_wait_parity")) {  // (emit.py:1990-1999)
+        Str dest = in.dest >= 0 ? reg(in.dest) : S("%r0");
+        Str mb = na ? opnd(arg(0)) : S("%rd0");
+        Str ph = na > 1 ? opnd(arg(1)) : S("0");
+        uint32_t n = in.dest >= 0 ? V((uint32_t)in.dest).id : 0;
+        uint32_t pt = new_value(nm("_mbar_p_", n), S_BOOL);
+        add_pred(V(pt).id);
+        Str pr = reg(pt);
+        SB b = sb();
+        b.s("    mbarrier.try_wait.parity.shared::cta.b64 ").s(pr).s(", [").s(mb).s("], ").s(ph).c(';');
+        put(b);
+        SB b2 = sb();
+        b2.s("    selp.s32 ").s(dest).s(", 1, 0, ").s(pr).c(';');
+        put(b2);
+        return;
+    }
     if (sstarts(f, "atomic")) {
         const char *aop = eq(f, "atomicAdd") ? "add" : eq(f, "atomicMin") ? "min" :
                           eq(f, "atomicMax") ? "max" : eq(f, "atomicAnd") ? "and" :
@@ -1325,7 +1391,173 @@ OCB_HD inline void Emit::emit_inst(uint32_t ix) {
     case I_LOAD: emit_load(in); break;
     case I_STORE: emit_store(in); break;
     case I_CALL: emit_call(in); break;
+    case I_PRINTF: emit_printf(in); break;
+    case I_ASM: emit_asm(in); break;
     default: unsup(); break;
+    }
+}
+
+// printf -> vprintf (emit.py:1661-1740): the format string's address, the
+// arguments widened to 8-byte slots of a .local buffer (f32 to f64, 32-bit
+// integers sign- or zero-extended), its generic address, and the call.
+OCB_HD inline void Emit::emit_printf(const Inst &in) {
+    if (pf_idx >= pfs.n) return;
+    Str label = pfs[pf_idx++].label;
+    uint32_t nargs = in.args.n;
+    uint32_t n = pf_count++;
+    bool ok = true;
+    Ty gptr = ty_ptr(S_VOID, AS_GLOBAL, false, ok);
+    Ty lptr = ty_ptr(S_VOID, AS_LOCAL, false, ok);
+    Ty vptr = ty_ptr(S_VOID, AS_GENERIC, false, ok);
+    uint32_t fa = new_value(nm("_fmt_addr_", n), gptr);
+    {
+        Str r = reg(fa);
+        SB b = sb();
+        b.s("    mov.u64 ").s(r).s(", ").s(label).c(';');
+        put(b);
+    }
+    Str va;
+    if (nargs > 0) {
+        uint32_t vl = new_value(nm("_valist_", n), lptr);
+        {
+            SB b = sb();
+            b.s("    .local .align 8 .b8 _valist_").i(n).c('[').i(8 * (pyint)nargs).s("];");
+            put(b);
+            Str r = reg(vl);
+            SB b2 = sb();
+            b2.s("    mov.u64 ").s(r).s(", _valist_").i(n).c(';');
+            put(b2);
+        }
+        for (uint32_t i = 0; i < nargs && !bad(); ++i) {
+            Opnd a = in.args[i];
+            Ty at = (a.k == O_VAL || a.k == O_CONST) ? m.opty(a) : (Ty)S_INT32;
+            bool fl = ty_is_scalar(at) && ty_is_float(at);
+            bool w64 = is_ptr(at) || (ty_is_scalar(at) && ty_size(at) == 8);
+            Str sv;
+            const char *sty;
+            if (fl && !w64) {
+                uint32_t pr = new_value(nm2("_va_arg_", n, "_", i), S_DOUBLE);
+                Str r = reg(pr);
+                Str o = opnd(a);
+                SB b = sb();
+                b.s("    cvt.f64.f32 ").s(r).s(", ").s(o).c(';');
+                put(b);
+                sv = r;
+                sty = "f64";
+            } else if (!w64 && !fl) {
+                uint32_t wv = new_value(nm2("_va_arg_", n, "_", i), gptr);
+                Str r = reg(wv);
+                Str o = opnd(a);
+                SB b = sb();
+                b.s(ty_is_scalar(at) && ty_is_signed(at) ? "    cvt.s64.s32 " : "    cvt.u64.u32 ")
+                    .s(r).s(", ").s(o).c(';');
+                put(b);
+                sv = r;
+                sty = "u64";
+            } else {
+                sv = opnd(a);
+                sty = ptx_type(at);
+            }
+            Str slot;
+            if (i == 0) {
+                slot = reg(vl);
+            } else {
+                uint32_t offv = new_value(nm2("_va_off_", n, "_", i), lptr);
+                Str r = reg(offv);
+                Str base = reg(vl);
+                SB b = sb();
+                b.s("    add.u64 ").s(r).s(", ").s(base).s(", ").i(8 * (pyint)i).c(';');
+                put(b);
+                slot = r;
+            }
+            SB b = sb();
+            b.s("    st.local.").s(sty).s(" [").s(slot).s("], ").s(sv).c(';');
+            put(b);
+        }
+        uint32_t vg = new_value(nm("_valist_gen_", n), vptr);
+        Str r = reg(vg);
+        Str lr = reg(vl);
+        SB b = sb();
+        b.s("    cvta.local.u64 ").s(r).s(", ").s(lr).c(';');
+        put(b);
+        va = r;
+    } else {
+        uint32_t nv = new_value(nm("_valist_null_", n), gptr);
+        Str r = reg(nv);
+        SB b = sb();
+        b.s("    mov.u64 ").s(r).s(", 0;");
+        put(b);
+        va = r;
+    }
+    uint32_t rv = new_value(nm("_vprintf_rv_", n), S_INT32);
+    put("    {");
+    SB b0 = sb();
+    b0.s("    .param .b64 _p0_").i(n).c(';');
+    put(b0);
+    SB b1 = sb();
+    b1.s("    .param .b64 _p1_").i(n).c(';');
+    put(b1);
+    SB b2 = sb();
+    b2.s("    .param .b32 _rv_").i(n).c(';');
+    put(b2);
+    Str far = reg(fa);
+    SB b3 = sb();
+    b3.s("    st.param.b64 [_p0_").i(n).s("], ").s(far).c(';');
+    put(b3);
+    SB b4 = sb();
+    b4.s("    st.param.b64 [_p1_").i(n).s("], ").s(va).c(';');
+    put(b4);
+    SB b5 = sb();
+    b5.s("    call.uni (_rv_").i(n).s("), vprintf, (_p0_").i(n).s(", _p1_").i(n).s(");");
+    put(b5);
+    Str rr = reg(rv);
+    SB b6 = sb();
+    b6.s("    ld.param.b32 ").s(rr).s(", [_rv_").i(n).s("];");
+    put(b6);
+    put("    }");
+}
+
+// Inline PTX (emit.py:1151-1168): %N -> the N-th operand (outputs, then
+// inputs; replaced from the highest N down), then one line per
+// ';'-separated statement, stripped of surrounding whitespace.
+OCB_HD inline void Emit::emit_asm(const Inst &in) {
+    uint32_t n = in.args.n;
+    Str *ops = (Str *)tmp.alloc(sizeof(Str) * (n + 1), 8);
+    if (!ops) { unsup(); return; }
+    for (uint32_t q = 0; q < n; ++q) ops[q] = q < in.pidx ? reg(in.args[q]) : opnd(in.args[q]);
+    for (uint32_t q = 0; q < in.func.n; ++q)
+        if ((uint8_t)in.func.p[q] >= 0x80) { unsup(); return; }  // str.strip()'s Unicode set
+    Str t = in.func;
+    for (uint32_t q = n; q-- > 0;) {
+        SB key = sb();
+        key.c('%').i(q);
+        Str kk = key.str();
+        SB r = sb();
+        bool any = false;
+        for (uint32_t i = 0; i < t.n;) {
+            if (i + kk.n <= t.n && mem_eq(t.p + i, kk.p, kk.n)) {
+                r.s(ops[q]);
+                i += kk.n;
+                any = true;
+            } else {
+                r.c(t.p[i++]);
+            }
+        }
+        if (any) t = r.str();
+    }
+    auto ws = [](char c) { return c == ' ' || (c >= 9 && c <= 13) || (c >= 0x1c && c <= 0x1f); };
+    uint32_t st = 0;
+    for (uint32_t i = 0; i <= t.n; ++i) {
+        if (i < t.n && t.p[i] != ';') continue;
+        uint32_t a = st, e = i;
+        while (a < e && ws(t.p[a])) ++a;
+        while (e > a && ws(t.p[e - 1])) --e;
+        if (e > a) {
+            SB b = sb();
+            b.s("    ").s(Str{t.p + a, e - a}).c(';');
+            put(b);
+        }
+        st = i + 1;
     }
 }
 

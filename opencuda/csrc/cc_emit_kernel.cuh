@@ -573,6 +573,19 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
             }
         }
     }
+    // printf format strings of this kernel, in block order (emit.py:681-690)
+    pfs.init();
+    pf_idx = pf_count = 0;
+    for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+        Block &b = B(k->blocks[bi]);
+        for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+            const Inst &in = I(b.insts[ii]);
+            if (in.kind != I_PRINTF) continue;
+            SB lb = sb();
+            lb.s("_fmt_").s(k->name).c('_').i(pfs.n);
+            pfs.push(ar, PFmt{lb.str(), in.func});
+        }
+    }
     Vec<Str> body;
     body.init();
     lines = &body;
@@ -758,6 +771,28 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
     }
     for (uint32_t i = 0; i < body.n; ++i) out.push(ar, body[i]);
     out.push(ar, S("}"));
+    // the vprintf declaration (once per module) and this kernel's format
+    // strings as byte arrays join the module preamble (emit.py:1110-1125)
+    if (pfs.n) {
+        if (!vprintf_decl) {
+            vprintf_decl = true;
+            preamble.push(ar, S(".extern .func (.param .b32 func_retval0) vprintf(.param .b64 fmt, "
+                                ".param .b64 valist);"));
+            preamble.push(ar, S(""));
+        }
+        for (uint32_t q = 0; q < pfs.n; ++q) {
+            bool dup = false;
+            for (uint32_t z = 0; z < fmt_done.n && !dup; ++z) dup = eq(fmt_done[z], pfs[q].label);
+            if (dup) continue;
+            fmt_done.push(ar, pfs[q].label);
+            Str f = pfs[q].fmt;
+            SB b = sb();
+            b.s(".global .align 1 .b8 ").s(pfs[q].label).c('[').i((pyint)f.n + 1).s("] = {");
+            for (uint32_t z = 0; z < f.n; ++z) b.i((uint8_t)f.p[z]).s(", ");
+            b.s("0};");
+            preamble.push(ar, b.str());
+        }
+    }
     return !bad();
 }
 

@@ -371,7 +371,12 @@ OCB_HD inline const char *cmpop_name(uint8_t o) {
 
 // I_GADDR: the address of a module symbol into a u64 register (GlobalAddrInst,
 // ir/nodes.py:166-178); func = symbol name, op = its address space.
-enum : uint8_t { I_BIN = 0, I_CMP, I_SELECT, I_LOAD, I_STORE, I_CVT, I_CALL, I_PARAM, I_GADDR };
+// I_PRINTF: printf(fmt, args...) (PrintfInst, ir/nodes.py:159-163); func =
+// the format string with the parser's escapes resolved, args = the values.
+// I_ASM: inline PTX (AsmInst, ir/nodes.py:180-189); func = the template,
+// args = the output values then the input operands, pidx = output count.
+enum : uint8_t { I_BIN = 0, I_CMP, I_SELECT, I_LOAD, I_STORE, I_CVT, I_CALL, I_PARAM, I_GADDR,
+                 I_PRINTF, I_ASM };
 struct Inst {
     uint8_t kind, op;
     int32_t dest;     // value index, -1 = none

@@ -602,6 +602,10 @@ struct Opt {
                 } else if (in.kind == I_STORE) {
                     in.a = rep1(in.a);
                     in.b = rep1(in.b);
+                } else if (in.kind == I_PRINTF && in.args.n) {
+                    Vec<Opnd> na = in.args.copy(ar);
+                    for (uint32_t q = 0; q < na.n; ++q) na[q] = rep1(na[q]);
+                    in.args = na;
                 }
                 if (bad()) return eliminated;
                 if (keep) b.insts[w++] = ix;
@@ -641,6 +645,7 @@ struct Opt {
                     case I_CVT:
                     case I_LOAD: in.a = chase(in.a); break;
                     case I_CALL:
+                    case I_PRINTF:
                         if (in.args.n) {
                             Vec<Opnd> na = in.args.copy(ar);
                             for (uint32_t q = 0; q < na.n; ++q) na[q] = chase(na[q]);
@@ -769,6 +774,7 @@ struct Opt {
                 case I_LOAD:
                 case I_CVT: in.a = resolve(in.a); break;
                 case I_CALL:
+                case I_PRINTF:
                     if (in.args.n) {
                         Vec<Opnd> na = in.args.copy(ar);
                         for (uint32_t q = 0; q < na.n; ++q) na[q] = resolve(na[q]);
@@ -820,6 +826,7 @@ struct Opt {
             case I_LOAD: f(in.a); break;
             default: break;
             }
+            if (in.kind == I_ASM) return;  // AsmInst has no attribute the pass reads
             for (uint32_t q = 0; q < in.args.n; ++q) f(in.args[q]);
         };
         uint32_t total = 0;
@@ -1775,6 +1782,10 @@ struct Opt {
                         ni.args = in.args.copy(ar);
                         for (uint32_t q = 0; q < ni.args.n; ++q) ni.args[q] = R(ni.args[q]);
                         has_new_dest = in.dest >= 0;
+                        break;
+                    case I_PRINTF:
+                        ni.args = in.args.copy(ar);
+                        for (uint32_t q = 0; q < ni.args.n; ++q) ni.args[q] = R(ni.args[q]);
                         break;
                     default: break;
                     }

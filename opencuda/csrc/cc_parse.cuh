@@ -205,6 +205,7 @@ struct Parser {
     Vec<FieldArr> farrs;
     uint32_t farr_groups;
     Vec<ISRF> isrf;
+    Str last_string_lit;           // the last string literal's text (printf format)
 
     OCB_HD Parser(Arena &a, Module &mod, Tokens t) : ar(a), m(mod), tk(t) {
         pos = 0;
@@ -235,6 +236,7 @@ struct Parser {
         farrs.init();
         farr_groups = 0;
         isrf.init();
+        last_string_lit = Str{"", 0};
     }
 
     // ---- status ----------------------------------------------------------
@@ -481,6 +483,44 @@ struct Parser {
         return ov(s);
     }
 
+    // str.replace(a, b) (all non-overlapping occurrences, left to right)
+    OCB_HD Str str_replace(Str s, const char *a, const char *b) {
+        uint32_t na = cstrlen(a), nb = cstrlen(b), cnt = 0;
+        for (uint32_t i = 0; i + na <= s.n;) {
+            if (mem_eq(s.p + i, a, na)) {
+                cnt++;
+                i += na;
+            } else {
+                i++;
+            }
+        }
+        if (!cnt) return s;
+        char *d = (char *)ar.alloc(s.n + cnt * nb + 1, 1);
+        if (!d) return s;
+        uint32_t k = 0;
+        for (uint32_t i = 0; i < s.n;) {
+            if (i + na <= s.n && mem_eq(s.p + i, a, na)) {
+                for (uint32_t j = 0; j < nb; ++j) d[k++] = b[j];
+                i += na;
+            } else {
+                d[k++] = s.p[i++];
+            }
+        }
+        d[k] = 0;
+        return Str{d, k};
+    }
+    // a string literal token as the parser keeps it (parser.py:2203-2209):
+    // the quotes dropped, then \n, \t, \r, \\ and \" replaced in that order
+    OCB_HD Str string_lit_text(Str tokv) {
+        Str raw{tokv.p + 1, tokv.n >= 2 ? tokv.n - 2 : 0};
+        raw = str_replace(raw, "\\n", "\n");
+        raw = str_replace(raw, "\\t", "\t");
+        raw = str_replace(raw, "\\r", "\r");
+        raw = str_replace(raw, "\\\\", "\\");
+        raw = str_replace(raw, "\\\"", "\"");
+        return raw;
+    }
+
     // int(const.value) of an array dimension (1 for a non-constant); float
     // dimensions are outside the subset
     OCB_HD bool const_dim_of(Opnd o, int64_t &out) {
@@ -699,6 +739,7 @@ struct Parser {
         return -1;
     }
     OCB_HD OCB_NI void parse_switch();
+    OCB_HD OCB_NI void parse_asm();
     OCB_HD OCB_NI void parse_decl(Ty ty, bool vol);
     OCB_HD OCB_NI void parse_shared(bool vol);
     OCB_HD OCB_NI void parse_if();

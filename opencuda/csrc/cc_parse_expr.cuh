@@ -1321,11 +1321,31 @@ OCB_HD inline Opnd Parser::parse_primary_expr() {
 OCB_HD inline Opnd Parser::parse_call(Str name) {
     Vec<Opnd> args;
     args.init();
+    bool is_printf = eq(name, "printf");
+    // one argument; a printf argument that is one string literal is the
+    // Const(VOID, 0) the reference's primary parser returns for it, its text
+    // kept as the format (parser.py:2203-2209)
+    auto arg = [&]() -> Opnd {
+        if (is_printf && at(TK_STRING_LIT) && pos + 1 < tk.n &&
+            (kind_at(pos + 1) == TK_COMMA || kind_at(pos + 1) == TK_RPAREN)) {
+            last_string_lit = string_lit_text(peekv());
+            advance();
+            return m.cint(S_VOID, 0);
+        }
+        return parse_assign_expr();
+    };
     if (!at(TK_RPAREN)) {
-        args.push(ar, parse_assign_expr());
-        while (!bad() && match(TK_COMMA)) args.push(ar, parse_assign_expr());
+        args.push(ar, arg());
+        while (!bad() && match(TK_COMMA)) args.push(ar, arg());
     }
     if (bad() || !expect(TK_RPAREN)) return onone();
+    if (is_printf) {  // PrintfInst(fmt, args[1:]) (parser.py:1732-1738)
+        Inst pi = mk_inst(I_PRINTF, 0, -1, onone(), onone());
+        pi.func = last_string_lit;
+        for (uint32_t q = 1; q < args.n; ++q) pi.args.push(ar, args[q]);
+        emit(pi);
+        return m.cint(S_VOID, 0);
+    }
     auto call = [&](int32_t dest, Str func) {
         Inst c = mk_inst(I_CALL, 0, dest, onone(), onone());
         c.func = func;
@@ -1382,11 +1402,19 @@ OCB_HD inline Opnd Parser::parse_call(Str name) {
         }
         return m.cint(S_INT32, 0);
     }
-    if (in_list(name, kTexFetch) || in_list(name, kSurfVoid) || eq(name, "printf") ||
-        in_list(name, " surf1Dread __cp_async_bulk_tensor_1d __cp_async_bulk_tensor_2d"
-                      " __cp_async_bulk_commit_group __cp_async_bulk_wait_group __mbarrier_init"
-                      " __mbarrier_try_wait_parity ")) {
-        unsup();  // texture/surface/TMA/mbarrier intrinsics and printf
+    // texture, surface and mbarrier intrinsics (parser.py:1645-1679)
+    if (in_list(name, kTexFetch) || eq(name, "surf1Dread") || eq(name, "__mbarrier_try_wait_parity")) {
+        uint32_t d = new_val(name, in_list(name, kTexFetch) ? (Ty)S_FLOAT : (Ty)S_INT32);
+        call((int32_t)d, name);
+        return ov(d);
+    }
+    if (in_list(name, kSurfVoid) || eq(name, "__mbarrier_init")) {
+        call(-1, name);
+        return m.cint(S_VOID, 0);
+    }
+    if (in_list(name, " __cp_async_bulk_tensor_1d __cp_async_bulk_tensor_2d"
+                      " __cp_async_bulk_commit_group __cp_async_bulk_wait_group ")) {
+        unsup();  // the bulk tensor copy intrinsics are not emitted by this engine
         return onone();
     }
     // __device__ functions: expanded in place (parser.py:1749-1929)

@@ -928,6 +928,66 @@ OCB_HD inline void Parser::parse_expr_stmt() {
     if (!bad()) expect(TK_SEMI);
 }
 
+// asm [volatile] ("template" : "=r"(out), ... : "r"(expr), ... : clobbers);
+// (parser.py:2326-2375): each output names a variable that gets a fresh value
+// of its old type (int when unbound); the template is kept as written.
+OCB_HD inline void Parser::parse_asm() {
+    advance();
+    if (at(TK_VOLATILE) || (at(TK_IDENT) && eq(peekv(), "volatile"))) advance();
+    if (!expect(TK_LPAREN)) return;
+    Str tmpl{"", 0};
+    if (at(TK_STRING_LIT)) {
+        Str v = peekv();
+        tmpl = Str{v.p + 1, v.n >= 2 ? v.n - 2 : 0};
+        advance();
+    }
+    Vec<Opnd> outs, ins;
+    outs.init();
+    ins.init();
+    if (match(TK_COLON)) {
+        while (at(TK_STRING_LIT)) {
+            advance();
+            if (!expect(TK_LPAREN)) return;
+            if (!at(TK_IDENT)) { perr(); return; }
+            Str vn = peekv();
+            advance();
+            if (!expect(TK_RPAREN)) return;
+            Opnd *old = vars.get(vn);
+            Ty t = old ? tyof(*old) : (Ty)S_INT32;
+            uint32_t nv = new_val(vn, t);
+            outs.push(ar, ov(nv));
+            vars.set(ar, vn, ov(nv));
+            if (!match(TK_COMMA)) break;
+        }
+        if (bad()) return;
+        if (match(TK_COLON)) {
+            while (at(TK_STRING_LIT)) {
+                advance();
+                if (!expect(TK_LPAREN)) return;
+                Opnd e = parse_assign_expr();
+                if (bad() || !expect(TK_RPAREN)) return;
+                ins.push(ar, e);
+                if (!match(TK_COMMA)) break;
+            }
+            if (bad()) return;
+            if (match(TK_COLON)) {
+                while (at(TK_STRING_LIT)) {
+                    advance();
+                    if (!match(TK_COMMA)) break;
+                }
+            }
+        }
+    }
+    if (bad() || !expect(TK_RPAREN) || !expect(TK_SEMI)) return;
+    if (!tmpl.n) return;
+    Inst ai = mk_inst(I_ASM, 0, -1, onone(), onone());
+    ai.func = tmpl;
+    ai.pidx = outs.n;
+    for (uint32_t q = 0; q < outs.n; ++q) ai.args.push(ar, outs[q]);
+    for (uint32_t q = 0; q < ins.n; ++q) ai.args.push(ar, ins[q]);
+    emit(ai);
+}
+
 // _parse_stmt (parser.py:2287-3412)
 OCB_HD inline void Parser::parse_stmt() {
     if (++nest > MAX_NEST) { unsup(); --nest; return; }
@@ -958,7 +1018,7 @@ OCB_HD inline void Parser::parse_stmt_inner() {
     if (k == TK_LBRACE) { parse_stmt_or_block(); return; }
     if (k == TK_IDENT) {
         Str v = peekv();
-        if (eq(v, "asm") || eq(v, "__asm__") || eq(v, "__asm")) { unsup(); return; }
+        if (eq(v, "asm") || eq(v, "__asm__") || eq(v, "__asm")) { parse_asm(); return; }
     }
     if (k == TK_SHARED) { parse_shared(vol); return; }
     bool decl = is_decl_start_kind(k);

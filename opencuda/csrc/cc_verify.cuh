@@ -41,6 +41,8 @@ struct Verifier {
         case I_CVT: return "CvtInst";
         case I_CALL: return "CallInst";
         case I_PARAM: return "ParamInst";
+        case I_PRINTF: return "PrintfInst";
+        case I_ASM: return "AsmInst";
         default: return "GlobalAddrInst";
         }
     }
@@ -62,6 +64,7 @@ struct Verifier {
             break;
         default: break;
         }
+        if (in.kind == I_ASM) return;  // AsmInst has no operand attribute read here
         for (uint32_t q = 0; q < in.args.n; ++q)
             if (in.args[q].k == O_VAL) f(in.args[q].x);
     }
@@ -196,6 +199,16 @@ struct Verifier {
             const Block &b = B(k.blocks[i]);
             for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
                 const Inst &in = m.insts[b.insts[ii]];
+                if (in.kind == I_ASM) {  // the outputs are defined here
+                    for (uint32_t q = 0; q < in.pidx; ++q) {
+                        if (in.args[q].k != O_VAL) continue;
+                        uint32_t id = m.vals[in.args[q].x].id;
+                        if (id >= nid) return false;
+                        dcount.set(id, dcount.get(id) + 1);
+                        if (dblock.get(id) == 0xFFFFFFFFu) dblock.set(id, lab[i]);
+                    }
+                    continue;
+                }
                 if (in.dest < 0) continue;
                 uint32_t id = m.vals[(uint32_t)in.dest].id;
                 if (id >= nid) return false;

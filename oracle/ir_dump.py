@@ -37,6 +37,8 @@ def ty_str(t) -> str:
     if isinstance(t, PtrTy):
         asp = t.addr_space.value if hasattr(t.addr_space, "value") else str(t.addr_space)
         return f"ptr({ty_str(t.pointee)},{asp},{1 if t.volatile else 0})"
+    if type(t).__name__ == "StructTy":
+        return f"struct({t.name})"
     return f"?{type(t).__name__}"
 
 
@@ -81,6 +83,14 @@ def inst_str(i) -> str:
         return f"{op_str(i.dest)} = gaddr @{i.sym_name} {asp}"
     if isinstance(i, N.ParamInst):
         return f"{op_str(i.dest)} = param {i.param_index} {i.param_name}"
+    if isinstance(i, N.PrintfInst):
+        fmt = i.fmt.encode("utf-8", "surrogateescape").hex()
+        return f"printf {fmt}({', '.join(op_str(a) for a in i.args)})"
+    if isinstance(i, N.AsmInst):
+        tmpl = i.template.encode("utf-8", "surrogateescape").hex()
+        outs = ', '.join(op_str(v) for _, v in i.outputs)
+        ins = ', '.join(op_str(v) for _, v in i.inputs)
+        return f"asm {tmpl}({outs}; {ins})"
     return f"?{type(i).__name__}"
 
 
