@@ -1107,3 +1107,86 @@ def struct_sources(n: int, seed: int):
         body.append("}")
         out.append("\n".join(text + body) + "\n")
     return out
+
+
+# printf, inline asm and the texture / surface / mbarrier intrinsics
+# (parser.py:1645-1679, :1732-1738, :2326-2375; codegen/emit.py:1151-1168,
+# :1661-1740, :1919-1999)
+PRINTF_ASM_CASES = [
+    # printf with no argument, int / unsigned / float / double / pointer / 64-bit
+    """__global__ void p0(const float *a, int n) {
+    int t = threadIdx.x;
+    printf("start\\n");
+    printf("t=%d u=%u f=%f d=%f p=%p l=%lld\\n", t, (unsigned int)n, a[t], (double)a[t], a, (long long)t);
+}""",
+    # printf in a branch and in a loop (unrolled), escapes in the format
+    """__global__ void p1(int *o, int n) {
+    int t = threadIdx.x;
+    if (t == 0) printf("tab\\there \\"q\\" back\\\\slash %d\\r\\n", n);
+    for (int i = 0; i < 3; i++) printf("i=%d\\n", i + t);
+    o[t] = n;
+}""",
+    # two kernels with printf: one vprintf declaration, per-kernel labels
+    """__global__ void pa(int x) { printf("a %d\\n", x); }
+__global__ void pb(int x, float y) { printf("b %d %f\\n", x, y); printf("b2\\n"); }""",
+    # a string argument: the last string literal becomes the format
+    """__global__ void p2(int x) { printf("%s=%d\\n", "x", x); }""",
+    # inline PTX with outputs and inputs, volatile, clobbers, several statements
+    """__global__ void p3(unsigned int *o, unsigned int a, unsigned int b) {
+    unsigned int lane, r;
+    asm volatile("mov.u32 %0, %%laneid;" : "=r"(lane));
+    asm("add.u32 %0, %1, %2; add.u32 %0, %0, 1;" : "=r"(r) : "r"(a), "r"(b) : "memory");
+    o[threadIdx.x] = r + lane;
+}""",
+    # asm output into a fresh name; empty template emits nothing
+    """__global__ void p4(int *o) {
+    __asm__("mov.u32 %0, %%tid.x;" : "=r"(fresh));
+    asm volatile("" ::: "memory");
+    o[0] = fresh;
+}""",
+    # texture, surface and mbarrier intrinsics (PTX text only)
+    """__global__ void p5(float *o, unsigned long long tex, unsigned long long surf, int n) {
+    int t = threadIdx.x;
+    float a = tex1Dfetch(tex, t);
+    float b = tex2D(tex, 0.5f, 1.5f);
+    float c = tex3D(tex, 0.5f, 1.5f, 2.5f);
+    int s = surf1Dread(surf, t * 4);
+    surf1Dwrite(s + 1, surf, t * 4);
+    __shared__ unsigned long long bar[1];
+    if (t == 0) __mbarrier_init(bar, 32);
+    __syncthreads();
+    int ok = __mbarrier_try_wait_parity(bar, 0);
+    o[t] = a + b + c + (float)ok;
+}""",
+]
+
+
+def printf_sources(n: int, seed: int):
+    """Seeded kernels with printf calls of random argument mixes inside
+    branches and loops, and inline asm adds."""
+    r = random.Random(seed)
+    out = []
+    tys = [("int", "%d"), ("unsigned int", "%u"), ("float", "%f"), ("double", "%f"),
+           ("long long", "%lld")]
+    for i in range(n):
+        body = [f"__global__ void pf{i}(float *o, const int *in, int n) {{",
+                "    int t = threadIdx.x;", "    float acc = (float)in[t & 7];"]
+        for k in range(r.randint(1, 4)):
+            args = [r.choice(tys) for _ in range(r.randint(0, 5))]
+            fmt = " ".join(f"v{j}={f}" for j, (_, f) in enumerate(args)) + "\\n"
+            vals = [f"({ty})(acc + {j})" for j, (ty, _) in enumerate(args)]
+            call = f'printf("k{k} {fmt}"{"".join(", " + v for v in vals)});'
+            c = r.random()
+            if c < 0.3:
+                body.append(f"    if (t < n) {call}")
+            elif c < 0.5:
+                body.append(f"    for (int i = 0; i < {r.randint(2, 4)}; i++) {{ acc = acc + 1.0f; {call} }}")
+            else:
+                body.append(f"    {call}")
+            if r.random() < 0.3:
+                body.append('    int q; asm("add.s32 %0, %1, %2;" : "=r"(q) : "r"(t), "r"(n));')
+                body.append("    acc = acc + (float)q;")
+        body.append("    o[t] = acc;")
+        body.append("}")
+        out.append("\n".join(body) + "\n")
+    return out

@@ -14,16 +14,18 @@ pytestmark = pytest.mark.gpu
 RAISE_STATUS = {"ValueError": 1, "OverflowError": 2, "ParseError": 3, "KeyError": 4}
 
 
-def test_structs_against_live_reference(ctx):
-    srcs = STRUCT_CASES + struct_sources(400, 31)
-    tb = ctx.compile_batch(srcs)
+@pytest.mark.parametrize("stage", ["ir", "opt", "ptx"])
+def test_structs_against_live_reference(ctx, stage):
+    srcs = STRUCT_CASES + struct_sources(400 if stage == "ptx" else 150, 31)
+    fn = {"ir": ctx.parse_batch, "opt": ctx.optimize_batch, "ptx": ctx.compile_batch}[stage]
+    tb = fn(srcs)
     with ref_runner.RefPool() as pool:
-        ref = pool.run(srcs, what=("ptx",), chunksize=4)
+        ref = pool.run(srcs, what=(stage,), chunksize=4)
     for i, (s, r) in enumerate(zip(srcs, ref)):
         st = int(tb.status[i])
         assert st != TU_UNSUPPORTED, (i, s[:300])
-        if "ptx" not in r:
+        if stage not in r:
             assert st == RAISE_STATUS.get(r["error"][0], 6), (i, r["error"], st)
             continue
         assert st == 0, (i, st, s[:300])
-        assert tb.text(i) == r["ptx"], (i, s)
+        assert tb.text(i) == r[stage], (i, s)
