@@ -266,7 +266,7 @@ OCB_HD inline void dump_module(Out &o, const Module &m) {
             dump_term(o, m, b.term);
         }
     }
-    if (m.gvars.n) {
+    if (m.gvars.n || m.funcs.n) {
         if (m.kernels.n) o.put('\n');
         o.put("module-extras");
     }

@@ -745,6 +745,8 @@ struct Emit {
     OCB_HD OCB_NI void emit_term(const Term &t);
     OCB_HD OCB_NI void emit_block(uint32_t b);
     OCB_HD OCB_NI void peepholes(Vec<Str> &body);
+    OCB_HD OCB_NI bool rd_compact(Vec<Str> &L);
+    OCB_HD OCB_NI bool emit_devfn(Kernel &f, Vec<Str> &out);
     OCB_HD OCB_NI bool emit_kernel(Kernel &kk, Vec<Str> &out);
     OCB_HD int32_t block_by_label(Str l);
     OCB_HD uint32_t pred_count_of(Str l);

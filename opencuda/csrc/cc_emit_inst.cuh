@@ -378,7 +378,55 @@ OCB_HD inline void Emit::emit_call(const Inst &in) {
     Str f = in.func;
     uint32_t na = in.args.n;
     auto arg = [&](uint32_t i) { return in.args[i]; };
-    if (sstarts(f, "__devfn_")) { unsup(); return; }
+    if (sstarts(f, "__devfn_")) {  // call.uni of a recursive device function (emit.py:1744-1776)
+        uint32_t n = pf_count++;
+        put("    {");
+        auto aty = [&](uint32_t i) -> const char * {
+            Opnd a = arg(i);
+            const char *t = (a.k == O_VAL || a.k == O_CONST) ? ptx_type(m.opty(a)) : "s32";
+            return cstr_eq(t, "f16") ? "b16" : t;
+        };
+        for (uint32_t i = 0; i < na; ++i) {
+            SB b = sb();
+            b.s("        .param .").s(aty(i)).s(" _ca").i(i).c('_').i(n).c(';');
+            put(b);
+        }
+        const char *rt = nullptr;
+        if (in.dest >= 0) {
+            rt = ptx_type(V((uint32_t)in.dest).ty);
+            if (cstr_eq(rt, "f16")) rt = "b16";
+            SB b = sb();
+            b.s("        .param .").s(rt).s(" _cr_").i(n).c(';');
+            put(b);
+        }
+        for (uint32_t i = 0; i < na; ++i) {
+            Str src = opnd(arg(i));
+            SB b = sb();
+            b.s("        st.param.").s(aty(i)).s(" [_ca").i(i).c('_').i(n).s("], ").s(src).c(';');
+            put(b);
+        }
+        SB al = sb();
+        for (uint32_t i = 0; i < na; ++i) {
+            if (i) al.s(", ");
+            al.s("_ca").i(i).c('_').i(n);
+        }
+        Str args = al.str();
+        if (rt) {
+            SB b = sb();
+            b.s("        call.uni (_cr_").i(n).s("), ").s(f).s(", (").s(args).s(");");
+            put(b);
+            Str d = reg(in.dest);
+            SB b2 = sb();
+            b2.s("        ld.param.").s(rt).c(' ').s(d).s(", [_cr_").i(n).s("];");
+            put(b2);
+        } else {
+            SB b = sb();
+            b.s("        call.uni ").s(f).s(", (").s(args).s(");");
+            put(b);
+        }
+        put("    }");
+        return;
+    }
     if (eq(f, "tex1Dfetch") || eq(f, "tex2D") || eq(f, "tex3D")) {
         // texture fetch: a v4 read, the first component into dest (emit.py:1919-1952)
         Str dest = in.dest >= 0 ? reg(in.dest) : S("%f0");

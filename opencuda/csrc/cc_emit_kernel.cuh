@@ -359,6 +359,16 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
         }
     }
     // (5) rd compaction through in-place address adds
+    rd_compact(L);
+}
+
+// The %rd compaction of the text peepholes (emit.py:556-614 for .func bodies,
+// the same logic as the kernel entry's): when a cvt writes the highest %rd
+// and two or more add.u64 read it, the adds write their pointer operand in
+// place; then the highest register is renamed into each gap.  True when the
+// rewrite ran.
+OCB_HD inline bool Emit::rd_compact(Vec<Str> &L) {
+    bool ran = false;
     {
         int64_t rd_max = -1;
         for (uint32_t i = 0; i < L.n; ++i) each_rd(L[i], [&](int64_t v) { if (v > rd_max) rd_max = v; });
@@ -378,7 +388,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                 while (a < l.n && is_wsc(l.p[a])) ++a;
                 uint32_t b = a;
                 while (b < l.n && !is_wsc(l.p[b])) ++b;
-                if (a == b) { unsup(); return; }  // split()[1] raises IndexError
+                if (a == b) { unsup(); return false; }  // split()[1] raises IndexError
                 Str tok{l.p + a, b - a};
                 while (tok.n && tok.p[tok.n - 1] == ',') tok.n--;
                 if (eq(tok, highest)) cvt_idx = i;
@@ -418,6 +428,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                 }
             }
             if (cvt_idx >= 0 && adds.n >= 2) {
+                ran = true;
                 for (int64_t q = (int64_t)adds.n - 1; q >= 0; --q) {
                     Add &A = adds[(uint32_t)q];
                     if (eq(A.dst, A.ptr)) continue;
@@ -447,7 +458,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
                 if (top >= 0) {
                     cap = (uint32_t)top + 1;
                     uint8_t *used = (uint8_t *)tmp.alloc(cap + 1, 16);
-                    if (!used) { unsup(); return; }
+                    if (!used) { unsup(); return false; }
                     for (uint32_t i = 0; i <= cap; ++i) used[i] = 0;
                     for (uint32_t i = 0; i < L.n; ++i) each_rd(L[i], [&](int64_t v) { used[v] = 1; });
                     int64_t cur_top = top;
@@ -472,6 +483,7 @@ OCB_HD inline void Emit::peepholes(Vec<Str> &L) {
             }
         }
     }
+    return ran;
 }
 
 // ---- if_convert_diamonds gate (optimizer/if_convert.py:88-228) ------------------
@@ -796,6 +808,134 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
     return !bad();
 }
 
+// `.param .<type> <name>` list of a device function (f16 spelled b16)
+OCB_HD inline Str devfn_params(Emit &E, const Kernel &f) {
+    SB b = E.sb();
+    for (uint32_t i = 0; i < f.params.n; ++i) {
+        const char *t = ptx_type(f.params[i].ty);
+        if (cstr_eq(t, "f16")) t = "b16";
+        if (i) b.s(", ");
+        b.s(".param .").s(t).c(' ').s(f.params[i].name);
+    }
+    return b.str();
+}
+// `.func [(.param .<ret> retval0) ]__devfn_<name>(`
+OCB_HD inline void devfn_head(SB &b, const Kernel &f) {
+    b.s(".func ");
+    if (!(ty_is_scalar(f.ret) && ty_scalar(f.ret) == S_VOID)) {
+        const char *t = ptx_type(f.ret);
+        if (cstr_eq(t, "f16")) t = "b16";
+        b.s("(.param .").s(t).s(" retval0) ");
+    }
+    b.s("__devfn_").s(f.name).c('(');
+}
+
+// ---- emit_device_function (emit.py:506-646) --------------------------------------
+// The body as in a kernel but without the kernel's text peepholes (only the
+// %rd compaction), registers declared from the text in prefix order, locals
+// by their variable names.  The fallback registers of emission-time values
+// count from zero: the reference keeps the allocation counts of the previous
+// kernel there, and device functions are emitted before any kernel.
+OCB_HD inline bool Emit::emit_devfn(Kernel &kk, Vec<Str> &out) {
+    k = &kk;
+    tmp.used = 0;
+    nid0 = k->next_id;
+    fb_alloc = nullptr;
+    fb_cap = 0;
+    widen = nullptr;
+    widen_cap = 0;
+    for (int p = 0; p < PF_N; ++p) fb_count[p] = reg_counts[p] = 0;
+    skip.init(tmp, 2 * k->blocks.n + 8);
+    term_depth = 0;
+    pfs.init();
+    pf_idx = pf_count = 0;
+    for (uint32_t i = 0; i < k->params.n; ++i)
+        for (uint32_t q = 0; q < k->params[i].name.n; ++q)
+            if ((uint8_t)k->params[i].name.p[q] >= 0x80) { unsup(); return false; }
+    build_alloc();
+    if (bad()) return false;
+    for (int p = 0; p < PF_N; ++p) alloc_max[p] = 0;
+    Vec<Str> body;
+    body.init();
+    lines = &body;
+    for (uint32_t bi = 0; bi < k->blocks.n && !bad(); ++bi) emit_block(k->blocks[bi]);
+    if (bad()) return false;
+    // %(\w+?)(\d+) over the body: the count per register prefix
+    int cnt[PF_N];
+    bool any = false;
+    for (int p = 0; p < PF_N; ++p) cnt[p] = 0;
+    for (uint32_t i = 0; i < body.n; ++i) {
+        Str l = body[i];
+        for (uint32_t j = 0; j < l.n; ++j) {
+            if (l.p[j] != '%') continue;
+            uint32_t a = j + 1, e = a;
+            auto wch = [](char c) {
+                return (c >= 'a' && c <= 'z') || (c >= 'A' && c <= 'Z') || (c >= '0' && c <= '9') || c == '_';
+            };
+            while (e < l.n && wch(l.p[e])) ++e;
+            // the shortest \w+ prefix followed by digits (then as many digits as follow)
+            uint32_t ps = a + 1;
+            bool hit = false;
+            for (; ps < e; ++ps)
+                if (l.p[ps] >= '0' && l.p[ps] <= '9') { hit = true; break; }
+            if (!hit) { j = e > j ? e - 1 : j; continue; }
+            uint32_t de = ps;
+            while (de < l.n && l.p[de] >= '0' && l.p[de] <= '9') ++de;
+            Str pre{l.p + a, ps - a};
+            int pf = eq(pre, "rd") ? PF_RD : eq(pre, "fd") ? PF_FD : eq(pre, "r") ? PF_R :
+                     eq(pre, "f") ? PF_F : eq(pre, "h") ? PF_H : eq(pre, "p") ? PF_P : -1;
+            if (pf >= 0) {
+                int64_t v = 0;
+                for (uint32_t q = ps; q < de && v < 100000000; ++q) v = v * 10 + (l.p[q] - '0');
+                if (cnt[pf] < v + 1) cnt[pf] = (int)(v + 1);
+                any = true;
+            }
+            j = de - 1;
+        }
+    }
+    bool any_rd_prefix = any;
+    if (cnt[PF_RD] > 3 && rd_compact(body)) {
+        int64_t top = -1;
+        for (uint32_t i = 0; i < body.n; ++i) each_rd(body[i], [&](int64_t v) { if (v > top) top = v; });
+        cnt[PF_RD] = (int)(top + 1);
+    }
+    if (bad()) return false;
+    (void)any_rd_prefix;
+    SB hb = sb();
+    devfn_head(hb, *k);
+    out.push(ar, hb.str());
+    SB pb = sb();
+    pb.s("    ").s(devfn_params(*this, *k)).c(')');
+    out.push(ar, pb.str());
+    out.push(ar, S("{"));
+    // sorted prefix names: f, fd, h, p, r, rd
+    int order[] = {PF_F, PF_FD, PF_H, PF_P, PF_R, PF_RD};
+    for (int oi = 0; oi < PF_N; ++oi) {
+        int p = order[oi];
+        int c = any ? cnt[p] : reg_counts[p];
+        bool present = any ? cnt[p] > 0 : reg_counts[p] > 0;
+        if (!present) continue;
+        SB b = sb();
+        const char *t = p == PF_P ? ".pred" : p == PF_H ? ".f16" : p == PF_F ? ".f32" :
+                        p == PF_FD ? ".f64" : p == PF_RD ? ".b64" : ".b32";
+        b.s("    .reg ").s(t).s(" %").s(pf_name(p)).c('<').i(c).s(">;");
+        out.push(ar, b.str());
+    }
+    for (uint32_t q = 0; q < k->locals.n; ++q) {
+        const LocalDecl &d = k->locals[q];
+        int64_t es = ty_is_scalar(d.ty) ? (int64_t)ty_size(d.ty) : 8;
+        int64_t al = es < 16 ? es : 16;
+        SB b = sb();
+        b.s("    .local .align ").i(al).s(" .b8 ").s(d.name).c('[').i(es * d.count).s("];");
+        out.push(ar, b.str());
+    }
+    out.push(ar, S(""));
+    for (uint32_t i = 0; i < body.n; ++i) out.push(ar, body[i]);
+    out.push(ar, S("}"));
+    out.push(ar, S(""));
+    return !bad();
+}
+
 // ---- module text: ir_to_ptx + the CLI's --emit-ptx assembly ----------------------
 OCB_HD inline bool emit_module(Module &m, Arena &tmp, Out &o, const char *arch) {
     Emit E(m, tmp);
@@ -804,6 +944,26 @@ OCB_HD inline bool emit_module(Module &m, Arena &tmp, Out &o, const char *arch) 
             m.unsup = true;
             return false;
         }
+    // recursive device functions: forward declarations, then definitions,
+    // lead the module preamble (emit.py:3136-3154)
+    for (uint32_t fi = 0; fi < m.funcs.n; ++fi) {
+        SB b = E.sb();
+        devfn_head(b, m.funcs[fi]);
+        b.s(devfn_params(E, m.funcs[fi])).s(");");
+        E.preamble.push(*m.ar, b.str());
+    }
+    for (uint32_t fi = 0; fi < m.funcs.n; ++fi) {
+        Vec<Str> lines;
+        lines.init();
+        if (!E.emit_devfn(m.funcs[fi], lines)) return false;
+        // the definition is one preamble entry: its lines joined by newlines
+        SB b = E.sb();
+        for (uint32_t q = 0; q < lines.n; ++q) {
+            if (q) b.c('\n');
+            b.s(lines[q]);
+        }
+        E.preamble.push(*m.ar, b.str());
+    }
     // kernel texts, keyed by name in dict order (a later kernel with the same
     // name replaces the earlier text but keeps its position)
     struct KT { Str name; Vec<Str> lines; };

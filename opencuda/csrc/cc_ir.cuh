@@ -425,6 +425,7 @@ struct Kernel {
     Vec<SharedDecl> shared;
     Vec<LocalDecl> locals;
     bool has_locals;           // the reference created _local_decls
+    Ty ret;                    // a device function's return type (S_VOID for kernels)
 };
 
 // A module-level variable (Module.global_vars, ir/nodes.py:289): element
@@ -457,6 +458,7 @@ struct Module {
     Vec<Inst> insts;
     Vec<Block> blocks;
     Vec<Kernel> kernels;
+    Vec<Kernel> funcs;        // recursive __device__ functions (DeviceFunction), .func
     Vec<GVar> gvars;          // in declaration order
     Vec<StructDef> structs;   // every StructTy of the TU (Ty bits 16-31 index it)
     Vec<SField> sfields;
@@ -470,6 +472,7 @@ struct Module {
         insts.init();
         blocks.init();
         kernels.init();
+        funcs.init();
         gvars.init();
         structs.init();
         sfields.init();

@@ -1891,6 +1891,35 @@ struct Opt {
         reset_tmp();
     }
 
+    // The pass schedule of a recursive device function's body
+    // (optimize.py:1606-1627); the final loop stops at the first pass of a
+    // round that changed something, as `and` does there.
+    OCB_HD void run_devfn() {
+        OCB_PASS(unroll_loops(16));
+        OCB_PASS(constant_fold());
+        OCB_PASS(cse());
+        OCB_PASS(dead_block_elim());
+        OCB_PASS(identity_fold());
+        OCB_PASS(constant_fold());
+        OCB_PASS(dead_inst_elim());
+        OCB_PASS(licm());
+        OCB_PASS(fma_fuse());
+        OCB_PASS(cse());
+        OCB_PASS(identity_fold());
+        OCB_PASS(constant_fold());
+        OCB_PASS(dead_inst_elim());
+        OCB_PASS(thread_empty_blocks());
+        OCB_PASS(fold_empty_ret_blocks());
+        for (int r = 0; r < 8 && !bad(); ++r) {
+            if (OCB_PASS(dead_block_elim()) != 0) continue;
+            if (OCB_PASS(dead_inst_elim()) != 0) continue;
+            if (OCB_PASS(thread_empty_blocks()) != 0) continue;
+            if (OCB_PASS(fold_empty_ret_blocks()) != 0) continue;
+            break;
+        }
+        reset_tmp();
+    }
+
     // Content hash of the kernel's IR: blocks (labels, order, terminators),
     // instructions with their operands (values by id/type/name, constants by
     // type and Python value) and the next value id.
@@ -1962,6 +1991,10 @@ OCB_HD inline void optimize_module(Module &m, Arena &tmp) {
     for (uint32_t ki = 0; ki < m.kernels.n && !o.bad(); ++ki) {
         o.k = &m.kernels[ki];
         o.run();
+    }
+    for (uint32_t fi = 0; fi < m.funcs.n && !o.bad(); ++fi) {
+        o.k = &m.funcs[fi];
+        o.run_devfn();
     }
 }
 

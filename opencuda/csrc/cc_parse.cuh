@@ -206,6 +206,7 @@ struct Parser {
     uint32_t farr_groups;
     Vec<ISRF> isrf;
     Str last_string_lit;           // the last string literal's text (printf format)
+    Vec<uint32_t> rec_funcs;       // recursive __device__ functions (dfuncs indices)
 
     OCB_HD Parser(Arena &a, Module &mod, Tokens t) : ar(a), m(mod), tk(t) {
         pos = 0;
@@ -237,6 +238,7 @@ struct Parser {
         farr_groups = 0;
         isrf.init();
         last_string_lit = Str{"", 0};
+        rec_funcs.init();
     }
 
     // ---- status ----------------------------------------------------------
@@ -730,7 +732,14 @@ struct Parser {
     OCB_HD OCB_NI Opnd spill_scalar(Str name, Opnd value);
     OCB_HD OCB_NI void parse_device_func();
     OCB_HD OCB_NI Opnd inline_call(uint32_t fi, Vec<Opnd> &args, Str name);
-    OCB_HD OCB_NI bool dfunc_cycle();
+    OCB_HD OCB_NI bool recursive_funcs(Vec<uint32_t> &out);
+    OCB_HD OCB_NI void compile_devfn(uint32_t fi);
+    // a name in the reference's _recursive_device_funcs
+    OCB_HD bool is_recursive(Str v) const {
+        for (uint32_t i = 0; i < rec_funcs.n; ++i)
+            if (eq(dfuncs[rec_funcs[i]].name, v)) return true;
+        return false;
+    }
     // the definition a call resolves to (a later definition replaces an
     // earlier one, as a dict assignment does)
     OCB_HD int32_t find_dfunc(Str v) const {

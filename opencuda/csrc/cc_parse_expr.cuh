@@ -1417,6 +1417,14 @@ OCB_HD inline Opnd Parser::parse_call(Str name) {
         unsup();  // the bulk tensor copy intrinsics are not emitted by this engine
         return onone();
     }
+    // recursive __device__ functions: a real call (parser.py:1739-1748)
+    if (is_recursive(name)) {
+        Ty rt = dfuncs[(uint32_t)find_dfunc(name)].ret;
+        int32_t d = -1;
+        if (!(ty_is_scalar(rt) && ty_scalar(rt) == S_VOID)) d = (int32_t)new_val(cat(ar, name, S("_ret")), rt);
+        call(d, cat(ar, S("__devfn_"), name));
+        return d >= 0 ? ov((uint32_t)d) : m.cint(S_VOID, 0);
+    }
     // __device__ functions: expanded in place (parser.py:1749-1929)
     int32_t fi = find_dfunc(name);
     if (fi >= 0) return inline_call((uint32_t)fi, args, name);

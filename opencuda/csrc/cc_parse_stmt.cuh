@@ -2,7 +2,7 @@
 // _parse_lvalue_or_expr, _parse_stmt_or_block), :3701-3874 (_parse_kernel)
 // and :4194-4443 (parse_module), restated for the supported subset.
 #pragma once
-#include "cc_parse_struct.cuh"
+#include "cc_parse_devfn.cuh"
 
 namespace ocb {
 namespace cc {
@@ -1214,6 +1214,7 @@ OCB_HD inline void Parser::parse_kernel() {
     kk.shared.init();
     kk.locals.init();
     kk.has_locals = false;
+    kk.ret = S_VOID;
     if (!m.kernels.push(ar, kk)) return;  // arena exhausted
     kern = &m.kernels.back();
     kidx = m.kernels.n - 1;
@@ -1440,52 +1441,6 @@ OCB_HD inline void Parser::parse_device_func() {
         advance();
     }
     dfuncs.push(ar, DevFunc{name, rt, params, bs, pos});
-}
-
-// Recursion (parser.py:4396-4431): a call graph over the identifiers in each
-// body; any cycle means functions the reference compiles as .func, which
-// this engine does not.
-OCB_HD inline bool Parser::dfunc_cycle() {
-    uint32_t n = dfuncs.n;
-    if (!n) return false;
-    // state per function: 0 unvisited, 1 on the path, 2 done (iterative DFS)
-    uint8_t *color = (uint8_t *)ar.alloc(n, 1);
-    uint32_t *stack = (uint32_t *)ar.alloc(4ull * n, 4);
-    uint32_t *scan = (uint32_t *)ar.alloc(4ull * n, 4);
-    if (!color || !stack || !scan) return false;
-    for (uint32_t i = 0; i < n; ++i) color[i] = 0;
-    for (uint32_t root = 0; root < n; ++root) {
-        if (color[root] || find_dfunc(dfuncs[root].name) != (int32_t)root) continue;
-        uint32_t sp = 0;
-        stack[sp] = root;
-        scan[sp] = dfuncs[root].body_start;
-        color[root] = 1;
-        ++sp;
-        while (sp) {
-            uint32_t f = stack[sp - 1];
-            uint32_t &q = scan[sp - 1];
-            int32_t callee = -1;
-            while (q < dfuncs[f].body_end && q < tk.n) {
-                uint32_t t = q++;
-                if (kind_at(t) != TK_IDENT) continue;
-                callee = find_dfunc(val_at(t));
-                if (callee >= 0) break;
-            }
-            if (callee < 0) {
-                color[f] = 2;
-                --sp;
-                continue;
-            }
-            if (color[callee] == 1) return true;
-            if (color[callee] == 0) {
-                color[callee] = 1;
-                stack[sp] = (uint32_t)callee;
-                scan[sp] = dfuncs[callee].body_start;
-                ++sp;
-            }
-        }
-    }
-    return false;
 }
 
 // Call of a __device__ function (parser.py:1749-1929, scalar form): the
@@ -1843,10 +1798,13 @@ OCB_HD inline void Parser::parse_module() {
         }
     }
     if (bad()) return;
-    if (dfunc_cycle()) {  // recursive __device__ functions (.func) are outside the subset
+    // recursion detection, then each recursive function compiled as a .func
+    // in the order of the reference's set (parser.py:4392-4435)
+    if (!recursive_funcs(rec_funcs)) {
         unsup();
         return;
     }
+    for (uint32_t i = 0; i < rec_funcs.n && !bad(); ++i) compile_devfn(rec_funcs[i]);
     for (uint32_t i = 0; i < kpos.n && !bad(); ++i) {
         pos = kpos[i];
         parse_kernel();
