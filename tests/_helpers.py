@@ -1190,3 +1190,63 @@ def printf_sources(n: int, seed: int):
         body.append("}")
         out.append("\n".join(body) + "\n")
     return out
+
+
+# recursive __device__ functions compiled as .func (parser.py:4089-4153,
+# :4392-4435; codegen/emit.py:506-646, :1744-1776, :3126-3154)
+RECURSIVE_CASES = [
+    """__device__ int fact(int n) { if (n <= 1) return 1; return n * fact(n - 1); }
+__global__ void r0(int *o) { o[threadIdx.x] = fact(threadIdx.x & 7); }""",
+    # mutual recursion through a prototype
+    """__device__ int ping(int n);
+__device__ int pong(int n) { return n <= 0 ? 0 : ping(n - 1) + 1; }
+__device__ int ping(int n) { return n <= 0 ? 0 : pong(n - 1) + 2; }
+__global__ void r1(int *o) { o[threadIdx.x] = ping(5); }""",
+    # float and pointer parameters, a void recursive function, a loop inside
+    """__device__ float powr(float x, int e) { if (e == 0) return 1.0f; return x * powr(x, e - 1); }
+__device__ void fill(float *p, int n, float v) { if (n <= 0) return; p[n - 1] = v; fill(p, n - 1, v * 0.5f); }
+__device__ int sum_to(int n) { int s = 0; for (int i = 0; i < 4; i++) s += i; if (n > 0) s += sum_to(n - 1); return s; }
+__global__ void r2(float *o, int k) {
+    o[threadIdx.x] = powr(1.5f, k);
+    fill(o + 32, 8, 1.0f);
+    o[64 + threadIdx.x] = (float)sum_to(k);
+}""",
+    # a non-recursive helper calling a recursive one (inlined at its call)
+    """__device__ int fib(int n) { if (n < 2) return n; return fib(n - 1) + fib(n - 2); }
+__device__ int twice_fib(int n) { return 2 * fib(n); }
+__global__ void r3(int *o, int n) { o[threadIdx.x] = twice_fib(n) + fib(3); }""",
+]
+
+
+def recursive_sources(n: int, seed: int):
+    """Seeded modules of 1-6 __device__ functions with random call graphs
+    (self calls, mutual cycles, chains into cycles) and names of random
+    lengths, called from a kernel."""
+    r = random.Random(seed)
+    out = []
+    alpha = "abcdefghijklmnopqrstuvwxyz_"
+    for i in range(n):
+        k = r.randint(1, 6)
+        names = []
+        while len(names) < k:
+            nm = r.choice("abcdefghijklmnopqrstuvwxyz") + "".join(
+                r.choice(alpha + "0123456789") for _ in range(r.randint(0, 17)))
+            if nm not in names:
+                names.append(nm)
+        tys = [r.choice(["int", "float", "unsigned int"]) for _ in range(k)]
+        edges = [sorted(set(r.randrange(k) for _ in range(r.randint(0, 3)))) for _ in range(k)]
+        protos = [f"__device__ {tys[j]} {names[j]}(int n);" for j in range(k)]
+        defs = []
+        for j in range(k):
+            terms = [f"({tys[j]}){names[c]}(n - {r.randint(1, 3)})" for c in edges[j]]
+            body = " + ".join(terms) if terms else f"({tys[j]})n"
+            defs.append(f"__device__ {tys[j]} {names[j]}(int n) {{ if (n <= 0) return ({tys[j]})1; "
+                        f"return {body}; }}")
+        order = list(range(k))
+        r.shuffle(order)
+        calls = " + ".join(f"(float){names[j]}(t & {r.randint(1, 7)})"
+                           for j in r.sample(range(k), r.randint(1, k)))
+        text = "\n".join(protos) + "\n" + "\n".join(defs[j] for j in order) + \
+            f"\n__global__ void rk{i}(float *o) {{ int t = threadIdx.x; o[t] = {calls}; }}\n"
+        out.append(text)
+    return out

@@ -4,12 +4,12 @@ void helpers, nested calls, prototypes and qualifiers, helpers defined after
 their callers, `&x` out-parameters spilled to .local, calls the reference's emitter has no
 case for -- compared with the live reference as parsed IR, optimized IR
 and PTX.  Recursive helpers, which the reference compiles to .func bodies,
-must come back as `unsupported`, never as different output."""
+are covered by test_recursive_gpu.py."""
 import pytest
 
 from oracle import ref_runner
 from opencuda.api import TU_UNSUPPORTED
-from tests._helpers import (ADDR_OF_CASES, CAST_CASES, DEVFUNC_CASES, DEVFUNC_RECURSIVE_CASES,
+from tests._helpers import (ADDR_OF_CASES, CAST_CASES, DEVFUNC_CASES,
                             ARRAY_PARAM_CASES, HEXFLOAT_CASES, INTRINSIC_CASES,
                             HALF_REDUCE_CASES, MORE_INTRINSIC_CASES, UNKNOWN_CALL_CASES,
                             devfunc_sources)
@@ -37,7 +37,3 @@ def test_device_functions_against_live_reference(ctx, stage):
         assert st == 0, (i, st, s[:300])
         assert tb.text(i) == r[stage], (i, s)
 
-
-def test_recursive_device_functions_are_reported_unsupported(ctx):
-    tb = ctx.compile_batch(DEVFUNC_RECURSIVE_CASES)
-    assert [int(s) for s in tb.status] == [TU_UNSUPPORTED] * len(DEVFUNC_RECURSIVE_CASES)
