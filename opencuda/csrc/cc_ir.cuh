@@ -242,7 +242,8 @@ OCB_HD inline Str utoa(Arena &a, uint64_t v) {
 // ---------------------------------------------------------------------------
 // types (ir/types.py): packed so that == is the reference's structural ==
 //   bits 0-3 scalar, 4-5 pointer depth, 6-8 outer address space,
-//   9 volatile of the innermost pointer, 10 volatile of the outer pointer
+//   9 volatile of the innermost pointer, 10 volatile of the outer pointer,
+//   16-31 the struct index of a StructTy (scalar code S_STRUCT)
 // ---------------------------------------------------------------------------
 typedef uint32_t Ty;
 enum : uint32_t {
@@ -262,21 +263,22 @@ OCB_HD inline uint32_t ty_as(Ty t) { return (t >> 6) & 7; }
 OCB_HD inline bool ty_vol(Ty t) {  // PtrTy.volatile of the outermost pointer
     return ty_depth(t) == 1 ? ((t >> 9) & 1) : ((t >> 10) & 1);
 }
-// PtrTy(pointee, as, vol); representable when only the outermost pointer has a
-// non-global address space and volatile sits on the innermost or outer one.
+// PtrTy(pointee, as, vol), up to three levels; representable when only the
+// outermost pointer has a non-global address space and volatile sits on the
+// innermost or outermost one.
 OCB_HD inline Ty ty_ptr(Ty pointee, uint32_t as, bool vol, bool &ok) {
     uint32_t d = ty_depth(pointee);
     if (d == 0) return pointee | (1u << 4) | (as << 6) | (vol ? 1u << 9 : 0);
-    if (d >= 2 || ty_as(pointee) != AS_GLOBAL || ((pointee >> 10) & 1)) {
+    if (d >= 3 || ty_as(pointee) != AS_GLOBAL || ((pointee >> 10) & 1)) {
         ok = false;
         return pointee;
     }
-    return (pointee & ~((3u << 4) | (7u << 6))) | (2u << 4) | (as << 6) | (vol ? 1u << 10 : 0);
+    return (pointee & ~((3u << 4) | (7u << 6))) | ((d + 1) << 4) | (as << 6) | (vol ? 1u << 10 : 0);
 }
 OCB_HD inline Ty ty_pointee(Ty t) {
     uint32_t d = ty_depth(t);
     if (d <= 1) return t & (15u | 0xFFFF0000u);
-    return (t & ~((3u << 4) | (7u << 6) | (1u << 10))) | (1u << 4) | (AS_GLOBAL << 6);
+    return (t & ~((3u << 4) | (7u << 6) | (1u << 10))) | ((d - 1) << 4) | (AS_GLOBAL << 6);
 }
 OCB_HD inline Ty ty_struct(uint32_t idx) { return S_STRUCT | (idx << 16); }
 OCB_HD inline bool ty_is_struct(Ty t) { return !is_ptr(t) && (t & 15) == S_STRUCT; }
