@@ -52,6 +52,40 @@ __device__ __forceinline__ bool pyspace(uint32_t c) {
 __device__ __forceinline__ bool isw(uint32_t c) {
     return (c | 0x20u) - 'a' < 26u || c - '0' < 10u || c == '_';
 }
+// A code point that Python's `\w` and `\s` both reject (Latin-1 signs and
+// punctuation, general punctuation without the spaces, currency signs,
+// arrows, mathematical operators, technical symbols, box drawing, shapes,
+// dingbats without the circled digits, Braille, more arrows): in such a
+// character the byte-wise scans here see what the reference's str-wise
+// regexes see.
+__device__ __forceinline__ bool neutral_cp(uint32_t c) {
+    if (c >= 0x80 && c <= 0xA9) return c != 0x85 && c != 0xA0;
+    if ((c >= 0xAB && c <= 0xB1) || c == 0xB4 || (c >= 0xB6 && c <= 0xB8) || c == 0xBB ||
+        c == 0xBF || c == 0xD7 || c == 0xF7)
+        return true;
+    if (c >= 0x2000 && c <= 0x206F)
+        return c > 0x200A && c != 0x2028 && c != 0x2029 && c != 0x202F && c != 0x205F;
+    return (c >= 0x20A0 && c <= 0x20CF) || (c >= 0x2190 && c <= 0x23FF) ||
+           (c >= 0x2500 && c <= 0x2775) || (c >= 0x2794 && c <= 0x2BFF);
+}
+// True when every non-ASCII character of the bytes is well-formed UTF-8 and
+// neutral (above).
+__device__ __forceinline__ bool neutral_utf8(const uint8_t *p, uint32_t n) {
+    for (uint32_t i = 0; i < n;) {
+        uint32_t b = p[i];
+        if (b < 0x80) { ++i; continue; }
+        uint32_t len = b >= 0xF0 ? 4 : b >= 0xE0 ? 3 : b >= 0xC0 ? 2 : 0;
+        if (!len || b >= 0xF8 || i + len > n) return false;
+        uint32_t cp = b & (0x7Fu >> len);
+        for (uint32_t q = 1; q < len; ++q) {
+            if ((p[i + q] & 0xC0) != 0x80) return false;
+            cp = (cp << 6) | (p[i + q] & 0x3F);
+        }
+        if (!neutral_cp(cp)) return false;
+        i += len;
+    }
+    return true;
+}
 
 enum : int { ST_OK = 0, ST_RE = OCB_TU_RAISES_REERROR, ST_UNSUP = OCB_TU_UNSUPPORTED,
              ST_OVF = OCB_TU_OVERFLOW, ST_TIMEOUT = OCB_TU_TIMEOUT };
@@ -1123,9 +1157,7 @@ struct TU {
         LBuf a{c.wb, 0, c.wcap / 2}, b{c.wb + c.wcap / 2, 0, c.wcap / 2};
         if (!a.append(c, line, n)) return;
         bool has_macros = any_live(fn) || any_live(obj);
-        if (has_macros)
-            for (uint32_t i = 0; i < n; ++i)
-                if (line[i] >= 0x80) { c.set(ST_UNSUP); return; }
+        if (has_macros && !neutral_utf8(line, n)) { c.set(ST_UNSUP); return; }
         Macro **order;
         uint32_t nf = dict_sorted(c, fn, order);
         if (nf) {
