@@ -104,6 +104,16 @@ void ocb_destroy(ocb_ctx *ctx) {
                       &ctx->rt_in_status, &ctx->rt_text, &ctx->rt_off, &ctx->rt_status,
                       &ctx->rt_qinc, &ctx->mg_text, &ctx->mg_off, &ctx->mg_status})
         b->release();
+    ctx->cc_ptext.release();
+    ctx->cc_pmeta.release();
+    for (int s = 0; s < ocb_ctx::kCCStreams; ++s) {
+        if (ctx->cc_streams[s]) {
+            stream_wait(ctx->cc_streams[s]);
+            cudaStreamDestroy(ctx->cc_streams[s]);
+        }
+        ctx->cc_arena_s[s].release();
+        ctx->cc_spill_s[s].release();
+    }
     ctx->h_stage.release();
     for (cudaEvent_t &e : ctx->kev)
         if (e) cudaEventDestroy(e);

@@ -42,10 +42,39 @@ __global__ void k_cc_pack(const uint8_t *out, const uint64_t *cap_off, const uin
     for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) d[k] = s[k];
 }
 
-// out_off[a + j] = base + pack_off[j] for the chunk's TUs (and the end entry)
-__global__ void k_cc_out_off(const uint64_t *pack_off, uint64_t base, uint64_t *out_off, uint32_t n) {
+// The batch gathered into processing order: TU perm[j] to position j; one
+// block per TU.
+__global__ void k_cc_gather(const uint8_t *src, const uint64_t *off, const uint32_t *perm,
+                            const uint64_t *poff, uint8_t *dst, uint32_t n_tu) {
+    uint32_t j = blockIdx.x;
+    if (j >= n_tu) return;
+    const uint8_t *s = src + off[perm[j]];
+    uint8_t *d = dst + poff[j];
+    uint64_t n = poff[j + 1] - poff[j];
+    for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) d[k] = s[k];
+}
+
+// st_p[j] = st[perm[j]]: the earlier stages' verdicts in processing order
+__global__ void k_cc_permute_status(const uint32_t *perm, const int32_t *st, int32_t *st_p,
+                                    uint32_t n) {
     uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j <= n) out_off[j] = base + pack_off[j];
+    if (j < n) st_p[j] = st[perm[j]];
+}
+
+// Back to input order: verdicts, output lengths and output slice offsets of
+// position j belong to TU perm[j]; len[n] = 0 closes the length scan.
+__global__ void k_cc_unpermute(const uint32_t *perm, const int32_t *st_p, const uint64_t *len_p,
+                               const uint64_t *cap_p, int32_t *st, uint64_t *len, uint64_t *cap,
+                               uint32_t n) {
+    uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) {
+        uint32_t i = perm[j];
+        st[i] = st_p[j];
+        len[i] = len_p[j];
+        cap[i] = cap_p[j];
+    } else if (j == n) {
+        len[n] = 0;
+    }
 }
 
 }  // namespace cc
@@ -60,10 +89,15 @@ static uint64_t env_u64(const char *name, uint64_t dflt) {
     return strtoull(v, nullptr, 10);
 }
 
-// Lex the batch, then parse/optimize/emit it chunk by chunk: each chunk's
-// per-TU arena slices (sized from the TU's token count) fit a memory budget
-// taken from the free device memory.  Outputs are packed back to back into
-// `out_text` with d_out_off[n_tu+1].
+// Compile a batch: gather its TUs largest first, lex them, then
+// parse/optimize/emit in chunks of consecutive TUs whose per-TU arena slices
+// (sized from the token count) fit a memory budget.  The chunks run on
+// several streams, each with its own arena, so the longest compiles (the
+// first chunks) overlap with the rest of the batch instead of forming a tail
+// of every chunk.  Every TU writes into its own slice of one output buffer;
+// at the end the texts are packed back to back in input order into
+// `out_text` with d_out_off[n_tu+1], and the verdicts go to d_status in input
+// order.
 int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d_off,
               uint32_t n_tu, const int32_t *d_in_status, int stage, uint32_t scale,
               DevBuf &out_text, uint64_t *d_out_off, int32_t *d_status, uint64_t *h_total,
@@ -75,32 +109,63 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
         return 0;
     }
     size_t n1 = (size_t)n_tu + 1;
+    PhaseTimer T(st);
+    // processing order: largest source first (stable), OCB_CC_ORDER=0 keeps input order
+    std::vector<uint64_t> h_off(n1);
+    OCB_TRY("cc: d2h", cudaMemcpyAsync(h_off.data(), d_off, 8 * n1, cudaMemcpyDeviceToHost, st));
+    OCB_TRY("cc: sync", stream_wait(st));
+    std::vector<uint32_t> h_perm(n_tu);
+    for (uint32_t i = 0; i < n_tu; ++i) h_perm[i] = i;
+    if (env_u64("OCB_CC_ORDER", 1) != 0)
+        std::stable_sort(h_perm.begin(), h_perm.end(), [&](uint32_t x, uint32_t y) {
+            return h_off[x + 1] - h_off[x] > h_off[y + 1] - h_off[y];
+        });
+    std::vector<uint64_t> h_poff(n1);
+    h_poff[0] = 0;
+    for (uint32_t j = 0; j < n_tu; ++j)
+        h_poff[j + 1] = h_poff[j] + (h_off[h_perm[j] + 1] - h_off[h_perm[j]]);
+    // meta: perm u32[n1] | poff | len_p | cap_p | len_o | cap_o (u64[n1] each)
+    //       | st_p i32[n1] | arena offsets u64[2 n1]
+    size_t m_perm = (4 * n1 + 15) & ~(size_t)15;
+    size_t m_u64 = 8 * n1;
+    size_t m_st = (4 * n1 + 15) & ~(size_t)15;
+    OCB_TRY("cc: meta", ctx->cc_pmeta.ensure(m_perm + 5 * m_u64 + m_st + 16 * n1 + 64));
+    uint8_t *mb = ctx->cc_pmeta.as<uint8_t>();
+    uint32_t *perm = (uint32_t *)mb;
+    uint64_t *poff = (uint64_t *)(mb + m_perm);
+    uint64_t *len_p = poff + n1;
+    uint64_t *cap_p = len_p + n1;
+    uint64_t *len_o = cap_p + n1;
+    uint64_t *cap_o = len_o + n1;
+    int32_t *st_p = (int32_t *)(cap_o + n1);
+    uint64_t *aoff_all = (uint64_t *)((uint8_t *)st_p + m_st);
+    OCB_TRY("cc: text", ctx->cc_ptext.ensure(N + 64));
+    uint8_t *ptext = ctx->cc_ptext.as<uint8_t>();
+    OCB_TRY("cc: h2d", cudaMemcpyAsync(perm, h_perm.data(), 4 * (size_t)n_tu,
+                                       cudaMemcpyHostToDevice, st));
+    OCB_TRY("cc: h2d", cudaMemcpyAsync(poff, h_poff.data(), 8 * n1, cudaMemcpyHostToDevice, st));
+    k_cc_gather<<<n_tu, 256, 0, st>>>(d_text, d_off, perm, poff, ptext, n_tu);
+    OCB_TRY("cc: gather", cudaGetLastError());
+    // lex the gathered batch (token starts are offsets into ptext)
     uint64_t tok_cap = N + n_tu + 16;
     OCB_TRY("cc: tokens", ctx->cc_tok.ensure(12 * tok_cap + 16));
-    OCB_TRY("cc: scratch", ctx->cc_scratch.ensure(8 * n1 * 5 + 8 + 4 * n1 + 64 + 16));
+    OCB_TRY("cc: scratch", ctx->cc_scratch.ensure(8 * n1 + 8 + 4 * n1 + 64 +
+                                                  16 * ocb_ctx::kCCStreams + 16));
     uint32_t *tstart = ctx->cc_tok.as<uint32_t>();
     uint32_t *tkl = tstart + tok_cap;
-    uint32_t *tline = tkl + tok_cap;
     uint64_t *tu_tok = ctx->cc_scratch.as<uint64_t>();
-    uint64_t *arena_off = tu_tok + n1;
-    uint64_t *out_cap_off = arena_off + n1;
-    uint64_t *out_len = out_cap_off + n1;
-    uint64_t *pack_off = out_len + n1;
-    uint64_t *n_tok = pack_off + n1;
+    uint64_t *n_tok = tu_tok + n1;
     int32_t *lex_status = (int32_t *)(n_tok + 1);
     unsigned long long *spill_top =
         (unsigned long long *)(((uintptr_t)(lex_status + n1) + 15) & ~(uintptr_t)15);
-    PhaseTimer T(st);
-    // the parser reads token starts and kinds only: no per-token lines
-    (void)tline;
-    int rc = lex_device(ctx, d_text, N, d_off, n_tu, tstart, tkl, nullptr, tok_cap, tu_tok,
+    int rc = lex_device(ctx, ptext, N, poff, n_tu, tstart, tkl, nullptr, tok_cap, tu_tok,
                         lex_status, n_tok, st);
     if (rc) return rc;
     T.mark("cc: lex");
-    OCB_TRY("cc: status", cudaMemcpyAsync(d_status, d_in_status, 4 * (size_t)n_tu,
-                                          cudaMemcpyDeviceToDevice, st));
     unsigned grid = (unsigned)((n1 + 255) / 256);
-    merge_status<<<grid, 256, 0, st>>>(d_status, lex_status, n_tu);
+    k_cc_permute_status<<<grid, 256, 0, st>>>(perm, d_in_status, st_p, n_tu);
+    merge_status<<<grid, 256, 0, st>>>(st_p, lex_status, n_tu);
+    OCB_TRY("cc: status", cudaGetLastError());
     std::vector<uint64_t> h_tok(n1);
     OCB_TRY("cc: d2h", cudaMemcpyAsync(h_tok.data(), tu_tok, 8 * n1, cudaMemcpyDeviceToHost, st));
     OCB_TRY("cc: sync", stream_wait(st));
@@ -117,124 +182,139 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     uint32_t spread = (uint32_t)env_u64("OCB_CC_SPREAD", 1);
     if (spread < 1) spread = 1;
     if (spread > 32) spread = 32;
+    // every TU's output slice, in processing order, in one buffer
+    std::vector<uint64_t> h_cap(n1);
+    h_cap[0] = 0;
+    for (uint32_t j = 0; j < n_tu; ++j)
+        h_cap[j + 1] = h_cap[j] + (((o0 + o1 * (h_tok[j + 1] - h_tok[j])) * scale + 15) & ~15ull);
     size_t free_b = 0, total_b = 0;
     OCB_TRY("cc: meminfo", cudaMemGetInfo(&free_b, &total_b));
-    uint64_t budget = (uint64_t)((double)(free_b + ctx->cc_arena.cap + ctx->cc_out.cap) * 0.45);
-    uint64_t budget_cap = env_u64("OCB_CC_BUDGET_MB", 24576) << 20;
+    uint64_t owned = ctx->cc_out.cap;
+    for (int q = 0; q < ocb_ctx::kCCStreams; ++q) owned += ctx->cc_arena_s[q].cap + ctx->cc_spill_s[q].cap;
+    uint64_t budget = (uint64_t)((double)(free_b + owned) * 0.45);
+    uint64_t budget_cap = env_u64("OCB_CC_BUDGET_MB", 73728) << 20;
     if (budget > budget_cap) budget = budget_cap;
-    if (budget < (256ull << 20)) budget = 256ull << 20;
-    // One eighth of the budget is the spill pool that TUs outgrowing their
-    // slice draw from (shared by every TU of a chunk, reset per chunk).
-    uint64_t spill_b = env_u64("OCB_CC_SPILL_MB", budget >> 23) << 20;
-    if (spill_b) {
-        OCB_TRY("cc: spill pool", ctx->cc_spill.ensure(spill_b));
-        budget -= spill_b < budget / 2 ? spill_b : budget / 2;
-    }
-    bool order_on = env_u64("OCB_CC_ORDER", 1) != 0;
-    OCB_TRY("cc: order", ctx->cc_order.ensure(4 * (size_t)n_tu + 16));
-    std::vector<uint32_t> h_order;
-    std::vector<uint64_t> h_aoff, h_ooff;
-    uint64_t running = 0;
-    uint32_t a = 0;
-    while (a < n_tu) {
-        // chunk [a, b): arena + output slices within the budget (at least one TU)
-        h_aoff.assign(1, 0);
-        h_ooff.assign(1, 0);
+    uint64_t out_total = h_cap[n_tu] + 64;
+    OCB_TRY("cc: out", ctx->cc_out.ensure(out_total));
+    uint64_t arena_budget = budget > out_total + (768ull << 20) ? budget - out_total : (768ull << 20);
+    int S = (int)env_u64("OCB_CC_STREAMS", 3);
+    if (S < 1) S = 1;
+    if (S > ocb_ctx::kCCStreams) S = ocb_ctx::kCCStreams;
+    uint64_t per_stream = arena_budget / S;
+    if (per_stream < (256ull << 20)) per_stream = 256ull << 20;
+    // One eighth of a stream's budget is the spill pool that its TUs outgrowing
+    // their slice draw from (shared by every TU of a chunk, reset per chunk).
+    uint64_t spill_b = env_u64("OCB_CC_SPILL_MB", per_stream >> 23) << 20;
+    uint64_t slice_budget = per_stream - (spill_b < per_stream / 2 ? spill_b : per_stream / 2);
+    // chunks: consecutive TUs of the processing order whose slices fit
+    std::vector<uint32_t> ch_a;
+    std::vector<uint64_t> h_aoff_all;
+    h_aoff_all.reserve(2 * n1);
+    uint64_t stream_need[ocb_ctx::kCCStreams] = {};
+    for (uint32_t a = 0; a < n_tu;) {
+        ch_a.push_back(a);
+        uint64_t run = 0;
+        h_aoff_all.push_back(0);
         uint32_t b = a;
         while (b < n_tu) {
-            uint64_t nt = h_tok[b + 1] - h_tok[b];
-            uint64_t as = ((a0 + a1 * nt) * scale + 15) & ~15ull;
-            uint64_t os = ((o0 + o1 * nt) * scale + 15) & ~15ull;
-            if (b > a && h_aoff.back() + as + h_ooff.back() + os > budget) break;
-            h_aoff.push_back(h_aoff.back() + as);
-            h_ooff.push_back(h_ooff.back() + os);
+            uint64_t as = ((a0 + a1 * (h_tok[b + 1] - h_tok[b])) * scale + 15) & ~15ull;
+            if (b > a && run + as > slice_budget) break;
+            run += as;
+            h_aoff_all.push_back(run);
             ++b;
         }
-        uint32_t nc = b - a;
-        OCB_TRY("cc: arena", ctx->cc_arena.ensure(h_aoff.back() + 64));
-        OCB_TRY("cc: out", ctx->cc_out.ensure(h_ooff.back() + 64));
-        OCB_TRY("cc: h2d", cudaMemcpyAsync(arena_off, h_aoff.data(), 8 * (size_t)(nc + 1),
-                                           cudaMemcpyHostToDevice, st));
-        OCB_TRY("cc: h2d", cudaMemcpyAsync(out_cap_off, h_ooff.data(), 8 * (size_t)(nc + 1),
-                                           cudaMemcpyHostToDevice, st));
-        OCB_TRY("cc: zero", cudaMemsetAsync(out_len, 0, 8 * (size_t)(nc + 1), st));
-        OCB_TRY("cc: zero", cudaMemsetAsync(spill_top, 0, 8, st));
-        if (order_on) {
-            // largest TUs (by tokens) first: the longest-running threads start
-            // in the first wave instead of forming the tail
-            h_order.resize(nc);
-            for (uint32_t j = 0; j < nc; ++j) h_order[j] = j;
-            std::stable_sort(h_order.begin(), h_order.end(), [&](uint32_t x, uint32_t y) {
-                return h_tok[a + x + 1] - h_tok[a + x] > h_tok[a + y + 1] - h_tok[a + y];
-            });
-            OCB_TRY("cc: h2d", cudaMemcpyAsync(ctx->cc_order.p, h_order.data(), 4 * (size_t)nc,
-                                               cudaMemcpyHostToDevice, st));
-        }
-        CCArgs A{d_text, tstart, tkl, tu_tok + a, nc, ctx->cc_arena.as<uint8_t>(), arena_off,
-                 ctx->cc_out.as<uint8_t>(), out_cap_off, out_len, d_status + a, stage, spread,
-                 ir_pm, nullptr, {}, order_on ? ctx->cc_order.as<uint32_t>() : nullptr,
-                 SpillPool{spill_b ? ctx->cc_spill.as<uint8_t>() : nullptr,
-                           spill_b ? spill_top : nullptr, spill_b}};
+        int s_ = (int)((ch_a.size() - 1) % S);
+        if (run + 64 > stream_need[s_]) stream_need[s_] = run + 64;
+        a = b;
+    }
+    ch_a.push_back(n_tu);
+    size_t n_ch = ch_a.size() - 1;
+    OCB_TRY("cc: h2d", cudaMemcpyAsync(cap_p, h_cap.data(), 8 * n1, cudaMemcpyHostToDevice, st));
+    OCB_TRY("cc: h2d", cudaMemcpyAsync(aoff_all, h_aoff_all.data(), 8 * h_aoff_all.size(),
+                                       cudaMemcpyHostToDevice, st));
+    OCB_TRY("cc: zero", cudaMemsetAsync(len_p, 0, 8 * n1, st));
+    OCB_TRY("cc: zero", cudaMemsetAsync(spill_top, 0, 16 * ocb_ctx::kCCStreams, st));
+    int used_streams = n_ch < (size_t)S ? (int)n_ch : S;
+    for (int q = 0; q < used_streams; ++q) {
+        if (!ctx->cc_streams[q])
+            OCB_TRY("cc: stream", cudaStreamCreateWithFlags(&ctx->cc_streams[q], cudaStreamNonBlocking));
+        OCB_TRY("cc: arena", ctx->cc_arena_s[q].ensure(stream_need[q]));
+        if (spill_b) OCB_TRY("cc: spill pool", ctx->cc_spill_s[q].ensure(spill_b));
+    }
+    cudaEvent_t ready;
+    OCB_TRY("cc: event", cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+    OCB_TRY("cc: event", cudaEventRecord(ready, st));
+    for (int q = 0; q < used_streams; ++q)
+        OCB_TRY("cc: event", cudaStreamWaitEvent(ctx->cc_streams[q], ready, 0));
+    T.mark("cc: setup");
+    bool kp = ctx->kprof_on;
+    std::vector<cudaEvent_t> kev;
+    if (kp) {
+        kev.resize(4 * n_ch);
+        for (auto &e : kev) OCB_TRY("cc: event", cudaEventCreate(&e));
+    }
+    unsigned long long *tops = spill_top;
+    for (size_t c = 0; c < n_ch; ++c) {
+        int q = (int)(c % S);
+        cudaStream_t ss = ctx->cc_streams[q];
+        uint32_t a = ch_a[c], nc = ch_a[c + 1] - a;
+        if (c >= (size_t)S)  // the stream's previous chunk drew on the same spill pool
+            OCB_TRY("cc: zero", cudaMemsetAsync(tops + 2 * q, 0, 8, ss));
+        CCArgs A{ptext, tstart, tkl, tu_tok + a, nc, ctx->cc_arena_s[q].as<uint8_t>(),
+                 aoff_all + a + c, ctx->cc_out.as<uint8_t>(), cap_p + a, len_p + a, st_p + a,
+                 stage, spread, ir_pm, nullptr, {}, nullptr,
+                 SpillPool{spill_b ? ctx->cc_spill_s[q].as<uint8_t>() : nullptr,
+                           spill_b ? tops + 2 * q : nullptr, spill_b}};
         memcpy(A.target, ctx->target, sizeof A.target);
         unsigned warps = (nc + spread - 1) / spread;
         unsigned blocks = (warps + 3) / 4;  // 4 warps (128 threads) per block
-        T.mark("cc: chunk setup");
-        bool kp = ctx->kprof_on;
-        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[0], st));
-        OCB_TRY("cc: parse launch", launch_k_cc_parse(A, blocks, 128, st));
-        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[1], st));
-        T.mark("cc: k_cc_parse");
-        if (stage_runs_opt(stage)) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, blocks, 128, st));
-        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[2], st));
-        T.mark("cc: k_cc_opt");
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(kev[4 * c], ss));
+        OCB_TRY("cc: parse launch", launch_k_cc_parse(A, blocks, 128, ss));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(kev[4 * c + 1], ss));
+        if (stage_runs_opt(stage)) OCB_TRY("cc: optimize launch", launch_k_cc_opt(A, blocks, 128, ss));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(kev[4 * c + 2], ss));
         if (stage <= CC_STAGE_PTX)
-            OCB_TRY("cc: emit launch", launch_k_cc_emit(A, blocks, 128, st));
+            OCB_TRY("cc: emit launch", launch_k_cc_emit(A, blocks, 128, ss));
         else
             OCB_TRY("cc: verify launch",
-                    launch_k_cc_verify(A, stage >= CC_STAGE_VERIFY_IR_REACH, blocks, 128, st));
-        if (kp) OCB_TRY("cc: event", cudaEventRecord(ctx->kev[3], st));
-        T.mark("cc: k_cc_emit");
-        size_t t1 = 0;
-        cub::DeviceScan::ExclusiveSum(nullptr, t1, out_len, pack_off, (int)(nc + 1), st);
-        OCB_TRY("cc: cub scratch", ctx->cub_tmp.ensure(t1));
-        OCB_TRY("cc: pack scan",
-                cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, out_len, pack_off, (int)(nc + 1), st));
-        uint64_t tot = 0;
-        OCB_TRY("cc: d2h", cudaMemcpyAsync(&tot, pack_off + nc, 8, cudaMemcpyDeviceToHost, st));
-        OCB_TRY("cc: sync", stream_wait(st));
-        if (kp) {
+                    launch_k_cc_verify(A, stage >= CC_STAGE_VERIFY_IR_REACH, blocks, 128, ss));
+        if (kp) OCB_TRY("cc: event", cudaEventRecord(kev[4 * c + 3], ss));
+    }
+    for (int q = 0; q < used_streams; ++q) {
+        OCB_TRY("cc: event", cudaEventRecord(ready, ctx->cc_streams[q]));
+        OCB_TRY("cc: event", cudaStreamWaitEvent(st, ready, 0));
+    }
+    cudaEventDestroy(ready);
+    T.mark("cc: chunks");
+    // back to input order, then the texts packed back to back
+    k_cc_unpermute<<<grid, 256, 0, st>>>(perm, st_p, len_p, cap_p, d_status, len_o, cap_o, n_tu);
+    OCB_TRY("cc: unpermute", cudaGetLastError());
+    size_t t1 = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, t1, len_o, d_out_off, (int)n1, st);
+    OCB_TRY("cc: cub scratch", ctx->cub_tmp.ensure(t1));
+    OCB_TRY("cc: pack scan",
+            cub::DeviceScan::ExclusiveSum(ctx->cub_tmp.p, t1, len_o, d_out_off, (int)n1, st));
+    uint64_t tot = 0;
+    OCB_TRY("cc: d2h", cudaMemcpyAsync(&tot, d_out_off + n_tu, 8, cudaMemcpyDeviceToHost, st));
+    OCB_TRY("cc: sync", stream_wait(st));
+    if (kp) {
+        for (size_t c = 0; c < n_ch; ++c)
             for (int k = 0; k < 3; ++k) {
                 if (k == 1 && !stage_runs_opt(stage)) continue;
                 float ms = 0;
-                OCB_TRY("cc: event time", cudaEventElapsedTime(&ms, ctx->kev[k], ctx->kev[k + 1]));
+                OCB_TRY("cc: event time", cudaEventElapsedTime(&ms, kev[4 * c + k], kev[4 * c + k + 1]));
                 ctx->kms[k] += ms;
                 ctx->kn[k] += 1;
             }
-        }
-        if (running + tot + 64 > out_text.cap) {  // grow, keeping what is packed so far
-            DevBuf nb;
-            size_t want = out_text.cap * 2;
-            if (want < running + tot + 64) want = running + tot + 64;
-            OCB_TRY("cc: output", nb.ensure(want));
-            if (running) OCB_TRY("cc: d2d", cudaMemcpyAsync(nb.p, out_text.p, running,
-                                                           cudaMemcpyDeviceToDevice, st));
-            OCB_TRY("cc: sync", stream_wait(st));
-            out_text.release();
-            out_text = nb;
-            nb.p = nullptr;
-            nb.cap = 0;
-        }
-        cc::k_cc_pack<<<nc, 128, 0, st>>>(ctx->cc_out.as<uint8_t>(), out_cap_off, pack_off,
-                                          out_text.as<uint8_t>() + running, nc);
-        cc::k_cc_out_off<<<(nc + 256) / 256, 256, 0, st>>>(pack_off, running, d_out_off + a, nc);
-        OCB_TRY("cc: pack launch", cudaGetLastError());
-        running += tot;
-        a = b;
-        T.mark("cc: pack");
+        for (auto &e : kev) cudaEventDestroy(e);
     }
+    OCB_TRY("cc: output", out_text.ensure(tot + 64));
+    cc::k_cc_pack<<<n_tu, 128, 0, st>>>(ctx->cc_out.as<uint8_t>(), cap_o, d_out_off,
+                                        out_text.as<uint8_t>(), n_tu);
+    OCB_TRY("cc: pack launch", cudaGetLastError());
     OCB_TRY("cc: sync", stream_wait(st));
-    *h_total = running;
+    T.mark("cc: pack");
+    *h_total = tot;
     return 0;
 }
-
 }  // namespace ocb

@@ -73,6 +73,13 @@ struct ocb_ctx {
     ocb::DevBuf cc_tok, cc_scratch, cc_arena, cc_out, cc_text, cc_off, cc_status, cc_in_status;
     // compiler: per-chunk TU order (largest first) and the shared spill pool
     ocb::DevBuf cc_order, cc_spill;
+    // compiler: the batch gathered largest first (text, offsets, permutation,
+    // statuses and lengths in that order) and the chunk streams, each with
+    // its own arena and spill pool
+    static constexpr int kCCStreams = 4;
+    ocb::DevBuf cc_ptext, cc_pmeta;
+    cudaStream_t cc_streams[kCCStreams] = {};
+    ocb::DevBuf cc_arena_s[kCCStreams], cc_spill_s[kCCStreams];
     // whole-pipeline result (res_*), rerun sub-batches (rt_*) and merge targets (mg_*)
     ocb::DevBuf res_text, res_off, res_status;
     ocb::DevBuf rt_src, rt_src_off, rt_idx, rt_map, rt_len, rt_in_status, rt_text, rt_off,
