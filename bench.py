@@ -8,12 +8,12 @@ Workload: the 262,144 seeded lognormal-size kernels (median 3 KB, sigma 1,
 f32 arithmetic, if/else depth <= 3, unrollable for loops of trip 2-16,
 atomics and __shfl_sync), compiled to PTX: preprocess -> lex -> parse ->
 optimize -> register allocation -> PTX text.  The batch, ordered by size
-(largest first), is cut into ``--slices`` consecutive slices of about equal
-bytes; one step compiles one slice, step k slice k % S, so K >= S timed
+(largest first), is cut into ``--slices`` (20) consecutive slices of about
+equal bytes; one step compiles one slice, step k slice k % S, so K = S timed
 steps compile the whole batch once (``value`` is then the whole job's
-throughput).  With N ranks (one per GPU) every slice is split across the
-ranks by bytes with greedy LPT (strong scaling: the job's total work does
-not depend on N).
+throughput).  Warm-up steps compile the smallest slices.  With N ranks
+(one per GPU) every slice is split across the ranks by bytes with greedy
+LPT (strong scaling: the job's total work does not depend on N).
 The working set of a step (GBs of compiler arenas) is far larger than L2, so
 no flush is needed between steps.
 
@@ -472,10 +472,10 @@ def compile_config(ctx, torch, dev, stream, srcs, gold_name, reps=1):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--slices", type=int, default=16,
+    ap.add_argument("--slices", type=int, default=20,
                     help="slices of the size-ordered batch; one step compiles one slice")
     ap.add_argument("--tus", type=int, default=C5_N,
                     help="first TUs of the batch to use (smaller only for profiling)")
@@ -530,8 +530,9 @@ def main():
         return ctx.compile_device(sh["d_src"].data_ptr(), sh["bytes"], sh["d_off"].data_ptr(),
                                   sh["n"], 2)
 
+    # warm-up on the smallest slices (module load, buffers, clocks)
     for w in range(args.warmup):
-        step(w % S)
+        step(S - 1 - (w % S))
     torch.cuda.synchronize()
     launches, launch_names = None, None
     if not args.no_launch_count:
