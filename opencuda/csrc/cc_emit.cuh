@@ -286,6 +286,17 @@ struct Emit {
     uint32_t pf_count;    // printf calls emitted in this kernel
     bool vprintf_decl;    // the module preamble declares vprintf
     Vec<Str> fmt_done;    // format labels already in the module preamble
+    // per kernel, by label: the last block with it and the number of blocks
+    // whose terminator targets it (built on first use; terminators do not
+    // change while a kernel is emitted)
+    struct LblEnt {
+        Str l;
+        int32_t blk;
+        uint32_t preds;
+    };
+    LblEnt *lt;
+    uint32_t lt_cap;
+    bool lt_ok;
 
     OCB_HD Emit(Module &mod, Arena &tmp_) : m(mod), ar(*mod.ar), tmp(tmp_), k(nullptr), fail(false) {
         preamble.init();
@@ -294,6 +305,9 @@ struct Emit {
         pf_idx = pf_count = 0;
         vprintf_decl = false;
         fmt_done.init();
+        lt = nullptr;
+        lt_cap = 0;
+        lt_ok = false;
     }
 #ifdef OCB_TRAP_UNSUP
     void unsup(int line = __builtin_LINE()) {
@@ -749,6 +763,7 @@ struct Emit {
     OCB_HD OCB_NI bool emit_devfn(Kernel &f, Vec<Str> &out);
     OCB_HD OCB_NI bool emit_kernel(Kernel &kk, Vec<Str> &out);
     OCB_HD int32_t block_by_label(Str l);
+    OCB_HD OCB_NI LblEnt *label_slot(Str l, bool create);
     OCB_HD uint32_t pred_count_of(Str l);
 };
 

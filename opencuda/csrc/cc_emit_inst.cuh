@@ -1609,20 +1609,54 @@ OCB_HD inline void Emit::emit_asm(const Inst &in) {
     }
 }
 
+// The label table of the kernel being emitted: open addressing over labels,
+// filled on first use with every block label and branch target.
+OCB_HD inline Emit::LblEnt *Emit::label_slot(Str l, bool create) {
+    if (!lt_ok) {
+        lt_ok = true;
+        uint32_t want = 3 * k->blocks.n + 8;
+        lt_cap = 16;
+        while (lt_cap < 2 * want) lt_cap *= 2;
+        lt = (LblEnt *)tmp.alloc(sizeof(LblEnt) * (uint64_t)lt_cap, 16);
+        if (!lt) { lt_cap = 0; unsup(); return nullptr; }
+        for (uint32_t i = 0; i < lt_cap; ++i) lt[i] = LblEnt{Str{nullptr, 0}, -1, 0};
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {  // the last block with a label wins
+            LblEnt *e = label_slot(B(k->blocks[i]).label, true);
+            if (e) e->blk = (int32_t)k->blocks[i];
+        }
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {  // a CondBrTerm counts once per label
+            const Term &t = B(k->blocks[i]).term;
+            if (t.kind == T_BR) {
+                LblEnt *e = label_slot(t.t, true);
+                if (e) e->preds++;
+            } else if (t.kind == T_CBR) {
+                LblEnt *e = label_slot(t.t, true);
+                if (e) e->preds++;
+                if (!eq(t.f, t.t)) {
+                    e = label_slot(t.f, true);
+                    if (e) e->preds++;
+                }
+            }
+        }
+    }
+    if (!lt_cap) return nullptr;
+    uint32_t h = hash(l) & (lt_cap - 1);
+    while (lt[h].l.p) {
+        if (eq(lt[h].l, l)) return &lt[h];
+        h = (h + 1) & (lt_cap - 1);
+    }
+    if (!create) return nullptr;
+    lt[h].l = l;
+    return &lt[h];
+}
 OCB_HD inline int32_t Emit::block_by_label(Str l) {
-    int32_t r = -1;
-    for (uint32_t i = 0; i < k->blocks.n; ++i)
-        if (eq(B(k->blocks[i]).label, l)) r = (int32_t)k->blocks[i];
-    return r;
+    LblEnt *e = label_slot(l, false);
+    return e ? e->blk : -1;
 }
 // number of blocks whose terminator targets `l` (a CondBrTerm counts once)
 OCB_HD inline uint32_t Emit::pred_count_of(Str l) {
-    uint32_t c = 0;
-    for (uint32_t i = 0; i < k->blocks.n; ++i) {
-        const Term &t = B(k->blocks[i]).term;
-        if ((t.kind == T_BR && eq(t.t, l)) || (t.kind == T_CBR && (eq(t.t, l) || eq(t.f, l)))) c++;
-    }
-    return c;
+    LblEnt *e = label_slot(l, false);
+    return e ? e->preds : 0;
 }
 
 // ---- _emit_term (emit.py:2887-3123) --------------------------------------------

@@ -552,6 +552,7 @@ OCB_HD inline bool Emit::emit_kernel(Kernel &kk, Vec<Str> &out) {
     for (int p = 0; p < PF_N; ++p) fb_count[p] = reg_counts[p] = 0;
     skip.init(tmp, 2 * k->blocks.n + 8);
     term_depth = 0;
+    lt_ok = false;
     // names must stay ASCII (the reference's \w is Unicode-aware)
     for (uint32_t i = 0; i < k->params.n; ++i)
         for (uint32_t q = 0; q < k->params[i].name.n; ++q)
@@ -847,6 +848,7 @@ OCB_HD inline bool Emit::emit_devfn(Kernel &kk, Vec<Str> &out) {
     for (int p = 0; p < PF_N; ++p) fb_count[p] = reg_counts[p] = 0;
     skip.init(tmp, 2 * k->blocks.n + 8);
     term_depth = 0;
+    lt_ok = false;
     pfs.init();
     pf_idx = pf_count = 0;
     for (uint32_t i = 0; i < k->params.n; ++i)

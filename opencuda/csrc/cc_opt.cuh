@@ -1499,6 +1499,44 @@ struct Opt {
         LabelMap lm;
         lm.build(tmp, m, k->blocks);
         build_const_defs();
+        // `add` definitions per value id in block-then-instruction order: the
+        // init scans below visit a value's definitions only, in the order
+        // the reference's scans over every block reach them.
+        uint32_t nv = nid();
+        uint32_t *astart = (uint32_t *)tmp.alloc(4ull * (nv + 2), 16);
+        if (!astart) return false;
+        for (uint32_t q = 0; q <= nv + 1; ++q) astart[q] = 0;
+        uint32_t nadd = 0;
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind != I_BIN || in.op != BO_ADD || in.dest < 0) continue;
+                uint32_t d = did(in);
+                if (d < nv) {
+                    astart[d + 1]++;
+                    nadd++;
+                }
+            }
+        }
+        for (uint32_t q = 0; q < nv; ++q) astart[q + 1] += astart[q];
+        uint32_t *aref_b = (uint32_t *)tmp.alloc(4ull * (nadd + 1), 16);
+        uint32_t *aref_i = (uint32_t *)tmp.alloc(4ull * (nadd + 1), 16);
+        uint32_t *afill = (uint32_t *)tmp.alloc(4ull * (nv + 1), 16);
+        if (!aref_b || !aref_i || !afill) return false;
+        for (uint32_t q = 0; q < nv; ++q) afill[q] = astart[q];
+        for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
+            Block &b = B(k->blocks[bi]);
+            for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
+                const Inst &in = I(b.insts[ii]);
+                if (in.kind != I_BIN || in.op != BO_ADD || in.dest < 0) continue;
+                uint32_t d = did(in);
+                if (d >= nv) continue;
+                aref_b[afill[d]] = bi;
+                aref_i[afill[d]] = b.insts[ii];
+                afill[d]++;
+            }
+        }
         for (uint32_t bi = 0; bi < k->blocks.n; ++bi) {
             uint32_t cb = k->blocks[bi];
             sat_seen = false;
@@ -1582,12 +1620,12 @@ struct Opt {
             auto in_loop = [&](Str l) { return eq(l, ll[0]) || eq(l, ll[1]) || eq(l, ll[2]); };
             uint32_t ind_id = vid(ind);
             pyint init = 0;
-            for (uint32_t sb = 0; sb < k->blocks.n; ++sb) {
-                Block &b = B(k->blocks[sb]);
+            for (uint32_t ap = ind_id < nv ? astart[ind_id] : 0;
+                 ind_id < nv && ap < astart[ind_id + 1]; ++ap) {
+                Block &b = B(k->blocks[aref_b[ap]]);
                 if (in_loop(b.label)) continue;
-                for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
-                    const Inst &in = I(b.insts[ii]);
-                    if (in.kind != I_BIN || in.op != BO_ADD || did(in) != ind_id) continue;
+                {
+                    const Inst &in = I(aref_i[ap]);
                     pyint z;
                     if (in.b.k == O_CONST) {
                         if (!opnd_int(in.b, z)) return false;
@@ -1649,12 +1687,12 @@ struct Opt {
                 }
                 bool have_init = false;
                 pyint sinit = 0;
-                for (uint32_t sb = 0; sb < k->blocks.n; ++sb) {
-                    Block &b = B(k->blocks[sb]);
+                for (uint32_t ap = c.cid < nv ? astart[c.cid] : 0;
+                     c.cid < nv && ap < astart[c.cid + 1]; ++ap) {
+                    Block &b = B(k->blocks[aref_b[ap]]);
                     if (in_loop(b.label)) continue;
-                    for (uint32_t ii = 0; ii < b.insts.n; ++ii) {
-                        const Inst &in = I(b.insts[ii]);
-                        if (in.kind != I_BIN || in.op != BO_ADD || did(in) != c.cid) continue;
+                    {
+                        const Inst &in = I(aref_i[ap]);
                         pyint z;
                         if (in.b.k == O_CONST) {
                             if (!opnd_int(in.b, z)) return false;
@@ -1701,6 +1739,8 @@ struct Opt {
         Vec<ULoop> loops;
         if (!find_unrollable(loops)) return 0;
         uint32_t count = 0;
+        Vec<Str> gone;  // labels of the unrolled loops' body and increment blocks
+        gone.init();
         // Id-indexed tables shared by every loop of this call, sized for the
         // values all of them can add, filled once and told apart by stamps:
         // remap entries by iteration (gen), carried remaps by loop, the
@@ -1815,14 +1855,21 @@ struct Opt {
             }
             B(L.cond_b).insts = all;
             set_br(L.cond_b, B(L.exit_b).label);
-            Str bl = B(L.body_b).label, il = B(L.inc_b).label;
-            uint32_t w = 0;
-            for (uint32_t j = 0; j < k->blocks.n; ++j) {
-                Str l = B(k->blocks[j]).label;
-                if (!eq(l, bl) && !eq(l, il)) k->blocks[w++] = k->blocks[j];
-            }
-            k->blocks.n = w;
+            // the loop's body and increment blocks leave the kernel (by label);
+            // the filter runs once for every unrolled loop of this call, which
+            // removes the same blocks as a filter per loop
+            gone.push(tmp, B(L.body_b).label);
+            gone.push(tmp, B(L.inc_b).label);
             count++;
+        }
+        if (count) {
+            LabelSet gs;
+            gs.init(tmp, gone.n + 8);
+            for (uint32_t q = 0; q < gone.n; ++q) gs.add(gone[q]);
+            uint32_t w = 0;
+            for (uint32_t j = 0; j < k->blocks.n; ++j)
+                if (!gs.has(B(k->blocks[j]).label)) k->blocks[w++] = k->blocks[j];
+            k->blocks.n = w;
         }
         return count;
     }
