@@ -1140,9 +1140,69 @@ struct Opt {
     }
 
     // ---- merge_linear_chains (optimize.py:1076-1131) ---------------------------
+    // The reference restarts its scan from the first block after every merge.
+    // With unique labels a merge leaves every remaining label's predecessor
+    // count as it was (A takes over B's terminator, B disappears), so no block
+    // before the merge point can start to qualify: one forward scan that
+    // re-examines the merging block until it stops qualifying performs the
+    // same merges in the same order.  Duplicate labels take the restarting
+    // scan.
+    OCB_HD bool merge_linear_chains_fast(uint32_t &merged) {
+        size_t mark = tmp.used;
+        LabelSet seen;
+        seen.init(tmp, k->blocks.n + 2);
+        for (uint32_t i = 0; i < k->blocks.n; ++i)
+            if (!seen.add(B(k->blocks[i]).label)) {
+                tmp.used = mark;
+                return false;
+            }
+        LabelMap lm;
+        lm.build(tmp, m, k->blocks);
+        const uint32_t GONE = 0xffffffffu;
+        IdArr<uint32_t> pc;
+        pc.init(tmp, m.blocks.n, 0);
+        if (!pc.n || !lm.cap) {
+            tmp.used = mark;
+            return false;
+        }
+        for (uint32_t i = 0; i < k->blocks.n; ++i) {
+            Str s[2];
+            int ns = succs(k->blocks[i], s);
+            for (int q = 0; q < ns; ++q) {
+                int32_t b = lm.get(s[q]);
+                if (b >= 0) pc.set((uint32_t)b, pc.get((uint32_t)b) + 1);
+            }
+        }
+        uint32_t i = 0, removed = 0;
+        while (i < k->blocks.n && !bad()) {
+            uint32_t bb = k->blocks[i];
+            if (pc.get(bb) != GONE && B(bb).term.kind == T_BR) {
+                int32_t tb = lm.get(B(bb).term.t);
+                if (tb >= 0 && pc.get((uint32_t)tb) == 1) {
+                    uint32_t tn = B((uint32_t)tb).insts.n;
+                    for (uint32_t q = 0; q < tn; ++q) B(bb).insts.push(ar, B((uint32_t)tb).insts[q]);
+                    B(bb).term = B((uint32_t)tb).term;
+                    pc.set((uint32_t)tb, GONE);
+                    merged++;
+                    removed++;
+                    continue;
+                }
+            }
+            ++i;
+        }
+        if (removed) {
+            uint32_t w = 0;
+            for (uint32_t j = 0; j < k->blocks.n; ++j)
+                if (pc.get(k->blocks[j]) != GONE) k->blocks[w++] = k->blocks[j];
+            k->blocks.n = w;
+        }
+        tmp.used = mark;
+        return true;
+    }
     OCB_HD uint32_t merge_linear_chains() {
         if (!k->blocks.n) return 0;
         uint32_t merged = 0;
+        if (merge_linear_chains_fast(merged)) return merged;
         bool changed = true;
         while (changed && !bad()) {
             changed = false;
