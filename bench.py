@@ -207,23 +207,34 @@ def synth_pack(srcs):
     return api.pack_sources(srcs)
 
 
-def slice_plan(sizes, n_slices: int, world: int):
-    """Per slice, per rank: the TU indices that rank compiles.  The batch is
-    ordered by size, largest first, and cut into ``n_slices`` consecutive
-    slices of about equal bytes (so one slice holds the largest kernels and
-    the last the smallest); each slice is split across ranks by bytes with
-    greedy LPT (``opencuda.partition_lpt``), largest TUs first."""
+def slice_plan(sizes, n_slices: int, world: int, mode: str = "sorted"):
+    """Per slice, per rank: the TU indices that rank compiles.
+
+    ``sorted``: the batch is ordered by size, largest first, and cut into
+    ``n_slices`` consecutive slices of about equal bytes (one slice holds the
+    largest kernels, the last the smallest).  ``dealt``: the TUs are dealt to
+    the slices by bytes with greedy LPT, so every slice holds the same mix of
+    sizes (and one of the largest kernels each).  Each slice is then split
+    across ranks by bytes with greedy LPT (``opencuda.partition_lpt``),
+    largest TUs first."""
     from opencuda import partition_lpt
     sizes = np.asarray(sizes, dtype=np.int64)
-    order = np.argsort(-sizes, kind="stable")
-    cum = np.cumsum(sizes[order])
-    total = int(cum[-1]) if len(cum) else 0
-    # slice of each position: by the bytes before it
-    before = cum - sizes[order]
-    sl = np.minimum((before * n_slices) // max(total, 1), n_slices - 1)
+    if mode == "dealt":
+        slices = [np.asarray(p, dtype=np.int64)
+                  for p in partition_lpt(sizes.tolist(), n_slices)]
+    elif mode == "sorted":
+        order = np.argsort(-sizes, kind="stable")
+        cum = np.cumsum(sizes[order])
+        total = int(cum[-1]) if len(cum) else 0
+        # slice of each position: by the bytes before it
+        before = cum - sizes[order]
+        sl = np.minimum((before * n_slices) // max(total, 1), n_slices - 1)
+        slices = [order[sl == j] for j in range(n_slices)]
+    else:
+        raise ValueError(f"slice mode {mode!r}")
     plan = []
     for j in range(n_slices):
-        idx = order[sl == j]
+        idx = slices[j]
         parts = partition_lpt(sizes[idx].tolist(), world)
         plan.append([idx[np.asarray(p, dtype=np.int64)] if p else np.zeros(0, np.int64)
                      for p in parts])
@@ -476,7 +487,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--slices", type=int, default=20,
-                    help="slices of the size-ordered batch; one step compiles one slice")
+                    help="slices of the batch; one step compiles one slice")
+    ap.add_argument("--slicing", choices=["sorted", "dealt"], default="sorted",
+                    help="sorted: consecutive slices of the size-ordered batch; "
+                         "dealt: TUs dealt to slices by bytes (same size mix in every slice)")
     ap.add_argument("--tus", type=int, default=C5_N,
                     help="first TUs of the batch to use (smaller only for profiling)")
     ap.add_argument("--e2e-steps", type=int, default=None,
@@ -510,7 +524,7 @@ def main():
     n_all = min(args.tus, len(off_all) - 1)
     sizes = np.diff(off_all[:n_all + 1]).astype(np.int64)
     S = max(1, min(args.slices, n_all))
-    plan = slice_plan(sizes, S, world)
+    plan = slice_plan(sizes, S, world, args.slicing)
     mine = [plan[j][rank] for j in range(S)]
     ctx = api.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream, device=dev)
@@ -683,7 +697,7 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": {"workload": WORKLOAD if n_all == C5_N
                        else f"first {n_all} of the 262,144 lognormal-size kernels",
-                       "n_kernels": n_all, "seed": C5_SEED, "slices": S,
+                       "n_kernels": n_all, "seed": C5_SEED, "slices": S, "slicing": args.slicing,
                        "slices_timed": distinct, "tus_timed": int(
                            allreduce(float(n_tus_timed), world, dev, "sum")),
                        "source_bytes_timed": int(total_src),

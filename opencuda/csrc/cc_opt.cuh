@@ -2028,8 +2028,10 @@ struct Opt {
     }
 
     // Content hash of the kernel's IR: blocks (labels, order, terminators),
-    // instructions with their operands (values by id/type/name, constants by
-    // type and Python value) and the next value id.
+    // instructions with their operands (values by record, constants by type
+    // and Python value) and the next value id.  A value record (id, type,
+    // name) is immutable and new ones advance the next value id, so equal
+    // hashes across a round still mean equal content.
     OCB_HD void fingerprint(uint64_t out[2]) {
         uint64_t h1 = 1469598103934665603ull, h2 = 0x9E3779B97F4A7C15ull;
         auto mix = [&](uint64_t v) {
@@ -2043,10 +2045,7 @@ struct Opt {
         auto mix_op = [&](Opnd o) {
             mix(o.k);
             if (o.k == O_VAL) {
-                const Value &v = m.vals[o.x];
-                mix(v.id);
-                mix(v.ty);
-                mix_str(v.name);
+                mix(o.x);  // value records are never changed once made
             } else if (o.k == O_CONST) {
                 const Const &c = m.consts[o.x];
                 mix(c.ty);

@@ -66,3 +66,24 @@ def test_two_gloo_ranks_shard_and_reduce():
     assert t0 == t1 == b0 + b1 == n0      # whole-job bytes
     assert abs(b0 - b1) < 0.25 * n0       # balanced by bytes
     assert m0 == m1 == 2.0                # max over ranks
+
+
+def test_slice_plans_cover_the_batch_once():
+    sys.path.insert(0, str(ROOT))
+    import numpy as np
+
+    import bench
+    rng = np.random.default_rng(3)
+    sizes = rng.lognormal(8.0, 1.0, 5000).astype(np.int64) + 1
+    for mode in ("sorted", "dealt"):
+        for world in (1, 3):
+            plan = bench.slice_plan(sizes, 7, world, mode)
+            got = np.sort(np.concatenate([p for sl in plan for p in sl]))
+            assert np.array_equal(got, np.arange(len(sizes)))
+            per_slice = [int(sum(sizes[p].sum() for p in sl)) for sl in plan]
+            assert abs(max(per_slice) - min(per_slice)) <= int(sizes.max())
+    sorted_plan = bench.slice_plan(sizes, 7, 1, "sorted")
+    assert int(sizes[sorted_plan[0][0]].min()) >= int(sizes[sorted_plan[1][0]].max())
+    dealt = bench.slice_plan(sizes, 7, 1, "dealt")
+    top7 = set(np.argsort(-sizes, kind="stable")[:7].tolist())
+    assert {int(sl[0][0]) for sl in dealt} == top7    # one of the largest per slice
