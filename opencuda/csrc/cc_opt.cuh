@@ -434,6 +434,25 @@ struct Opt {
                 npred[o]++;
             }
         }
+        // With unique labels a block's final table is read only by the later
+        // blocks whose single predecessor it is; the last of them takes the
+        // table itself instead of a copy (nothing reads it afterwards).
+        uint32_t *readers = nullptr;
+        {
+            size_t mark = tmp.used;
+            LabelSet ls;
+            ls.init(tmp, nb + 2);
+            bool uniq = ls.cap != 0;
+            for (uint32_t i = 0; i < nb && uniq; ++i) uniq = ls.add(B(k->blocks[i]).label);
+            tmp.used = mark;
+            if (uniq) {
+                readers = (uint32_t *)tmp.alloc(4ull * (nb + 1), 16);
+                if (!readers) return 0;
+                for (uint32_t i = 0; i < nb; ++i) readers[i] = 0;
+                for (uint32_t i = 0; i < nb; ++i)
+                    if (npred[i] == 1 && pred0[i] >= 0 && (uint32_t)pred0[i] < i) readers[pred0[i]]++;
+            }
+        }
         IdArr<uint32_t> rstamp;  // per-block replacements: stamp = ordinal
         rstamp.init(tmp, n0, 0xFFFFFFFFu);
         uint32_t *rval = (uint32_t *)tmp.alloc(4ull * (n0 ? n0 : 1), 16);
@@ -450,7 +469,9 @@ struct Opt {
             uint32_t np = my >= 0 ? npred[my] : 0;
             int32_t p0 = my >= 0 ? pred0[my] : -1;
             if (np == 1 && p0 >= 0 && has_final[lab_ord(B(k->blocks[p0]).label)]) {
-                if (!seen.copy_from(tmp, final_seen[lab_ord(B(k->blocks[p0]).label)])) return eliminated;
+                int32_t po = lab_ord(B(k->blocks[p0]).label);
+                if (readers && --readers[po] == 0) seen = final_seen[po];
+                else if (!seen.copy_from(tmp, final_seen[po])) return eliminated;
             } else {
                 if (!seen.init(tmp, 64, m.consts.p)) return eliminated;
             }
