@@ -16,6 +16,30 @@ cudaError_t launch_k_cc_opt(const CCArgs &A, unsigned grid, unsigned block, cuda
 cudaError_t launch_k_cc_emit(const CCArgs &A, unsigned grid, unsigned block, cudaStream_t st);
 cudaError_t launch_k_cc_verify(const CCArgs &A, int check_reach, unsigned grid, unsigned block,
                                cudaStream_t st);
+const void *k_cc_parse_entry();
+const void *k_cc_opt_entry();
+const void *k_cc_emit_entry();
+
+// The compiler kernels use no shared memory and wait mostly on loads of their
+// TU's IR, so the unified L1/shared array is offered to L1 (carveout 0 = all
+// of it).  OCB_CC_CARVEOUT selects another percentage, -1 leaves the driver's
+// choice.  Set once per process.
+static cudaError_t cc_set_carveout() {
+    static int done = 0;
+    if (done) return cudaSuccess;
+    const char *v = getenv("OCB_CC_CARVEOUT");
+    long c = (v && *v) ? atol(v) : 0;
+    if (c >= 0) {
+        if (c > 100) c = 100;
+        const void *fs[3] = {k_cc_parse_entry(), k_cc_opt_entry(), k_cc_emit_entry()};
+        for (const void *f : fs) {
+            cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, (int)c);
+            if (e != cudaSuccess) return e;
+        }
+    }
+    done = 1;
+    return cudaSuccess;
+}
 
 // Stages beyond CC_STAGE_PTX: the IR verifier's error text after parse (3)
 // or after optimize (4); 5 and 6 are the same with check_reachability.
@@ -169,6 +193,7 @@ int cc_device(ocb_ctx *ctx, const uint8_t *d_text, uint64_t N, const uint64_t *d
     std::vector<uint64_t> h_tok(n1);
     OCB_TRY("cc: d2h", cudaMemcpyAsync(h_tok.data(), tu_tok, 8 * n1, cudaMemcpyDeviceToHost, st));
     OCB_TRY("cc: sync", stream_wait(st));
+    OCB_TRY("cc: carveout", cc_set_carveout());
     size_t cur_stack = 0;
     OCB_TRY("cc: stack limit", cudaDeviceGetLimit(&cur_stack, cudaLimitStackSize));
     if (cur_stack < kCCStack) OCB_TRY("cc: stack limit", cudaDeviceSetLimit(cudaLimitStackSize, kCCStack));
