@@ -1,6 +1,12 @@
 // Compiler kernel 2 of 3: optimize each TU's IR in place (one thread per TU).
 #include <cuda_runtime.h>
 #include "../../include/ocb.h"
+// Four resident blocks per SM (128 registers, 16 warps): a few spills, more
+// TUs in flight than at the uncapped 168 registers (12 warps); faster on the
+// lognormal batch.
+#ifndef OCB_CC_MIN_BLOCKS_OPT
+#define OCB_CC_MIN_BLOCKS_OPT 4
+#endif
 #include "cc_state.cuh"
 #include "cc_opt.cuh"
 
