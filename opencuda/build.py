@@ -11,6 +11,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -63,8 +64,12 @@ def _compile(nvcc: str, src: Path, verbose: bool) -> Path:
            "-c", str(src), "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
+    t0 = time.time()
     subprocess.run(cmd, check=True)
     os.replace(tmp, obj)
+    # the object is as new as the sources it was compiled from: an edit made
+    # while nvcc ran leaves it stale
+    os.utime(obj, (t0, t0))
     return obj
 
 
@@ -82,7 +87,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if stale or any(o.stat().st_mtime > lib_t for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
         cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
-               "-Xcompiler", "-fPIC", "-o", str(tmp), *map(str, objs)]
+               "-Xcompiler", "-fPIC", "-Xlinker", "--no-undefined",
+               "-o", str(tmp), *map(str, objs)]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
