@@ -33,7 +33,7 @@ TUs whose PTX is byte-identical.
                  reference_raises, unsupported, mismatched).
 * ``roofline``-- the dominant kernel: compile bytes (source + PTX of the TUs
                  of one launch) / mean launch time, against the measured HBM
-                 copy peak; ``traffic`` from an ncu capture, per TU.
+                 copy peak; ``traffic`` from an ncu capture, per algorithmic byte.
 * ``cpu_baseline`` -- the reference compiler (pure Python) on all host cores
                  over an evenly spaced sample of the batch.
 * ``lexer``   -- the batch lexer over 1 GiB of lexer stress text per GPU.
@@ -75,11 +75,12 @@ WORKLOAD = ("262,144 seeded lognormal-size kernels (median 3 KB, sigma 1, 1.20 G
             "compiled to PTX")
 CACHE = ROOT / "baseline" / "_ref" / "cache"
 
-# DRAM bytes (read + write) per TU of k_cc_opt from an ncu capture of one
-# launch over the first 256 kernels of the random-kernel workload (370.5 MB
-# read + 760.2 MB written); a full launch is too large to capture under ncu,
-# so the figure is scaled by the TUs of one launch.
-NCU_OPT_DRAM_BYTES_PER_TU = (370.5e6 + 760.2e6) / 256
+# DRAM bytes (read + write) of k_cc_opt per algorithmic byte (source + PTX of
+# the TUs of the launch), from an ncu capture of one launch over the ~400
+# smallest of the first 512 lognormal kernels (65.3 MB read + 76.4 MB written
+# for 5.5 MB of source and PTX); a full launch is too large to capture under
+# ncu, so the figure is scaled by the algorithmic bytes of one launch.
+NCU_OPT_DRAM_BYTES_PER_ALG_BYTE = (65.26e6 + 76.41e6) / 5.54e6
 
 
 def measured_peak():
@@ -604,7 +605,7 @@ def main():
     alg_per_launch = (src_bytes + ptx_bytes) / max(dom_n, 1)
     t_launch = dom_ms / 1e3 / max(dom_n, 1)
     achieved = alg_per_launch / t_launch / 1e9 if t_launch > 0 else 0.0
-    traffic = (NCU_OPT_DRAM_BYTES_PER_TU * tus_per_launch if dom == "k_cc_opt" else None)
+    traffic = (NCU_OPT_DRAM_BYTES_PER_ALG_BYTE * alg_per_launch if dom == "k_cc_opt" else None)
     ktot = sum(v[0] for v in ktimes.values())
     kernels = {x: {"ms_total": v[0], "launches": v[1],
                    "share_of_compile_kernels": (v[0] / ktot if ktot else None),
