@@ -187,7 +187,7 @@ struct Parser {
     uint32_t cur;         // current block index
     VarMap vars;
     uint32_t block_count;
-    Vec<uint64_t> copy_chain;  // (dest id << 32 | value index + 1) pairs
+    Vec<uint32_t> copy_src;  // by dest id: value index + 1 of its latest identity copy (0 none)
     VarMap row_strides;        // name -> Const index holding the row stride
     VarMap global_consts;      // module-level names bound to constants
     Vec<TypedefEnt> user_typedefs;  // typedef / enum tag names of this TU, in order
@@ -217,7 +217,7 @@ struct Parser {
         cur = 0;
         vars.init();
         block_count = 0;
-        copy_chain.init();
+        copy_src.init();
         row_strides.init();
         global_consts.init();
         user_typedefs.init();
@@ -345,12 +345,11 @@ struct Parser {
         if (i.kind == I_BIN && i.op == BO_ADD && i.b.k == O_CONST && i.a.k == O_VAL &&
             i.dest >= 0 && const_is_zero(i.b)) {
             uint32_t id = m.vals[i.dest].id;
-            for (uint32_t k = 0; k < copy_chain.n; ++k)
-                if ((uint32_t)(copy_chain[k] >> 32) == id) {
-                    copy_chain[k] = ((uint64_t)id << 32) | (i.a.x + 1);
-                    return;
-                }
-            copy_chain.push(ar, ((uint64_t)id << 32) | (i.a.x + 1));
+            if (id >= copy_src.n) {
+                if (!copy_src.reserve(ar, id + 1)) return;
+                while (copy_src.n <= id) copy_src.p[copy_src.n++] = 0;
+            }
+            copy_src.p[id] = i.a.x + 1;
         }
     }
     OCB_HD bool const_is_zero(Opnd o) {  // inst.rhs.value == 0 (Python 0 == 0.0)
@@ -553,9 +552,7 @@ struct Parser {
 
     // _loop_writeback (parser.py:256-364)
     OCB_HD Opnd chain_src(uint32_t id) {
-        for (uint32_t k = 0; k < copy_chain.n; ++k)
-            if ((uint32_t)(copy_chain[k] >> 32) == id)
-                return ov((uint32_t)(copy_chain[k] & 0xFFFFFFFFu) - 1);
+        if (id < copy_src.n && copy_src.p[id]) return ov(copy_src.p[id] - 1);
         return onone();
     }
     OCB_HD Opnd root(Opnd v) {

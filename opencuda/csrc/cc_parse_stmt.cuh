@@ -1221,7 +1221,7 @@ OCB_HD inline void Parser::parse_kernel() {
     vars.init();
     block_count = 0;
     isrf.init();
-    copy_chain.init();
+    copy_src.init();
     uint32_t entry = new_block("entry");
     cur = entry;
     NameSet seen;
